@@ -1,0 +1,20 @@
+"""B200-native (sm_100a) activation-sparse FFN hot path with the reference's API.
+
+Reference: Maccy-Z/autoresearch2 (old/lib_sparse/sparse.py, old/sparse_pack.py,
+old/sparse_unpack.py, old/full_matmul/sparse_pack.py).  All compute runs in
+libsparseffn.so (hand-written CUDA for sm_100a behind a C ABI,
+include/sparseffn.h); there is no CPU or fallback path.
+"""
+from .bitsparse import (BitsparseTensor, TensorBuffer, bitsparse_pack, bitsparse_unpack,
+                        check_status, dense_to_tilesparse, get_globals, grad_relu2_,
+                        init_sparse_buffer, mask_with_bitmask_, reset_sparse_globals, spAx,
+                        tile_unpack)
+from .ffn import FFNSparse, FFNSpRelu2
+from . import tiled
+
+__all__ = [
+    "BitsparseTensor", "TensorBuffer", "bitsparse_pack", "bitsparse_unpack", "check_status",
+    "dense_to_tilesparse", "get_globals", "grad_relu2_", "init_sparse_buffer",
+    "mask_with_bitmask_", "reset_sparse_globals", "spAx", "tile_unpack", "FFNSparse",
+    "FFNSpRelu2", "tiled",
+]

@@ -1,0 +1,139 @@
+"""ctypes binding of libsparseffn.so (the C ABI declared in include/sparseffn.h).
+
+The library is the only compute path: if it is missing, every operation
+raises instead of falling back to another implementation.
+"""
+import ctypes
+import os
+
+import torch
+
+PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(PKG, "libsparseffn.so")
+
+F32, BF16, F16 = 0, 1, 2
+_DTYPES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+STATUS_BITS = {
+    1: "vals capacity exceeded (output clipped)",
+    2: "bounded device wait timed out",
+    4: "int32 arena cursor overflow",
+    8: "mask has more set bits than vals holds",
+}
+
+
+class SparseFFNError(RuntimeError):
+    """Raised when the CUDA library reports an error."""
+
+
+_vp, _i64, _i32, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int, ctypes.c_size_t
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "sffn_version": (_int, []),
+    "sffn_error_string": (ctypes.c_char_p, [_int]),
+    "sffn_last_cuda_error": (ctypes.c_char_p, []),
+    "sffn_flat_workspace_bytes": (_sz, [_i64]),
+    "sffn_flat_pack": (_int, [_vp, _int, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp, _vp]),
+    "sffn_flat_unpack": (_int, [_vp, _i64, _vp, _int, _i64, _vp, _vp, _sz, _vp, _vp]),
+    "sffn_tile_workspace_bytes": (_sz, [_i64, _i64, _int, _int]),
+    "sffn_tile_pack": (_int, [_vp, _int, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp,
+                              _vp, _vp, _sz, _vp, _vp]),
+    "sffn_tile_unpack": (_int, [_vp, _i64, _vp, _vp, _vp, _int, _i64, _i64, _int, _int, _i64,
+                                _i64, _int, _vp, _int, _i64, _vp]),
+    "sffn_tile_mask_grad": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _int, _vp]),
+    "sffn_tile_grad_relu2": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
+                                    _int, _int, _vp]),
+}
+
+_lib = None
+
+
+def load():
+    """Load libsparseffn.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `python -m autoresearch2_b200.build` "
+                "(this package has no CPU or fallback path)")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+# Entry points that launch exactly one kernel of this library per call.
+LAUNCHING = {"sffn_flat_pack", "sffn_flat_unpack", "sffn_tile_pack", "sffn_tile_unpack",
+             "sffn_tile_mask_grad", "sffn_tile_grad_relu2"}
+launch_count = 0
+
+
+def call(name, *args):
+    """Call a C-ABI entry point and raise SparseFFNError on a non-zero code."""
+    global launch_count
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc == 0 and name in LAUNCHING:
+        launch_count += 1
+    if rc != 0:
+        msg = lib.sffn_error_string(rc).decode()
+        if rc == 5:
+            msg += f" ({lib.sffn_last_cuda_error().decode()})"
+        raise SparseFFNError(f"{name} failed: {msg}")
+    return rc
+
+
+def dtype_code(t):
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32, bfloat16 or float16") from None
+
+
+def ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def stream_ptr(device=None):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if not (isinstance(t, torch.Tensor) and t.is_cuda):
+            raise ValueError("autoresearch2_b200 runs on CUDA tensors only (no CPU path)")
+
+
+# Sticky per-device status word: kernels OR SFFN_STATUS_* bits into it.
+_status = {}
+
+
+def status_word(device):
+    idx = torch.device(device).index
+    if idx is None:
+        idx = torch.cuda.current_device()
+    t = _status.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        _status[idx] = t
+    return t
+
+
+def check_status(device=None, raise_on_error=True):
+    """Synchronise-read and clear the device status word; raise if bits are set."""
+    st = status_word(device if device is not None else torch.cuda.current_device())
+    v = int(st.item())
+    if v:
+        st.zero_()
+        if raise_on_error:
+            what = ", ".join(m for b, m in STATUS_BITS.items() if v & b)
+            raise SparseFFNError(f"device status 0x{v:x}: {what}")
+    return v
+
+
+def workspace(nbytes, device):
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)

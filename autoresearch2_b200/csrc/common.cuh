@@ -1,0 +1,166 @@
+// Shared device helpers for the sparse-FFN kernels (sm_100a).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <type_traits>
+
+#include "../../include/sparseffn.h"
+
+namespace sffn {
+
+constexpr unsigned FULL = 0xffffffffu;
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing
+// ---------------------------------------------------------------------------
+void set_cuda_error(cudaError_t e);
+
+#define SFFN_CHECK_LAUNCH()                                  \
+    do {                                                     \
+        cudaError_t _e = cudaGetLastError();                 \
+        if (_e != cudaSuccess) {                             \
+            ::sffn::set_cuda_error(_e);                      \
+            return SFFN_ERR_CUDA;                            \
+        }                                                    \
+    } while (0)
+
+#define SFFN_CUDA_TRY(call)                                  \
+    do {                                                     \
+        cudaError_t _e = (call);                             \
+        if (_e != cudaSuccess) {                             \
+            ::sffn::set_cuda_error(_e);                      \
+            return SFFN_ERR_CUDA;                            \
+        }                                                    \
+    } while (0)
+
+inline int esize_of(int dtype) { return dtype == SFFN_F32 ? 4 : 2; }
+inline bool dtype_ok(int dtype) { return dtype == SFFN_F32 || dtype == SFFN_BF16 || dtype == SFFN_F16; }
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------
+// Element predicates on raw bit patterns (exactly IEEE compares)
+// ---------------------------------------------------------------------------
+// x != 0: magnitude bits non-zero (-0.0 -> false, NaN -> true).
+__device__ __forceinline__ bool nonzero_bits(uint16_t b) { return (b & 0x7FFFu) != 0; }
+__device__ __forceinline__ bool nonzero_bits(uint32_t b) { return (b & 0x7FFFFFFFu) != 0; }
+
+// x > 0: sign clear, non-zero, not NaN.  INF16 is the +inf pattern of the
+// 16-bit type (0x7F80 bf16, 0x7C00 fp16).
+__device__ __forceinline__ bool positive_bits(uint16_t b, uint16_t inf16) {
+    return (int16_t)b > 0 && b <= inf16;
+}
+__device__ __forceinline__ bool positive_bits(uint32_t b, uint16_t) {
+    return (int32_t)b > 0 && b <= 0x7F800000u;
+}
+
+inline uint16_t inf16_of(int dtype) { return dtype == SFFN_F16 ? 0x7C00 : 0x7F80; }
+
+// Storage-dtype arithmetic (products of two 16-bit floats are exact in fp32,
+// so computing in fp32 and rounding once equals the 16-bit operation).
+template <int DT> struct Elt;
+template <> struct Elt<SFFN_F32> {
+    using bits = uint32_t;
+    __device__ static float to_f(bits b) { return __uint_as_float(b); }
+    __device__ static bits from_f(float f) { return __float_as_uint(f); }
+};
+template <> struct Elt<SFFN_BF16> {
+    using bits = uint16_t;
+    __device__ static float to_f(bits b) { return __uint_as_float(((uint32_t)b) << 16); }
+    __device__ static bits from_f(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
+};
+template <> struct Elt<SFFN_F16> {
+    using bits = uint16_t;
+    __device__ static float to_f(bits b) { return __half2float(__ushort_as_half(b)); }
+    __device__ static bits from_f(float f) { return __half_as_ushort(__float2half_rn(f)); }
+};
+
+// ---------------------------------------------------------------------------
+// Warp helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int warp_incl_scan(int v, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(FULL, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ unsigned long long warp_sum_u64(unsigned long long v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// Combine one mask byte per lane into little-endian 32-bit words: lanes
+// 4k..4k+3 hold consecutive bytes; every lane gets its group's word.
+__device__ __forceinline__ uint32_t bytes_to_word(uint32_t byte, int lane) {
+    uint32_t w = byte << (8 * (lane & 3));
+    w |= __shfl_xor_sync(FULL, w, 1);
+    w |= __shfl_xor_sync(FULL, w, 2);
+    return w;
+}
+
+// ---------------------------------------------------------------------------
+// Decoupled look-back over a sequence of partitions (single-pass scan).
+// State word per partition: bits 63:62 = flag (0 none, 1 aggregate, 2 inclusive),
+// bits 61:0 = value.  Partitions take ordered tickets, so every predecessor of a
+// running partition has started and the wait ends; it is still bounded: after
+// kLookbackSpinLimit polls the partition records SFFN_STATUS_WAIT_TIMEOUT,
+// publishes what it has and returns.
+// ---------------------------------------------------------------------------
+constexpr unsigned long long LB_AGG = 1ull << 62;
+constexpr unsigned long long LB_INCL = 2ull << 62;
+constexpr unsigned long long LB_VAL = (1ull << 62) - 1;
+constexpr unsigned kLookbackSpinLimit = 1u << 22;
+
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Called by one full warp.  Returns the exclusive prefix of partition `part`.
+__device__ __forceinline__ unsigned long long lookback(unsigned long long* states, long long part,
+                                                      unsigned long long agg, uint32_t* status,
+                                                      int lane) {
+    if (part == 0) {
+        if (lane == 0) st_release_u64(&states[0], LB_INCL | agg);
+        return 0;
+    }
+    if (lane == 0) st_release_u64(&states[part], LB_AGG | agg);
+    unsigned long long excl = 0;
+    long long pred = part - 1;
+    unsigned spins = 0;
+    while (true) {
+        long long idx = pred - lane;
+        unsigned long long s = idx >= 0 ? ld_acquire_u64(&states[idx]) : LB_INCL;
+        unsigned flag = (unsigned)(s >> 62);
+        unsigned incl = __ballot_sync(FULL, flag == 2);
+        unsigned none = __ballot_sync(FULL, flag == 0);
+        unsigned need = incl ? ((incl & (0u - incl)) << 1) - 1 : FULL;  // lanes up to the first inclusive
+        if (none & need) {
+            if (++spins > kLookbackSpinLimit) {
+                if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            __nanosleep(40);
+            continue;
+        }
+        unsigned long long v = ((need >> lane) & 1u) ? (s & LB_VAL) : 0ull;
+        excl += warp_sum_u64(v);
+        if (incl) break;
+        pred -= 32;
+    }
+    if (lane == 0) st_release_u64(&states[part], LB_INCL | ((excl + agg) & LB_VAL));
+    return excl;
+}
+
+}  // namespace sffn

@@ -1,0 +1,567 @@
+// Tiled bitmask format: pack (with arena cursor), unpack, ReLU-mask and
+// ReLU^2-gradient kernels (sm_100a).
+//
+// Reference: old/lib_sparse/sparse_pack.py:27-92 + sparse.py:154-210 (pack:
+// tile kernel, torch.cumsum, compaction kernel that re-reads the tile, cursor
+// index_add_), old/lib_sparse/sparse_unpack.py:5-147 (unpack / mask / grad).
+// Pack here is ONE kernel: each CTA owns one tile (taken by ticket, so tiles
+// run in order), builds mask words and in-tile ranks in registers, stages the
+// compacted values in shared memory, finds its offset by decoupled look-back
+// over the preceding tiles, and the last tile writes prefix[num_tiles] and
+// advances the device cursor.
+//
+// Thread layout per tile: NT = min(256, BM*BN/8) threads, U iterations, 8
+// consecutive in-tile elements (one mask byte) per thread per iteration; in
+// iteration `it` thread `tid` owns in-tile offsets f = 8*(it*NT + tid) + j.
+#include "common.cuh"
+
+namespace sffn {
+namespace {
+
+template <int BM, int BN>
+struct TileCfg {
+    static constexpr int TILE = BM * BN;
+    static constexpr int TB = TILE / 8;  // mask bytes per tile
+    static constexpr int NT = TILE / 8 < 256 ? TILE / 8 : 256;
+    static constexpr int U = TILE / (8 * NT);
+    static constexpr int NW = NT / 32;
+    static constexpr int NE = U * NW;  // (iteration, warp) partial counts
+    static_assert(BN % 32 == 0, "a mask word never straddles tile rows");
+    static_assert(NE <= 32 || NE == 64, "scan_small handles up to 32 or exactly 64 entries");
+};
+
+// Exclusive scan, by warp 0, of NE ints in shared memory; total -> *s_total.
+template <int NE>
+__device__ __forceinline__ void scan_small(int* s, int* s_total, int lane) {
+    if constexpr (NE <= 32) {
+        int t = lane < NE ? s[lane] : 0;
+        int inc = warp_incl_scan(t, lane);
+        if (lane < NE) s[lane] = inc - t;
+        if (lane == 31) *s_total = inc;
+    } else {
+        int a = s[2 * lane], b = s[2 * lane + 1];
+        int inc = warp_incl_scan(a + b, lane);
+        int ex = inc - a - b;
+        s[2 * lane] = ex;
+        s[2 * lane + 1] = ex + a;
+        if (lane == 31) *s_total = inc;
+    }
+}
+
+template <typename B>
+__device__ __forceinline__ void load8_row(const B* __restrict__ row, long long gc, long long N,
+                                          bool vec, B (&v)[8]) {
+    if (vec && gc + 8 <= N) {
+        if constexpr (sizeof(B) == 2) {
+            uint4 q = __ldcs(reinterpret_cast<const uint4*>(row + gc));
+            const B* s = reinterpret_cast<const B*>(&q);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = s[j];
+        } else {
+            uint4 q0 = __ldcs(reinterpret_cast<const uint4*>(row + gc));
+            uint4 q1 = __ldcs(reinterpret_cast<const uint4*>(row + gc) + 1);
+            v[0] = q0.x; v[1] = q0.y; v[2] = q0.z; v[3] = q0.w;
+            v[4] = q1.x; v[5] = q1.y; v[6] = q1.z; v[7] = q1.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = (gc + j < N) ? row[gc + j] : B(0);
+    }
+}
+
+template <typename O>
+__device__ __forceinline__ void store8_row(O* __restrict__ row, long long gc, long long N, bool vec,
+                                           const O (&o)[8]) {
+    if (vec && gc + 8 <= N) {
+        if constexpr (sizeof(O) == 2) {
+            uint4 q;
+            O* d = reinterpret_cast<O*>(&q);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) d[j] = o[j];
+            *reinterpret_cast<uint4*>(row + gc) = q;
+        } else {
+            reinterpret_cast<uint4*>(row + gc)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+            reinterpret_cast<uint4*>(row + gc)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (gc + j < N) row[gc + j] = o[j];
+    }
+}
+
+// Mask byte of this thread's 8 elements, read as whole little-endian words by
+// lanes 4k and shared within the group of four.
+template <int TB>
+__device__ __forceinline__ uint32_t mask_byte(const uint8_t* __restrict__ tile_mask, int f, int lane) {
+    uint32_t w = 0;
+    if ((lane & 3) == 0) w = __ldg(reinterpret_cast<const unsigned int*>(tile_mask + (f >> 3)));
+    w = __shfl_sync(FULL, w, lane & ~3);
+    return (w >> (8 * (lane & 3))) & 0xFFu;
+}
+
+// ----------------------------------------------------------------- pack ----
+template <typename B, int BM, int BN>
+__global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
+    const B* __restrict__ dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
+    uint8_t* __restrict__ bitmask, int* __restrict__ prefix, B* __restrict__ vals, long long cap,
+    int* __restrict__ cursor, int* __restrict__ vals_offset_out,
+    unsigned long long* __restrict__ states, unsigned* __restrict__ ticket,
+    uint32_t* __restrict__ status, long long gn, long long ntiles) {
+    using C = TileCfg<BM, BN>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    B* s_vals = reinterpret_cast<B*>(smem_raw);
+    __shared__ int s_wx[C::NE];
+    __shared__ int s_agg;
+    __shared__ int s_cursor;
+    __shared__ long long s_tile;
+    __shared__ unsigned long long s_excl;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        s_tile = atomicAdd(ticket, 1u);
+        // Every tile reads the cursor before publishing its count; the last
+        // tile writes it only after seeing all counts (see lookback()).
+        s_cursor = *reinterpret_cast<volatile int*>(cursor);
+    }
+    __syncthreads();
+    const long long t = s_tile;
+    const long long tm = t / gn, tn = t % gn;
+    const long long row0 = tm * BM, col0 = tn * BN;
+    uint8_t* tmask = bitmask + t * C::TB;
+
+    B v[C::U][8];
+    uint32_t bits[C::U];
+    int lex[C::U];
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const long long gr = row0 + f / BN, gc = col0 + f % BN;
+        if (gr < M) {
+            load8_row(dense + gr * ld, gc, N, vec != 0, v[it]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[it][j] = B(0);
+        }
+        uint32_t b = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) b |= (uint32_t)positive_bits(v[it][j], inf16) << j;
+        bits[it] = b;
+        const uint32_t w = bytes_to_word(b, lane);
+        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(tmask + (f >> 3)) = w;
+        const int c = __popc(b);
+        const int inc = warp_incl_scan(c, lane);
+        lex[it] = inc - c;
+        if (lane == 31) s_wx[it * C::NW + warp] = inc;
+    }
+    __syncthreads();
+    if (warp == 0) scan_small<C::NE>(s_wx, &s_agg, lane);
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        int r = s_wx[it * C::NW + warp] + lex[it];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if ((bits[it] >> j) & 1u) s_vals[r++] = v[it][j];
+    }
+    const int agg = s_agg;
+    if (warp == 0) {
+        unsigned long long ex = lookback(states, t, (unsigned long long)agg, status, lane);
+        if (lane == 0) s_excl = ex;
+    }
+    __syncthreads();
+    const long long ex = (long long)s_excl;
+    const long long base = (long long)s_cursor + ex;
+    for (int i = tid; i < agg; i += C::NT) {
+        const long long p = base + i;
+        if (p >= 0 && p < cap) vals[p] = s_vals[i];
+    }
+    if (tid == 0) {
+        prefix[t] = (int)ex;
+        if (base < 0 || base + agg > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+        if (t == 0) *vals_offset_out = s_cursor;
+        if (t == ntiles - 1) {
+            const long long total = ex + agg;
+            prefix[ntiles] = (int)total;
+            const long long next = (long long)s_cursor + total;
+            if (next > 0x7FFFFFFFll) atomicOr(status, SFFN_STATUS_CURSOR_OVERFLOW);
+            *reinterpret_cast<volatile int*>(cursor) = (int)(next > 0x7FFFFFFFll ? 0x7FFFFFFFll : next);
+        }
+    }
+}
+
+// --------------------------------------------------------------- unpack ----
+template <int DT, bool OUT_F32, int BM, int BN>
+__global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_unpack_kernel(
+    const typename Elt<DT>::bits* __restrict__ vals, const uint8_t* __restrict__ bitmask,
+    long long vals_len, const int* __restrict__ prefix, const int* __restrict__ vals_offset,
+    long long M, long long N, long long gn, long long tile_row0, int square,
+    typename std::conditional<OUT_F32, uint32_t, typename Elt<DT>::bits>::type* __restrict__ out,
+    long long ld_out, int vec) {
+    using C = TileCfg<BM, BN>;
+    using B = typename Elt<DT>::bits;
+    using O = typename std::conditional<OUT_F32, uint32_t, B>::type;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    B* s_vals = reinterpret_cast<B*>(smem_raw);
+    __shared__ int s_wx[C::NE];
+    __shared__ int s_agg;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long tl = blockIdx.x;
+    const long long tm = tile_row0 + tl / gn, tn = tl % gn;
+    const long long t = tm * gn + tn;
+    const long long row0 = tm * BM, col0 = tn * BN;
+    const long long start = (long long)*vals_offset + prefix[t];
+    const int cnt = prefix[t + 1] - prefix[t];
+    for (int i = tid; i < cnt && i < C::TILE; i += C::NT)
+        s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+
+    uint32_t bits[C::U];
+    int lex[C::U];
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const uint32_t b = mask_byte<C::TB>(bitmask + t * C::TB, f, lane);
+        bits[it] = b;
+        const int c = __popc(b);
+        const int inc = warp_incl_scan(c, lane);
+        lex[it] = inc - c;
+        if (lane == 31) s_wx[it * C::NW + warp] = inc;
+    }
+    __syncthreads();
+    if (warp == 0) scan_small<C::NE>(s_wx, &s_agg, lane);
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const long long gr = row0 + f / BN, gc = col0 + f % BN;
+        int r = s_wx[it * C::NW + warp] + lex[it];
+        O o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            B z = B(0);
+            if ((bits[it] >> j) & 1u) {
+                z = r < C::TILE ? s_vals[r] : B(0);
+                ++r;
+            }
+            if (square) {
+                const float zf = Elt<DT>::to_f(z);
+                z = Elt<DT>::from_f(zf * zf);
+            }
+            if constexpr (OUT_F32) o[j] = __float_as_uint(Elt<DT>::to_f(z));
+            else o[j] = z;
+        }
+        if (gr < M) store8_row(out + (gr - tile_row0 * BM) * ld_out, gc, N, vec != 0, o);
+    }
+}
+
+// ------------------------------------------------------------ mask grad ----
+template <typename B, int BM, int BN>
+__global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_mask_kernel(
+    B* __restrict__ grad, long long M, long long N, long long ld, const uint8_t* __restrict__ bitmask,
+    long long gn, int vec) {
+    using C = TileCfg<BM, BN>;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const long long t = blockIdx.x;
+    const long long row0 = (t / gn) * BM, col0 = (t % gn) * BN;
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const uint32_t b = mask_byte<C::TB>(bitmask + t * C::TB, f, lane);
+        const long long gr = row0 + f / BN, gc = col0 + f % BN;
+        if (gr >= M) continue;
+        B g[8];
+        load8_row(grad + gr * ld, gc, N, vec != 0, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = ((b >> j) & 1u) ? g[j] : B(0);
+        store8_row(grad + gr * ld, gc, N, vec != 0, g);
+    }
+}
+
+// ----------------------------------------------------------- relu^2 grad ----
+template <int DT, int BM, int BN>
+__global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_grad_relu2_kernel(
+    typename Elt<DT>::bits* __restrict__ grad, long long M, long long N, long long ld,
+    typename Elt<DT>::bits* __restrict__ vals, long long vals_len,
+    const uint8_t* __restrict__ bitmask, const int* __restrict__ prefix,
+    const int* __restrict__ vals_offset, long long gn, int square, int vec) {
+    using C = TileCfg<BM, BN>;
+    using B = typename Elt<DT>::bits;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    B* s_vals = reinterpret_cast<B*>(smem_raw);
+    __shared__ int s_wx[C::NE];
+    __shared__ int s_agg;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long t = blockIdx.x;
+    const long long row0 = (t / gn) * BM, col0 = (t % gn) * BN;
+    const long long start = (long long)*vals_offset + prefix[t];
+    const int cnt = prefix[t + 1] - prefix[t];
+    for (int i = tid; i < cnt && i < C::TILE; i += C::NT)
+        s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+
+    uint32_t bits[C::U];
+    int lex[C::U];
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const uint32_t b = mask_byte<C::TB>(bitmask + t * C::TB, f, lane);
+        bits[it] = b;
+        const int c = __popc(b);
+        const int inc = warp_incl_scan(c, lane);
+        lex[it] = inc - c;
+        if (lane == 31) s_wx[it * C::NW + warp] = inc;
+    }
+    __syncthreads();
+    if (warp == 0) scan_small<C::NE>(s_wx, &s_agg, lane);
+    __syncthreads();
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {
+        const int f = 8 * (it * C::NT + tid);
+        const long long gr = row0 + f / BN, gc = col0 + f % BN;
+        if (gr >= M) continue;
+        int r = s_wx[it * C::NW + warp] + lex[it];
+        B g[8];
+        load8_row(grad + gr * ld, gc, N, vec != 0, g);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float z = 0.0f;
+            if ((bits[it] >> j) & 1u) {
+                z = r < C::TILE ? Elt<DT>::to_f(s_vals[r]) : 0.0f;
+                ++r;
+            }
+            // (g * 2.0) * z rounded to the storage dtype; g*2 is exact.
+            g[j] = Elt<DT>::from_f((Elt<DT>::to_f(g[j]) * 2.0f) * z);
+        }
+        store8_row(grad + gr * ld, gc, N, vec != 0, g);
+    }
+    if (square) {
+        for (int i = tid; i < cnt && i < C::TILE; i += C::NT) {
+            if (start + i < 0 || start + i >= vals_len) continue;
+            const float z = Elt<DT>::to_f(s_vals[i]);
+            vals[start + i] = Elt<DT>::from_f(z * z);
+        }
+    }
+}
+
+// ------------------------------------------------------------ dispatch ----
+// Supported tile shapes.
+#define SFFN_TILE_SHAPES(X) X(32, 32) X(64, 64) X(128, 128) X(64, 128) X(128, 64)
+
+inline bool tile_shape_ok(int BM, int BN) {
+#define SFFN_OK_SHAPE(a, b) if (BM == a && BN == b) return true;
+    SFFN_TILE_SHAPES(SFFN_OK_SHAPE)
+#undef SFFN_OK_SHAPE
+    return false;
+}
+
+template <typename K>
+inline cudaError_t prep_smem(K kernel, int bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+struct TileWs {
+    unsigned* ticket;
+    unsigned long long* states;
+    size_t used;
+};
+
+inline long long num_tiles(long long M, long long N, int BM, int BN) {
+    return ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+}
+
+template <typename B, int BM, int BN>
+int launch_pack(const void* dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
+                uint8_t* bitmask, int* prefix, void* vals, long long cap, int* cursor,
+                int* vals_offset_out, const TileWs& w, uint32_t* status, cudaStream_t st) {
+    using C = TileCfg<BM, BN>;
+    const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
+    const int smem = C::TILE * (int)sizeof(B);
+    auto k = tile_pack_kernel<B, BM, BN>;
+    SFFN_CUDA_TRY(prep_smem(k, smem));
+    k<<<(unsigned)nt, C::NT, smem, st>>>((const B*)dense, M, N, ld, vec, inf16, bitmask, prefix,
+                                         (B*)vals, cap, cursor, vals_offset_out, w.states, w.ticket,
+                                         status, gn, nt);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+template <int DT, bool OF, int BM, int BN>
+int launch_unpack(const void* vals, long long vals_len, const uint8_t* bitmask, const int* prefix,
+                  const int* voff, long long M, long long N, long long tr0, long long trows, int square, void* out,
+                  long long ld_out, int vec, cudaStream_t st) {
+    using C = TileCfg<BM, BN>;
+    using B = typename Elt<DT>::bits;
+    using O = typename std::conditional<OF, uint32_t, B>::type;
+    const long long gn = (N + BN - 1) / BN;
+    const int smem = C::TILE * (int)sizeof(B);
+    auto k = tile_unpack_kernel<DT, OF, BM, BN>;
+    SFFN_CUDA_TRY(prep_smem(k, smem));
+    k<<<(unsigned)(trows * gn), C::NT, smem, st>>>((const B*)vals, bitmask, vals_len, prefix, voff,
+                                                    M, N, gn, tr0, square, (O*)out, ld_out, vec);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+template <typename B, int BM, int BN>
+int launch_mask(void* grad, long long M, long long N, long long ld, const uint8_t* bitmask, int vec,
+                cudaStream_t st) {
+    using C = TileCfg<BM, BN>;
+    const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
+    tile_mask_kernel<B, BM, BN><<<(unsigned)nt, C::NT, 0, st>>>((B*)grad, M, N, ld, bitmask, gn, vec);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+template <int DT, int BM, int BN>
+int launch_relu2(void* grad, long long M, long long N, long long ld, void* vals, long long vals_len,
+                 const uint8_t* bitmask, const int* prefix, const int* voff, int square, int vec,
+                 cudaStream_t st) {
+    using C = TileCfg<BM, BN>;
+    using B = typename Elt<DT>::bits;
+    const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
+    const int smem = C::TILE * (int)sizeof(B);
+    auto k = tile_grad_relu2_kernel<DT, BM, BN>;
+    SFFN_CUDA_TRY(prep_smem(k, smem));
+    k<<<(unsigned)nt, C::NT, smem, st>>>((B*)grad, M, N, ld, (B*)vals, vals_len, bitmask, prefix,
+                                         voff, gn, square, vec);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+inline bool vec_ok(const void* p, long long ld, int esz) {
+    return aligned16(p) && ((ld * esz) % 16 == 0);
+}
+
+}  // namespace
+}  // namespace sffn
+
+using namespace sffn;
+
+extern "C" size_t sffn_tile_workspace_bytes(int64_t M, int64_t N, int BM, int BN) {
+    if (M < 0 || N < 0 || BM <= 0 || BN <= 0) return 0;
+    return 16 + (size_t)num_tiles(M, N, BM, BN) * 8;
+}
+
+extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld, int BM,
+                              int BN, uint8_t* bitmask, int32_t* prefix, void* vals,
+                              int64_t vals_capacity, int32_t* offset_dev, int32_t* vals_offset_dev,
+                              void* workspace, size_t workspace_bytes, uint32_t* status_dev,
+                              void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
+    if (M <= 0 || N <= 0 || ld < N || vals_capacity < 0) return SFFN_ERR_ARG;
+    if (M * N > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // int32 prefix, as in the reference
+    if (!dense || !bitmask || !prefix || !offset_dev || !vals_offset_dev || !status_dev || !workspace)
+        return SFFN_ERR_ARG;
+    if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
+    if (workspace_bytes < sffn_tile_workspace_bytes(M, N, BM, BN)) return SFFN_ERR_WORKSPACE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    TileWs w;
+    w.ticket = reinterpret_cast<unsigned*>(workspace);
+    w.states = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) + 16);
+    w.used = sffn_tile_workspace_bytes(M, N, BM, BN);
+    SFFN_CUDA_TRY(cudaMemsetAsync(workspace, 0, w.used, st));
+    const int esz = esize_of(dtype);
+    const int vec = vec_ok(dense, ld, esz) ? 1 : 0;
+    const uint16_t inf16 = inf16_of(dtype);
+#define SFFN_PACK_CASE(a, b)                                                                         \
+    if (BM == a && BN == b) {                                                                        \
+        if (esz == 4)                                                                                \
+            return launch_pack<uint32_t, a, b>(dense, M, N, ld, vec, inf16, bitmask, prefix, vals,   \
+                                               vals_capacity, offset_dev, vals_offset_dev, w,        \
+                                               status_dev, st);                                      \
+        return launch_pack<uint16_t, a, b>(dense, M, N, ld, vec, inf16, bitmask, prefix, vals,       \
+                                           vals_capacity, offset_dev, vals_offset_dev, w,            \
+                                           status_dev, st);                                          \
+    }
+    SFFN_TILE_SHAPES(SFFN_PACK_CASE)
+#undef SFFN_PACK_CASE
+    return SFFN_ERR_UNSUPPORTED;
+}
+
+extern "C" int sffn_tile_unpack(const void* vals, int64_t vals_len, const uint8_t* bitmask,
+                                const int32_t* prefix, const int32_t* vals_offset_dev, int dtype, int64_t M, int64_t N,
+                                int BM, int BN, int64_t tile_row0, int64_t tile_rows, int square,
+                                void* out, int out_dtype, int64_t ld_out, void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (out_dtype != dtype && out_dtype != SFFN_F32) return SFFN_ERR_DTYPE;
+    if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
+    const long long gm = (M + BM - 1) / BM;
+    if (M <= 0 || N <= 0 || ld_out < N || tile_row0 < 0 || tile_rows < 0 || tile_row0 + tile_rows > gm)
+        return SFFN_ERR_ARG;
+    if (tile_rows == 0) return SFFN_OK;
+    if (!vals || !bitmask || !prefix || !vals_offset_dev || !out) return SFFN_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const bool of = (out_dtype == SFFN_F32) && (dtype != SFFN_F32);
+    const int vec = vec_ok(out, ld_out, esize_of(out_dtype)) ? 1 : 0;
+#define SFFN_UNPACK_CASE(a, b)                                                                         \
+    if (BM == a && BN == b) {                                                                          \
+        if (dtype == SFFN_F32)                                                                         \
+            return launch_unpack<SFFN_F32, false, a, b>(vals, vals_len, bitmask, prefix, vals_offset_dev, M, N,  \
+                                                        tile_row0, tile_rows, square, out, ld_out,     \
+                                                        vec, st);                                      \
+        if (dtype == SFFN_BF16)                                                                        \
+            return of ? launch_unpack<SFFN_BF16, true, a, b>(vals, vals_len, bitmask, prefix, vals_offset_dev,   \
+                                                             M, N, tile_row0, tile_rows, square, out,  \
+                                                             ld_out, vec, st)                          \
+                      : launch_unpack<SFFN_BF16, false, a, b>(vals, vals_len, bitmask, prefix, vals_offset_dev,  \
+                                                              M, N, tile_row0, tile_rows, square, out, \
+                                                              ld_out, vec, st);                        \
+        return of ? launch_unpack<SFFN_F16, true, a, b>(vals, vals_len, bitmask, prefix, vals_offset_dev, M, N,  \
+                                                        tile_row0, tile_rows, square, out, ld_out,     \
+                                                        vec, st)                                       \
+                  : launch_unpack<SFFN_F16, false, a, b>(vals, vals_len, bitmask, prefix, vals_offset_dev, M, N, \
+                                                         tile_row0, tile_rows, square, out, ld_out,    \
+                                                         vec, st);                                     \
+    }
+    SFFN_TILE_SHAPES(SFFN_UNPACK_CASE)
+#undef SFFN_UNPACK_CASE
+    return SFFN_ERR_UNSUPPORTED;
+}
+
+extern "C" int sffn_tile_mask_grad(void* grad, int dtype, int64_t M, int64_t N, int64_t ld,
+                                   const uint8_t* bitmask, int BM, int BN, void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
+    if (M <= 0 || N <= 0 || ld < N || !grad || !bitmask) return SFFN_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int esz = esize_of(dtype);
+    const int vec = vec_ok(grad, ld, esz) ? 1 : 0;
+#define SFFN_MASK_CASE(a, b)                                                              \
+    if (BM == a && BN == b) {                                                             \
+        if (esz == 4) return launch_mask<uint32_t, a, b>(grad, M, N, ld, bitmask, vec, st); \
+        return launch_mask<uint16_t, a, b>(grad, M, N, ld, bitmask, vec, st);             \
+    }
+    SFFN_TILE_SHAPES(SFFN_MASK_CASE)
+#undef SFFN_MASK_CASE
+    return SFFN_ERR_UNSUPPORTED;
+}
+
+extern "C" int sffn_tile_grad_relu2(void* grad, int dtype, int64_t M, int64_t N, int64_t ld,
+                                    void* vals, int64_t vals_len, const uint8_t* bitmask, const int32_t* prefix,
+                                    const int32_t* vals_offset_dev, int BM, int BN, int square,
+                                    void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
+    if (M <= 0 || N <= 0 || ld < N || !grad || !vals || !bitmask || !prefix || !vals_offset_dev)
+        return SFFN_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int vec = vec_ok(grad, ld, esize_of(dtype)) ? 1 : 0;
+#define SFFN_RELU2_CASE(a, b)                                                                     \
+    if (BM == a && BN == b) {                                                                     \
+        if (dtype == SFFN_F32)                                                                    \
+            return launch_relu2<SFFN_F32, a, b>(grad, M, N, ld, vals, vals_len, bitmask, prefix,           \
+                                                vals_offset_dev, square, vec, st);               \
+        if (dtype == SFFN_BF16)                                                                   \
+            return launch_relu2<SFFN_BF16, a, b>(grad, M, N, ld, vals, vals_len, bitmask, prefix,          \
+                                                 vals_offset_dev, square, vec, st);              \
+        return launch_relu2<SFFN_F16, a, b>(grad, M, N, ld, vals, vals_len, bitmask, prefix,               \
+                                            vals_offset_dev, square, vec, st);                   \
+    }
+    SFFN_TILE_SHAPES(SFFN_RELU2_CASE)
+#undef SFFN_RELU2_CASE
+    return SFFN_ERR_UNSUPPORTED;
+}

@@ -1,0 +1,410 @@
+"""Benchmark of the activation-sparse ReLU^2 FFN hot path on B200.
+
+Headline workload: one ReLU^2 FFN layer, forward + backward, d_model=4096,
+d_ff=14336, 16384 tokens per GPU, bf16, up-projection bias shifted so that
+90% of the activations are zero (the d=4096/14336 sparsity sweep).  Synthetic
+seeded data: x ~ N(0,1), W_up ~ N(0, 1/4096), W_down ~ N(0, 1/14336),
+upstream gradient ~ N(0,1).  Every tensor of a step is larger than L2 or is
+rewritten each step, so no explicit L2 flush is used (inputs larger than L2).
+
+Multi-GPU: one process per GPU (torchrun), tokens sharded (16384 per rank,
+weak scaling); the only exchange is the NCCL all-reduce of dW1/dW2.
+
+Also reported in the same JSON line: the dense cuBLAS bf16 FFN at the same
+config, the sparsity sweep, standalone pack/unpack GB/s on [65536, 4096]
+bf16 (p = 0.1), the roofline of the dominant kernel, and a CPU baseline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+T_PER_GPU, D_MODEL, D_FF = 16384, 4096, 14336
+SPARSITY = 0.9
+SWEEP = (0.5, 0.8, 0.95, 0.99)
+PACK_SHAPE, PACK_P = (65536, 4096), 0.1
+METRIC = "sparse FFN fwd+bwd tokens/s vs cuBLAS dense @80-95% sparsity; pack GB/s"
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks ----
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# -------------------------------------------------------------- workload ----
+def make_ffn_inputs(T, D, F, sparsity, device, seed=0):
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(T, D, device=device, generator=g).to(torch.bfloat16)
+    W1 = (torch.randn(F, D, device=device, generator=g) / D ** 0.5).to(torch.bfloat16)
+    W2 = (torch.randn(D, F, device=device, generator=g) / F ** 0.5).to(torch.bfloat16)
+    dout = torch.randn(T, D, device=device, generator=g).to(torch.bfloat16)
+    b1 = torch.full((F,), bias_for_sparsity(x, W1, sparsity), device=device, dtype=torch.bfloat16)
+    return x, W1, W2, b1, dout
+
+
+def bias_for_sparsity(x, W1, s):
+    """Scalar up-projection bias giving a fraction s of zeros after ReLU, from
+    the quantile of the pre-activation on 1024 sampled tokens."""
+    pre = (x[:1024] @ W1.T).float().flatten()
+    return float(-torch.quantile(pre[:: max(1, pre.numel() // 8_000_000)], s))
+
+
+class Step:
+    """One forward + backward of the sparse ReLU^2 FFN through the public API."""
+
+    def __init__(self, x, W1, W2, b1, dout, group=None):
+        import autoresearch2_b200 as sf
+        self.sf = sf
+        self.x, self.dout = x, dout
+        self.W1 = W1.clone().requires_grad_()
+        self.W2 = W2.clone().requires_grad_()
+        self.b1 = b1.clone().requires_grad_()
+        T, F = x.shape[0], W1.shape[0]
+        self.buf = sf.TensorBuffer(T * F, x.device, x.dtype).init_buffer()
+        self.group = group
+
+    def __call__(self, x=None):
+        x = self.x if x is None else x
+        self.buf.reset_buffer()
+        for p in (self.W1, self.W2, self.b1):
+            p.grad = None
+        out = self.sf.FFNSpRelu2.apply(x, self.W1, self.W2, self.buf.as_sparse_data(), self.b1)
+        out.backward(self.dout)
+        if self.group is not None:
+            for p in (self.W1, self.W2):
+                dist.all_reduce(p.grad, group=self.group)
+        return out
+
+
+class DenseStep:
+    """Dense cuBLAS bf16 ReLU^2 FFN, autograd of the reference's FFNrelu2
+    (old/lib_sparse/prepare_layer.py:12-29) plus the bias."""
+
+    def __init__(self, x, W1, W2, b1, dout):
+        self.x, self.dout = x, dout
+        self.W1 = W1.clone().requires_grad_()
+        self.W2 = W2.clone().requires_grad_()
+        self.b1 = b1.clone().requires_grad_()
+
+    def __call__(self):
+        for p in (self.W1, self.W2, self.b1):
+            p.grad = None
+        z = torch.relu(self.x @ self.W1.T + self.b1) ** 2
+        out = z @ self.W2.T
+        out.backward(self.dout)
+        return out
+
+
+def time_steps(fn, steps, warmup, device):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(device)
+    if dist.is_initialized():
+        dist.barrier()
+    ms = a.elapsed_time(b)
+    if dist.is_initialized():
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms / steps
+
+
+# ------------------------------------------------------------------ pack ----
+def bench_pack(device, reps=20):
+    import autoresearch2_b200 as sf
+    rows, cols = PACK_SHAPE
+    g = torch.Generator(device=device).manual_seed(0)
+    keep = torch.rand(rows, cols, device=device, generator=g) < PACK_P
+    d = torch.where(keep, torch.randn(rows, cols, device=device, generator=g).abs() + 1e-3,
+                    torch.zeros((), device=device)).to(torch.bfloat16)
+    del keep
+    n = d.numel()
+    vals, mask = sf.bitsparse_pack(d)
+    nnz = vals.numel()
+    algo = 2 * n + n / 8 + 2 * nnz  # bytes moved per pack (and per unpack)
+    # time the kernels through the C ABI with preallocated buffers
+    from autoresearch2_b200 import _lib
+    L = _lib.load()
+    vbuf = torch.empty(n, dtype=d.dtype, device=device)
+    nnz_d = torch.zeros(2, dtype=torch.int64, device=device)
+    ws = _lib.workspace(L.sffn_flat_workspace_bytes(n), device)
+    out = torch.empty_like(d)
+    st = _lib.stream_ptr(device)
+    status = _lib.status_word(device)
+
+    def pack():
+        _lib.call("sffn_flat_pack", _lib.ptr(d), 1, n, _lib.ptr(mask), _lib.ptr(vbuf), n,
+                  _lib.ptr(nnz_d), _lib.ptr(ws), ws.numel(), _lib.ptr(status), st)
+
+    def unpack():
+        _lib.call("sffn_flat_unpack", _lib.ptr(vals), nnz, _lib.ptr(mask), 1, n, _lib.ptr(out),
+                  _lib.ptr(ws), ws.numel(), _lib.ptr(status), st)
+
+    res = {}
+    for name, fn in (("pack", pack), ("unpack", unpack)):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2 * reps)]
+        for i in range(reps):
+            ev[2 * i].record()
+            fn()
+            ev[2 * i + 1].record()
+        torch.cuda.synchronize(device)
+        ms = statistics.median(ev[2 * i].elapsed_time(ev[2 * i + 1]) for i in range(reps))
+        res[name] = {"gbs": algo / ms / 1e6, "ms": ms}
+    _lib.check_status(device)
+    assert torch.equal(out, d)
+    return {"shape": list(PACK_SHAPE), "p": PACK_P, "dtype": "bf16", "algo_bytes": algo,
+            "pack_gbs": round(res["pack"]["gbs"], 1), "unpack_gbs": round(res["unpack"]["gbs"], 1),
+            "pack_ms": round(res["pack"]["ms"], 4), "unpack_ms": round(res["unpack"]["ms"], 4)}
+
+
+# ---------------------------------------------------------- CPU baseline ----
+def cpu_baseline(sample_tokens):
+    """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
+    the C restatement of its pack) on the host cores, on `sample_tokens`
+    tokens of the headline workload.  Returns tokens/s."""
+    import numpy as np
+    import oracle
+    try:
+        from threadpoolctl import threadpool_info
+        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    rng = np.random.default_rng(0)
+    T, D, F = sample_tokens, D_MODEL, D_FF
+    x = rng.standard_normal((T, D), dtype=np.float32)
+    W1 = (rng.standard_normal((F, D), dtype=np.float32) / np.sqrt(D)).astype(np.float32)
+    W2 = (rng.standard_normal((D, F), dtype=np.float32) / np.sqrt(F)).astype(np.float32)
+    dout = rng.standard_normal((T, D), dtype=np.float32)
+    pre = x @ W1.T
+    b1 = np.full(F, -np.quantile(pre[:256], SPARSITY), dtype=np.float32)
+    t0 = time.perf_counter()
+    r = oracle.ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=b1, code=oracle.F32,
+                           compute=np.float32)
+    z = r["z"].astype(np.float32)
+    arena = np.empty(z.size, dtype=np.float32)
+    oracle.tile_pack(z, 128, 128, arena, 0)
+    dt = time.perf_counter() - t0
+    return {"value": round(T / dt, 1), "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": f"{T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
+                      f"+ tiled pack of z; {dt:.1f} s"}
+
+
+# ------------------------------------------------------------------ main ----
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-tokens", type=int, default=1024)
+    ap.add_argument("--no-sweep", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        if rank == 0:
+            cb = cpu_baseline(args.cpu_tokens)
+            line = {"impl": "reference", "metric": METRIC, "value": cb["value"],
+                    "unit": "tokens/s", "n_gpus": args.gpus, "steps": 1, "warmup": 0,
+                    "higher_is_better": True, "dtype": "f32", "data": "synthetic",
+                    "config": {"workload": "relu2_ffn_fwd_bwd_d4096_f14336_s0.9 (CPU sample)",
+                               "tokens_per_gpu": T_PER_GPU},
+                    "cpu_baseline": cb,
+                    "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                            "d2h_bytes_per_step": 0}}
+            print(json.dumps(line), flush=True)
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+        group = dist.group.WORLD
+    torch.backends.cuda.matmul.allow_tf32 = False
+
+    x, W1, W2, b1, dout = make_ffn_inputs(T_PER_GPU, D_MODEL, D_FF, SPARSITY, device, seed=rank)
+    step = Step(x, W1, W2, b1, dout, group)
+    step()
+    torch.cuda.synchronize(device)
+    s_meas = 1.0 - step.buf.used() / (T_PER_GPU * D_FF)
+
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import _lib
+    sf.check_status(device)
+    n0 = _lib.launch_count
+    step()
+    launches_per_step = _lib.launch_count - n0
+    with ClockSampler(local) as clk:
+        ms = time_steps(step, args.steps, args.warmup, device)
+    clocks = clk.summary()
+    tokens = T_PER_GPU * world
+    value = tokens / (ms / 1e3)
+
+    # end to end: pinned host input -> device, step, loss read back each step
+    x_host = x.cpu().pin_memory()
+    loss_holder = {}
+
+    def e2e_step():
+        xd = x_host.to(device, non_blocking=True)
+        out = step(xd)
+        loss_holder["l"] = float(out.float().pow(2).mean().item())
+
+    e2e_ms = time_steps(e2e_step, max(3, args.steps // 2), 1, device)
+    e2e = {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+           "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4}
+
+    extras = {}
+    if rank == 0:
+        dense = DenseStep(x, W1, W2, b1, dout)
+        d_ms = time_steps(dense, args.steps, args.warmup, device) if world == 1 else None
+        if d_ms is not None:
+            extras["dense_cublas"] = {"tokens_per_s": round(T_PER_GPU / (d_ms / 1e3), 1),
+                                      "ms_per_step": round(d_ms, 3)}
+            extras["speedup_vs_dense"] = round(d_ms / ms, 3)
+        del dense
+    if world == 1 and not args.no_sweep:
+        sweep = {}
+        for s in SWEEP:
+            xs, W1s, W2s, b1s, dos = make_ffn_inputs(T_PER_GPU, D_MODEL, D_FF, s, device)
+            st = Step(xs, W1s, W2s, b1s, dos)
+            sm = time_steps(st, max(3, args.steps // 2), 2, device)
+            dm = time_steps(DenseStep(xs, W1s, W2s, b1s, dos), max(3, args.steps // 2), 2, device)
+            sweep[str(s)] = {"tokens_per_s": round(T_PER_GPU / (sm / 1e3), 1),
+                             "dense_tokens_per_s": round(T_PER_GPU / (dm / 1e3), 1),
+                             "measured_sparsity": round(1.0 - st.buf.used() / (T_PER_GPU * D_FF), 4)}
+            del st, xs, W1s, W2s, b1s, dos
+            torch.cuda.empty_cache()
+        extras["sweep"] = sweep
+
+    pk = peaks()
+    roof = None
+    pack = None
+    if rank == 0:
+        pack = bench_pack(device)
+        roof = {"bound": "hbm", "kernel": "flat_pack_kernel<uint16_t>",
+                "achieved": pack["pack_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(pack["pack_gbs"] / pk["hbm_gbs"], 3), "traffic": None,
+                "peak_source": pk["source"]}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; inputs larger than L2, no flush)",
+            "config": {"workload": "relu2_ffn_fwd_bwd_d4096_f14336_t16384_s0.9",
+                       "tokens_per_gpu": T_PER_GPU, "global_tokens": tokens, "d_model": D_MODEL,
+                       "d_ff": D_FF, "target_sparsity": SPARSITY,
+                       "measured_sparsity": round(s_meas, 4), "parallelism": f"dp{world}",
+                       "l2": "inputs larger than L2"},
+            "e2e": e2e, "clocks": clocks, "roofline": roof, "pack": pack,
+            "gpu_launches": launches_per_step * args.steps,
+        }
+        line.update(extras)
+        if world == 1:
+            try:
+                line["cpu_baseline"] = cpu_baseline(args.cpu_tokens)
+            except Exception as e:  # noqa: BLE001
+                line["cpu_baseline"] = {"error": repr(e)}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,161 @@
+/*
+ * sparseffn.h -- C ABI of the B200 (sm_100a) activation-sparse FFN library
+ * (libsparseffn.so, sources in autoresearch2_b200/csrc/).
+ *
+ * Every entry point takes plain device pointers, int64 sizes, a dtype code and
+ * a CUDA stream (as void*; NULL = the legacy default stream).  Nothing here
+ * allocates device memory: callers pass every buffer, including scratch
+ * ("workspace") whose size the *_workspace_bytes() query returns.  Work is
+ * enqueued on the stream and the call returns without synchronising.
+ *
+ * Return value: SFFN_OK (0) or an SFFN_ERR_* code for errors found on the
+ * host (bad argument, misalignment, launch failure).  Errors that only the
+ * device can see (vals arena too small, a bounded wait that ran out) are
+ * OR-ed into a caller-owned uint32 status word (SFFN_STATUS_* bits); read it
+ * after the stream has been synchronised.
+ *
+ * dtype codes: SFFN_F32 = 0, SFFN_BF16 = 1, SFFN_F16 = 2.
+ *
+ * Each declaration names the reference function (Maccy-Z/autoresearch2,
+ * path:line) whose behaviour it reproduces.
+ */
+#ifndef SPARSEFFN_H
+#define SPARSEFFN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SFFN_F32 = 0,
+    SFFN_BF16 = 1,
+    SFFN_F16 = 2
+};
+
+enum {
+    SFFN_OK = 0,
+    SFFN_ERR_ARG = 1,         /* null pointer, negative or inconsistent size   */
+    SFFN_ERR_DTYPE = 2,       /* dtype code not supported by this entry point  */
+    SFFN_ERR_ALIGN = 3,       /* pointer or stride misaligned for this kernel  */
+    SFFN_ERR_WORKSPACE = 4,   /* workspace smaller than *_workspace_bytes()    */
+    SFFN_ERR_CUDA = 5,        /* a CUDA runtime call or kernel launch failed   */
+    SFFN_ERR_UNSUPPORTED = 6, /* tile shape or GEMM layout not built           */
+    SFFN_ERR_DEVICE = 7       /* current device is not sm_100                  */
+};
+
+/* Bits OR-ed into the device status word. */
+enum {
+    SFFN_STATUS_VALS_OVERFLOW = 1u,  /* output would pass vals capacity; clipped  */
+    SFFN_STATUS_WAIT_TIMEOUT = 2u,   /* a bounded spin-wait gave up               */
+    SFFN_STATUS_CURSOR_OVERFLOW = 4u,/* int32 arena cursor would pass 2^31-1      */
+    SFFN_STATUS_VALS_SHORT = 8u      /* mask has more set bits than vals holds    */
+};
+
+/* ---- library ----------------------------------------------------------- */
+
+/* Version as 10000*major + 100*minor + patch. */
+int sffn_version(void);
+
+/* Static string for an SFFN_ERR_* code. */
+const char* sffn_error_string(int code);
+
+/* Text of the last CUDA error seen by this thread inside the library. */
+const char* sffn_last_cuda_error(void);
+
+/* ---- flat format --------------------------------------------------------
+ * Element f of the row-major tensor -> byte f/8, bit f%8 of packed_mask (LSB
+ * first; equal to bit f%32 of little-endian uint32 word f/32).  A bit is set
+ * iff the element != 0 (-0.0 gives 0, NaN gives 1).  vals holds the set
+ * elements in row-major order.  Tail bits of the last byte are 0.
+ */
+
+/* Scratch needed by sffn_flat_pack / sffn_flat_unpack for n elements. */
+size_t sffn_flat_workspace_bytes(int64_t n);
+
+/* bitsparse_pack(dense, block) -> (vals, packed_mask)
+ *   replaces old/sparse_pack.py:66-106 (kernels :6-63) and
+ *   old/bitpack/train.py:65-103 (compress_dense).
+ * One pass over dense.  Writes ceil(n/8) bytes to packed_mask, the nonzeros
+ * to vals[0, nnz) (at most vals_capacity are written; more sets
+ * SFFN_STATUS_VALS_OVERFLOW), and nnz to *nnz_dev (device int64).
+ * dense must be 16-byte aligned, packed_mask 4-byte aligned. */
+int sffn_flat_pack(const void* dense, int dtype, int64_t n,
+                   uint8_t* packed_mask, void* vals, int64_t vals_capacity,
+                   int64_t* nnz_dev, void* workspace, size_t workspace_bytes,
+                   uint32_t* status_dev, void* stream);
+
+/* bitsparse_unpack(vals, packed_mask, shape, block) -> dense
+ *   replaces old/sparse_unpack.py:57-97 (kernels :6-54) and
+ *   old/bitunpack/train.py:55-90 (reconstruct_bitmask).
+ * out[f] = bit f ? vals[rank(f)] : 0 for f < n.  Reads at most vals_len
+ * values (a mask with more set bits sets SFFN_STATUS_VALS_SHORT).
+ * out must be 16-byte aligned, packed_mask 4-byte aligned. */
+int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_t* packed_mask,
+                     int dtype, int64_t n, void* out,
+                     void* workspace, size_t workspace_bytes,
+                     uint32_t* status_dev, void* stream);
+
+/* ---- tiled format -------------------------------------------------------
+ * A row-major [M, N] matrix (row stride ld elements) is cut into BM x BN tiles;
+ * tile t = tm * grid_n + tn.  In-tile offset f = r*BN + c -> byte
+ * t*BM*BN/8 + f/8, bit f%8.  A bit is set iff the element > 0 (negatives,
+ * +-0 and NaN give 0); elements outside the matrix give 0 bits.
+ * prefix[t] = number of set bits in tiles < t, prefix[num_tiles] = total.
+ * Tile t's values, row-major in the tile, sit at vals[vals_offset + prefix[t]].
+ * Supported (BM, BN): (32, 32), (64, 64), (128, 128), (64, 128), (128, 64).
+ * Readers take the length of the vals buffer (vals_len) and never read or
+ * write outside it; M*N must stay below 2^31 (int32 prefix, as in the reference).
+ */
+
+/* Scratch needed by sffn_tile_pack for an [M, N] matrix. */
+size_t sffn_tile_workspace_bytes(int64_t M, int64_t N, int BM, int BN);
+
+/* dense_to_tilesparse(dense, vals, offset, BLOCK_M, BLOCK_N) -> BitsparseTensor
+ *   replaces old/lib_sparse/sparse.py:154-210 (kernels sparse_pack.py:27-92)
+ *   and old/full_matmul/sparse_pack.py:95-146.
+ * One pass.  Reads the int32 arena cursor *offset_dev, writes it to
+ * *vals_offset_dev, writes bitmask, prefix[num_tiles+1] and the values to
+ * vals[cursor + prefix[t] ...] (never past vals_capacity), then advances
+ * *offset_dev by the total -- all on the device, no host sync. */
+int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld,
+                   int BM, int BN, uint8_t* bitmask, int32_t* prefix,
+                   void* vals, int64_t vals_capacity,
+                   int32_t* offset_dev, int32_t* vals_offset_dev,
+                   void* workspace, size_t workspace_bytes,
+                   uint32_t* status_dev, void* stream);
+
+/* Unpack tile rows [tile_row0, tile_row0 + tile_rows) into out (row stride
+ * ld_out; out row 0 = matrix row tile_row0*BM), optionally squaring each value
+ * in the storage dtype (spAx(..., square=True)).  out_dtype is dtype or
+ * SFFN_F32 (old/full_matmul/sparse_unpack.py:62 returns float32).
+ *   replaces old/lib_sparse/sparse_unpack.py:5-55 (_unpack_batch_kernel, with
+ *   column bounds added), old/full_matmul/sparse_unpack.py:6-73,
+ *   old/full_matmul/train.py:89-137. */
+int sffn_tile_unpack(const void* vals, int64_t vals_len, const uint8_t* bitmask,
+                     const int32_t* prefix, const int32_t* vals_offset_dev, int dtype,
+                     int64_t M, int64_t N, int BM, int BN,
+                     int64_t tile_row0, int64_t tile_rows, int square,
+                     void* out, int out_dtype, int64_t ld_out, void* stream);
+
+/* grad[r, c] = bit ? grad[r, c] : 0, in place (ReLU backward from the mask).
+ *   replaces old/lib_sparse/sparse_unpack.py:72-107 (_mask_with_bitmask_kernel). */
+int sffn_tile_mask_grad(void* grad, int dtype, int64_t M, int64_t N, int64_t ld,
+                        const uint8_t* bitmask, int BM, int BN, void* stream);
+
+/* grad <- (grad * 2) * z in the storage dtype, z gathered from vals (0 off the
+ * mask, so a NaN/Inf grad there gives NaN like the reference); if square,
+ * vals <- z*z in place.
+ *   replaces old/lib_sparse/sparse_unpack.py:110-147 (_grad_relu2_kernel). */
+int sffn_tile_grad_relu2(void* grad, int dtype, int64_t M, int64_t N, int64_t ld,
+                         void* vals, int64_t vals_len, const uint8_t* bitmask, const int32_t* prefix,
+                         const int32_t* vals_offset_dev, int BM, int BN, int square,
+                         void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARSEFFN_H */

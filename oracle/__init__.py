@@ -1,0 +1,258 @@
+"""CPU oracle for the activation-sparse FFN path -- TEST INFRASTRUCTURE ONLY.
+
+This package restates the reference's algorithms on the CPU so that tests,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg can check and
+time the CUDA library against them.  The product package never imports it.
+
+Pinning: every function here is checked in ``tests/test_oracle_golden.py``
+against golden vectors produced by running the reference's own Triton code
+under Triton's CPU interpreter (``tests/golden/make_golden.py``).
+
+Byte/bit work (flat and tiled pack/unpack) is in C (``oracle.c`` ->
+``liboracle.so``, built by ``oracle/Makefile``); floating-point work (mask
+kernels, spAx, FFN forward/backward) is numpy.
+
+Conventions: arrays are numpy; bfloat16 data is carried as its uint16 bit
+pattern.  dtype codes: 0 = float32, 1 = bfloat16, 2 = float16.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+F32, BF16, F16 = 0, 1, 2
+
+_lib = None
+
+
+def build():
+    """Compile liboracle.so (idempotent)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    """Load liboracle.so, building it first if it is missing."""
+    global _lib
+    if _lib is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        L = ctypes.CDLL(path)
+        i64, i32, vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p
+        L.orc_num_threads.restype = ctypes.c_int
+        L.orc_flat_pack.argtypes = [vp, ctypes.c_int, i64, vp, vp, i64, ctypes.c_int]
+        L.orc_flat_pack.restype = i64
+        L.orc_flat_unpack.argtypes = [vp, i64, vp, ctypes.c_int, i64, vp, ctypes.c_int]
+        L.orc_flat_unpack.restype = i64
+        L.orc_tile_pack.argtypes = [vp, ctypes.c_int, i64, i64, i64, ctypes.c_int, ctypes.c_int,
+                                    vp, vp, vp, i64, i64]
+        L.orc_tile_pack.restype = i64
+        L.orc_tile_unpack.argtypes = [vp, vp, vp, i64, ctypes.c_int, i64, i64, ctypes.c_int,
+                                      ctypes.c_int, i64, i64, vp, i64]
+        L.orc_tile_unpack.restype = None
+        del i32
+        _lib = L
+    return _lib
+
+
+def num_threads():
+    return lib().orc_num_threads()
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def dtype_code(a):
+    if a.dtype == np.float32:
+        return F32
+    if a.dtype == np.uint16:
+        return BF16
+    if a.dtype == np.float16:
+        return F16
+    raise TypeError(f"unsupported oracle dtype {a.dtype}")
+
+
+# ---------------------------------------------------------------------------
+# bf16 helpers (bit patterns <-> float32)
+# ---------------------------------------------------------------------------
+def bf16_to_f32(u16):
+    return (np.asarray(u16, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16(f):
+    """Round-to-nearest-even float32 -> bf16 bits (NaN kept quiet)."""
+    f = np.ascontiguousarray(f, dtype=np.float32)
+    u = f.view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    nan = np.isnan(f)
+    r[nan] = ((u[nan] >> 16) | 0x40).astype(np.uint16)
+    return r
+
+
+def to_f64(a, code):
+    if code == BF16:
+        return bf16_to_f32(a).astype(np.float64)
+    return np.asarray(a, dtype=np.float64)
+
+
+def from_f64(x, code):
+    """Round a float64 array to the storage dtype (via float32 for bf16)."""
+    if code == BF16:
+        return f32_to_bf16(np.asarray(x, dtype=np.float32))
+    if code == F16:
+        return np.asarray(x, dtype=np.float16)
+    return np.asarray(x, dtype=np.float32)
+
+
+# ---------------------------------------------------------------------------
+# Flat format (old/sparse_pack.py:66-106, old/sparse_unpack.py:57-97)
+# ---------------------------------------------------------------------------
+def pack_bool_mask(mask):
+    """Golden packer of old/bitpack/prepare.py:6-23: bit i -> byte i//8, bit i%8."""
+    mask = np.asarray(mask, dtype=bool).ravel()
+    n = mask.size
+    nb = (n + 7) // 8
+    padded = np.zeros(nb * 8, dtype=np.uint8)
+    padded[:n] = mask
+    return (padded.reshape(nb, 8) << np.arange(8, dtype=np.uint8)).sum(axis=1).astype(np.uint8)
+
+
+def flat_pack(dense, nthreads=1):
+    """(vals, packed_mask) for a dense array (any shape, row-major)."""
+    d = np.ascontiguousarray(dense).ravel()
+    code = dtype_code(d)
+    n = d.size
+    mask = np.zeros((n + 7) // 8, dtype=np.uint8)
+    vals = np.empty(n, dtype=d.dtype)
+    nnz = lib().orc_flat_pack(_ptr(d), code, n, _ptr(mask), _ptr(vals), n, nthreads)
+    assert nnz >= 0
+    return vals[:nnz].copy(), mask
+
+
+def flat_unpack(vals, packed_mask, shape, nthreads=1):
+    vals = np.ascontiguousarray(vals)
+    mask = np.ascontiguousarray(packed_mask, dtype=np.uint8)
+    n = int(np.prod(shape))
+    out = np.empty(n, dtype=vals.dtype)
+    used = lib().orc_flat_unpack(_ptr(vals), vals.size, _ptr(mask), dtype_code(vals), n,
+                                 _ptr(out), nthreads)
+    if used < 0:
+        raise ValueError("packed mask has more set bits than vals holds")
+    return out.reshape(shape)
+
+
+# ---------------------------------------------------------------------------
+# Tiled format (old/lib_sparse/sparse.py:154-210, sparse_pack.py, sparse_unpack.py)
+# ---------------------------------------------------------------------------
+def tile_pack(dense, BM, BN, vals_arena, offset):
+    """Pack ``dense`` [M, N] into (bitmask, prefix) and write its values into
+    ``vals_arena`` from ``offset``.  Returns (bitmask, prefix, total)."""
+    d = np.ascontiguousarray(dense)
+    M, N = d.shape
+    gm, gn = -(-M // BM), -(-N // BN)
+    bitmask = np.zeros(gm * gn * BM * BN // 8, dtype=np.uint8)
+    prefix = np.zeros(gm * gn + 1, dtype=np.int32)
+    assert vals_arena.dtype == d.dtype and vals_arena.flags.c_contiguous
+    total = lib().orc_tile_pack(_ptr(d), dtype_code(d), M, N, N, BM, BN, _ptr(bitmask),
+                                _ptr(prefix), _ptr(vals_arena), vals_arena.size, int(offset))
+    if total < 0:
+        raise ValueError("vals arena too small")
+    return bitmask, prefix, total
+
+
+def tile_unpack(vals, bitmask, prefix, offset, shape, BM, BN, row0=0, rows=None):
+    vals = np.ascontiguousarray(vals)
+    M, N = shape
+    rows = M - row0 if rows is None else rows
+    out = np.zeros((rows, N), dtype=vals.dtype)
+    lib().orc_tile_unpack(_ptr(vals), _ptr(np.ascontiguousarray(bitmask)),
+                          _ptr(np.ascontiguousarray(prefix, dtype=np.int32)), int(offset),
+                          dtype_code(vals), M, N, BM, BN, row0, rows, _ptr(out), N)
+    return out
+
+
+def tile_bits(bitmask, shape, BM, BN):
+    """Boolean [M, N] mask from a tiled bitmask."""
+    M, N = shape
+    gm, gn = -(-M // BM), -(-N // BN)
+    bits = np.unpackbits(np.asarray(bitmask, dtype=np.uint8), bitorder="little")
+    bits = bits.reshape(gm, gn, BM, BN).transpose(0, 2, 1, 3).reshape(gm * BM, gn * BN)
+    return bits[:M, :N].astype(bool)
+
+
+def mask_with_bitmask(grad, bitmask, BM, BN):
+    """K7 (old/lib_sparse/sparse_unpack.py:72-107): where(bit, grad, 0)."""
+    code = dtype_code(grad)
+    bits = tile_bits(bitmask, grad.shape, BM, BN)
+    g = grad.copy()
+    g[~bits] = 0
+    return g if code != F32 else g.astype(np.float32)
+
+
+def grad_relu2(grad, vals, bitmask, prefix, offset, BM, BN):
+    """K8 (old/lib_sparse/sparse_unpack.py:110-147) with square=True:
+    returns (grad * 2 * z rounded to the storage dtype, vals with z -> z*z).
+    Off-mask z is 0, so grad*0 (NaN/Inf grad gives NaN there, as in the reference)."""
+    code = dtype_code(grad)
+    M, N = grad.shape
+    z = tile_unpack(vals, bitmask, prefix, offset, (M, N), BM, BN)
+    g = to_f64(grad, code)
+    zf = to_f64(z, code)
+    # Triton evaluates (gz * 2.0) * z in the storage dtype; 2.0 scaling is exact.
+    out = from_f64(to_f64(from_f64(g * 2.0, code), code) * zf, code)
+    v = vals.copy()
+    nnz = int(prefix[-1])
+    seg = to_f64(v[offset:offset + nnz], code)
+    v[offset:offset + nnz] = from_f64(seg * seg, code)
+    return out, v
+
+
+def spAx(vals, bitmask, prefix, offset, shape, BM, BN, W, square=False):
+    """spAx (old/lib_sparse/sparse.py:305-351): W @ unpack(x) (optionally squared),
+    computed in float64 and rounded to W's dtype."""
+    code = dtype_code(W)
+    dense = to_f64(tile_unpack(vals, bitmask, prefix, offset, shape, BM, BN), code)
+    if square:
+        dense = to_f64(from_f64(dense * dense, code), code)
+    return from_f64(to_f64(W, code) @ dense, code)
+
+
+# ---------------------------------------------------------------------------
+# FFN forward / backward (sparse.py:56-151, prepare_layer.py:12-29,117-162)
+# ---------------------------------------------------------------------------
+def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.float64):
+    """Forward and backward of out = act(x @ W1.T [+ b1]) @ W2.T.
+
+    act = "relu" follows FFNSparse / FFNv3; act = "relu2" follows FFNSpRelu2 /
+    FFNrelu2 (a = relu(pre)^2, d pre = d a * 2 z on the mask).  Products are
+    accumulated in float64; every intermediate that the reference stores in
+    the storage dtype (pre, z, a, d a, d pre) is rounded to it.
+    `compute` = np.float32 runs the products in float32 (the timed CPU
+    baseline); the default float64 is the checker.
+    Returns dict(out, dx, dW1, dW2, z, mask)."""
+    def r(t):  # round to the storage dtype
+        return to_f64(from_f64(t, code), code).astype(compute, copy=False)
+    xf, W1f, W2f, gf = (to_f64(t, code).astype(compute, copy=False) for t in (x, W1, W2, dout))
+    pre = xf @ W1f.T
+    if b1 is not None:
+        pre = pre + to_f64(b1, code).astype(compute, copy=False)
+    pre = r(pre)
+    z = np.maximum(pre, 0.0)
+    mask = z > 0
+    a = r(z * z) if act == "relu2" else z
+    out = a @ W2f.T
+    dA = r(gf @ W2f)
+    dW2 = gf.T @ a
+    if act == "relu2":
+        dpre = r(r(dA * 2.0) * z)
+    else:
+        dpre = np.where(mask, dA, np.zeros((), dtype=compute))
+    dx = dpre @ W1f
+    dW1 = dpre.T @ xf
+    res = dict(out=out, dx=dx, dW1=dW1, dW2=dW2, z=z, mask=mask, dpre=dpre, a=a)
+    if b1 is not None:
+        res["db1"] = dpre.sum(axis=0)
+    return res

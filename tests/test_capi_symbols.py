@@ -1,0 +1,83 @@
+"""CPU-side checks of the C-ABI library: it loads without a GPU, exports every
+entry point include/sparseffn.h declares, and its host-side argument checks
+reject bad calls before touching the device."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+HEADER = os.path.join(ROOT, "include", "sparseffn.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sffn_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from autoresearch2_b200 import _lib
+    return _lib.load()
+
+
+def test_library_exports_every_declared_symbol(lib):
+    syms = declared_symbols()
+    assert len(syms) >= 10
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_python_binding_covers_every_symbol():
+    from autoresearch2_b200 import _lib
+    assert sorted(_lib.SIGNATURES) == declared_symbols()
+
+
+def test_library_is_built_for_sm100a_only():
+    from autoresearch2_b200 import build
+    assert "arch=compute_100a,code=sm_100a" in " ".join(build.ARCH)
+
+
+def test_version_and_errors(lib):
+    assert lib.sffn_version() >= 100
+    assert lib.sffn_error_string(0) == b"ok"
+    assert b"dtype" in lib.sffn_error_string(2)
+
+
+def test_workspace_queries(lib):
+    assert lib.sffn_flat_workspace_bytes(0) == 16
+    assert lib.sffn_flat_workspace_bytes(8192) == 16 + 8
+    assert lib.sffn_flat_workspace_bytes(8193) == 16 + 16
+    assert lib.sffn_tile_workspace_bytes(130, 192, 64, 64) == 16 + 3 * 3 * 8
+
+
+def test_host_side_rejections(lib):
+    vp = ctypes.c_void_p
+    dummy = vp(256)  # never dereferenced: every call below fails its host checks
+    # unsupported dtype
+    assert lib.sffn_flat_pack(dummy, 9, 10, dummy, dummy, 10, dummy, dummy, 64, dummy, None) == 2
+    # negative size
+    assert lib.sffn_flat_pack(dummy, 1, -1, dummy, dummy, 10, dummy, dummy, 64, dummy, None) == 1
+    # misaligned dense pointer
+    assert lib.sffn_flat_pack(vp(258), 1, 10, dummy, dummy, 10, dummy, dummy, 64, dummy, None) == 3
+    # workspace too small
+    assert lib.sffn_flat_pack(dummy, 1, 10 ** 6, dummy, dummy, 10, dummy, dummy, 8, dummy, None) == 4
+    # unsupported tile shape
+    assert lib.sffn_tile_pack(dummy, 1, 64, 64, 64, 48, 64, dummy, dummy, dummy, 10, dummy,
+                              vp(512), dummy, 4096, dummy, None) == 6
+    # cursor and vals_offset aliasing
+    assert lib.sffn_tile_pack(dummy, 1, 64, 64, 64, 64, 64, dummy, dummy, dummy, 10, dummy,
+                              dummy, dummy, 4096, dummy, None) == 1
+    # unpack row range past the matrix
+    assert lib.sffn_tile_unpack(dummy, 10, dummy, dummy, dummy, 1, 64, 64, 64, 64, 0, 2, 0, dummy,
+                                1, 64, None) == 1
+
+
+def test_python_api_refuses_cpu_tensors():
+    import torch
+    import autoresearch2_b200 as sf
+    with pytest.raises(ValueError, match="CUDA"):
+        sf.bitsparse_pack(torch.zeros(4, 4))

@@ -1,0 +1,77 @@
+"""GPU parity of the sparse FFN autograd functions against the reference's
+golden vectors and the float64 oracle.
+
+Tolerances (elementwise, with an absolute floor scaled to the tensor's
+largest magnitude): fp32 rtol = atol/max|ref| = 1e-5; bf16 2e-2."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def close(got, want, tol):
+    got = got.detach().double().cpu().numpy()
+    want = np.asarray(want, dtype=np.float64)
+    np.testing.assert_allclose(got, want, rtol=tol, atol=tol * np.abs(want).max())
+
+
+@pytest.fixture(autouse=True)
+def _fp32_exact():
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    import autoresearch2_b200 as sf
+    sf.check_status()
+
+
+@pytest.mark.parametrize("act", ["relu", "relu2"])
+def test_ffn_fp32_golden(act):
+    import autoresearch2_b200 as sf
+    g = golden(f"ffn_{act}")
+    x, W1, W2, dout = (torch.from_numpy(g[k]).to(DEV).requires_grad_(k != "dout")
+                       for k in ("x", "W1", "W2", "dout"))
+    fn = sf.FFNSparse if act == "relu" else sf.FFNSpRelu2
+    T, F = x.shape[0], W1.shape[0]
+    arena = torch.empty(T * F, device=DEV)
+    off = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = fn.apply(x, W1, W2, (arena, off))
+    out.backward(dout)
+    close(out, g["out"], 1e-5)
+    close(x.grad, g["dx"], 1e-5)
+    close(W1.grad, g["dW1"], 1e-5)
+    close(W2.grad, g["dW2"], 1e-5)
+    assert int(off.item()) == int(g["nnz"][0])
+
+
+@pytest.mark.parametrize("act", ["relu", "relu2"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("T,D,F", [(256, 128, 384), (512, 256, 1024)])
+def test_ffn_against_oracle(act, dtype, T, D, F):
+    import autoresearch2_b200 as sf
+    g = torch.Generator().manual_seed(T + D + F)
+    x = torch.randn(T, D, generator=g)
+    W1 = torch.randn(F, D, generator=g) / D ** 0.5
+    W2 = torch.randn(D, F, generator=g) / F ** 0.5
+    b1 = torch.full((F,), -0.8)
+    dout = torch.randn(T, D, generator=g)
+    cast = [t.to(dtype) for t in (x, W1, W2, b1, dout)]
+    xg, W1g, W2g, b1g = (t.to(DEV).requires_grad_() for t in cast[:4])
+    fn = sf.FFNSparse if act == "relu" else sf.FFNSpRelu2
+    out = fn.apply(xg, W1g, W2g, None, b1g)
+    out.backward(cast[4].to(DEV))
+    np_in = [oracle.f32_to_bf16(t.float().numpy()) if dtype == torch.bfloat16 else t.numpy()
+             for t in cast]
+    code = oracle.BF16 if dtype == torch.bfloat16 else oracle.F32
+    r = oracle.ffn_fwd_bwd(np_in[0], np_in[1], np_in[2], np_in[4], act=act, b1=np_in[3], code=code)
+    tol = 1e-5 if dtype == torch.float32 else 2e-2
+    close(out, r["out"], tol)
+    close(xg.grad, r["dx"], tol)
+    close(W1g.grad, r["dW1"], tol)
+    close(W2g.grad, r["dW2"], tol)
+    close(b1g.grad, r["db1"], tol)
