@@ -175,11 +175,14 @@ def tile_unpack(x: BitsparseTensor, row_start: int = 0, row_end: int = None, squ
     rows = row_end - row_start
     if out is None:
         out = torch.empty(rows, N, dtype=out_dtype, device=x.vals.device)
+    if out.shape[0] < rows or out.shape[1] != N or out.stride(1) != 1 or out.dtype != out_dtype:
+        raise ValueError("out must be a row-major [rows, N] tensor of out_dtype")
     tr0 = row_start // BM
     trows = (row_end + BM - 1) // BM - tr0
+    # Passing row_end as the row count makes the kernel skip rows past it.
     call("sffn_tile_unpack", ptr(x.vals), x.vals.numel(), ptr(x.bitmask), ptr(x.prefix),
-         ptr(x.vals_offset), code, M, N, BM, BN, tr0, trows, int(bool(square)), ptr(out), ocode,
-         out.stride(0), stream_ptr(x.vals.device))
+         ptr(x.vals_offset), code, row_end, N, BM, BN, tr0, trows, int(bool(square)), ptr(out),
+         ocode, out.stride(0), stream_ptr(x.vals.device))
     return out
 
 

@@ -127,37 +127,71 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     return v;
 }
 
-// Called by one full warp.  Returns the exclusive prefix of partition `part`.
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Publish this partition's aggregate (or, for partition 0, its inclusive
+// prefix).  Called by one thread, before lookback().  The release orders
+// every earlier memory access of that thread before the publication.
+__device__ __forceinline__ void lookback_publish(unsigned long long* states, long long part,
+                                                 unsigned long long agg) {
+    st_release_u64(&states[part], (part == 0 ? LB_INCL : LB_AGG) | (agg & LB_VAL));
+}
+
+// Called by one full warp after lookback_publish().  Returns the exclusive
+// prefix of partition `part` and publishes its inclusive prefix.  Each lane
+// inspects W consecutive predecessors per round, so one round covers 32*W
+// partitions: the resolved frontier advances 32*W partitions per L2 round
+// trip, which bounds the scan's throughput.
+template <int W>
 __device__ __forceinline__ unsigned long long lookback(unsigned long long* states, long long part,
                                                       unsigned long long agg, uint32_t* status,
                                                       int lane) {
-    if (part == 0) {
-        if (lane == 0) st_release_u64(&states[0], LB_INCL | agg);
-        return 0;
-    }
-    if (lane == 0) st_release_u64(&states[part], LB_AGG | agg);
+    if (part == 0) return 0;
     unsigned long long excl = 0;
     long long pred = part - 1;
     unsigned spins = 0;
     while (true) {
-        long long idx = pred - lane;
-        unsigned long long s = idx >= 0 ? ld_acquire_u64(&states[idx]) : LB_INCL;
-        unsigned flag = (unsigned)(s >> 62);
-        unsigned incl = __ballot_sync(FULL, flag == 2);
-        unsigned none = __ballot_sync(FULL, flag == 0);
-        unsigned need = incl ? ((incl & (0u - incl)) << 1) - 1 : FULL;  // lanes up to the first inclusive
-        if (none & need) {
+        unsigned long long s[W];
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const long long idx = pred - (long long)lane * W - k;
+            s[k] = idx >= 0 ? ld_relaxed_u64(&states[idx]) : LB_INCL;
+        }
+        // nearest inclusive entry of this lane, and whether an empty entry precedes it
+        int kin = W;
+#pragma unroll
+        for (int k = W - 1; k >= 0; --k)
+            if ((s[k] >> 62) == 2) kin = k;
+        bool empty_before = false;
+#pragma unroll
+        for (int k = 0; k < W; ++k)
+            if (k <= kin && k < W && (s[k] >> 62) == 0) empty_before = true;
+        const unsigned incl = __ballot_sync(FULL, kin < W);
+        const int first = incl ? __ffs(incl) - 1 : 32;  // nearest lane holding an inclusive entry
+        const bool need_lane = lane <= first;
+        const unsigned waiting = __ballot_sync(FULL, need_lane && empty_before);
+        if (waiting) {
             if (++spins > kLookbackSpinLimit) {
                 if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
                 break;
             }
-            __nanosleep(40);
+            __nanosleep(32);
             continue;
         }
-        unsigned long long v = ((need >> lane) & 1u) ? (s & LB_VAL) : 0ull;
+        unsigned long long v = 0;
+        if (need_lane) {
+            const int upto = lane == first ? kin : W - 1;
+#pragma unroll
+            for (int k = 0; k < W; ++k)
+                if (k <= upto) v += s[k] & LB_VAL;
+        }
         excl += warp_sum_u64(v);
         if (incl) break;
-        pred -= 32;
+        pred -= 32LL * W;
     }
     if (lane == 0) st_release_u64(&states[part], LB_INCL | ((excl + agg) & LB_VAL));
     return excl;

@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
     unsigned long long* __restrict__ states, unsigned* __restrict__ ticket,
     uint32_t* __restrict__ status, long long gn, long long ntiles) {
     using C = TileCfg<BM, BN>;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     B* s_vals = reinterpret_cast<B*>(smem_raw);
     __shared__ int s_wx[C::NE];
     __shared__ int s_agg;
@@ -165,7 +165,9 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
     }
     const int agg = s_agg;
     if (warp == 0) {
-        unsigned long long ex = lookback(states, t, (unsigned long long)agg, status, lane);
+        if (lane == 0) lookback_publish(states, t, (unsigned long long)agg);
+        __syncwarp();
+        unsigned long long ex = lookback<4>(states, t, (unsigned long long)agg, status, lane);
         if (lane == 0) s_excl = ex;
     }
     __syncthreads();
@@ -180,6 +182,9 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
         if (base < 0 || base + agg > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
         if (t == 0) *vals_offset_out = s_cursor;
         if (t == ntiles - 1) {
+            // Every other tile read the cursor before publishing its count,
+            // and this tile has seen all counts: the cursor can now move.
+            __threadfence();
             const long long total = ex + agg;
             prefix[ntiles] = (int)total;
             const long long next = (long long)s_cursor + total;
@@ -200,7 +205,7 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_unpack_kernel(
     using C = TileCfg<BM, BN>;
     using B = typename Elt<DT>::bits;
     using O = typename std::conditional<OUT_F32, uint32_t, B>::type;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     B* s_vals = reinterpret_cast<B*>(smem_raw);
     __shared__ int s_wx[C::NE];
     __shared__ int s_agg;
@@ -285,7 +290,7 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_grad_relu2_kernel(
     const int* __restrict__ vals_offset, long long gn, int square, int vec) {
     using C = TileCfg<BM, BN>;
     using B = typename Elt<DT>::bits;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];
     B* s_vals = reinterpret_cast<B*>(smem_raw);
     __shared__ int s_wx[C::NE];
     __shared__ int s_agg;

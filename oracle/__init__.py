@@ -223,7 +223,7 @@ def spAx(vals, bitmask, prefix, offset, shape, BM, BN, W, square=False):
 # ---------------------------------------------------------------------------
 # FFN forward / backward (sparse.py:56-151, prepare_layer.py:12-29,117-162)
 # ---------------------------------------------------------------------------
-def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.float64):
+def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.float64, mask=None):
     """Forward and backward of out = act(x @ W1.T [+ b1]) @ W2.T.
 
     act = "relu" follows FFNSparse / FFNv3; act = "relu2" follows FFNSpRelu2 /
@@ -231,7 +231,10 @@ def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.floa
     accumulated in float64; every intermediate that the reference stores in
     the storage dtype (pre, z, a, d a, d pre) is rounded to it.
     `compute` = np.float32 runs the products in float32 (the timed CPU
-    baseline); the default float64 is the checker.
+    baseline); the default float64 is the checker.  `mask` (bool [T, F])
+    overrides the ReLU mask, so a device result can be checked with the mask
+    it actually produced (elements whose pre-activation rounds across zero
+    differently in another GEMM flip the ReLU derivative).
     Returns dict(out, dx, dW1, dW2, z, mask)."""
     def r(t):  # round to the storage dtype
         return to_f64(from_f64(t, code), code).astype(compute, copy=False)
@@ -240,8 +243,9 @@ def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.floa
     if b1 is not None:
         pre = pre + to_f64(b1, code).astype(compute, copy=False)
     pre = r(pre)
-    z = np.maximum(pre, 0.0)
-    mask = z > 0
+    if mask is None:
+        mask = pre > 0
+    z = np.where(mask, np.maximum(pre, 0.0), np.zeros((), dtype=compute))
     a = r(z * z) if act == "relu2" else z
     out = a @ W2f.T
     dA = r(gf @ W2f)
@@ -252,7 +256,7 @@ def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.floa
         dpre = np.where(mask, dA, np.zeros((), dtype=compute))
     dx = dpre @ W1f
     dW1 = dpre.T @ xf
-    res = dict(out=out, dx=dx, dW1=dW1, dW2=dW2, z=z, mask=mask, dpre=dpre, a=a)
+    res = dict(out=out, dx=dx, dW1=dW1, dW2=dW2, z=z, mask=mask, dpre=dpre, a=a, pre=pre)
     if b1 is not None:
         res["db1"] = dpre.sum(axis=0)
     return res
