@@ -4,13 +4,16 @@
 // prefix, vals kernel -- the dense tensor is read twice) and
 // old/sparse_unpack.py:6-97 (popcount, one-program serial prefix, rebuild).
 //
-// Pack is ONE persistent kernel.  Each CTA takes 32 KB chunks of the dense
-// tensor in ticket order and streams them through a 3-stage ring of shared
-// memory filled by 1-D TMA bulk copies.  Per chunk: mask bytes and counts in
-// registers, a block scan, the compacted values written back into the stage
-// buffer, a decoupled look-back (128 predecessors per round) for the chunk's
-// global offset, then a coalesced copy of the values to `vals`.  The dense
-// tensor is read exactly once.
+// Pack is ONE persistent kernel, launched cooperatively so that all its CTAs
+// are resident.  CTA c owns chunks c, c+G, c+2G, ... (G = grid size) of 32 KB
+// and streams them through a 3-stage ring of shared memory filled by 1-D TMA
+// bulk copies, so the copies of its next two chunks are in flight while it
+// works on one.  Per chunk: mask bytes and counts in registers, a block scan,
+// the compacted values written back into the stage buffer, a decoupled
+// look-back (256 predecessors per round) for the chunk's global offset, then a
+// coalesced copy of the values to `vals`.  Because every chunk of round k is
+// being worked on at the same time and round k-1 is resolved, a look-back
+// needs at most two rounds of loads.  The dense tensor is read exactly once.
 //
 // Unpack needs no look-back: a small kernel popcounts the mask per 16K-element
 // chunk and the last CTA to finish scans the counts; the expand kernel then
@@ -32,7 +35,7 @@ constexpr int FL_NT = 256;
 constexpr int FL_NW = FL_NT / 32;
 constexpr int PACK_CHUNK_BYTES = 32768;
 constexpr int PACK_STAGES = 3;
-constexpr int LB_W = 4;  // look-back: 4 states per lane, 128 per round
+constexpr int LB_W = 8;  // look-back: 8 states per lane, 256 per round
 
 template <typename B>
 struct PackCfg {
@@ -104,7 +107,7 @@ template <typename B>
 __global__ void __launch_bounds__(FL_NT, 2) flat_pack_kernel(
     const B* __restrict__ dense, long long n, uint8_t* __restrict__ mask, B* __restrict__ vals,
     long long cap, long long* __restrict__ nnz_out, unsigned long long* __restrict__ states,
-    unsigned* __restrict__ ticket, uint32_t* __restrict__ status, long long nchunks) {
+    uint32_t* __restrict__ status, long long nchunks) {
     using C = PackCfg<B>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     B* stage = reinterpret_cast<B*>(smem_raw);  // [PACK_STAGES][CE]
@@ -116,9 +119,9 @@ __global__ void __launch_bounds__(FL_NT, 2) flat_pack_kernel(
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const long long nbytes = (n + 7) >> 3;
 
-    // Producer (thread 0): take the next chunk and start its bulk copy into stage s.
-    auto issue = [&](int s) {
-        const long long t = (long long)atomicAdd(ticket, 1u);
+    // Producer (thread 0): start the bulk copy of this CTA's k-th chunk into stage s.
+    auto issue = [&](int s, long long k) {
+        const long long t = (long long)blockIdx.x + k * gridDim.x;
         s_tick[s] = t;
         if (t < nchunks) {
             const long long nvalid = min((long long)C::CE, n - t * C::CE);
@@ -134,7 +137,7 @@ __global__ void __launch_bounds__(FL_NT, 2) flat_pack_kernel(
     }
     __syncthreads();
     if (tid == 0)
-        for (int s = 0; s < PACK_STAGES; ++s) issue(s);
+        for (int s = 0; s < PACK_STAGES; ++s) issue(s, s);
     __syncthreads();
 
     for (int it = 0;; ++it) {
@@ -232,7 +235,7 @@ __global__ void __launch_bounds__(FL_NT, 2) flat_pack_kernel(
         // the next bulk copy (async proxy) into it.
         fence_proxy_async_smem();
         __syncthreads();  // stage s fully consumed
-        if (tid == 0) issue(s);
+        if (tid == 0) issue(s, it + PACK_STAGES);
         __syncthreads();
     }
 }
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(FL_NT, 2) flat_pack_kernel(
 constexpr int UNP_CE = 16384;               // elements per unpack chunk
 constexpr int UNP_SUBS = UNP_CE / (FL_NT * 8);  // 8
 constexpr int UNP_NE = UNP_SUBS * FL_NW;        // 64
-constexpr int CNT_CHUNKS_PER_CTA = 64;
+constexpr int CNT_CHUNKS_PER_CTA = 16;
 
 // Popcount of each chunk's mask; the last CTA to finish scans all counts into
 // cprefix[0..nchunks] (exclusive prefix, cprefix[nchunks] = total).
@@ -256,12 +259,22 @@ __global__ void __launch_bounds__(FL_NT) flat_count_kernel(
         if (c >= nchunks) break;
         const long long b0 = c * (UNP_CE / 8), b1 = min(b0 + UNP_CE / 8, nbytes);
         int cnt = 0;
-        // 2 KB per chunk: 32 lanes x 16 words, coalesced 128 B per warp load
-        for (long long b = b0 + lane * 4; b < b1; b += 32 * 4) {
-            if (b + 4 <= b1) {
-                cnt += __popc(__ldcs(reinterpret_cast<const unsigned int*>(mask + b)));
-            } else {
-                for (long long e = b; e < b1; ++e) cnt += __popc((uint32_t)mask[e]);
+        // 2 KB per chunk: 32 lanes x 16 words, coalesced 128 B per warp load;
+        // all 16 loads are issued before any is used.
+        if (b0 + UNP_CE / 8 <= nbytes) {
+            unsigned int w[16];
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                w[k] = __ldcs(reinterpret_cast<const unsigned int*>(mask + b0 + 4 * (lane + 32 * k)));
+#pragma unroll
+            for (int k = 0; k < 16; ++k) cnt += __popc(w[k]);
+        } else {
+            for (long long b = b0 + lane * 4; b < b1; b += 32 * 4) {
+                if (b + 4 <= b1) {
+                    cnt += __popc(__ldcs(reinterpret_cast<const unsigned int*>(mask + b)));
+                } else {
+                    for (long long e = b; e < b1; ++e) cnt += __popc((uint32_t)mask[e]);
+                }
             }
         }
         // bits of the last byte past n are ignored
@@ -393,6 +406,29 @@ cudaError_t allow_smem(K kernel, int bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// Cooperative launch: every CTA is resident, which the look-back's waits on
+// the other CTAs of the same round rely on.
+template <typename B>
+int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long long cap,
+                int64_t* nnz_dev, unsigned long long* states, uint32_t* status, long long nch,
+                cudaStream_t st) {
+    const int smem = PACK_STAGES * PACK_CHUNK_BYTES;
+    auto k = flat_pack_kernel<B>;
+    SFFN_CUDA_TRY(allow_smem(k, smem));
+    int per_sm = 0;
+    SFFN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, FL_NT, smem));
+    if (per_sm < 1) return SFFN_ERR_CUDA;
+    const long long grid = std::min<long long>(nch, (long long)per_sm * num_sms());
+    const B* d = static_cast<const B*>(dense);
+    B* v = static_cast<B*>(vals);
+    long long* nz = reinterpret_cast<long long*>(nnz_dev);
+    void* args[] = {(void*)&d, (void*)&n, (void*)&mask, (void*)&v, (void*)&cap, (void*)&nz,
+                    (void*)&states, (void*)&status, (void*)&nch};
+    SFFN_CUDA_TRY(cudaLaunchCooperativeKernel((const void*)k, dim3((unsigned)grid), dim3(FL_NT), args,
+                                              (size_t)smem, st));
+    return SFFN_OK;
+}
+
 }  // namespace
 }  // namespace sffn
 
@@ -423,26 +459,13 @@ extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* 
     if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
     const int esz = esize_of(dtype);
     const long long nch = pack_chunks(n, esz);
-    unsigned* ticket = reinterpret_cast<unsigned*>(workspace);
     auto* states = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) + 16);
     SFFN_CUDA_TRY(cudaMemsetAsync(workspace, 0, 16 + (size_t)nch * 8, st));
-    const int smem = PACK_STAGES * PACK_CHUNK_BYTES;
-    const long long grid = std::min<long long>(nch, 2LL * num_sms());
-    if (esz == 4) {
-        auto k = flat_pack_kernel<uint32_t>;
-        SFFN_CUDA_TRY(allow_smem(k, smem));
-        k<<<(unsigned)grid, FL_NT, smem, st>>>((const uint32_t*)dense, n, packed_mask, (uint32_t*)vals,
-                                              vals_capacity, (long long*)nnz_dev, states, ticket,
-                                              status_dev, nch);
-    } else {
-        auto k = flat_pack_kernel<uint16_t>;
-        SFFN_CUDA_TRY(allow_smem(k, smem));
-        k<<<(unsigned)grid, FL_NT, smem, st>>>((const uint16_t*)dense, n, packed_mask, (uint16_t*)vals,
-                                              vals_capacity, (long long*)nnz_dev, states, ticket,
-                                              status_dev, nch);
-    }
-    SFFN_CHECK_LAUNCH();
-    return SFFN_OK;
+    if (esz == 4)
+        return launch_pack<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, states,
+                                     status_dev, nch, st);
+    return launch_pack<uint16_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, states,
+                                 status_dev, nch, st);
 }
 
 extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_t* packed_mask,
