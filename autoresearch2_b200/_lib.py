@@ -44,6 +44,15 @@ SIGNATURES = {
     "sffn_tile_mask_grad": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _int, _vp]),
     "sffn_tile_grad_relu2": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _int,
                                     _int, _int, _vp]),
+    "sffn_gemm_bf16": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp,
+                              _vp, _int, _vp, _vp]),
+    "sffn_ffn_up": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
+                           _vp, _vp, _vp]),
+    "sffn_tile_scan_counts": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "sffn_tile_gather_slots": (_int, [_vp, _int, _vp, _vp, _i64, _vp, _i64, _int, _vp, _vp]),
+    "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
+                              _vp, _vp, _vp, _i64, _vp, _vp]),
 }
 
 _lib = None
@@ -66,9 +75,11 @@ def load():
     return _lib
 
 
-# Entry points that launch exactly one kernel of this library per call.
-LAUNCHING = {"sffn_flat_pack", "sffn_flat_unpack", "sffn_tile_pack", "sffn_tile_unpack",
-             "sffn_tile_mask_grad", "sffn_tile_grad_relu2"}
+# Kernels of this library each entry point launches per call.
+LAUNCHING = {"sffn_flat_pack": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
+             "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
+             "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
+             "sffn_tile_gather_slots": 1, "sffn_live_kblocks": 1, "sffn_ffn_dgrad": 1}
 launch_count = 0
 
 
@@ -77,8 +88,8 @@ def call(name, *args):
     global launch_count
     lib = load()
     rc = getattr(lib, name)(*args)
-    if rc == 0 and name in LAUNCHING:
-        launch_count += 1
+    if rc == 0:
+        launch_count += LAUNCHING.get(name, 0)
     if rc != 0:
         msg = lib.sffn_error_string(rc).decode()
         if rc == 5:

@@ -9,18 +9,76 @@ tiled BitsparseTensor on ctx.z_sparse (the activation-memory saving);
 backward clears it and returns one gradient per input (None for the arena).
 Weights use nn.Linear layout: W1 [F, D], W2 [D, F]; x [T, D].
 
+bf16 inputs run the fused tcgen05 path: the up-projection GEMM's epilogue
+applies bias + ReLU/ReLU^2 and emits the bitmask, counts and compacted z (a
+128x128-tile BitsparseTensor); the down-projection skips 64-wide K blocks
+that are zero in a whole 128-row tile; the backward's dout @ W2 epilogue
+applies the mask / 2z gradient from the packed z and emits the activation
+for dW2, so no dense z is kept between forward and backward.  float32 and
+float16 inputs run cuBLAS matmuls with this library's pack/mask kernels
+(64x64 tiles, as in the reference).
+
 Differences (documented, not inherited defects): FFNSpRelu2 accepts the vals
 arena (the reference's forward omits it and raises TypeError,
-sparse.py:120), and both accept an optional up-projection bias b1 [F] as a
-trailing argument (the reference has none).
+sparse.py:120), both accept an optional up-projection bias b1 [F] as a
+trailing argument (the reference has none), and the fused bf16 backward
+leaves the stored z values unchanged (the reference squares them in place,
+sparse.py:136-144).
 """
 import torch
 import torch.nn.functional as F
 from torch.autograd import Function
 
 from . import bitsparse as bs
+from . import gemm as G
 
 __all__ = ["FFNSparse", "FFNSpRelu2"]
+
+
+def _fused_ok(x, W1, W2, b1, vals):
+    """bf16 tensors laid out for the tcgen05 path (16-byte aligned rows)."""
+    ts = [x, W1, W2, vals] + ([b1] if b1 is not None else [])
+    if not all(t.is_cuda and t.dtype == torch.bfloat16 for t in ts):
+        return False
+    if not (x.is_contiguous() and W1.is_contiguous() and W2.is_contiguous()):
+        return False
+    if b1 is not None and not b1.is_contiguous():
+        return False
+    D, Fd = x.shape[1], W1.shape[0]
+    return D % 8 == 0 and Fd % 8 == 0 and x.shape[0] * Fd < 2 ** 31
+
+
+def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
+    T, D = x.shape
+    Fd = W1.shape[0]
+    a, bitmask, prefix, voff = G.ffn_up(x, W1, b1, act, vals, offset)
+    kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
+    out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
+    del a
+    z_sparse = bs.BitsparseTensor(vals, bitmask, prefix, voff, -(-T // 128), -(-Fd // 128), 128, 128,
+                                  (T, Fd))
+    ctx.save_for_backward(x, W1, W2)
+    ctx.z_sparse = z_sparse
+    ctx.kb = (kb_list, kb_count)
+    ctx.has_bias = b1 is not None
+    ctx.fused = True
+    return out
+
+
+def _fused_backward(ctx, grad_output, act):
+    x, W1, W2 = ctx.saved_tensors
+    z_sparse = ctx.z_sparse
+    ctx.z_sparse = None
+    kb_list, kb_count = ctx.kb
+    ctx.kb = None
+    grad_output = grad_output.contiguous()
+    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse)
+    grad_W2 = G.mm(grad_output.T, a)
+    del a
+    grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
+    grad_W1 = G.mm(dpre.T, x)
+    grad_b1 = dpre.sum(0, dtype=torch.float32).to(dpre.dtype) if ctx.has_bias else None
+    return grad_x, grad_W1, grad_W2, None, grad_b1
 
 
 def _arena(sparse_data, numel, like):
@@ -37,6 +95,9 @@ class FFNSparse(Function):
     @staticmethod
     def forward(ctx, x, W1, W2, sparse_data, b1=None):
         vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
+        if _fused_ok(x, W1, W2, b1, vals):
+            return _fused_forward(ctx, x, W1, W2, vals, offset, b1, G.ACT_RELU)
+        ctx.fused = False
         preact = x @ W1.T
         if b1 is not None:
             preact += b1
@@ -51,6 +112,8 @@ class FFNSparse(Function):
 
     @staticmethod
     def backward(ctx, grad_output):
+        if ctx.fused:
+            return _fused_backward(ctx, grad_output, G.ACT_RELU)
         x, W1, W2 = ctx.saved_tensors
         z_sparse = ctx.z_sparse
         ctx.z_sparse = None
@@ -70,6 +133,9 @@ class FFNSpRelu2(Function):
     @staticmethod
     def forward(ctx, x, W1, W2, sparse_data=None, b1=None):
         vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
+        if _fused_ok(x, W1, W2, b1, vals):
+            return _fused_forward(ctx, x, W1, W2, vals, offset, b1, G.ACT_RELU2)
+        ctx.fused = False
         preact = x @ W1.T
         if b1 is not None:
             preact += b1
@@ -84,6 +150,8 @@ class FFNSpRelu2(Function):
 
     @staticmethod
     def backward(ctx, grad_output):
+        if ctx.fused:
+            return _fused_backward(ctx, grad_output, G.ACT_RELU2)
         x, W1, W2 = ctx.saved_tensors
         z_sparse = ctx.z_sparse
         ctx.z_sparse = None

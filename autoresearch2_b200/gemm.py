@@ -1,0 +1,108 @@
+"""bf16 tcgen05 GEMM and the fused FFN kernels, called through the C ABI.
+
+mm(A, B) computes A @ B for 2-D bf16 CUDA tensors that are row-major or
+transposed views of row-major tensors (the kernel reads either major order
+directly, so no transposed copies are made).
+"""
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream_ptr
+
+ACT_RELU, ACT_RELU2 = 0, 1
+FORMAT_TILE = 128
+
+
+def _operand(t, rows_dim):
+    """(ld, mn_major) of a 2-D operand whose row index is dim `rows_dim` of
+    the mathematical [rows, K] (A) or [K, cols] (B) view."""
+    s0, s1 = t.stride()
+    if rows_dim == 0:  # A [M, K]
+        if s1 == 1:
+            return s0, 0
+        if s0 == 1:
+            return s1, 1
+    else:  # B [K, N]: the kernel wants the [N, K] operand
+        if s0 == 1:
+            return s1, 0
+        if s1 == 1:
+            return s0, 1
+    raise ValueError("operands must be row-major or transposed views of row-major tensors")
+
+
+def mm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, kb_list=None, kb_count=None):
+    """C = A @ B (bf16 in, fp32 accumulate, bf16 out) on the tcgen05 kernel.
+
+    kb_list / kb_count (int32, from live_kblocks) restrict row tile m of A to
+    the listed 64-wide K blocks (the rest of A's row tile must be zero there)."""
+    _lib.require_cuda(A, B)
+    if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
+        raise TypeError("mm takes bfloat16 operands")
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(B.shape)}")
+    lda, a_mn = _operand(A, 0)
+    ldb, b_mn = _operand(B, 1)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=A.device)
+    if out.stride(1) != 1 or tuple(out.shape) != (M, N):
+        raise ValueError("out must be a row-major [M, N] tensor")
+    stride = 0
+    if kb_list is not None:
+        stride = kb_list.shape[1]
+    call("sffn_gemm_bf16", ptr(A), lda, a_mn, ptr(B), ldb, b_mn, ptr(out), out.stride(0), M, N, K,
+         ptr(kb_list), ptr(kb_count), stride, ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+    return out
+
+
+def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
+    """(kb_list [ceil(M/128), ceil(N/64)] int32, kb_count [ceil(M/128)] int32)
+    of the 64-column blocks holding any set bit of a tiled 128x128 bitmask."""
+    gm, nkb = -(-M // 128), -(-N // 64)
+    kb_list = torch.empty(gm, nkb, dtype=torch.int32, device=bitmask.device)
+    kb_count = torch.empty(gm, dtype=torch.int32, device=bitmask.device)
+    call("sffn_live_kblocks", ptr(bitmask), M, N, ptr(kb_list), ptr(kb_count),
+         stream_ptr(bitmask.device))
+    return kb_list, kb_count
+
+
+def ffn_up(x, W1, b1, act, vals, offset):
+    """Fused x @ W1.T (+ b1) -> act(z) dense plus the tiled 128x128 sparse z.
+
+    Returns (act_dense [T, F], bitmask, prefix, vals_offset)."""
+    T, D = x.shape
+    F = W1.shape[0]
+    dev = x.device
+    gm, gn = -(-T // 128), -(-F // 128)
+    nt = gm * gn
+    act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+    bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
+    counts = torch.empty(nt, dtype=torch.int32, device=dev)
+    slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
+    prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
+    vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
+    status = ptr(_lib.status_word(dev))
+    st = stream_ptr(dev)
+    call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
+         ptr(act_out), act_out.stride(0), ptr(bitmask), ptr(counts), ptr(slots), status, st)
+    call("sffn_tile_scan_counts", ptr(counts), nt, ptr(prefix), ptr(offset), ptr(vals_offset),
+         status, st)
+    call("sffn_tile_gather_slots", ptr(slots), 128 * 128, ptr(prefix), ptr(vals_offset), nt,
+         ptr(vals), vals.numel(), _lib.BF16, status, st)
+    return act_out, bitmask, prefix, vals_offset
+
+
+def ffn_dgrad(dout, W2, act, z_sparse):
+    """Fused dout @ W2 with the activation gradient; returns (dpre, act2)
+    where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F]."""
+    T, D = dout.shape
+    F = W2.shape[1]
+    dev = dout.device
+    dpre = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+    act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+    call("sffn_ffn_dgrad", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,
+         ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(z_sparse.prefix),
+         ptr(z_sparse.vals_offset), ptr(dpre), ptr(act2), dpre.stride(0),
+         ptr(_lib.status_word(dev)), stream_ptr(dev))
+    return dpre, act2

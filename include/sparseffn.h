@@ -154,6 +154,73 @@ int sffn_tile_grad_relu2(void* grad, int dtype, int64_t M, int64_t N, int64_t ld
                          const int32_t* vals_offset_dev, int BM, int BN, int square,
                          void* stream);
 
+/* ---- tensor-core GEMMs and the fused sparse FFN ---------------------------
+ * bf16 operands, fp32 accumulation in tensor memory (tcgen05), bf16 output.
+ * Operand bases and row strides must be 16-byte aligned (ld % 8 == 0).
+ */
+
+/* C[M, N] = A[M, K] @ B[N, K]^T.
+ * a_mn = 0: A stored [M][lda] (K contiguous); a_mn = 1: A stored [K][lda]
+ * (M contiguous, i.e. the transpose of a row-major [K, M] tensor).  Same for
+ * B with N.  Optional kb_list/kb_count (both or neither): for row tile
+ * m = row/128, only the kb_count[m] 64-wide K blocks listed in
+ * kb_list[m*kb_stride ...] are accumulated (the others are known to be zero).
+ *   replaces the torch/cuBLAS matmuls of old/lib_sparse/sparse.py:72-149 and
+ *   prepare_layer.py:25-27,131-160 (x@W1.T, z@W2.T, grad@W2, grad.T@z,
+ *   grad@W1, grad.T@x). */
+int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                   void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                   const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
+                   uint32_t* status_dev, void* stream);
+
+/* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
+ * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely, the
+ * tiled 128x128 bitmask of z > 0 (ceil(T/128)*ceil(F/128) tiles of 2048 B),
+ * the per-tile counts, and each tile's z values, row-major in the tile, to
+ * slots[t*16384 ...].  Follow with sffn_tile_scan_counts and
+ * sffn_tile_gather_slots to finish the BitsparseTensor.
+ *   replaces old/lib_sparse/sparse.py:72-77,116-120 (matmul, relu, square,
+ *   dense_to_tilesparse) and old/matmul_bitsparse/train.py:11-116
+ *   (_matmul_sparse_kernel + compaction). */
+int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
+                int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
+                uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
+                void* stream);
+
+/* prefix[t] = sum of tile_counts[< t], prefix[ntiles] = total; *vals_offset_dev
+ * = *offset_dev; *offset_dev += total.
+ *   replaces old/lib_sparse/sparse.py:181-186,200-204 (cumsum, cursor). */
+int sffn_tile_scan_counts(const int32_t* tile_counts, int64_t ntiles, int32_t* prefix,
+                          int32_t* offset_dev, int32_t* vals_offset_dev, uint32_t* status_dev,
+                          void* stream);
+
+/* vals[*vals_offset_dev + prefix[t] + i] = slots[t*tile_elems + i] for
+ * i < prefix[t+1]-prefix[t] (16-bit dtypes; never past vals_capacity).
+ *   replaces old/lib_sparse/sparse_pack.py:65-92 (_compact_vals_kernel). */
+int sffn_tile_gather_slots(const void* slots, int tile_elems, const int32_t* prefix,
+                           const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
+                           int64_t vals_capacity, int dtype, uint32_t* status_dev, void* stream);
+
+/* For a tiled 128x128 bitmask of an [M, N] matrix: kb_count[m] and the
+ * ascending list kb_list[m*ceil(N/64) ...] of 64-column blocks of row tile m
+ * that hold any set bit (no reference counterpart: the reference's
+ * down-projection is dense, sparse.py:75,118). */
+int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
+                      int32_t* kb_count, void* stream);
+
+/* Fused activation gradient: g = bf16(dout @ W2) ([T, F]; W2 is [D, F]).
+ * ReLU^2 (act = 1): dpre = bf16((g*2) * z) and act_out = bf16(z*z); ReLU
+ * (act = 0): dpre = bit ? g : 0 and act_out = z -- z gathered from the
+ * tiled 128x128 BitsparseTensor (vals, bitmask, prefix, *vals_offset_dev).
+ *   replaces old/lib_sparse/sparse.py:92-102,132-145 (grad_output @ W2 with
+ *   _mask_with_bitmask_kernel / _grad_relu2_kernel) and the unpack inside spAx
+ *   (sparse.py:305-351). */
+int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2,
+                   int64_t T, int64_t D, int64_t F, int act, const void* vals, int64_t vals_len,
+                   const uint8_t* bitmask, const int32_t* prefix, const int32_t* vals_offset_dev,
+                   void* dpre_out, void* act_out, int64_t ld_out, uint32_t* status_dev,
+                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

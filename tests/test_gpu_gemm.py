@@ -1,0 +1,138 @@
+"""GPU tests of the tcgen05 GEMM and the fused FFN epilogues.
+
+GEMM numerics are checked against an fp32 torch product of the same bf16
+operands (tolerance: 1e-2 relative to the largest |C|, bf16 output rounding
+plus accumulation order).  The fused up-projection is checked for
+self-consistency bit for bit: its bitmask, prefix and vals must equal what the
+standalone packer produces from the z it wrote."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _status_clean():
+    import autoresearch2_b200 as sf
+    yield
+    sf.check_status()
+
+
+def ref_mm(A, B):
+    return (A.float() @ B.float())
+
+
+def assert_close_rel(got, want, tol=1e-2):
+    err = (got.float() - want).abs().max().item()
+    scale = want.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max err {err} vs scale {scale}"
+
+
+def rand(*shape, seed=0, scale=1.0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, device=DEV, generator=g) * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (200, 300, 72), (1000, 776, 520),
+                                   (2048, 2048, 4096), (129, 8, 8)])
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+def test_mm_layouts(M, N, K, a_t, b_t):
+    from autoresearch2_b200 import gemm
+    A = rand(K, M, seed=1).T if a_t else rand(M, K, seed=1)   # a_t: transposed view
+    B = rand(N, K, seed=2).T if b_t else rand(K, N, seed=2)
+    C = gemm.mm(A, B)
+    assert_close_rel(C, ref_mm(A, B))
+
+
+def test_mm_out_and_strided_output():
+    from autoresearch2_b200 import gemm
+    A, B = rand(256, 128, seed=3), rand(128, 256, seed=4)
+    big = torch.zeros(256, 320, dtype=torch.bfloat16, device=DEV)
+    out = big[:, :256]
+    gemm.mm(A, B, out=out)
+    assert_close_rel(out, ref_mm(A, B))
+    assert torch.count_nonzero(big[:, 256:]) == 0
+
+
+def test_mm_k_skip_lists():
+    """Row tiles skip 64-wide K blocks that are zero in the whole tile."""
+    from autoresearch2_b200 import gemm
+    M, N, K = 384, 256, 512
+    A = rand(M, K, seed=5)
+    keep = torch.rand(M // 128, K // 64, generator=torch.Generator().manual_seed(0)) < 0.5
+    keep[1] = False  # one row tile with no live block at all
+    mask = keep.repeat_interleave(128, 0).repeat_interleave(64, 1).to(DEV)
+    A = torch.where(mask, A, torch.zeros((), dtype=A.dtype, device=DEV))
+    B = rand(K, N, seed=6)
+    kb_list = torch.zeros(M // 128, K // 64, dtype=torch.int32)
+    kb_count = torch.zeros(M // 128, dtype=torch.int32)
+    for m in range(M // 128):
+        live = torch.nonzero(keep[m]).flatten()
+        kb_list[m, :live.numel()] = live.int()
+        kb_count[m] = live.numel()
+    C = gemm.mm(A, B, kb_list=kb_list.to(DEV), kb_count=kb_count.to(DEV))
+    assert_close_rel(C, ref_mm(A, B))
+    assert torch.count_nonzero(C[128:256]) == 0
+
+
+@pytest.mark.parametrize("act", [0, 1])
+@pytest.mark.parametrize("T,D,F,bias", [(256, 128, 384, True), (300, 72, 200, False),
+                                        (1024, 512, 1536, True)])
+def test_ffn_up_fused(act, T, D, F, bias):
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    x = rand(T, D, seed=7)
+    W1 = rand(F, D, seed=8, scale=D ** -0.5)
+    b1 = torch.full((F,), -0.7, device=DEV, dtype=torch.bfloat16) if bias else None
+    arena = torch.full((T * F + 50,), 9.0, device=DEV, dtype=torch.bfloat16)
+    offset = torch.tensor([17], dtype=torch.int32, device=DEV)
+    a, bitmask, prefix, voff = gemm.ffn_up(x, W1, b1, act, arena, offset)
+    pre = x.float() @ W1.float().T + (b1.float() if bias else 0)
+    z_ref = torch.relu(pre)
+    # the device z: the kernel's own dense output (ReLU) or the unpacked values
+    x_sp = sf.BitsparseTensor(arena, bitmask, prefix, voff, -(-T // 128), -(-F // 128), 128, 128, (T, F))
+    z_dev = x_sp.to_dense()
+    assert_close_rel(z_dev, z_ref, 1e-2)
+    if act == 0:
+        assert torch.equal(a, z_dev)
+    else:
+        assert torch.equal(a, (z_dev.float() * z_dev.float()).to(torch.bfloat16))
+    # self-consistency: the standalone packer on z_dev gives the same format
+    arena2 = torch.full_like(arena, 9.0)
+    off2 = torch.tensor([17], dtype=torch.int32, device=DEV)
+    y = sf.dense_to_tilesparse(z_dev, arena2, off2, 128, 128)
+    assert torch.equal(y.bitmask, bitmask)
+    assert torch.equal(y.prefix, prefix)
+    assert torch.equal(arena2.view(torch.int16), arena.view(torch.int16))
+    assert int(offset.item()) == int(off2.item()) == 17 + int((z_dev > 0).sum())
+    assert int(voff.item()) == 17
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_ffn_dgrad_fused(act):
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    T, D, F = 384, 256, 640
+    x = rand(T, D, seed=9)
+    W1 = rand(F, D, seed=10, scale=D ** -0.5)
+    W2 = rand(D, F, seed=11, scale=F ** -0.5)
+    dout = rand(T, D, seed=12)
+    b1 = torch.full((F,), -0.5, device=DEV, dtype=torch.bfloat16)
+    arena = torch.empty(T * F, device=DEV, dtype=torch.bfloat16)
+    offset = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _, bitmask, prefix, voff = gemm.ffn_up(x, W1, b1, act, arena, offset)
+    zs = sf.BitsparseTensor(arena, bitmask, prefix, voff, -(-T // 128), -(-F // 128), 128, 128, (T, F))
+    dpre, act2 = gemm.ffn_dgrad(dout, W2, act, zs)
+    z = zs.to_dense().float()
+    g = (dout.float() @ W2.float()).to(torch.bfloat16).float()
+    if act == 1:
+        want_d = (g * 2 * z)
+        want_a = z * z
+    else:
+        want_d = torch.where(z > 0, g, torch.zeros_like(g))
+        want_a = z
+    assert_close_rel(dpre, want_d, 2e-2)
+    assert torch.equal(act2, want_a.to(torch.bfloat16))
+    # exact: elements off the mask are (signed) zero
+    assert torch.count_nonzero(dpre[z == 0]) == 0
