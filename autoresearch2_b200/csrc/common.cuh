@@ -108,15 +108,15 @@ __device__ __forceinline__ uint32_t bytes_to_word(uint32_t byte, int lane) {
 // ---------------------------------------------------------------------------
 // Decoupled look-back over a sequence of partitions (single-pass scan).
 // State word per partition: bits 63:62 = flag (0 none, 1 aggregate, 2 inclusive),
-// bits 61:0 = value.  Partitions take ordered tickets, so every predecessor of a
-// running partition has started and the wait ends; it is still bounded: after
-// kLookbackSpinLimit polls the partition records SFFN_STATUS_WAIT_TIMEOUT,
-// publishes what it has and returns.
+// bits 61:0 = value.  Partitions are processed in an order in which every
+// predecessor of a running partition has started, so the wait ends; it is
+// still bounded: after kLookbackLimitNs of wall time the partition records
+// SFFN_STATUS_WAIT_TIMEOUT, publishes what it has and returns.
 // ---------------------------------------------------------------------------
 constexpr unsigned long long LB_AGG = 1ull << 62;
 constexpr unsigned long long LB_INCL = 2ull << 62;
 constexpr unsigned long long LB_VAL = (1ull << 62) - 1;
-constexpr unsigned kLookbackSpinLimit = 1u << 22;
+constexpr unsigned long long kLookbackLimitNs = 500ull * 1000 * 1000;  // wall-time bound
 
 __device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
     asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -153,7 +153,7 @@ __device__ __forceinline__ unsigned long long lookback(unsigned long long* state
     if (part == 0) return 0;
     unsigned long long excl = 0;
     long long pred = part - 1;
-    unsigned spins = 0;
+    unsigned long long t0 = 0;
     while (true) {
         unsigned long long s[W];
 #pragma unroll
@@ -175,7 +175,11 @@ __device__ __forceinline__ unsigned long long lookback(unsigned long long* state
         const bool need_lane = lane <= first;
         const unsigned waiting = __ballot_sync(FULL, need_lane && empty_before);
         if (waiting) {
-            if (++spins > kLookbackSpinLimit) {
+            unsigned long long now;
+            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
+            if (t0 == 0) t0 = now;
+            // lane 0's clock decides for the whole warp
+            if (__shfl_sync(FULL, now - t0 > kLookbackLimitNs ? 1 : 0, 0)) {
                 if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
                 break;
             }

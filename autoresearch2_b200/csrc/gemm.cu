@@ -280,8 +280,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             int tm, tn;
             raster(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int nkb = args.kb_count ? args.kb_count[tm] : nkb_full;
-            const bool ok = mbar_wait_bounded(&tfull_bar[acc], acc_phase);
-            if (!ok || s_abort) {
+            // every lane must take the same branch before the warp-collective tcgen05.ld
+            const bool ok = __all_sync(FULL, mbar_wait_bounded(&tfull_bar[acc], acc_phase));
+            if (!ok || __any_sync(FULL, s_abort != 0)) {
                 if (lane == 0) atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
                 break;
             }
@@ -356,7 +357,8 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     int k = 0;
 #pragma unroll 1
                     for (int c = 0; c < 4; ++c) {
-                        if (!words[c]) continue;
+                        // tcgen05.ld is warp-collective: skip only if no lane needs it
+                        if (!__any_sync(FULL, words[c] != 0)) continue;
                         uint32_t r[32];
                         tmem_ld32(tbase + h * FT + c * 32, r);
                         tmem_wait_ld();

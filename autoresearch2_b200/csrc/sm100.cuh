@@ -40,14 +40,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity; false if it gave up.
-// 2^24 polls is >= ~0.3 s even when every poll returns at once -- far longer
-// than any legitimate wait here (one output tile), far shorter than a hang.
-constexpr uint32_t kMbarSpinLimit = 1u << 24;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
+// try_wait with a suspend-time hint (ns): the thread sleeps at most that long.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase with the given parity, giving up after kWaitLimitNs of
+// wall time (far longer than any legitimate wait in these kernels -- one
+// output tile or one chunk -- far shorter than a hang); false if it gave up.
+constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kMbarSpinLimit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait_hint(bar, parity, 2000)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    }
 }
 
 // 1-D bulk copy global -> shared (TMA), completing `bytes` on `bar`.
