@@ -11,6 +11,7 @@ void set_cuda_error(cudaError_t e) {
     snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s: %s", cudaGetErrorName(e),
              cudaGetErrorString(e));
 }
+void set_error_text(const char* msg) { snprintf(g_last_cuda_error, sizeof(g_last_cuda_error), "%s", msg); }
 }  // namespace sffn
 
 extern "C" int sffn_version(void) { return 100; }

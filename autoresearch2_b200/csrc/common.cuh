@@ -18,6 +18,7 @@ constexpr unsigned FULL = 0xffffffffu;
 // Host-side error plumbing
 // ---------------------------------------------------------------------------
 void set_cuda_error(cudaError_t e);
+void set_error_text(const char* msg);
 
 #define SFFN_CHECK_LAUNCH()                                  \
     do {                                                     \
@@ -36,6 +37,27 @@ void set_cuda_error(cudaError_t e);
             return SFFN_ERR_CUDA;                            \
         }                                                    \
     } while (0)
+
+// Make the device that owns `p` current for this thread (and its primary
+// context current, which driver calls such as cuTensorMapEncodeTiled need).
+// Callers may arrive on any host thread -- e.g. an autograd worker -- on which
+// this library's runtime has not selected a device yet.
+inline int bind_device_of(const void* p) {
+    cudaPointerAttributes a;
+    if (p && cudaPointerGetAttributes(&a, p) == cudaSuccess &&
+        (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)) {
+        int cur = -1;
+        if (cudaGetDevice(&cur) != cudaSuccess || cur != a.device) {
+            if (cudaSetDevice(a.device) != cudaSuccess) return SFFN_ERR_CUDA;
+        }
+        // cudaSetDevice does not bind the context when the device is already
+        // current; cudaFree(0) initialises and binds it.
+        if (cudaFree(nullptr) != cudaSuccess) return SFFN_ERR_CUDA;
+        return SFFN_OK;
+    }
+    cudaGetLastError();  // clear a failed pointer query
+    return SFFN_ERR_ARG;
+}
 
 inline int esize_of(int dtype) { return dtype == SFFN_F32 ? 4 : 2; }
 inline bool dtype_ok(int dtype) { return dtype == SFFN_F32 || dtype == SFFN_BF16 || dtype == SFFN_F16; }

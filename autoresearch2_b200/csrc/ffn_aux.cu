@@ -107,6 +107,7 @@ extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int64_t ntiles,
     if (ntiles <= 0 || !tile_counts || !prefix || !offset_dev || !vals_offset_dev || !status_dev)
         return SFFN_ERR_ARG;
     if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
+    if (int rc = bind_device_of(tile_counts)) return rc;
     tile_scan_kernel<<<1, SCAN_NT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         tile_counts, ntiles, prefix, offset_dev, vals_offset_dev, status_dev);
     SFFN_CHECK_LAUNCH();
@@ -119,6 +120,7 @@ extern "C" int sffn_tile_gather_slots(const void* slots, int tile_elems, const i
     if (dtype != SFFN_BF16 && dtype != SFFN_F16) return SFFN_ERR_DTYPE;
     if (ntiles <= 0 || tile_elems <= 0 || !slots || !prefix || !vals_offset_dev || !vals || !status_dev)
         return SFFN_ERR_ARG;
+    if (int rc = bind_device_of(vals)) return rc;
     slot_gather_kernel<<<(unsigned)ntiles, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t*>(slots), tile_elems, prefix, vals_offset_dev, static_cast<uint16_t*>(vals),
         vals_capacity, status_dev);
@@ -132,6 +134,7 @@ extern "C" int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, i
     if (reinterpret_cast<uintptr_t>(bitmask) & 7u) return SFFN_ERR_ALIGN;
     const long long gm = (M + 127) / 128, gn_f = (N + 127) / 128, nkb = (N + 63) / 64;
     if (nkb > 12288) return SFFN_ERR_UNSUPPORTED;  // shared-memory flag array
+    if (int rc = bind_device_of(bitmask)) return rc;
     live_kblocks_kernel<<<(unsigned)gm, 256, (size_t)nkb * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
         bitmask, (int)gn_f, (int)nkb, kb_list, kb_count);
     SFFN_CHECK_LAUNCH();

@@ -451,12 +451,14 @@ extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* 
     if (n < 0 || vals_capacity < 0 || !nnz_dev || !status_dev) return SFFN_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (n == 0) {
+        if (int rc = bind_device_of(nnz_dev)) return rc;
         SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
         return SFFN_OK;
     }
     if (!dense || !packed_mask || (!vals && vals_capacity > 0) || !workspace) return SFFN_ERR_ARG;
     if (!aligned16(dense) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u)) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
+    if (int rc = bind_device_of(dense)) return rc;
     const int esz = esize_of(dtype);
     const long long nch = pack_chunks(n, esz);
     auto* states = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) + 16);
@@ -477,6 +479,7 @@ extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_
     if (!packed_mask || !out || !workspace || (!vals && vals_len > 0)) return SFFN_ERR_ARG;
     if (!aligned16(out) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u)) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
+    if (int rc = bind_device_of(out)) return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const long long nch = unpack_chunks(n);
     unsigned* done = reinterpret_cast<unsigned*>(workspace);

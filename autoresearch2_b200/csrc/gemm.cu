@@ -34,6 +34,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <stdio.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -450,9 +452,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     if (!fn) {
         cudaDriverEntryPointQueryResult q;
         void* p = nullptr;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (e == cudaSuccess && q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            set_error_text("cuTensorMapEncodeTiled entry point not found");
     }
     return fn;
 }
@@ -467,9 +471,17 @@ bool make_tmap(CUtensorMap* m, const void* base, long long inner, long long oute
     cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        char msg[200];
+        snprintf(msg, sizeof(msg), "cuTensorMapEncodeTiled -> %d (base %p dims %lld x %lld ld %lld box %d x %d)",
+                 (int)r, base, inner, outer, ld, box_inner, box_outer);
+        set_error_text(msg);
+        return false;
+    }
+    return true;
 }
 
 int g_num_sms() {
@@ -530,6 +542,7 @@ int check_operands(const void* A, long long lda, bool a_mn, const void* B, long 
     if (!A || !B) return SFFN_ERR_ARG;
     if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16) return SFFN_ERR_ALIGN;
     if (lda < (a_mn ? M : K) || ldb < (b_mn ? N : K)) return SFFN_ERR_ARG;
+    if (int rc = bind_device_of(A)) return rc;
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     return SFFN_OK;
 }
