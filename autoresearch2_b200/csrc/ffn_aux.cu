@@ -8,7 +8,8 @@
 //                       (written by the up-projection epilogue, which cannot
 //                       know the tile's final offset) to
 //                       vals[vals_offset + prefix[t] ...].
-//   live_kblocks_kernel for each 128-row tile of a tiled 128x128 bitmask,
+//   live_kblocks_kernel for each 256-row tile (two rows of 128x128 format
+//                       tiles, the GEMM's CTA-pair tile) of a tiled bitmask,
 //                       the ascending list of 64-column blocks holding any set
 //                       bit: the down-projection skips the others.
 #include "common.cuh"
@@ -69,20 +70,25 @@ __global__ void __launch_bounds__(256) slot_gather_kernel(const uint16_t* __rest
     }
 }
 
-// One CTA per 128-row tile; one warp per 64-column block at a time.
-__global__ void __launch_bounds__(256) live_kblocks_kernel(const uint8_t* __restrict__ mask, int gn_f, int nkb,
-                                                           int* __restrict__ kb_list, int* __restrict__ kb_count) {
+// One CTA per 256-row tile; one warp per 64-column block at a time.
+__global__ void __launch_bounds__(256) live_kblocks_kernel(const uint8_t* __restrict__ mask, int gm_f, int gn_f,
+                                                           int nkb, int* __restrict__ kb_list,
+                                                           int* __restrict__ kb_count) {
     extern __shared__ int s_live[];  // [nkb]
-    const int tm = blockIdx.x;
+    const int tp = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int kb = warp; kb < nkb; kb += blockDim.x / 32) {
-        const long long tf = (long long)tm * gn_f + kb / 2;
-        const uint8_t* tmask = mask + tf * 2048 + (kb & 1) * 8;  // 2 words of each 16-byte row
         uint32_t any = 0;
+        for (int h = 0; h < 2; ++h) {
+            const int tm = 2 * tp + h;
+            if (tm >= gm_f) break;
+            const long long tf = (long long)tm * gn_f + kb / 2;
+            const uint8_t* tmask = mask + tf * 2048 + (kb & 1) * 8;  // 2 words of each 16-byte row
 #pragma unroll
-        for (int r = lane; r < 128; r += 32) {
-            const uint2 w = *reinterpret_cast<const uint2*>(tmask + r * 16);
-            any |= w.x | w.y;
+            for (int r = lane; r < 128; r += 32) {
+                const uint2 w = *reinterpret_cast<const uint2*>(tmask + r * 16);
+                any |= w.x | w.y;
+            }
         }
         any = __any_sync(FULL, any != 0);
         if (lane == 0) s_live[kb] = any ? 1 : 0;
@@ -91,8 +97,8 @@ __global__ void __launch_bounds__(256) live_kblocks_kernel(const uint8_t* __rest
     if (threadIdx.x == 0) {
         int n = 0;
         for (int kb = 0; kb < nkb; ++kb)
-            if (s_live[kb]) kb_list[(long long)tm * nkb + n++] = kb;
-        kb_count[tm] = n;
+            if (s_live[kb]) kb_list[(long long)tp * nkb + n++] = kb;
+        kb_count[tp] = n;
     }
 }
 
@@ -132,11 +138,11 @@ extern "C" int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, i
                                  int32_t* kb_count, void* stream) {
     if (M <= 0 || N <= 0 || !bitmask || !kb_list || !kb_count) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 7u) return SFFN_ERR_ALIGN;
-    const long long gm = (M + 127) / 128, gn_f = (N + 127) / 128, nkb = (N + 63) / 64;
+    const long long gm = (M + 127) / 128, gp = (M + 255) / 256, gn_f = (N + 127) / 128, nkb = (N + 63) / 64;
     if (nkb > 12288) return SFFN_ERR_UNSUPPORTED;  // shared-memory flag array
     if (int rc = bind_device_of(bitmask)) return rc;
-    live_kblocks_kernel<<<(unsigned)gm, 256, (size_t)nkb * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
-        bitmask, (int)gn_f, (int)nkb, kb_list, kb_count);
+    live_kblocks_kernel<<<(unsigned)gp, 256, (size_t)nkb * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
+        bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list, kb_count);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

@@ -5,20 +5,28 @@
 //   A is K-major ([M][lda], K contiguous) or MN-major ([K][lda], M contiguous);
 //   B likewise with N.  This covers all six FFN GEMMs without transposes.
 //
-// Design (one CTA per SM, persistent over output tiles of 128 x BN):
-//   warp 0       TMA producer: 2-D tiled bulk-tensor loads (128-byte swizzle)
-//                of A and B k-blocks (64 wide) into a 4-stage shared-memory ring.
-//   warp 1       MMA issuer: one thread issues tcgen05.mma (M=128, N=BN, K=16)
-//                into one of two TMEM accumulators, commits stage releases and
-//                accumulator-ready signals through mbarriers.
-//   warp 2       allocates / frees the 2*BN TMEM columns.
-//   warps 4..7   epilogue: each thread owns one accumulator row (TMEM lane),
+// Design (one CTA per SM, CTA pairs (clusters of 2) persistent over output
+// tiles of 256 x BN; each CTA of the pair owns 128 rows):
+//   warp 0       TMA producer (both CTAs): 2-D tiled bulk-tensor loads (128-byte
+//                swizzle) of this CTA's half of the A and B k-blocks (64 wide)
+//                into a 6-stage shared-memory ring; the bytes complete on the
+//                leader CTA's barrier.
+//   warp 1       MMA issuer (leader CTA only): one thread issues
+//                tcgen05.mma.cta_group::2 (M=256, N=BN, K=16), which reads the A
+//                and B halves from both CTAs' shared memory and accumulates rows
+//                0-127 in the leader's TMEM and 128-255 in the peer's, into one
+//                of two accumulators; commits are multicast to both CTAs.
+//   warp 2       allocates / frees the 2*BN TMEM columns (pair allocation).
+//   warps 4..11  epilogue, two warpgroups each owning half of the tile's
+//                columns: each thread owns one accumulator row (TMEM lane),
 //                reads 32 columns per tcgen05.ld, applies the epilogue and
 //                stores with 16-byte vector stores; the second accumulator
 //                lets the next tile's MMAs run meanwhile.
+// Splitting B between the two CTAs halves the shared-memory bytes each SM
+// needs per k-block (32 KB instead of 48 KB), which buys a 6-stage ring.
 // Tiles are visited in groups of 16 row-tiles so that a wave of CTAs shares
-// A and B tiles in L2.  An optional per-row-tile list of live k-blocks lets
-// the down-projection skip 64-wide K blocks whose activations are all zero.
+// A and B tiles in L2.  An optional per-256-row-tile list of live k-blocks
+// lets the down-projection skip 64-wide K blocks whose activations are all zero.
 //
 // Epilogues:
 //   STORE  bf16 C.
@@ -46,9 +54,10 @@ namespace {
 
 constexpr int G_BM = 128;
 constexpr int G_BK = 64;
-constexpr int G_THREADS = 256;
-constexpr int G_STAGES = 4;
-constexpr int G_GROUP_M = 16;
+constexpr int G_THREADS = 384;  // 4 control warps + 2 epilogue warpgroups
+constexpr int G_STAGES = 6;
+constexpr int G_GROUP_M = 8;  // pair-tile rows per raster group (16 row tiles of 128)
+constexpr int G_CTAS = 2;     // CTA pairs (cta_group::2)
 constexpr int FT = 128;            // format tile (BLOCK_M = BLOCK_N = 128)
 constexpr int FT_BYTES = FT * FT / 8;
 constexpr int FT_ELEMS = FT * FT;
@@ -112,10 +121,10 @@ __device__ __forceinline__ void store_row32(uint16_t* row, int gcol, int N, bool
 }
 
 // 128-thread exclusive scan of one count per epilogue thread (ew = warp 0..3).
-__device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_part, int* total) {
+__device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_part, int* total, int bar_id) {
     const int inc = warp_incl_scan(cnt, lane);
     if (lane == 31) s_part[ew] = inc;
-    named_bar_sync(1, 128);
+    named_bar_sync(bar_id, 128);
     int before = 0, all = 0;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
@@ -128,15 +137,17 @@ __device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_par
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(G_THREADS, 1)
+__global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmArgs args) {
+    constexpr int BN_CTA = BN / G_CTAS;  // B rows (N) loaded by each CTA
     constexpr int A_BYTES = G_BM * G_BK * 2;
-    constexpr int B_BYTES = BN * G_BK * 2;
+    constexpr int B_BYTES = BN_CTA * G_BK * 2;
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr uint32_t IDESC = idesc_bf16_f32(G_BM, BN, A_MN, B_MN);
+    constexpr uint32_t IDESC = idesc_bf16_f32(G_BM * G_CTAS, BN, A_MN, B_MN);
     constexpr int TMEM_COLS = 2 * BN;
     constexpr uint32_t MN_LBO = G_BK * 128;  // MN-major: 64-element blocks are K rows x 128 B apart
+    static_assert(BN_CTA % 64 == 0, "each CTA loads whole 64-row B blocks");
 
     extern __shared__ __align__(1024) unsigned char g_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -147,20 +158,27 @@ __global__ void __launch_bounds__(G_THREADS, 1)
     __shared__ __align__(8) uint64_t tempty_bar[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
-    __shared__ int s_scan[2][4];
+    __shared__ int s_scan[2][2][4];     // [warpgroup][tile parity][warp]
+    __shared__ float s_bias[2][2][FT];  // [warpgroup][tile parity][column]
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ntiles = args.tiles_m * args.tiles_n;
+    // Pair tiles: 256 rows (two 128-row tiles, one per CTA) x BN columns.
+    const int tiles_mp = (args.tiles_m + 1) / 2;
+    const int ntiles = tiles_mp * args.tiles_n;
     const int nkb_full = (args.K + G_BK - 1) / G_BK;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int first_tile = (int)cluster_id_x();
+    const int tile_stride = (int)cluster_count_x();
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < G_STAGES; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], 1);
+            mbar_init(&full_bar[s], 1);   // leader: its own arrive.expect_tx for both CTAs' bytes
+            mbar_init(&empty_bar[s], 1);  // one multicast commit per use
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
-            mbar_init(&tempty_bar[a], 4);
+            mbar_init(&tempty_bar[a], 8 * G_CTAS);  // every epilogue warp of both CTAs
         }
         s_abort = 0;
         fence_mbar_init();
@@ -168,11 +186,12 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         prefetch_tmap(&tmB);
     }
     if (warp == 2) {
-        tmem_alloc(&s_tmem, TMEM_COLS);
-        tmem_relinquish();
+        tmem_alloc_pair(&s_tmem, TMEM_COLS);
+        tmem_relinquish_pair();
     }
     tc_fence_before();
-    __syncthreads();
+    // barriers and TMEM of both CTAs are set up before any cross-CTA traffic
+    cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = s_tmem;
 
@@ -182,34 +201,39 @@ __global__ void __launch_bounds__(G_THREADS, 1)
             int stage = 0;
             uint32_t phase = 0;
             int armed[G_STAGES] = {0};
-            for (int tile = blockIdx.x; tile < ntiles && !s_abort; tile += gridDim.x) {
-                int tm, tn;
-                raster(tile, args.tiles_m, args.tiles_n, tm, tn);
-                const int nkb = args.kb_count ? args.kb_count[tm] : nkb_full;
+            for (int tile = first_tile; tile < ntiles && !s_abort; tile += tile_stride) {
+                int pm, tn;
+                raster(tile, tiles_mp, args.tiles_n, pm, tn);
+                const int nkb = args.kb_count ? args.kb_count[pm] : nkb_full;
+                const int arow = pm * G_BM * G_CTAS + (int)rank * G_BM;   // this CTA's A rows
+                const int brow = tn * BN + (int)rank * BN_CTA;            // this CTA's B rows (N)
                 for (int i = 0; i < nkb; ++i) {
-                    const int kb = args.kb_list ? args.kb_list[(size_t)tm * args.kb_stride + i] : i;
+                    const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : i;
+                    // the stage is free once the leader's MMAs reading it are done
                     if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
                         atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
                         s_abort = 1;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-                    ++armed[stage];
+                    if (leader) {
+                        mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES * G_CTAS);
+                        ++armed[stage];
+                    }
                     unsigned char* sa = smem + (size_t)stage * STAGE_BYTES;
                     unsigned char* sb = sa + A_BYTES;
                     if constexpr (!A_MN) {
-                        tma_load_2d(sa, &tmA, kb * G_BK, tm * G_BM, &full_bar[stage]);
+                        tma_load_2d_pair(sa, &tmA, kb * G_BK, arow, &full_bar[stage]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < G_BM / 64; ++j)
-                            tma_load_2d(sa + j * MN_LBO, &tmA, tm * G_BM + j * 64, kb * G_BK, &full_bar[stage]);
+                            tma_load_2d_pair(sa + j * MN_LBO, &tmA, arow + j * 64, kb * G_BK, &full_bar[stage]);
                     }
                     if constexpr (!B_MN) {
-                        tma_load_2d(sb, &tmB, kb * G_BK, tn * BN, &full_bar[stage]);
+                        tma_load_2d_pair(sb, &tmB, kb * G_BK, brow, &full_bar[stage]);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < BN / 64; ++j)
-                            tma_load_2d(sb + j * MN_LBO, &tmB, tn * BN + j * 64, kb * G_BK, &full_bar[stage]);
+                        for (int j = 0; j < BN_CTA / 64; ++j)
+                            tma_load_2d_pair(sb + j * MN_LBO, &tmB, brow + j * 64, kb * G_BK, &full_bar[stage]);
                     }
                     if (++stage == G_STAGES) {
                         stage = 0;
@@ -217,22 +241,24 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     }
                 }
             }
-            // No copy may still be landing in shared memory when the CTA exits.
-            for (int s = 0; s < G_STAGES; ++s)
-                if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
+            // The leader's full barriers count both CTAs' bytes: once their last
+            // armed phases complete, no copy is still landing in either CTA.
+            if (leader)
+                for (int s = 0; s < G_STAGES; ++s)
+                    if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
         }
         __syncwarp();
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             int stage = 0;
             uint32_t phase = 0;
             int acc = 0;
             uint32_t acc_phase = 0;
-            for (int tile = blockIdx.x; tile < ntiles && !s_abort; tile += gridDim.x) {
-                int tm, tn;
-                raster(tile, args.tiles_m, args.tiles_n, tm, tn);
-                const int nkb = args.kb_count ? args.kb_count[tm] : nkb_full;
+            for (int tile = first_tile; tile < ntiles && !s_abort; tile += tile_stride) {
+                int pm, tn;
+                raster(tile, tiles_mp, args.tiles_n, pm, tn);
+                const int nkb = args.kb_count ? args.kb_count[pm] : nkb_full;
                 if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u)) {
                     atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
                     s_abort = 1;
@@ -255,15 +281,15 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                                                  : umma_desc_sw128(sa + k * 32, 16, 1024);
                         const uint64_t bd = B_MN ? umma_desc_sw128(sb + k * 2048, MN_LBO, 1024)
                                                  : umma_desc_sw128(sb + k * 32, 16, 1024);
-                        tc_mma_f16(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
+                        tc_mma_f16_pair(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
                     }
-                    tc_commit(&empty_bar[stage]);
+                    tc_commit_pair_multicast(&empty_bar[stage], 0x3);
                     if (++stage == G_STAGES) {
                         stage = 0;
                         phase ^= 1u;
                     }
                 }
-                tc_commit(&tfull_bar[acc]);
+                tc_commit_pair_multicast(&tfull_bar[acc], 0x3);
                 if (++acc == 2) {
                     acc = 0;
                     acc_phase ^= 1u;
@@ -273,15 +299,28 @@ __global__ void __launch_bounds__(G_THREADS, 1)
         __syncwarp();
     } else if (warp >= 4) {
         // ------------------------------------------------------ epilogue --
-        const int ew = warp - 4;
+        // Two warpgroups: warps 4-7 own accumulator columns [0, BN/2), warps
+        // 8-11 own [BN/2, BN).  Warp w reads TMEM lanes 32*(w%4) .. +31 (the
+        // lane quarter tcgen05.ld gives it), so thread = accumulator row.
+        constexpr int HALF = BN / 2;
+        static_assert(EPI == EPI_STORE || HALF == FT, "fused epilogues map one warpgroup to one format tile");
+        const int wg = (warp - 4) >> 2;
+        const int ew = warp & 3;
         const int row = ew * 32 + lane;
         const int gn_f = (args.N + FT - 1) / FT;
+        const int bar_id = 1 + wg;
+        const uint16_t* __restrict__ vals = args.vals;
+        const uint16_t* __restrict__ bias = args.bias;
+        const uint32_t tempty_leader[2] = {leader_smem_addr(&tempty_bar[0]), leader_smem_addr(&tempty_bar[1])};
         int acc = 0;
         uint32_t acc_phase = 0;
-        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-            int tm, tn;
-            raster(tile, args.tiles_m, args.tiles_n, tm, tn);
-            const int nkb = args.kb_count ? args.kb_count[tm] : nkb_full;
+        int it = 0;
+        for (int tile = first_tile; tile < ntiles; tile += tile_stride, ++it) {
+            int pm, tn;
+            raster(tile, tiles_mp, args.tiles_n, pm, tn);
+            const int tm = pm * G_CTAS + (int)rank;  // this CTA's 128-row tile
+            const bool tile_ok = tm < args.tiles_m;   // false for the empty half of an odd last pair
+            const int nkb = args.kb_count ? args.kb_count[pm] : nkb_full;
             // every lane must take the same branch before the warp-collective tcgen05.ld
             const bool ok = __all_sync(FULL, mbar_wait_bounded(&tfull_bar[acc], acc_phase));
             if (!ok || __any_sync(FULL, s_abort != 0)) {
@@ -289,15 +328,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN);
+            const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * BN + wg * HALF);
             const int grow = tm * G_BM + row;
             const bool row_ok = grow < args.M;
+            const int gcol0 = tn * BN + wg * HALF;  // first column of this warpgroup
             uint16_t* orow = args.out + (size_t)grow * args.ldc;
             const bool vec = args.vec_out != 0;
+            const int par = it & 1;
 
             if constexpr (EPI == EPI_STORE) {
 #pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = 0; c < HALF / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld32(tbase + c * 32, r);
                     tmem_wait_ld();
@@ -305,21 +346,22 @@ __global__ void __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         w[q] = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])) : 0u;
-                    if (row_ok) store_row32(orow, tn * BN + c * 32, args.N, vec, w);
+                    if (row_ok) store_row32(orow, gcol0 + c * 32, args.N, vec, w);
                 }
             } else if constexpr (EPI == EPI_UP) {
-#pragma unroll 1
-                for (int h = 0; h < BN / FT; ++h) {
-                    const int tnf = tn * (BN / FT) + h;
-                    const int gcol0 = tnf * FT;
-                    if (gcol0 >= args.N) break;  // uniform over the 128 epilogue threads
-                    const long long tf = (long long)tm * gn_f + tnf;
+                if (gcol0 < args.N && tile_ok) {  // uniform over the warpgroup
+                    const long long tf = (long long)tm * gn_f + gcol0 / FT;
+                    float* sb = s_bias[wg][par];
+                    if (bias) {
+                        sb[row] = gcol0 + row < args.N ? bf16_to_f(bias[gcol0 + row]) : 0.f;
+                        named_bar_sync(bar_id, 128);
+                    }
                     uint32_t words[4];
                     int cnt = 0;
-#pragma unroll 1
+#pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         uint32_t r[32];
-                        tmem_ld32(tbase + h * FT + c * 32, r);
+                        tmem_ld32(tbase + c * 32, r);
                         tmem_wait_ld();
                         const int gcol = gcol0 + c * 32;
                         uint32_t bits = 0, w[16];
@@ -327,9 +369,9 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                         for (int j = 0; j < 32; j += 2) {
                             float v0 = nkb ? __uint_as_float(r[j]) : 0.f;
                             float v1 = nkb ? __uint_as_float(r[j + 1]) : 0.f;
-                            if (args.bias) {
-                                if (gcol + j < args.N) v0 += bf16_to_f(args.bias[gcol + j]);
-                                if (gcol + j + 1 < args.N) v1 += bf16_to_f(args.bias[gcol + j + 1]);
+                            if (bias) {
+                                v0 += sb[c * 32 + j];
+                                v1 += sb[c * 32 + j + 1];
                             }
                             // pre rounded to bf16, z = relu(pre) (NaN stays NaN, as in torch)
                             const uint16_t p0 = f_to_bf16(v0), p1 = f_to_bf16(v1);
@@ -352,51 +394,56 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     *reinterpret_cast<uint4*>(args.mask + tf * FT_BYTES + row * 16) =
                         make_uint4(words[0], words[1], words[2], words[3]);
                     int total;
-                    const int rex = epi_scan128(cnt, ew, lane, s_scan[h], &total);
+                    const int rex = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
                     if (row == FT - 1) args.tile_counts[tf] = total;
                     // second pass: z values of this row, compacted into the tile's slot
                     uint16_t* slot = args.slots + tf * FT_ELEMS + rex;
                     int k = 0;
-#pragma unroll 1
+#pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         // tcgen05.ld is warp-collective: skip only if no lane needs it
                         if (!__any_sync(FULL, words[c] != 0)) continue;
                         uint32_t r[32];
-                        tmem_ld32(tbase + h * FT + c * 32, r);
+                        tmem_ld32(tbase + c * 32, r);
                         tmem_wait_ld();
-                        const int gcol = gcol0 + c * 32;
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
                             if ((words[c] >> j) & 1u) {
                                 float v = __uint_as_float(r[j]);
-                                if (args.bias) v += bf16_to_f(args.bias[gcol + j]);
+                                if (bias) v += sb[c * 32 + j];
                                 slot[k++] = f_to_bf16(v);
                             }
                         }
                     }
                 }
             } else {  // EPI_DGRAD
-                uint16_t* orow2 = args.out2 + (size_t)grow * args.ldc;
-                const long long voff = (long long)*args.vals_offset;
-#pragma unroll 1
-                for (int h = 0; h < BN / FT; ++h) {
-                    const int tnf = tn * (BN / FT) + h;
-                    const int gcol0 = tnf * FT;
-                    if (gcol0 >= args.N) break;  // uniform over the 128 epilogue threads
-                    const long long tf = (long long)tm * gn_f + tnf;
+                if (gcol0 < args.N && tile_ok) {  // uniform over the warpgroup
+                    uint16_t* orow2 = args.out2 + (size_t)grow * args.ldc;
+                    const long long tf = (long long)tm * gn_f + gcol0 / FT;
                     uint4 mw = make_uint4(0, 0, 0, 0);
-                    if (row_ok) mw = *reinterpret_cast<const uint4*>(args.mask + tf * FT_BYTES + row * 16);
+                    if (row_ok) mw = __ldg(reinterpret_cast<const uint4*>(args.mask + tf * FT_BYTES + row * 16));
                     const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
                     const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
                     int total;
-                    const int rex = epi_scan128(cnt, ew, lane, s_scan[h], &total);
-                    long long vbase = voff + args.prefix[tf] + rex;
-#pragma unroll 1
+                    const int rex = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
+                    long long vbase = (long long)*args.vals_offset + args.prefix[tf] + rex;
+#pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        uint32_t r[32];
-                        tmem_ld32(tbase + h * FT + c * 32, r);
-                        tmem_wait_ld();
                         const uint32_t bits = words[c];
+                        // gather this chunk's z first: read-only loads, free to run ahead
+                        float z[32];
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            z[j] = 0.f;
+                            if ((bits >> j) & 1u) {
+                                const long long p = vbase + __popc(bits & ((1u << j) - 1u));
+                                if (p >= 0 && p < args.vals_len) z[j] = bf16_to_f(__ldg(vals + p));
+                            }
+                        }
+                        vbase += __popc(bits);
+                        uint32_t r[32];
+                        tmem_ld32(tbase + c * 32, r);
+                        tmem_wait_ld();
                         uint32_t wd[16], wa[16];
 #pragma unroll
                         for (int j = 0; j < 32; j += 2) {
@@ -405,23 +452,17 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                             for (int e = 0; e < 2; ++e) {
                                 const int jj = j + e;
                                 const float g = bf16_to_f(f_to_bf16(nkb ? __uint_as_float(r[jj]) : 0.f));
-                                float z = 0.f;
-                                if ((bits >> jj) & 1u) {
-                                    const long long p = vbase + __popc(bits & ((1u << jj) - 1u));
-                                    z = (p >= 0 && p < args.vals_len) ? bf16_to_f(args.vals[p]) : 0.f;
-                                }
                                 if (args.act == ACT_RELU2) {
-                                    out_v[e] = (g * 2.0f) * z;
-                                    act_v[e] = z * z;
+                                    out_v[e] = (g * 2.0f) * z[jj];
+                                    act_v[e] = z[jj] * z[jj];
                                 } else {
                                     out_v[e] = ((bits >> jj) & 1u) ? g : 0.f;
-                                    act_v[e] = z;
+                                    act_v[e] = z[jj];
                                 }
                             }
                             wd[j >> 1] = pack_bf16x2(out_v[0], out_v[1]);
                             wa[j >> 1] = pack_bf16x2(act_v[0], act_v[1]);
                         }
-                        vbase += __popc(bits);
                         if (row_ok) {
                             store_row32(orow, gcol0 + c * 32, args.N, vec, wd);
                             store_row32(orow2, gcol0 + c * 32, args.N, vec, wa);
@@ -429,20 +470,23 @@ __global__ void __launch_bounds__(G_THREADS, 1)
                     }
                 }
             }
-            // release this accumulator to the MMA warp
+            // release this accumulator to the leader's MMA warp
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
             if (++acc == 2) {
                 acc = 0;
                 acc_phase ^= 1u;
             }
         }
     }
-    __syncthreads();
+    // No CTA may leave while its peer can still touch its shared memory,
+    // barriers or TMEM.
+    tc_fence_before();
+    cluster_sync();
     if (warp == 2) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, TMEM_COLS);
+        tmem_dealloc_pair(tmem_base, TMEM_COLS);
     }
 }
 
@@ -495,6 +539,32 @@ int g_num_sms() {
     return sms;
 }
 
+// Clusters of G_CTAS that can be resident at once (each CTA fills an SM).
+template <typename K>
+int max_active_clusters(K kernel, int smem) {
+    static int cached = 0;
+    if (!cached) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(G_CTAS * 64);
+        cfg.blockDim = dim3(G_THREADS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = G_CTAS;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (void*)kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = g_num_sms() / G_CTAS;
+        }
+        cached = n;
+    }
+    return cached;
+}
+
 bool device_is_sm100() {
     int dev = 0, major = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
@@ -510,15 +580,15 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     const bool okA = A_MN ? make_tmap(&ta, A, args.M, args.K, lda, 64, G_BK)
                           : make_tmap(&ta, A, args.K, args.M, lda, G_BK, G_BM);
     const bool okB = B_MN ? make_tmap(&tb, B, args.N, args.K, ldb, 64, G_BK)
-                          : make_tmap(&tb, B, args.K, args.N, ldb, G_BK, BN);
+                          : make_tmap(&tb, B, args.K, args.N, ldb, G_BK, BN / G_CTAS);
     if (!okA || !okB) return SFFN_ERR_CUDA;
-    constexpr int smem = G_STAGES * (G_BM * G_BK * 2 + BN * G_BK * 2) + 1024;
+    constexpr int smem = G_STAGES * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 1024;
     auto k = gemm_kernel<BN, A_MN, B_MN, EPI>;
     SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    const int ntiles = args.tiles_m * args.tiles_n;
-    const int grid = std::min(ntiles, g_num_sms());
-    if (grid <= 0) return SFFN_OK;
-    k<<<grid, G_THREADS, smem, st>>>(ta, tb, args);
+    const int npairs = ((args.tiles_m + 1) / 2) * args.tiles_n;
+    const int clusters = std::min(npairs, max_active_clusters(k, smem));
+    if (clusters <= 0) return SFFN_OK;
+    k<<<clusters * G_CTAS, G_THREADS, smem, st>>>(ta, tb, args);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

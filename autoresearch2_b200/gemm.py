@@ -33,8 +33,8 @@ def _operand(t, rows_dim):
 def mm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, kb_list=None, kb_count=None):
     """C = A @ B (bf16 in, fp32 accumulate, bf16 out) on the tcgen05 kernel.
 
-    kb_list / kb_count (int32, from live_kblocks) restrict row tile m of A to
-    the listed 64-wide K blocks (the rest of A's row tile must be zero there)."""
+    kb_list / kb_count (int32, from live_kblocks) restrict 256-row tile m of A
+    to the listed 64-wide K blocks (the rest of A's row tile must be zero there)."""
     _lib.require_cuda(A, B)
     if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
         raise TypeError("mm takes bfloat16 operands")
@@ -57,9 +57,10 @@ def mm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, kb_list=None,
 
 
 def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
-    """(kb_list [ceil(M/128), ceil(N/64)] int32, kb_count [ceil(M/128)] int32)
-    of the 64-column blocks holding any set bit of a tiled 128x128 bitmask."""
-    gm, nkb = -(-M // 128), -(-N // 64)
+    """(kb_list [ceil(M/256), ceil(N/64)] int32, kb_count [ceil(M/256)] int32):
+    per 256-row tile, the 64-column blocks holding any set bit of a tiled
+    128x128 bitmask (the K-skip lists of mm)."""
+    gm, nkb = -(-M // 256), -(-N // 64)
     kb_list = torch.empty(gm, nkb, dtype=torch.int32, device=bitmask.device)
     kb_count = torch.empty(gm, dtype=torch.int32, device=bitmask.device)
     call("sffn_live_kblocks", ptr(bitmask), M, N, ptr(kb_list), ptr(kb_count),

@@ -163,7 +163,7 @@ int sffn_tile_grad_relu2(void* grad, int dtype, int64_t M, int64_t N, int64_t ld
  * a_mn = 0: A stored [M][lda] (K contiguous); a_mn = 1: A stored [K][lda]
  * (M contiguous, i.e. the transpose of a row-major [K, M] tensor).  Same for
  * B with N.  Optional kb_list/kb_count (both or neither): for row tile
- * m = row/128, only the kb_count[m] 64-wide K blocks listed in
+ * m = row/256, only the kb_count[m] 64-wide K blocks listed in
  * kb_list[m*kb_stride ...] are accumulated (the others are known to be zero).
  *   replaces the torch/cuBLAS matmuls of old/lib_sparse/sparse.py:72-149 and
  *   prepare_layer.py:25-27,131-160 (x@W1.T, z@W2.T, grad@W2, grad.T@z,
@@ -202,8 +202,9 @@ int sffn_tile_gather_slots(const void* slots, int tile_elems, const int32_t* pre
                            int64_t vals_capacity, int dtype, uint32_t* status_dev, void* stream);
 
 /* For a tiled 128x128 bitmask of an [M, N] matrix: kb_count[m] and the
- * ascending list kb_list[m*ceil(N/64) ...] of 64-column blocks of row tile m
- * that hold any set bit (no reference counterpart: the reference's
+ * ascending list kb_list[m*ceil(N/64) ...] of 64-column blocks of 256-row
+ * tile m (rows 256m .. 256m+255) that hold any set bit -- the K-skip lists
+ * sffn_gemm_bf16 takes (no reference counterpart: the reference's
  * down-projection is dense, sparse.py:75,118). */
 int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
                       int32_t* kb_count, void* stream);

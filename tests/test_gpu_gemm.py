@@ -58,22 +58,46 @@ def test_mm_out_and_strided_output():
 def test_mm_k_skip_lists():
     """Row tiles skip 64-wide K blocks that are zero in the whole tile."""
     from autoresearch2_b200 import gemm
-    M, N, K = 384, 256, 512
+    M, N, K = 768, 256, 512
     A = rand(M, K, seed=5)
-    keep = torch.rand(M // 128, K // 64, generator=torch.Generator().manual_seed(0)) < 0.5
-    keep[1] = False  # one row tile with no live block at all
-    mask = keep.repeat_interleave(128, 0).repeat_interleave(64, 1).to(DEV)
+    keep = torch.rand(M // 256, K // 64, generator=torch.Generator().manual_seed(0)) < 0.5
+    keep[1] = False  # one 256-row tile with no live block at all
+    mask = keep.repeat_interleave(256, 0).repeat_interleave(64, 1).to(DEV)
     A = torch.where(mask, A, torch.zeros((), dtype=A.dtype, device=DEV))
     B = rand(K, N, seed=6)
-    kb_list = torch.zeros(M // 128, K // 64, dtype=torch.int32)
-    kb_count = torch.zeros(M // 128, dtype=torch.int32)
-    for m in range(M // 128):
+    kb_list = torch.zeros(M // 256, K // 64, dtype=torch.int32)
+    kb_count = torch.zeros(M // 256, dtype=torch.int32)
+    for m in range(M // 256):
         live = torch.nonzero(keep[m]).flatten()
         kb_list[m, :live.numel()] = live.int()
         kb_count[m] = live.numel()
     C = gemm.mm(A, B, kb_list=kb_list.to(DEV), kb_count=kb_count.to(DEV))
     assert_close_rel(C, ref_mm(A, B))
-    assert torch.count_nonzero(C[128:256]) == 0
+    assert torch.count_nonzero(C[256:512]) == 0
+
+
+def test_live_kblocks_matches_mask():
+    """Live lists from a bitmask equal the 64-column blocks with any nonzero
+    in each 256-row tile (odd number of 128-row tiles included)."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    T, F = 384, 640
+    z = torch.zeros(T, F, device=DEV, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(3)
+    live = torch.rand(T // 128, F // 64, generator=g) < 0.3
+    for tm in range(T // 128):
+        for kb in range(F // 64):
+            if live[tm, kb]:
+                z[tm * 128 + 7, kb * 64 + 5] = 1.0
+    arena = torch.empty(T * F, device=DEV, dtype=torch.bfloat16)
+    off = torch.zeros(1, dtype=torch.int32, device=DEV)
+    x = sf.dense_to_tilesparse(z, arena, off, 128, 128)
+    kb_list, kb_count = gemm.live_kblocks(x.bitmask, T, F)
+    for tp in range(2):
+        want = torch.nonzero(live[2 * tp:2 * tp + 2].any(0)).flatten().int()
+        n = int(kb_count[tp])
+        assert n == want.numel()
+        assert torch.equal(kb_list[tp, :n].cpu(), want)
 
 
 @pytest.mark.parametrize("act", [0, 1])
