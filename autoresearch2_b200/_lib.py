@@ -48,8 +48,9 @@ SIGNATURES = {
                               _vp, _int, _vp, _vp]),
     "sffn_ffn_up": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
                            _vp, _vp, _vp]),
-    "sffn_tile_scan_counts": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp]),
-    "sffn_tile_gather_slots": (_int, [_vp, _int, _vp, _vp, _i64, _vp, _i64, _int, _vp, _vp]),
+    "sffn_tile_scan_counts": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "sffn_tile_gather_slots": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _int, _vp, _vp, _vp]),
+    "sffn_tile_row_offsets": (_int, [_vp, _vp, _i64, _vp, _vp]),
     "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
                               _vp, _vp, _vp, _i64, _vp, _vp]),
@@ -79,7 +80,8 @@ def load():
 LAUNCHING = {"sffn_flat_pack": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
-             "sffn_tile_gather_slots": 1, "sffn_live_kblocks": 1, "sffn_ffn_dgrad": 1}
+             "sffn_tile_gather_slots": 1, "sffn_tile_row_offsets": 1, "sffn_live_kblocks": 1,
+             "sffn_ffn_dgrad": 1}
 launch_count = 0
 
 

@@ -1,13 +1,15 @@
 // Small kernels around the fused FFN GEMMs (sm_100a).
 //
-//   tile_scan_kernel    per-tile counts -> exclusive prefix[num_tiles + 1];
-//                       reads the int32 arena cursor into vals_offset and
-//                       advances it by the total (sparse.py:181-204 without a
-//                       host round trip).
-//   slot_gather_kernel  moves each tile's compacted values from its fixed slot
-//                       (written by the up-projection epilogue, which cannot
-//                       know the tile's final offset) to
-//                       vals[vals_offset + prefix[t] ...].
+//   tile_scan_kernel    per-tile counts (summed over `parts` partial counts)
+//                       -> exclusive prefix[num_tiles + 1]; reads the int32
+//                       arena cursor into vals_offset and advances it by the
+//                       total (sparse.py:181-204 without a host round trip).
+//   tile_rows_kernel    per 128x128 tile: row counts from the bitmask, a
+//                       128-row scan, row_offsets[t][r] = prefix[t] + (values
+//                       in rows < r); optionally moves each row's values from
+//                       its fixed 128-element slot segment (written by the
+//                       up-projection epilogue, which cannot know the final
+//                       offsets) to vals[vals_offset + row_offsets[t][r] ...].
 //   live_kblocks_kernel for each 256-row tile (two rows of 128x128 format
 //                       tiles, the GEMM's CTA-pair tile) of a tiled bitmask,
 //                       the ascending list of 64-column blocks holding any set
@@ -19,16 +21,22 @@ namespace {
 
 constexpr int SCAN_NT = 1024;
 
-__global__ void __launch_bounds__(SCAN_NT) tile_scan_kernel(const int* __restrict__ counts, long long ntiles,
-                                                           int* __restrict__ prefix, int* __restrict__ cursor,
+__global__ void __launch_bounds__(SCAN_NT) tile_scan_kernel(const int* __restrict__ counts, int parts,
+                                                           long long ntiles, int* __restrict__ prefix,
+                                                           int* __restrict__ cursor,
                                                            int* __restrict__ vals_offset_out,
                                                            uint32_t* __restrict__ status) {
     __shared__ long long s_part[SCAN_NT];
     const int tid = threadIdx.x;
     const long long per = (ntiles + SCAN_NT - 1) / SCAN_NT;
     const long long lo = tid * per, hi = min(lo + per, ntiles);
+    auto count = [&](long long t) {
+        int c = 0;
+        for (int k = 0; k < parts; ++k) c += counts[t * parts + k];
+        return c;
+    };
     long long sum = 0;
-    for (long long t = lo; t < hi; ++t) sum += counts[t];
+    for (long long t = lo; t < hi; ++t) sum += count(t);
     s_part[tid] = sum;
     __syncthreads();
     // Hillis-Steele inclusive scan of the 1024 partial sums
@@ -41,7 +49,7 @@ __global__ void __launch_bounds__(SCAN_NT) tile_scan_kernel(const int* __restric
     long long run = s_part[tid] - sum;
     for (long long t = lo; t < hi; ++t) {
         prefix[t] = (int)run;
-        run += counts[t];
+        run += count(t);
     }
     if (tid == SCAN_NT - 1) {
         const long long total = s_part[SCAN_NT - 1];
@@ -54,19 +62,38 @@ __global__ void __launch_bounds__(SCAN_NT) tile_scan_kernel(const int* __restric
     }
 }
 
-__global__ void __launch_bounds__(256) slot_gather_kernel(const uint16_t* __restrict__ slots, int tile_elems,
-                                                          const int* __restrict__ prefix,
-                                                          const int* __restrict__ vals_offset,
-                                                          uint16_t* __restrict__ vals, long long cap,
-                                                          uint32_t* __restrict__ status) {
+// One CTA (128 threads, thread = tile row) per 128x128 tile.
+__global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restrict__ mask,
+                                                        const int* __restrict__ prefix,
+                                                        int* __restrict__ row_offsets,
+                                                        const uint16_t* __restrict__ slots,
+                                                        const int* __restrict__ vals_offset,
+                                                        uint16_t* __restrict__ vals, long long cap,
+                                                        uint32_t* __restrict__ status) {
+    __shared__ int s_warp[4];
     const long long t = blockIdx.x;
-    const int cnt = min(prefix[t + 1] - prefix[t], tile_elems);
-    const long long dst = (long long)*vals_offset + prefix[t];
-    const uint16_t* src = slots + t * tile_elems;
-    if (threadIdx.x == 0 && (dst < 0 || dst + cnt > cap)) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
-    for (int i = threadIdx.x; i < cnt; i += blockDim.x) {
-        const long long p = dst + i;
-        if (p >= 0 && p < cap) vals[p] = __ldcs(src + i);
+    const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
+    const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
+    const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
+    const int inc = warp_incl_scan(cnt, lane);
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += s_warp[w];
+    const int roff = prefix[t] + before + inc - cnt;
+    if (row_offsets) row_offsets[t * 128 + r] = roff;
+    if (!slots) return;
+    const long long base = (long long)*vals_offset;
+    // warp-cooperative, coalesced copy of the warp's 32 row segments
+    for (int i = 0; i < 32; ++i) {
+        const int c = __shfl_sync(FULL, cnt, i);
+        const long long d = base + __shfl_sync(FULL, roff, i);
+        const uint16_t* src = slots + t * 16384 + (warp * 32 + i) * 128;
+        for (int k = lane; k < c; k += 32) {
+            const long long p = d + k;
+            if (p >= 0 && p < cap) vals[p] = __ldcs(src + k);
+            else atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+        }
     }
 }
 
@@ -107,29 +134,42 @@ __global__ void __launch_bounds__(256) live_kblocks_kernel(const uint8_t* __rest
 
 using namespace sffn;
 
-extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int64_t ntiles, int32_t* prefix,
+extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int64_t ntiles, int32_t* prefix,
                                      int32_t* offset_dev, int32_t* vals_offset_dev, uint32_t* status_dev,
                                      void* stream) {
-    if (ntiles <= 0 || !tile_counts || !prefix || !offset_dev || !vals_offset_dev || !status_dev)
+    if (ntiles <= 0 || parts <= 0 || !tile_counts || !prefix || !offset_dev || !vals_offset_dev || !status_dev)
         return SFFN_ERR_ARG;
     if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
     if (int rc = bind_device_of(tile_counts)) return rc;
     tile_scan_kernel<<<1, SCAN_NT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        tile_counts, ntiles, prefix, offset_dev, vals_offset_dev, status_dev);
+        tile_counts, parts, ntiles, prefix, offset_dev, vals_offset_dev, status_dev);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
 
-extern "C" int sffn_tile_gather_slots(const void* slots, int tile_elems, const int32_t* prefix,
+extern "C" int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int32_t* prefix,
                                       const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
-                                      int64_t vals_capacity, int dtype, uint32_t* status_dev, void* stream) {
+                                      int64_t vals_capacity, int dtype, int32_t* row_offsets,
+                                      uint32_t* status_dev, void* stream) {
     if (dtype != SFFN_BF16 && dtype != SFFN_F16) return SFFN_ERR_DTYPE;
-    if (ntiles <= 0 || tile_elems <= 0 || !slots || !prefix || !vals_offset_dev || !vals || !status_dev)
+    if (ntiles <= 0 || !slots || !bitmask || !prefix || !vals_offset_dev || !vals || !status_dev)
         return SFFN_ERR_ARG;
+    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
     if (int rc = bind_device_of(vals)) return rc;
-    slot_gather_kernel<<<(unsigned)ntiles, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(slots), tile_elems, prefix, vals_offset_dev, static_cast<uint16_t*>(vals),
-        vals_capacity, status_dev);
+    tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        bitmask, prefix, row_offsets, static_cast<const uint16_t*>(slots), vals_offset_dev,
+        static_cast<uint16_t*>(vals), vals_capacity, status_dev);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t ntiles,
+                                     int32_t* row_offsets, void* stream) {
+    if (ntiles <= 0 || !bitmask || !prefix || !row_offsets) return SFFN_ERR_ARG;
+    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
+    if (int rc = bind_device_of(row_offsets)) return rc;
+    tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        bitmask, prefix, row_offsets, nullptr, nullptr, nullptr, 0, nullptr);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

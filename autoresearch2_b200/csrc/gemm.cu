@@ -33,10 +33,13 @@
 //   UP     (x @ W1^T + b1): pre = bf16(acc [+ b1]); z = relu(pre); writes
 //          act = z^2 (ReLU^2) or z (ReLU) densely for the down-projection, the
 //          tiled 128x128 bitmask of z > 0 (one 16-byte store of four uint32
-//          words per tile row), per-tile counts and z compacted, row-major in
-//          the tile, into a per-tile slot -- the arena offset is applied by
-//          sffn_tile_gather_slots once all counts are scanned.
-//   DGRAD  (dout @ W2): g = bf16(acc); with z gathered from the packed vals,
+//          words per tile row), per-warp partial tile counts, and each row's
+//          z values compacted into that row's own 128-element segment of the
+//          tile's slot -- no cross-thread scan in the epilogue; the tile scan
+//          and the in-tile row scan happen in sffn_tile_scan_counts /
+//          sffn_tile_gather_slots.
+//   DGRAD  (dout @ W2): g = bf16(acc); z gathered from the packed vals at
+//          the row's precomputed offset (sffn_tile_row_offsets);
 //          ReLU^2: dpre = bf16((g*2) * z) and act2 = bf16(z*z) (for dW2);
 //          ReLU:   dpre = bit ? g : 0 and act2 = z.
 #include <cuda.h>
@@ -77,12 +80,12 @@ struct GemmArgs {
     int act;
     const uint16_t* bias;  // UP: optional [N]
     uint8_t* mask;         // UP: written; DGRAD: read (tiled 128x128, grid_n = ceil(N/128))
-    int* tile_counts;      // UP
-    uint16_t* slots;       // UP: [num_tiles][128*128]
+    int* tile_counts;      // UP: [num_tiles][4] per-warp partial counts
+    uint16_t* slots;       // UP: [num_tiles][128 rows][128]: row r's z values at r*128
     uint16_t* out2;        // DGRAD: act2
     const uint16_t* vals;  // DGRAD
     long long vals_len;
-    const int* prefix;
+    const int* row_offsets;  // DGRAD: [num_tiles][128] prefix[t] + in-tile row prefix
     const int* vals_offset;
     uint32_t* status;
 };
@@ -356,6 +359,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         sb[row] = gcol0 + row < args.N ? bf16_to_f(bias[gcol0 + row]) : 0.f;
                         named_bar_sync(bar_id, 128);
                     }
+                    // this row's z values go to its own 128-element segment of the slot
+                    uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;
                     uint32_t words[4];
                     int cnt = 0;
 #pragma unroll
@@ -364,81 +369,82 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         tmem_ld32(tbase + c * 32, r);
                         tmem_wait_ld();
                         const int gcol = gcol0 + c * 32;
-                        uint32_t bits = 0, w[16];
+                        // columns past N (and rows past M) carry no bits
+                        const int ncol = row_ok ? min(32, args.N - gcol) : 0;
+                        const uint32_t colmask = ncol >= 32 ? 0xFFFFFFFFu : ((1u << max(ncol, 0)) - 1u);
+                        uint32_t zw[16], w[16], bits = 0;
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            float v0 = nkb ? __uint_as_float(r[j]) : 0.f;
-                            float v1 = nkb ? __uint_as_float(r[j + 1]) : 0.f;
+                        for (int q = 0; q < 16; ++q) {
+                            float v0 = nkb ? __uint_as_float(r[2 * q]) : 0.f;
+                            float v1 = nkb ? __uint_as_float(r[2 * q + 1]) : 0.f;
                             if (bias) {
-                                v0 += sb[c * 32 + j];
-                                v1 += sb[c * 32 + j + 1];
+                                v0 += sb[c * 32 + 2 * q];
+                                v1 += sb[c * 32 + 2 * q + 1];
                             }
-                            // pre rounded to bf16, z = relu(pre) (NaN stays NaN, as in torch)
-                            const uint16_t p0 = f_to_bf16(v0), p1 = f_to_bf16(v1);
-                            const uint16_t z0 = ((int16_t)p0 < 0 && (p0 & 0x7FFF) <= 0x7F80) ? 0 : p0;
-                            const uint16_t z1 = ((int16_t)p1 < 0 && (p1 & 0x7FFF) <= 0x7F80) ? 0 : p1;
-                            const bool in0 = row_ok && gcol + j < args.N, in1 = row_ok && gcol + j + 1 < args.N;
-                            bits |= (uint32_t)(in0 && positive_bits(z0, 0x7F80)) << j;
-                            bits |= (uint32_t)(in1 && positive_bits(z1, 0x7F80)) << (j + 1);
-                            float a0 = bf16_to_f(z0), a1 = bf16_to_f(z1);
+                            // pre = bf16(v); z = relu(pre) on the packed pair: negative
+                            // non-NaN halves become +0 (NaN stays NaN, as in torch)
+                            const uint32_t pw = pack_bf16x2(v0, v1);
+                            const uint32_t mag = pw & 0x7FFF7FFFu;
+                            const uint32_t neg = ((pw >> 15) & 0x00010001u) * 0xFFFFu;
+                            const uint32_t nan = __vcmpgtu2(mag, 0x7F807F80u);
+                            const uint32_t z = pw & ~(neg & ~nan);
+                            // z > 0: non-zero, sign clear, not NaN
+                            const uint32_t pos = __vcmpgtu2(z & 0x7FFF7FFFu, 0u) & ~nan & ~neg;
+                            bits |= ((pos & 1u) | ((pos >> 15) & 2u)) << (2 * q);
+                            zw[q] = z;
+                            float a0 = __uint_as_float(z << 16), a1 = __uint_as_float(z & 0xFFFF0000u);
                             if (args.act == ACT_RELU2) {
                                 a0 *= a0;
                                 a1 *= a1;
                             }
-                            w[j >> 1] = pack_bf16x2(a0, a1);
+                            w[q] = pack_bf16x2(a0, a1);
                         }
+                        bits &= colmask;
                         if (row_ok) store_row32(orow, gcol, args.N, vec, w);
+                        // compact this chunk's z values into the row's slot segment
+                        uint32_t rem = bits;
+                        while (rem) {
+                            const int j = __ffs(rem) - 1;
+                            rem &= rem - 1u;
+                            slot_row[cnt++] = (uint16_t)(zw[j >> 1] >> (16 * (j & 1)));
+                        }
                         words[c] = bits;
-                        cnt += __popc(bits);
                     }
                     *reinterpret_cast<uint4*>(args.mask + tf * FT_BYTES + row * 16) =
                         make_uint4(words[0], words[1], words[2], words[3]);
-                    int total;
-                    const int rex = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
-                    if (row == FT - 1) args.tile_counts[tf] = total;
-                    // second pass: z values of this row, compacted into the tile's slot
-                    uint16_t* slot = args.slots + tf * FT_ELEMS + rex;
-                    int k = 0;
+                    // per-warp partial count of the tile (summed by the scan kernel)
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        // tcgen05.ld is warp-collective: skip only if no lane needs it
-                        if (!__any_sync(FULL, words[c] != 0)) continue;
-                        uint32_t r[32];
-                        tmem_ld32(tbase + c * 32, r);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if ((words[c] >> j) & 1u) {
-                                float v = __uint_as_float(r[j]);
-                                if (bias) v += sb[c * 32 + j];
-                                slot[k++] = f_to_bf16(v);
-                            }
-                        }
-                    }
+                    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
+                    if (lane == 0) args.tile_counts[tf * 4 + ew] = cnt;
                 }
             } else {  // EPI_DGRAD
                 if (gcol0 < args.N && tile_ok) {  // uniform over the warpgroup
                     uint16_t* orow2 = args.out2 + (size_t)grow * args.ldc;
                     const long long tf = (long long)tm * gn_f + gcol0 / FT;
                     uint4 mw = make_uint4(0, 0, 0, 0);
-                    if (row_ok) mw = __ldg(reinterpret_cast<const uint4*>(args.mask + tf * FT_BYTES + row * 16));
+                    long long vbase = 0;
+                    if (row_ok) {
+                        mw = __ldg(reinterpret_cast<const uint4*>(args.mask + tf * FT_BYTES + row * 16));
+                        vbase = (long long)*args.vals_offset + __ldg(args.row_offsets + tf * FT + row);
+                    }
                     const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
-                    const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
-                    int total;
-                    const int rex = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
-                    long long vbase = (long long)*args.vals_offset + args.prefix[tf] + rex;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const uint32_t bits = words[c];
                         // gather this chunk's z first: read-only loads, free to run ahead
-                        float z[32];
+                        uint32_t zb[16];
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            z[j] = 0.f;
-                            if ((bits >> j) & 1u) {
-                                const long long p = vbase + __popc(bits & ((1u << j) - 1u));
-                                if (p >= 0 && p < args.vals_len) z[j] = bf16_to_f(__ldg(vals + p));
+                        for (int q = 0; q < 16; ++q) {
+                            uint32_t lo = 0, hi = 0;
+                            if ((bits >> (2 * q)) & 1u) {
+                                const long long p = vbase + __popc(bits & ((1u << (2 * q)) - 1u));
+                                if (p < args.vals_len) lo = __ldg(vals + p);
                             }
+                            if ((bits >> (2 * q + 1)) & 1u) {
+                                const long long p = vbase + __popc(bits & ((2u << (2 * q)) - 1u));
+                                if (p < args.vals_len) hi = __ldg(vals + p);
+                            }
+                            zb[q] = lo | (hi << 16);
                         }
                         vbase += __popc(bits);
                         uint32_t r[32];
@@ -446,22 +452,22 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         tmem_wait_ld();
                         uint32_t wd[16], wa[16];
 #pragma unroll
-                        for (int j = 0; j < 32; j += 2) {
-                            float out_v[2], act_v[2];
-#pragma unroll
-                            for (int e = 0; e < 2; ++e) {
-                                const int jj = j + e;
-                                const float g = bf16_to_f(f_to_bf16(nkb ? __uint_as_float(r[jj]) : 0.f));
-                                if (args.act == ACT_RELU2) {
-                                    out_v[e] = (g * 2.0f) * z[jj];
-                                    act_v[e] = z[jj] * z[jj];
-                                } else {
-                                    out_v[e] = ((bits >> jj) & 1u) ? g : 0.f;
-                                    act_v[e] = z[jj];
-                                }
+                        for (int q = 0; q < 16; ++q) {
+                            // g = bf16(acc); z from the packed values (0 off the mask)
+                            const uint32_t gw = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]),
+                                                                  __uint_as_float(r[2 * q + 1]))
+                                                    : 0u;
+                            const float g0 = __uint_as_float(gw << 16), g1 = __uint_as_float(gw & 0xFFFF0000u);
+                            const float z0 = __uint_as_float(zb[q] << 16), z1 = __uint_as_float(zb[q] & 0xFFFF0000u);
+                            if (args.act == ACT_RELU2) {
+                                wd[q] = pack_bf16x2((g0 * 2.0f) * z0, (g1 * 2.0f) * z1);
+                                wa[q] = pack_bf16x2(z0 * z0, z1 * z1);
+                            } else {
+                                const uint32_t keep = (((bits >> (2 * q)) & 1u) ? 0x0000FFFFu : 0u) |
+                                                      (((bits >> (2 * q + 1)) & 1u) ? 0xFFFF0000u : 0u);
+                                wd[q] = gw & keep;
+                                wa[q] = zb[q];
                             }
-                            wd[j >> 1] = pack_bf16x2(out_v[0], out_v[1]);
-                            wa[j >> 1] = pack_bf16x2(act_v[0], act_v[1]);
                         }
                         if (row_ok) {
                             store_row32(orow, gcol0 + c * 32, args.N, vec, wd);
@@ -673,14 +679,14 @@ extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t l
 
 extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2,
                               int64_t T, int64_t D, int64_t F, int act, const void* vals,
-                              int64_t vals_len, const uint8_t* bitmask, const int32_t* prefix,
+                              int64_t vals_len, const uint8_t* bitmask, const int32_t* row_offsets,
                               const int32_t* vals_offset_dev, void* dpre_out, void* act_out,
                               int64_t ld_out, uint32_t* status_dev, void* stream) {
     // dA[T, F] = dout[T, D] @ W2[D, F]: B = W2 is [K=D][N=F], N contiguous (MN-major).
     int rc = check_operands(dout, ld_dout, false, w2, ldw2, true, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
-    if (!vals || !bitmask || !prefix || !vals_offset_dev || !dpre_out || !act_out || ld_out < F ||
+    if (!vals || !bitmask || !row_offsets || !vals_offset_dev || !dpre_out || !act_out || ld_out < F ||
         !status_dev)
         return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
@@ -691,7 +697,7 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
     a.mask = const_cast<uint8_t*>(bitmask);
     a.vals = static_cast<const uint16_t*>(vals);
     a.vals_len = vals_len;
-    a.prefix = prefix;
+    a.row_offsets = row_offsets;
     a.vals_offset = vals_offset_dev;
     a.status = status_dev;
     return dispatch<EPI_DGRAD>(false, true, dout, ld_dout, w2, ldw2, a, reinterpret_cast<cudaStream_t>(stream));

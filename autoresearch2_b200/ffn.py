@@ -51,7 +51,7 @@ def _fused_ok(x, W1, W2, b1, vals):
 def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     T, D = x.shape
     Fd = W1.shape[0]
-    a, bitmask, prefix, voff = G.ffn_up(x, W1, b1, act, vals, offset)
+    a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset)
     kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
     out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
     del a
@@ -60,6 +60,7 @@ def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     ctx.save_for_backward(x, W1, W2)
     ctx.z_sparse = z_sparse
     ctx.kb = (kb_list, kb_count)
+    ctx.row_offsets = row_offsets
     ctx.has_bias = b1 is not None
     ctx.fused = True
     return out
@@ -72,7 +73,8 @@ def _fused_backward(ctx, grad_output, act):
     kb_list, kb_count = ctx.kb
     ctx.kb = None
     grad_output = grad_output.contiguous()
-    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse)
+    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets)
+    ctx.row_offsets = None
     grad_W2 = G.mm(grad_output.T, a)
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)

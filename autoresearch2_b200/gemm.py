@@ -71,7 +71,7 @@ def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
 def ffn_up(x, W1, b1, act, vals, offset):
     """Fused x @ W1.T (+ b1) -> act(z) dense plus the tiled 128x128 sparse z.
 
-    Returns (act_dense [T, F], bitmask, prefix, vals_offset)."""
+    Returns (act_dense [T, F], bitmask, prefix, vals_offset, row_offsets)."""
     T, D = x.shape
     F = W1.shape[0]
     dev = x.device
@@ -79,31 +79,47 @@ def ffn_up(x, W1, b1, act, vals, offset):
     nt = gm * gn
     act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
-    counts = torch.empty(nt, dtype=torch.int32, device=dev)
+    counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
     slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
     prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
     vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
+    row_offsets = torch.empty(nt * 128, dtype=torch.int32, device=dev)
     status = ptr(_lib.status_word(dev))
     st = stream_ptr(dev)
     call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
          ptr(act_out), act_out.stride(0), ptr(bitmask), ptr(counts), ptr(slots), status, st)
-    call("sffn_tile_scan_counts", ptr(counts), nt, ptr(prefix), ptr(offset), ptr(vals_offset),
+    call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
-    call("sffn_tile_gather_slots", ptr(slots), 128 * 128, ptr(prefix), ptr(vals_offset), nt,
-         ptr(vals), vals.numel(), _lib.BF16, status, st)
-    return act_out, bitmask, prefix, vals_offset
+    call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
+         ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), status, st)
+    return act_out, bitmask, prefix, vals_offset, row_offsets
 
 
-def ffn_dgrad(dout, W2, act, z_sparse):
+def tile_row_offsets(z_sparse):
+    """Per-row value offsets of a 128x128-tile BitsparseTensor (int32 [tiles*128])."""
+    nt = z_sparse.grid_m * z_sparse.grid_n
+    ro = torch.empty(nt * 128, dtype=torch.int32, device=z_sparse.bitmask.device)
+    call("sffn_tile_row_offsets", ptr(z_sparse.bitmask), ptr(z_sparse.prefix), nt, ptr(ro),
+         stream_ptr(ro.device))
+    return ro
+
+
+def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None):
     """Fused dout @ W2 with the activation gradient; returns (dpre, act2)
-    where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F]."""
+    where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F].  z_sparse is a
+    128x128-tile BitsparseTensor; row_offsets its per-row offsets (computed
+    here if not given)."""
     T, D = dout.shape
     F = W2.shape[1]
     dev = dout.device
+    if z_sparse.BLOCK_M != 128 or z_sparse.BLOCK_N != 128:
+        raise ValueError("the fused activation gradient reads 128x128 tiles")
+    if row_offsets is None:
+        row_offsets = tile_row_offsets(z_sparse)
     dpre = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     call("sffn_ffn_dgrad", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,
-         ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(z_sparse.prefix),
+         ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(row_offsets),
          ptr(z_sparse.vals_offset), ptr(dpre), ptr(act2), dpre.stride(0),
          ptr(_lib.status_word(dev)), stream_ptr(dev))
     return dpre, act2

@@ -176,9 +176,10 @@ int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely, the
  * tiled 128x128 bitmask of z > 0 (ceil(T/128)*ceil(F/128) tiles of 2048 B),
- * the per-tile counts, and each tile's z values, row-major in the tile, to
- * slots[t*16384 ...].  Follow with sffn_tile_scan_counts and
- * sffn_tile_gather_slots to finish the BitsparseTensor.
+ * four partial counts per tile (tile_counts[t*4 .. t*4+3]) and, for tile t,
+ * row r's z values in order at slots[t*16384 + r*128 ...].  Follow with
+ * sffn_tile_scan_counts (parts = 4) and sffn_tile_gather_slots to finish the
+ * BitsparseTensor.
  *   replaces old/lib_sparse/sparse.py:72-77,116-120 (matmul, relu, square,
  *   dense_to_tilesparse) and old/matmul_bitsparse/train.py:11-116
  *   (_matmul_sparse_kernel + compaction). */
@@ -187,19 +188,30 @@ int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const 
                 uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
                 void* stream);
 
-/* prefix[t] = sum of tile_counts[< t], prefix[ntiles] = total; *vals_offset_dev
- * = *offset_dev; *offset_dev += total.
+/* prefix[t] = sum over tiles < t of (tile_counts[t*parts] + ... + [t*parts+parts-1]),
+ * prefix[ntiles] = total; *vals_offset_dev = *offset_dev; *offset_dev += total.
  *   replaces old/lib_sparse/sparse.py:181-186,200-204 (cumsum, cursor). */
-int sffn_tile_scan_counts(const int32_t* tile_counts, int64_t ntiles, int32_t* prefix,
+int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int64_t ntiles, int32_t* prefix,
                           int32_t* offset_dev, int32_t* vals_offset_dev, uint32_t* status_dev,
                           void* stream);
 
-/* vals[*vals_offset_dev + prefix[t] + i] = slots[t*tile_elems + i] for
- * i < prefix[t+1]-prefix[t] (16-bit dtypes; never past vals_capacity).
+/* For 128x128 tiles: moves row r of tile t from slots[t*16384 + r*128 ...]
+ * (count = popcount of the row's mask) to
+ * vals[*vals_offset_dev + prefix[t] + values in rows < r ...] (16-bit
+ * dtypes; never past vals_capacity) and, if row_offsets is not NULL, writes
+ * row_offsets[t*128 + r] = prefix[t] + values in rows < r.
  *   replaces old/lib_sparse/sparse_pack.py:65-92 (_compact_vals_kernel). */
-int sffn_tile_gather_slots(const void* slots, int tile_elems, const int32_t* prefix,
+int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int32_t* prefix,
                            const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
-                           int64_t vals_capacity, int dtype, uint32_t* status_dev, void* stream);
+                           int64_t vals_capacity, int dtype, int32_t* row_offsets,
+                           uint32_t* status_dev, void* stream);
+
+/* row_offsets[t*128 + r] = prefix[t] + number of values in rows < r of tile t,
+ * for a tiled 128x128 bitmask (the per-row index sffn_ffn_dgrad reads; the
+ * reference recomputes ranks with tl.cumsum in every kernel,
+ * old/lib_sparse/sparse_unpack.py:142,237). */
+int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t ntiles,
+                          int32_t* row_offsets, void* stream);
 
 /* For a tiled 128x128 bitmask of an [M, N] matrix: kb_count[m] and the
  * ascending list kb_list[m*ceil(N/64) ...] of 64-column blocks of 256-row
@@ -212,13 +224,14 @@ int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_
 /* Fused activation gradient: g = bf16(dout @ W2) ([T, F]; W2 is [D, F]).
  * ReLU^2 (act = 1): dpre = bf16((g*2) * z) and act_out = bf16(z*z); ReLU
  * (act = 0): dpre = bit ? g : 0 and act_out = z -- z gathered from the
- * tiled 128x128 BitsparseTensor (vals, bitmask, prefix, *vals_offset_dev).
+ * tiled 128x128 BitsparseTensor (vals, bitmask, *vals_offset_dev) at the
+ * row offsets of sffn_tile_row_offsets.
  *   replaces old/lib_sparse/sparse.py:92-102,132-145 (grad_output @ W2 with
  *   _mask_with_bitmask_kernel / _grad_relu2_kernel) and the unpack inside spAx
  *   (sparse.py:305-351). */
 int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2,
                    int64_t T, int64_t D, int64_t F, int act, const void* vals, int64_t vals_len,
-                   const uint8_t* bitmask, const int32_t* prefix, const int32_t* vals_offset_dev,
+                   const uint8_t* bitmask, const int32_t* row_offsets, const int32_t* vals_offset_dev,
                    void* dpre_out, void* act_out, int64_t ld_out, uint32_t* status_dev,
                    void* stream);
 

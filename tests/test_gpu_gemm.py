@@ -111,7 +111,7 @@ def test_ffn_up_fused(act, T, D, F, bias):
     b1 = torch.full((F,), -0.7, device=DEV, dtype=torch.bfloat16) if bias else None
     arena = torch.full((T * F + 50,), 9.0, device=DEV, dtype=torch.bfloat16)
     offset = torch.tensor([17], dtype=torch.int32, device=DEV)
-    a, bitmask, prefix, voff = gemm.ffn_up(x, W1, b1, act, arena, offset)
+    a, bitmask, prefix, voff, _ = gemm.ffn_up(x, W1, b1, act, arena, offset)
     pre = x.float() @ W1.float().T + (b1.float() if bias else 0)
     z_ref = torch.relu(pre)
     # the device z: the kernel's own dense output (ReLU) or the unpacked values
@@ -145,7 +145,7 @@ def test_ffn_dgrad_fused(act):
     b1 = torch.full((F,), -0.5, device=DEV, dtype=torch.bfloat16)
     arena = torch.empty(T * F, device=DEV, dtype=torch.bfloat16)
     offset = torch.zeros(1, dtype=torch.int32, device=DEV)
-    _, bitmask, prefix, voff = gemm.ffn_up(x, W1, b1, act, arena, offset)
+    _, bitmask, prefix, voff, _ = gemm.ffn_up(x, W1, b1, act, arena, offset)
     zs = sf.BitsparseTensor(arena, bitmask, prefix, voff, -(-T // 128), -(-F // 128), 128, 128, (T, F))
     dpre, act2 = gemm.ffn_dgrad(dout, W2, act, zs)
     z = zs.to_dense().float()
