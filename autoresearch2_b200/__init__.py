@@ -10,11 +10,11 @@ from .bitsparse import (BitsparseTensor, TensorBuffer, bitsparse_pack, bitsparse
                         init_sparse_buffer, mask_with_bitmask_, reset_sparse_globals, spAx,
                         tile_unpack)
 from .ffn import FFNSparse, FFNSpRelu2
-from . import tiled
+from . import parallel, tiled
 
 __all__ = [
     "BitsparseTensor", "TensorBuffer", "bitsparse_pack", "bitsparse_unpack", "check_status",
     "dense_to_tilesparse", "get_globals", "grad_relu2_", "init_sparse_buffer",
     "mask_with_bitmask_", "reset_sparse_globals", "spAx", "tile_unpack", "FFNSparse",
-    "FFNSpRelu2", "tiled",
+    "FFNSpRelu2", "parallel", "tiled",
 ]

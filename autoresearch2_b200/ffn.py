@@ -31,6 +31,7 @@ from torch.autograd import Function
 
 from . import bitsparse as bs
 from . import gemm as G
+from .parallel import submit_grad
 
 __all__ = ["FFNSparse", "FFNSpRelu2"]
 
@@ -75,11 +76,11 @@ def _fused_backward(ctx, grad_output, act):
     grad_output = grad_output.contiguous()
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets)
     ctx.row_offsets = None
-    grad_W2 = G.mm(grad_output.T, a)
+    grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
-    grad_W1 = G.mm(dpre.T, x)
-    grad_b1 = dpre.sum(0, dtype=torch.float32).to(dpre.dtype) if ctx.has_bias else None
+    grad_W1 = submit_grad(G.mm(dpre.T, x))
+    grad_b1 = submit_grad(dpre.sum(0, dtype=torch.float32).to(dpre.dtype)) if ctx.has_bias else None
     return grad_x, grad_W1, grad_W2, None, grad_b1
 
 
@@ -121,11 +122,11 @@ class FFNSparse(Function):
         ctx.z_sparse = None
         grad_output = grad_output.contiguous()
         grad_z = grad_output @ W2
-        grad_W2 = bs.spAx(z_sparse, grad_output.T)
+        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T))
         bs.mask_with_bitmask_(grad_z, z_sparse)
         grad_x = grad_z @ W1
-        grad_W1 = grad_z.T @ x
-        grad_b1 = grad_z.sum(0) if ctx.has_bias else None
+        grad_W1 = submit_grad(grad_z.T @ x)
+        grad_b1 = submit_grad(grad_z.sum(0)) if ctx.has_bias else None
         return grad_x, grad_W1, grad_W2, None, grad_b1
 
 
@@ -161,8 +162,8 @@ class FFNSpRelu2(Function):
         grad_z = grad_output @ W2
         # grad_pre = grad_z * 2z; the stored z become z^2 for dW2 (sparse.py:136-147)
         bs.grad_relu2_(grad_z, z_sparse, square=True)
-        grad_W2 = bs.spAx(z_sparse, grad_output.T, square=False)
+        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T, square=False))
         grad_x = grad_z @ W1
-        grad_W1 = grad_z.T @ x
-        grad_b1 = grad_z.sum(0) if ctx.has_bias else None
+        grad_W1 = submit_grad(grad_z.T @ x)
+        grad_b1 = submit_grad(grad_z.sum(0)) if ctx.has_bias else None
         return grad_x, grad_W1, grad_W2, None, grad_b1

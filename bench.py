@@ -132,6 +132,7 @@ class Step:
     def __init__(self, x, W1, W2, b1, dout, group=None):
         import autoresearch2_b200 as sf
         self.sf = sf
+        self.comm = sf.parallel.GradAllReduce(group) if group is not None else None
         self.x, self.dout = x, dout
         self.W1 = W1.clone().requires_grad_()
         self.W2 = W2.clone().requires_grad_()
@@ -146,10 +147,13 @@ class Step:
         for p in (self.W1, self.W2, self.b1):
             p.grad = None
         out = self.sf.FFNSpRelu2.apply(x, self.W1, self.W2, self.buf.as_sparse_data(), self.b1)
-        out.backward(self.dout)
-        if self.group is not None:
-            for p in (self.W1, self.W2):
-                dist.all_reduce(p.grad, group=self.group)
+        if self.comm is None:
+            out.backward(self.dout)
+        else:
+            # dW sums over the token shards overlap the rest of the backward
+            with self.comm.attached():
+                out.backward(self.dout)
+            self.comm.wait()
         return out
 
 
