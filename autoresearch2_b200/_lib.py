@@ -36,6 +36,7 @@ SIGNATURES = {
     "sffn_flat_workspace_bytes": (_sz, [_i64]),
     "sffn_flat_pack": (_int, [_vp, _int, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp, _vp]),
     "sffn_flat_unpack": (_int, [_vp, _i64, _vp, _int, _i64, _vp, _vp, _sz, _vp, _vp]),
+    "sffn_flat_pack_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
     "sffn_tile_workspace_bytes": (_sz, [_i64, _i64, _int, _int]),
     "sffn_tile_pack": (_int, [_vp, _int, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp,
                               _vp, _vp, _sz, _vp, _vp]),
@@ -77,7 +78,7 @@ def load():
 
 
 # Kernels of this library each entry point launches per call.
-LAUNCHING = {"sffn_flat_pack": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
+LAUNCHING = {"sffn_flat_pack": 1, "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
              "sffn_tile_gather_slots": 1, "sffn_tile_row_offsets": 1, "sffn_live_kblocks": 1,

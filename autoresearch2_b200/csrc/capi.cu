@@ -26,6 +26,7 @@ extern "C" const char* sffn_error_string(int code) {
         case SFFN_ERR_CUDA: return "CUDA error";
         case SFFN_ERR_UNSUPPORTED: return "unsupported shape or layout";
         case SFFN_ERR_DEVICE: return "device is not sm_100";
+        case SFFN_ERR_TOO_LARGE: return "size exceeds the entry point's fixed capacity";
         default: return "unknown error";
     }
 }

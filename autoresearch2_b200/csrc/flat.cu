@@ -23,7 +23,10 @@
 // consecutive elements f = 8*(sub*256 + tid) .. +7 of its chunk, i.e. one mask
 // byte; lanes 4k..4k+3 form one little-endian uint32 mask word
 // (bit f%32 of word f/32 == bit f%8 of byte f/8).
+#include <stdio.h>
+
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -504,4 +507,99 @@ extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_
     }
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// sffn_flat_pack_noalloc: the flat pack for callers that cannot allocate.
+//
+// Some callers have no way to obtain device memory: plug-ins handed only their
+// input and output buffers by a host application, programs whose memory
+// manager owns the whole device or works to a fixed, pre-planned budget, and
+// latency-critical paths that cannot afford the device-wide synchronisation a
+// cudaMalloc may cause.  This entry point needs no workspace from them: the
+// look-back state lives in the fixed array below, which every GPU that loads
+// this library holds until the process exits.
+//
+// Set-up: the first call on a device looks up that device's address of the
+// array with cudaGetSymbolAddress (with the device current) and caches it;
+// make that first call before any stream capture.  Every call shares the
+// array and finds the previous call's contents in it, so each call clears the
+// part it uses before its kernel runs; calls that overlap on the GPU (other
+// streams, other host threads) race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+namespace sffn {
+namespace {
+
+constexpr long long kNoAllocMaxChunks = 4096;  // 4096 chunks of 32 KB of input
+static __device__ __align__(256) unsigned char g_noalloc_scratch[16 + kNoAllocMaxChunks * 8];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// Device address of the scratch array on `dev` (which must be current).
+int noalloc_scratch(int dev, void** out) {
+    if (dev < 0 || dev >= kMaxDevices) return SFFN_ERR_ARG;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p) {
+            set_cuda_error(e);
+            return SFFN_ERR_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    *out = g_noalloc_addr[dev];
+    return SFFN_OK;
+}
+
+}  // namespace
+}  // namespace sffn
+
+// Largest n accepted: 67,108,864 elements of 2 bytes, 33,554,432 of 4 bytes.
+static long long noalloc_max_elements(int dtype) {
+    return kNoAllocMaxChunks * (PACK_CHUNK_BYTES / esize_of(dtype));
+}
+
+extern "C" int sffn_flat_pack_noalloc(const void* dense, int dtype, int64_t n, uint8_t* packed_mask,
+                                      void* vals, int64_t vals_capacity, int64_t* nnz_dev,
+                                      uint32_t* status_dev, void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (n < 0 || vals_capacity < 0 || !nnz_dev || !status_dev) return SFFN_ERR_ARG;
+    if (n > noalloc_max_elements(dtype)) {
+        char msg[160];
+        snprintf(msg, sizeof(msg), "sffn_flat_pack_noalloc: %lld elements exceed its fixed scratch capacity of %lld",
+                 (long long)n, noalloc_max_elements(dtype));
+        set_error_text(msg);
+        return SFFN_ERR_TOO_LARGE;
+    }
+    if (n > 0 && (!dense || !packed_mask || (!vals && vals_capacity > 0))) return SFFN_ERR_ARG;
+    if (n > 0 && (!aligned16(dense) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u))) return SFFN_ERR_ALIGN;
+    // Select the device that owns the output (cudaSetDevice initialises its
+    // context); nothing on this path allocates or frees device memory.
+    cudaPointerAttributes attr;
+    if (cudaPointerGetAttributes(&attr, nnz_dev) != cudaSuccess ||
+        (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
+        cudaGetLastError();
+        return SFFN_ERR_ARG;
+    }
+    SFFN_CUDA_TRY(cudaSetDevice(attr.device));
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n == 0) {
+        SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
+        return SFFN_OK;
+    }
+    void* scratch = nullptr;
+    if (int rc = noalloc_scratch(attr.device, &scratch)) return rc;
+    const int esz = esize_of(dtype);
+    const long long nch = pack_chunks(n, esz);
+    auto* states = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + 16);
+    // clear what the look-back needs at zero (the previous call left its states)
+    SFFN_CUDA_TRY(cudaMemsetAsync(scratch, 0, 16 + (size_t)nch * 8, st));
+    if (esz == 4)
+        return launch_pack<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, states,
+                                     status_dev, nch, st);
+    return launch_pack<uint16_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, states,
+                                 status_dev, nch, st);
 }

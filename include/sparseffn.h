@@ -43,7 +43,8 @@ enum {
     SFFN_ERR_WORKSPACE = 4,   /* workspace smaller than *_workspace_bytes()    */
     SFFN_ERR_CUDA = 5,        /* a CUDA runtime call or kernel launch failed   */
     SFFN_ERR_UNSUPPORTED = 6, /* tile shape or GEMM layout not built           */
-    SFFN_ERR_DEVICE = 7       /* current device is not sm_100                  */
+    SFFN_ERR_DEVICE = 7,      /* current device is not sm_100                  */
+    SFFN_ERR_TOO_LARGE = 8    /* size beyond a fixed-capacity entry point      */
 };
 
 /* Bits OR-ed into the device status word. */
@@ -97,6 +98,22 @@ int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_t* packed_m
                      int dtype, int64_t n, void* out,
                      void* workspace, size_t workspace_bytes,
                      uint32_t* status_dev, void* stream);
+
+/* sffn_flat_pack without a workspace argument, for callers that cannot
+ * allocate device memory (plug-ins given only their buffers, programs whose
+ * memory manager owns the device, paths that must not risk the
+ * synchronisation of a cudaMalloc).  No counterpart in the reference.  Same
+ * inputs, outputs and results as sffn_flat_pack; the look-back scratch is a
+ * fixed 32 KB array in this library's device memory (held on every GPU that
+ * loads the library until exit).  Allocates and frees nothing.  n is at most
+ * 67,108,864 (bf16, fp16) or 33,554,432 (fp32); larger n returns
+ * SFFN_ERR_TOO_LARGE with the limit in sffn_last_cuda_error().  The
+ * first call on a device looks up the array's address (make it before any
+ * stream capture); calls share the array, so calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+int sffn_flat_pack_noalloc(const void* dense, int dtype, int64_t n,
+                           uint8_t* packed_mask, void* vals, int64_t vals_capacity,
+                           int64_t* nnz_dev, uint32_t* status_dev, void* stream);
 
 /* ---- tiled format -------------------------------------------------------
  * A row-major [M, N] matrix (row stride ld elements) is cut into BM x BN tiles;
