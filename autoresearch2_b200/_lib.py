@@ -85,12 +85,49 @@ LAUNCHING = {"sffn_flat_pack": 1, "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack
              "sffn_ffn_dgrad": 1}
 launch_count = 0
 
+# Per-entry-point CUDA event pairs, recorded while a KernelTimer is active.
+_timer = None
+
+
+class KernelTimer:
+    """Brackets every launching entry point called inside ``with`` with CUDA
+    events on the current stream (the stream the library launches on), so the
+    device time of each kernel can be read inside a timed region without
+    synchronising.  ``summary()`` (after a synchronize) gives per entry point
+    the call count and mean/total milliseconds."""
+
+    def __init__(self):
+        self.events = {}
+
+    def __enter__(self):
+        global _timer
+        self._prev, _timer = _timer, self
+        return self
+
+    def __exit__(self, *exc):
+        global _timer
+        _timer = self._prev
+
+    def summary(self):
+        out = {}
+        for name, pairs in self.events.items():
+            ms = [a.elapsed_time(b) for a, b in pairs]
+            out[name] = {"calls": len(ms), "total_ms": sum(ms), "mean_ms": sum(ms) / len(ms)}
+        return out
+
 
 def call(name, *args):
     """Call a C-ABI entry point and raise SparseFFNError on a non-zero code."""
     global launch_count
     lib = load()
+    timer = _timer if name in LAUNCHING else None
+    if timer is not None:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
     rc = getattr(lib, name)(*args)
+    if timer is not None:
+        b.record()
+        timer.events.setdefault(name, []).append((a, b))
     if rc == 0:
         launch_count += LAUNCHING.get(name, 0)
     if rc != 0:

@@ -282,6 +282,47 @@ def cpu_baseline(sample_tokens):
                       f"+ tiled pack of z; {dt:.1f} s"}
 
 
+# -------------------------------------------------------------- roofline ----
+# DRAM traffic per launch of the roofline kernel (dram__bytes_read.sum +
+# dram__bytes_write.sum of one ncu capture, summarised under profiles/).
+TRAFFIC_BYTES = {}
+
+
+def kernel_breakdown(timer, steps_recorded, step_ms):
+    """Per C-ABI entry point: launches per step, mean device ms per launch (CUDA
+    events on the launching stream over warm-up + timed steps) and its share
+    of the step time."""
+    out = {}
+    for name, v in sorted(timer.summary().items(), key=lambda kv: -kv[1]["total_ms"]):
+        per_step = v["calls"] / steps_recorded
+        out[name] = {"launches_per_step": round(per_step, 2), "mean_ms": round(v["mean_ms"], 4),
+                     "share_of_step": round(v["mean_ms"] * per_step / step_ms, 3)}
+    return out
+
+
+def roofline(kernels, tokens, pk):
+    """Tensor-core roofline of the largest single launch of the step.
+
+    The fused up-projection (x @ W1^T with the ReLU^2/bitmask epilogue) and the
+    fused activation-gradient GEMM (dout @ W2 with the ReLU^2 derivative) each
+    do 2*T*D*F flops, dense: nothing of either can be skipped, since the
+    sparsity is only known after the up-projection and dout is dense.  The
+    denominator is the sustained cuBLAS bf16 figure, as both kernels run
+    inside a long step at the power cap."""
+    cands = [k for k in ("sffn_ffn_dgrad", "sffn_ffn_up") if k in kernels]
+    if not cands:
+        return None
+    name = max(cands, key=lambda k: kernels[k]["mean_ms"])
+    flops = 2.0 * tokens * D_MODEL * D_FF
+    ms = kernels[name]["mean_ms"]
+    tf = flops / (ms * 1e-3) / 1e12
+    peak = pk["bf16_tflops_sustained"]
+    return {"bound": "tensor", "kernel": name, "achieved": round(tf, 1), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(tf / peak, 3),
+            "traffic": TRAFFIC_BYTES.get(name), "flops_per_launch": flops,
+            "ms_per_launch": ms, "peak_source": f"{pk['source']} (sustained bf16)"}
+
+
 # ------------------------------------------------------------------ main ----
 def main():
     ap = argparse.ArgumentParser()
@@ -291,7 +332,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=1024)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--tokens", type=int, default=T_PER_GPU,
+                    help="tokens per GPU (smaller cases are for profiling)")
+    ap.add_argument("--quick", action="store_true",
+                    help="time the sparse step only: no dense, sweep, e2e, pack or CPU legs")
     args = ap.parse_args()
+    tpg = args.tokens
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -320,11 +366,11 @@ def main():
         group = dist.group.WORLD
     torch.backends.cuda.matmul.allow_tf32 = False
 
-    x, W1, W2, b1, dout = make_ffn_inputs(T_PER_GPU, D_MODEL, D_FF, SPARSITY, device, seed=rank)
+    x, W1, W2, b1, dout = make_ffn_inputs(tpg, D_MODEL, D_FF, SPARSITY, device, seed=rank)
     step = Step(x, W1, W2, b1, dout, group)
     step()
     torch.cuda.synchronize(device)
-    s_meas = 1.0 - step.buf.used() / (T_PER_GPU * D_FF)
+    s_meas = 1.0 - step.buf.used() / (tpg * D_FF)
 
     import autoresearch2_b200 as sf
     from autoresearch2_b200 import _lib
@@ -332,11 +378,12 @@ def main():
     n0 = _lib.launch_count
     step()
     launches_per_step = _lib.launch_count - n0
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, _lib.KernelTimer() as ktimer:
         ms = time_steps(step, args.steps, args.warmup, device)
     clocks = clk.summary()
-    tokens = T_PER_GPU * world
+    tokens = tpg * world
     value = tokens / (ms / 1e3)
+    kernels = kernel_breakdown(ktimer, args.steps + args.warmup, ms)
 
     # end to end: pinned host input -> device, step, loss read back each step
     x_host = x.cpu().pin_memory()
@@ -347,42 +394,41 @@ def main():
         out = step(xd)
         loss_holder["l"] = float(out.float().pow(2).mean().item())
 
-    e2e_ms = time_steps(e2e_step, max(3, args.steps // 2), 1, device)
-    e2e = {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-           "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4}
+    e2e = None
+    if not args.quick:
+        e2e_ms = time_steps(e2e_step, max(3, args.steps // 2), 3, device)
+        e2e = {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4}
 
     extras = {}
-    if rank == 0:
+    if rank == 0 and not args.quick:
         dense = DenseStep(x, W1, W2, b1, dout)
         d_ms = time_steps(dense, args.steps, args.warmup, device) if world == 1 else None
         if d_ms is not None:
-            extras["dense_cublas"] = {"tokens_per_s": round(T_PER_GPU / (d_ms / 1e3), 1),
+            extras["dense_cublas"] = {"tokens_per_s": round(tpg / (d_ms / 1e3), 1),
                                       "ms_per_step": round(d_ms, 3)}
             extras["speedup_vs_dense"] = round(d_ms / ms, 3)
         del dense
-    if world == 1 and not args.no_sweep:
+    if world == 1 and not args.no_sweep and not args.quick:
         sweep = {}
         for s in SWEEP:
-            xs, W1s, W2s, b1s, dos = make_ffn_inputs(T_PER_GPU, D_MODEL, D_FF, s, device)
+            xs, W1s, W2s, b1s, dos = make_ffn_inputs(tpg, D_MODEL, D_FF, s, device)
             st = Step(xs, W1s, W2s, b1s, dos)
             sm = time_steps(st, max(3, args.steps // 2), 2, device)
             dm = time_steps(DenseStep(xs, W1s, W2s, b1s, dos), max(3, args.steps // 2), 2, device)
-            sweep[str(s)] = {"tokens_per_s": round(T_PER_GPU / (sm / 1e3), 1),
-                             "dense_tokens_per_s": round(T_PER_GPU / (dm / 1e3), 1),
-                             "measured_sparsity": round(1.0 - st.buf.used() / (T_PER_GPU * D_FF), 4)}
+            sweep[str(s)] = {"tokens_per_s": round(tpg / (sm / 1e3), 1),
+                             "dense_tokens_per_s": round(tpg / (dm / 1e3), 1),
+                             "measured_sparsity": round(1.0 - st.buf.used() / (tpg * D_FF), 4)}
             del st, xs, W1s, W2s, b1s, dos
             torch.cuda.empty_cache()
         extras["sweep"] = sweep
 
     pk = peaks()
-    roof = None
+    roof = roofline(kernels, tpg, pk)
     pack = None
-    if rank == 0:
+    if rank == 0 and not args.quick:
         pack = bench_pack(device)
-        roof = {"bound": "hbm", "kernel": "flat_pack_kernel<uint16_t>",
-                "achieved": pack["pack_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(pack["pack_gbs"] / pk["hbm_gbs"], 3), "traffic": None,
-                "peak_source": pk["source"]}
+        pack["frac_of_measured_hbm"] = round(pack["pack_gbs"] / pk["hbm_gbs"], 3)
 
     if rank == 0:
         line = {
@@ -390,16 +436,16 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
-            "config": {"workload": "relu2_ffn_fwd_bwd_d4096_f14336_t16384_s0.9",
-                       "tokens_per_gpu": T_PER_GPU, "global_tokens": tokens, "d_model": D_MODEL,
+            "config": {"workload": f"relu2_ffn_fwd_bwd_d4096_f14336_t{tpg}_s0.9",
+                       "tokens_per_gpu": tpg, "global_tokens": tokens, "d_model": D_MODEL,
                        "d_ff": D_FF, "target_sparsity": SPARSITY,
                        "measured_sparsity": round(s_meas, 4), "parallelism": f"dp{world}",
                        "l2": "inputs larger than L2"},
-            "e2e": e2e, "clocks": clocks, "roofline": roof, "pack": pack,
+            "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)
-        if world == 1:
+        if world == 1 and not args.quick:
             try:
                 line["cpu_baseline"] = cpu_baseline(args.cpu_tokens)
             except Exception as e:  # noqa: BLE001
