@@ -149,6 +149,10 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
     return v;
 }
 
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
     unsigned long long v;
     asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
@@ -220,6 +224,77 @@ __device__ __forceinline__ unsigned long long lookback(unsigned long long* state
         pred -= 32LL * W;
     }
     if (lane == 0) st_release_u64(&states[part], LB_INCL | ((excl + agg) & LB_VAL));
+    return excl;
+}
+
+// Publication for lookback_rows(): a relaxed store.  A state word carries
+// its flag and count together in one aligned 64-bit store, and no reader pairs
+// it with other data written by the publishing partition, so it needs no
+// release -- a release would stall until all of the thread's earlier stores
+// are acknowledged, which under full memory load takes microseconds.
+__device__ __forceinline__ void lookback_publish_relaxed(unsigned long long* states, long long part,
+                                                         unsigned long long agg) {
+    st_relaxed_u64(&states[part], (part == 0 ? LB_INCL : LB_AGG) | (agg & LB_VAL));
+}
+
+// Warp-collective look-back like lookback(), reading W*32 predecessors per
+// round in coalesced rows: in row k lane l reads partition pred - 32*k - l,
+// so each load instruction fetches 32 consecutive states (256 bytes).  The
+// nearest inclusive entry is the first (row, lane) in that order that holds
+// one; every entry before it must be at least an aggregate.  A wide window
+// lets the resolved frontier advance 32*W partitions per L2 round trip.
+template <int W>
+__device__ __forceinline__ unsigned long long lookback_rows(unsigned long long* states, long long part,
+                                                           unsigned long long agg, uint32_t* status,
+                                                           int lane) {
+    if (part == 0) return 0;
+    unsigned long long excl = 0;
+    long long pred = part - 1;
+    unsigned long long t0 = 0;
+    while (true) {
+        unsigned long long s[W];
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const long long idx = pred - 32LL * k - lane;
+            s[k] = idx >= 0 ? ld_relaxed_u64(&states[idx]) : LB_INCL;
+        }
+        int krow = W;  // first row holding an inclusive entry (warp-uniform)
+        unsigned lanes = 0;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            const unsigned b = __ballot_sync(FULL, (s[k] >> 62) == 2);
+            if (krow == W && b) {
+                krow = k;
+                lanes = b;
+            }
+        }
+        const int cut = krow < W ? 32 * krow + (__ffs(lanes) - 1) : 32 * W;  // position of that entry
+        bool empty = false;
+        unsigned long long v = 0;
+#pragma unroll
+        for (int k = 0; k < W; ++k) {
+            if (32 * k + lane <= cut) {
+                if ((s[k] >> 62) == 0) empty = true;
+                v += s[k] & LB_VAL;
+            }
+        }
+        if (__any_sync(FULL, empty)) {
+            unsigned long long now;
+            asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
+            if (t0 == 0) t0 = now;
+            // lane 0's clock decides for the whole warp
+            if (__shfl_sync(FULL, now - t0 > kLookbackLimitNs ? 1 : 0, 0)) {
+                if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            __nanosleep(32);
+            continue;
+        }
+        excl += warp_sum_u64(v);
+        if (krow < W) break;
+        pred -= 32LL * W;
+    }
+    if (lane == 0) st_relaxed_u64(&states[part], LB_INCL | ((excl + agg) & LB_VAL));
     return excl;
 }
 

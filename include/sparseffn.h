@@ -73,7 +73,8 @@ const char* sffn_last_cuda_error(void);
  * elements in row-major order.  Tail bits of the last byte are 0.
  */
 
-/* Scratch needed by sffn_flat_pack / sffn_flat_unpack for n elements. */
+/* Scratch needed by sffn_flat_pack / sffn_flat_unpack for n elements:
+ * 16 bytes plus 8 per 8192 elements. */
 size_t sffn_flat_workspace_bytes(int64_t n);
 
 /* bitsparse_pack(dense, block) -> (vals, packed_mask)

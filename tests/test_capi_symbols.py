@@ -50,9 +50,9 @@ def test_version_and_errors(lib):
 def test_workspace_queries(lib):
     # max of the pack look-back states (8 B per 16K bf16 elements) and the
     # unpack counts + prefix (12 B per 16K elements, + 8 for the total)
-    assert lib.sffn_flat_workspace_bytes(0) == 32
-    assert lib.sffn_flat_workspace_bytes(16384) == 16 + 12 + 16
-    assert lib.sffn_flat_workspace_bytes(16385) == 16 + 24 + 16
+    assert lib.sffn_flat_workspace_bytes(0) == 16
+    assert lib.sffn_flat_workspace_bytes(8192) == 16 + 8
+    assert lib.sffn_flat_workspace_bytes(8193) == 16 + 16
     assert lib.sffn_tile_workspace_bytes(130, 192, 64, 64) == 16 + 3 * 3 * 8
 
 
