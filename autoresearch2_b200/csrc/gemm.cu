@@ -20,8 +20,10 @@
 //   warps 4..11  epilogue, two warpgroups each owning half of the tile's
 //                columns: each thread owns one accumulator row (TMEM lane),
 //                reads 32 columns per tcgen05.ld, applies the epilogue and
-//                stores with 16-byte vector stores; the second accumulator
-//                lets the next tile's MMAs run meanwhile.
+//                stages the warp's 32 x 32 block in a 2 KB swizzled shared
+//                buffer that one bulk-tensor store writes out (whole 64-byte
+//                row segments instead of 32 scattered rows per instruction);
+//                the second accumulator lets the next tile's MMAs run meanwhile.
 // Splitting B between the two CTAs halves the shared-memory bytes each SM
 // needs per k-block (32 KB instead of 48 KB), which buys a 6-stage ring.
 // Tiles are visited in groups of 16 row-tiles so that a wave of CTAs shares
@@ -46,6 +48,7 @@
 #include <cudaTypedefs.h>
 
 #include <stdio.h>
+#include <string.h>
 
 #include <algorithm>
 
@@ -73,7 +76,7 @@ struct GemmArgs {
     int tiles_m, tiles_n;
     uint16_t* out;  // STORE: C; UP: act (z^2 or z); DGRAD: dpre
     long long ldc;
-    int vec_out;  // out (and out2) 16-byte aligned with ldc*2 % 16 == 0
+    int vec_out;  // out (and out2) 16-byte aligned with ldc*2 % 16 == 0: bulk-tensor stores
     const int* kb_list;  // optional live k-blocks per row tile
     const int* kb_count;
     int kb_stride;
@@ -123,6 +126,31 @@ __device__ __forceinline__ void store_row32(uint16_t* row, int gcol, int N, bool
     }
 }
 
+// Epilogue output through shared memory: the warp's 32 rows x 32 columns (lane
+// = row, 16 packed words) go to its 2 KB staging buffer in the layout of a
+// tensor map with 64-byte swizzle (16-byte chunk ch of row r at
+// r*64 + 16*(ch ^ ((r >> 1) & 3)), conflict-free for a quarter warp), then
+// one bulk-tensor store writes whole 64-byte row segments at (col, row0);
+// rows and columns past the tensor's extent are clipped by the store.
+__device__ __forceinline__ void stage_store32(const CUtensorMap* tmap, unsigned char* sbuf, int lane,
+                                              const uint32_t (&w)[16], int col, int row0) {
+    if (lane == 0) bulk_wait_group_read0();  // the previous store has read the buffer
+    __syncwarp();
+    const uint32_t rb = smem_u32(sbuf) + (uint32_t)lane * 64u;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + 16u * (uint32_t)(ch ^ sw)),
+                     "r"(w[4 * ch]), "r"(w[4 * ch + 1]), "r"(w[4 * ch + 2]), "r"(w[4 * ch + 3])
+                     : "memory");
+    fence_proxy_async_smem();  // these generic-proxy writes, before the async-proxy read
+    __syncwarp();
+    if (lane == 0) {
+        tma_store_2d(tmap, sbuf, col, row0);
+        bulk_commit_group();
+    }
+}
+
 // 128-thread exclusive scan of one count per epilogue thread (ew = warp 0..3).
 __device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_part, int* total, int bar_id) {
     const int inc = warp_incl_scan(cnt, lane);
@@ -142,6 +170,7 @@ __device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_par
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
                 const GemmArgs args) {
     constexpr int BN_CTA = BN / G_CTAS;  // B rows (N) loaded by each CTA
     constexpr int A_BYTES = G_BM * G_BK * 2;
@@ -338,6 +367,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
             uint16_t* orow = args.out + (size_t)grow * args.ldc;
             const bool vec = args.vec_out != 0;
             const int par = it & 1;
+            const int row0 = tm * G_BM + ew * 32;  // first row of this warp
+            unsigned char* sbuf = smem + (size_t)G_STAGES * STAGE_BYTES + (size_t)(warp - 4) * 2048;
 
             if constexpr (EPI == EPI_STORE) {
 #pragma unroll 1
@@ -349,7 +380,11 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         w[q] = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])) : 0u;
-                    if (row_ok) store_row32(orow, gcol0 + c * 32, args.N, vec, w);
+                    if (vec) {
+                        if (tile_ok) stage_store32(&tmC, sbuf, lane, w, gcol0 + c * 32, row0);
+                    } else if (row_ok) {
+                        store_row32(orow, gcol0 + c * 32, args.N, false, w);
+                    }
                 }
             } else if constexpr (EPI == EPI_UP) {
                 if (gcol0 < args.N && tile_ok) {  // uniform over the warpgroup
@@ -400,7 +435,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             w[q] = pack_bf16x2(a0, a1);
                         }
                         bits &= colmask;
-                        if (row_ok) store_row32(orow, gcol, args.N, vec, w);
+                        if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                        else if (row_ok) store_row32(orow, gcol, args.N, false, w);
                         // compact this chunk's z values into the row's slot segment
                         uint32_t rem = bits;
                         while (rem) {
@@ -469,9 +505,12 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                 wa[q] = zb[q];
                             }
                         }
-                        if (row_ok) {
-                            store_row32(orow, gcol0 + c * 32, args.N, vec, wd);
-                            store_row32(orow2, gcol0 + c * 32, args.N, vec, wa);
+                        if (vec) {
+                            stage_store32(&tmC, sbuf, lane, wd, gcol0 + c * 32, row0);
+                            stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
+                        } else if (row_ok) {
+                            store_row32(orow, gcol0 + c * 32, args.N, false, wd);
+                            store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
                         }
                     }
                 }
@@ -485,6 +524,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                 acc_phase ^= 1u;
             }
         }
+        if (lane == 0) bulk_wait_group0();  // this warp's stores are complete
+        __syncwarp();
     }
     // No CTA may leave while its peer can still touch its shared memory,
     // barriers or TMEM.
@@ -514,7 +555,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
 // row stride `ld` elements, box = box_inner x box_outer, 128-byte swizzle.
 bool make_tmap(CUtensorMap* m, const void* base, long long inner, long long outer, long long ld,
-               int box_inner, int box_outer) {
+               int box_inner, int box_outer,
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
@@ -522,7 +564,7 @@ bool make_tmap(CUtensorMap* m, const void* base, long long inner, long long oute
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
-                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         char msg[200];
@@ -588,13 +630,25 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     const bool okB = B_MN ? make_tmap(&tb, B, args.N, args.K, ldb, 64, G_BK)
                           : make_tmap(&tb, B, args.K, args.N, ldb, G_BK, BN / G_CTAS);
     if (!okA || !okB) return SFFN_ERR_CUDA;
-    constexpr int smem = G_STAGES * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 1024;
+    // outputs: 32 x 32 boxes with 64-byte swizzle for the epilogue's bulk stores
+    CUtensorMap tc, tc2;
+    memset(&tc, 0, sizeof(tc));
+    memset(&tc2, 0, sizeof(tc2));
+    if (args.vec_out) {
+        if (!make_tmap(&tc, args.out, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+            return SFFN_ERR_CUDA;
+        if (EPI == EPI_DGRAD &&
+            !make_tmap(&tc2, args.out2, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+            return SFFN_ERR_CUDA;
+    }
+    // stages + 8 epilogue warps x 2 KB staging + alignment slack
+    constexpr int smem = G_STAGES * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 8 * 2048 + 1024;
     auto k = gemm_kernel<BN, A_MN, B_MN, EPI>;
     SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int npairs = ((args.tiles_m + 1) / 2) * args.tiles_n;
     const int clusters = std::min(npairs, max_active_clusters(k, smem));
     if (clusters <= 0) return SFFN_OK;
-    k<<<clusters * G_CTAS, G_THREADS, smem, st>>>(ta, tb, args);
+    k<<<clusters * G_CTAS, G_THREADS, smem, st>>>(ta, tb, tc, tc2, args);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
