@@ -45,6 +45,7 @@
 //          ReLU^2: dpre = bf16((g*2) * z) and act2 = bf16(z*z) (for dW2);
 //          ReLU:   dpre = bit ? g : 0 and act2 = z.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include <stdio.h>
@@ -109,6 +110,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     return l | (h << 16);
 }
 __device__ __forceinline__ float bf16_to_f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
 __device__ __forceinline__ uint16_t f_to_bf16(float f) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(f));
 }
@@ -298,13 +300,17 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                 }
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                // The operands reach shared memory by TMA and are read by the MMAs
+                // through the async proxy, ordered by the full barrier alone: no
+                // tcgen05 fence per k-block.  The next k-block's barrier is
+                // tested while the current MMAs run, so its latency is hidden.
+                bool ready = nkb > 0 && mbar_try_wait(&full_bar[stage], phase);
                 for (int i = 0; i < nkb; ++i) {
-                    if (!mbar_wait_bounded(&full_bar[stage], phase)) {
+                    if (!ready && !mbar_wait_bounded(&full_bar[stage], phase)) {
                         atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
                         s_abort = 1;
                         break;
                     }
-                    tc_fence_after();
                     const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
                     const uint32_t sb = sa + A_BYTES;
 #pragma unroll
@@ -320,6 +326,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         stage = 0;
                         phase ^= 1u;
                     }
+                    ready = i + 1 < nkb && mbar_try_wait(&full_bar[stage], phase);
                 }
                 tc_commit_pair_multicast(&tfull_bar[acc], 0x3);
                 if (++acc == 2) {
@@ -416,33 +423,31 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                 v0 += sb[c * 32 + 2 * q];
                                 v1 += sb[c * 32 + 2 * q + 1];
                             }
-                            // pre = bf16(v); z = relu(pre) on the packed pair: negative
-                            // non-NaN halves become +0 (NaN stays NaN, as in torch)
-                            const uint32_t pw = pack_bf16x2(v0, v1);
-                            const uint32_t mag = pw & 0x7FFF7FFFu;
-                            const uint32_t neg = ((pw >> 15) & 0x00010001u) * 0xFFFFu;
-                            const uint32_t nan = __vcmpgtu2(mag, 0x7F807F80u);
-                            const uint32_t z = pw & ~(neg & ~nan);
-                            // z > 0: non-zero, sign clear, not NaN
-                            const uint32_t pos = __vcmpgtu2(z & 0x7FFF7FFFu, 0u) & ~nan & ~neg;
+                            // pre = bf16(v); z = relu(pre) on the packed pair (NaN stays NaN,
+                            // as in torch); the bf16 product z*z is exact before its one
+                            // rounding, so __hmul2 gives bf16(z^2) exactly
+                            const __nv_bfloat162 pre = __floats2bfloat162_rn(v0, v1);
+                            const __nv_bfloat162 zb = __hmax2_nan(pre, __float2bfloat162_rn(0.f));
+                            const uint32_t z = bf162_bits(zb);
+                            // z > 0: magnitude non-zero and not NaN (+inf counts)
+                            const uint32_t mag = z & 0x7FFF7FFFu;
+                            const uint32_t pos = __vcmpgtu2(mag, 0u) & __vcmpleu2(mag, 0x7F807F80u) &
+                                                 ~(((z >> 15) & 0x00010001u) * 0xFFFFu);
                             bits |= ((pos & 1u) | ((pos >> 15) & 2u)) << (2 * q);
                             zw[q] = z;
-                            float a0 = __uint_as_float(z << 16), a1 = __uint_as_float(z & 0xFFFF0000u);
-                            if (args.act == ACT_RELU2) {
-                                a0 *= a0;
-                                a1 *= a1;
-                            }
-                            w[q] = pack_bf16x2(a0, a1);
+                            w[q] = args.act == ACT_RELU2 ? bf162_bits(__hmul2(zb, zb)) : z;
                         }
                         bits &= colmask;
                         if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
                         else if (row_ok) store_row32(orow, gcol, args.N, false, w);
-                        // compact this chunk's z values into the row's slot segment
-                        uint32_t rem = bits;
-                        while (rem) {
-                            const int j = __ffs(rem) - 1;
-                            rem &= rem - 1u;
-                            slot_row[cnt++] = (uint16_t)(zw[j >> 1] >> (16 * (j & 1)));
+                        // this chunk's z values, in column order, to the row's slot segment
+#pragma unroll
+                        for (int q = 0; q < 16; ++q) {
+                            const uint32_t b2 = (bits >> (2 * q)) & 3u;
+                            if (b2) {
+                                if (b2 & 1u) slot_row[cnt++] = (uint16_t)zw[q];
+                                if (b2 & 2u) slot_row[cnt++] = (uint16_t)(zw[q] >> 16);
+                            }
                         }
                         words[c] = bits;
                     }
