@@ -7,8 +7,9 @@
 //
 // Design (one CTA per SM, CTA pairs (clusters of 2) persistent over output
 // tiles of 256 x BN; each CTA of the pair owns 128 rows):
-//   warp 0       TMA producer (both CTAs): 2-D tiled bulk-tensor loads (128-byte
-//                swizzle) of this CTA's half of the A and B k-blocks (64 wide)
+//   warps 0,2,3,12  TMA producers (both CTAs): 2-D tiled bulk-tensor loads
+//                (128-byte swizzle) of this CTA's half of the A (warps 0, 2)
+//                and B (warps 3, 12) k-blocks (64 wide; even / odd k-blocks)
 //                into a 6-stage shared-memory ring; the bytes complete on the
 //                leader CTA's barrier.
 //   warp 1       MMA issuer (leader CTA only): one thread issues
@@ -16,7 +17,7 @@
 //                and B halves from both CTAs' shared memory and accumulates rows
 //                0-127 in the leader's TMEM and 128-255 in the peer's, into one
 //                of two accumulators; commits are multicast to both CTAs.
-//   warp 2       allocates / frees the 2*BN TMEM columns (pair allocation).
+//   warp 2       also allocates / frees the 2*BN TMEM columns (pair allocation).
 //   warps 4..11  epilogue, two warpgroups each owning half of the tile's
 //                columns: each thread owns one accumulator row (TMEM lane),
 //                reads 32 columns per tcgen05.ld, applies the epilogue and
@@ -61,7 +62,7 @@ namespace {
 
 constexpr int G_BM = 128;
 constexpr int G_BK = 64;
-constexpr int G_THREADS = 384;  // 4 control warps + 2 epilogue warpgroups
+constexpr int G_THREADS = 416;  // 4 control warps, 2 epilogue warpgroups (warps 4-11), 1 more producer
 constexpr int G_STAGES = 6;
 constexpr int G_GROUP_M = 8;  // pair-tile rows per raster group (16 row tiles of 128)
 constexpr int G_CTAS = 2;     // CTA pairs (cta_group::2)
@@ -229,55 +230,70 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = s_tmem;
 
-    if (warp == 0) {
-        // ------------------------------------------------------ producer --
+    if (warp == 0 || warp == 2 || warp == 3 || warp == 12) {
+        // ----------------------------------------------------- producers --
+        // Four issuing threads, one per (operand, k-block parity): warps 0 / 2
+        // load A of the even / odd k-blocks and arm those stages (both
+        // operands' bytes of both CTAs, on the leader's barrier), warps 3 / 12
+        // load B of the even / odd k-blocks.  One thread's bulk-tensor copies
+        // complete one after another (about one per L2 round trip), so the
+        // four issuers keep four copies in flight per SM.  (B's bytes may land
+        // before the arming; the barrier's transaction count may go negative
+        // meanwhile, and the phase cannot complete before the arrival.)
+        const bool loads_a = warp == 0 || warp == 2;
+        const int par = (warp == 0 || warp == 3) ? 0 : 1;
         if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
             int armed[G_STAGES] = {0};
+            long long kc = 0;  // k-blocks of this CTA so far (all tiles)
             for (int tile = first_tile; tile < ntiles && !s_abort; tile += tile_stride) {
                 int pm, tn;
                 raster(tile, tiles_mp, args.tiles_n, pm, tn);
                 const int nkb = args.kb_count ? args.kb_count[pm] : nkb_full;
                 const int arow = pm * G_BM * G_CTAS + (int)rank * G_BM;   // this CTA's A rows
                 const int brow = tn * BN + (int)rank * BN_CTA;            // this CTA's B rows (N)
-                for (int i = 0; i < nkb; ++i) {
+                bool stop = false;
+                for (int i = 0; i < nkb; ++i, ++kc) {
+                    if ((int)(kc & 1) != par) continue;
+                    const int stage = (int)(kc % G_STAGES);
+                    const uint32_t phase = (uint32_t)((kc / G_STAGES) & 1);
                     const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : i;
                     // the stage is free once the leader's MMAs reading it are done
                     if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
                         atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
                         s_abort = 1;
+                        stop = true;
                         break;
-                    }
-                    if (leader) {
-                        mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES * G_CTAS);
-                        ++armed[stage];
                     }
                     unsigned char* sa = smem + (size_t)stage * STAGE_BYTES;
                     unsigned char* sb = sa + A_BYTES;
-                    if constexpr (!A_MN) {
-                        tma_load_2d_pair(sa, &tmA, kb * G_BK, arow, &full_bar[stage]);
-                    } else {
+                    if (loads_a) {
+                        if (leader) {
+                            mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES * G_CTAS);
+                            ++armed[stage];
+                        }
+                        if constexpr (!A_MN) {
+                            tma_load_2d_pair(sa, &tmA, kb * G_BK, arow, &full_bar[stage]);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < G_BM / 64; ++j)
-                            tma_load_2d_pair(sa + j * MN_LBO, &tmA, arow + j * 64, kb * G_BK, &full_bar[stage]);
-                    }
-                    if constexpr (!B_MN) {
-                        tma_load_2d_pair(sb, &tmB, kb * G_BK, brow, &full_bar[stage]);
+                            for (int j = 0; j < G_BM / 64; ++j)
+                                tma_load_2d_pair(sa + j * MN_LBO, &tmA, arow + j * 64, kb * G_BK, &full_bar[stage]);
+                        }
                     } else {
+                        if constexpr (!B_MN) {
+                            tma_load_2d_pair(sb, &tmB, kb * G_BK, brow, &full_bar[stage]);
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < BN_CTA / 64; ++j)
-                            tma_load_2d_pair(sb + j * MN_LBO, &tmB, brow + j * 64, kb * G_BK, &full_bar[stage]);
-                    }
-                    if (++stage == G_STAGES) {
-                        stage = 0;
-                        phase ^= 1u;
+                            for (int j = 0; j < BN_CTA / 64; ++j)
+                                tma_load_2d_pair(sb + j * MN_LBO, &tmB, brow + j * 64, kb * G_BK, &full_bar[stage]);
+                        }
                     }
                 }
+                if (stop) break;
             }
-            // The leader's full barriers count both CTAs' bytes: once their last
-            // armed phases complete, no copy is still landing in either CTA.
-            if (leader)
+            // The leader's full barriers count both CTAs' bytes of both
+            // operands: once the last phases armed by this thread complete, no
+            // copy of those stages is still landing in either CTA.
+            if (leader && loads_a)
                 for (int s = 0; s < G_STAGES; ++s)
                     if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
         }
@@ -336,7 +352,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
             }
         }
         __syncwarp();
-    } else if (warp >= 4) {
+    } else if (warp >= 4 && warp < 12) {
         // ------------------------------------------------------ epilogue --
         // Two warpgroups: warps 4-7 own accumulator columns [0, BN/2), warps
         // 8-11 own [BN/2, BN).  Warp w reads TMEM lanes 32*(w%4) .. +31 (the
