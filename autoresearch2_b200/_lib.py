@@ -54,7 +54,7 @@ SIGNATURES = {
     "sffn_tile_row_offsets": (_int, [_vp, _vp, _i64, _vp, _vp]),
     "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
-                              _vp, _vp, _vp, _i64, _vp, _vp]),
+                              _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
 }
 
 _lib = None

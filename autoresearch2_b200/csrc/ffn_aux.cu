@@ -13,7 +13,8 @@
 //   live_kblocks_kernel for each 256-row tile (two rows of 128x128 format
 //                       tiles, the GEMM's CTA-pair tile) of a tiled bitmask,
 //                       the ascending list of 64-column blocks holding any set
-//                       bit: the down-projection skips the others.
+//                       bit: the down-projection skips the others.  One warp
+//                       per k-block; the last CTA of a tile compacts.
 #include "common.cuh"
 
 namespace sffn {
@@ -21,38 +22,54 @@ namespace {
 
 constexpr int SCAN_NT = 1024;
 
+// One CTA: thread tid owns a contiguous run of tiles; run sums are scanned
+// with warp shuffles (two levels), then each thread writes its run's prefixes.
 __global__ void __launch_bounds__(SCAN_NT) tile_scan_kernel(const int* __restrict__ counts, int parts,
                                                            long long ntiles, int* __restrict__ prefix,
                                                            int* __restrict__ cursor,
                                                            int* __restrict__ vals_offset_out,
                                                            uint32_t* __restrict__ status) {
-    __shared__ long long s_part[SCAN_NT];
-    const int tid = threadIdx.x;
+    __shared__ long long s_warp[SCAN_NT / 32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const long long per = (ntiles + SCAN_NT - 1) / SCAN_NT;
     const long long lo = tid * per, hi = min(lo + per, ntiles);
+    const bool vec4 = parts == 4 && (reinterpret_cast<uintptr_t>(counts) & 15u) == 0;
     auto count = [&](long long t) {
+        if (vec4) {
+            const int4 c = __ldg(reinterpret_cast<const int4*>(counts) + t);
+            return c.x + c.y + c.z + c.w;
+        }
         int c = 0;
-        for (int k = 0; k < parts; ++k) c += counts[t * parts + k];
+        for (int k = 0; k < parts; ++k) c += __ldg(counts + t * parts + k);
         return c;
     };
     long long sum = 0;
     for (long long t = lo; t < hi; ++t) sum += count(t);
-    s_part[tid] = sum;
-    __syncthreads();
-    // Hillis-Steele inclusive scan of the 1024 partial sums
-    for (int o = 1; o < SCAN_NT; o <<= 1) {
-        const long long v = tid >= o ? s_part[tid - o] : 0;
-        __syncthreads();
-        s_part[tid] += v;
-        __syncthreads();
+    long long inc = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const long long v = __shfl_up_sync(FULL, inc, o);
+        if (lane >= o) inc += v;
     }
-    long long run = s_part[tid] - sum;
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        long long w = s_warp[lane], wi = w;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long v = __shfl_up_sync(FULL, wi, o);
+            if (lane >= o) wi += v;
+        }
+        s_warp[lane] = wi - w;  // exclusive prefix of each warp
+    }
+    __syncthreads();
+    long long run = s_warp[warp] + inc - sum;
     for (long long t = lo; t < hi; ++t) {
         prefix[t] = (int)run;
         run += count(t);
     }
     if (tid == SCAN_NT - 1) {
-        const long long total = s_part[SCAN_NT - 1];
+        const long long total = run;  // the last thread's run ends at the total
         prefix[ntiles] = (int)total;
         const int cur = *cursor;
         *vals_offset_out = cur;
@@ -84,49 +101,86 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
     if (row_offsets) row_offsets[t * 128 + r] = roff;
     if (!slots) return;
     const long long base = (long long)*vals_offset;
-    // warp-cooperative, coalesced copy of the warp's 32 row segments
-    for (int i = 0; i < 32; ++i) {
-        const int c = __shfl_sync(FULL, cnt, i);
-        const long long d = base + __shfl_sync(FULL, roff, i);
-        const uint16_t* src = slots + t * 16384 + (warp * 32 + i) * 128;
-        for (int k = lane; k < c; k += 32) {
-            const long long p = d + k;
-            if (p >= 0 && p < cap) vals[p] = __ldcs(src + k);
-            else atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+    // Warp-cooperative, coalesced copy of the warp's 32 row segments (lane k
+    // moves value k of a row), eight rows at a time with all loads issued
+    // before any store, so a warp waits for one memory round trip per batch.
+    int maxc = cnt;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) maxc = max(maxc, __shfl_xor_sync(FULL, maxc, o));
+    const uint16_t* wsrc = slots + t * 16384 + warp * 32 * 128;
+    for (int k0 = 0; k0 < maxc; k0 += 32) {
+        const int k = k0 + lane;
+#pragma unroll
+        for (int i0 = 0; i0 < 32; i0 += 8) {
+            uint16_t v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = __shfl_sync(FULL, cnt, i0 + u);
+                v[u] = k < c ? __ldcs(wsrc + (i0 + u) * 128 + k) : (uint16_t)0;
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = __shfl_sync(FULL, cnt, i0 + u);
+                const long long p = base + __shfl_sync(FULL, roff, i0 + u) + k;
+                if (k < c) {
+                    if (p >= 0 && p < cap) vals[p] = v[u];
+                    else atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+                }
+            }
         }
     }
 }
 
-// One CTA per 256-row tile; one warp per 64-column block at a time.
-__global__ void __launch_bounds__(256) live_kblocks_kernel(const uint8_t* __restrict__ mask, int gm_f, int gn_f,
-                                                           int nkb, int* __restrict__ kb_list,
-                                                           int* __restrict__ kb_count) {
-    extern __shared__ int s_live[];  // [nkb]
+// Grid (pair tile, group of 8 k-blocks); warp w of a CTA tests k-block
+// 8*group + w over the pair's two 128-row format tiles with all loads issued
+// at once, and writes a 0/1 flag into kb_list[tile][kb].  The last CTA of a
+// pair tile (counted in kb_count[tile], zeroed before the launch) compacts the
+// flags in place into the ascending list of live k-blocks and stores the count.
+constexpr int LIVE_WARPS = 8;
+__global__ void __launch_bounds__(LIVE_WARPS * 32) live_kblocks_kernel(const uint8_t* __restrict__ mask,
+                                                                      int gm_f, int gn_f, int nkb,
+                                                                      int* __restrict__ kb_list,
+                                                                      int* __restrict__ kb_count) {
     const int tp = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int kb = warp; kb < nkb; kb += blockDim.x / 32) {
-        uint32_t any = 0;
+    const int kb = blockIdx.y * LIVE_WARPS + warp;
+    int* flags = kb_list + (long long)tp * nkb;
+    if (kb < nkb) {
+        uint2 w[2][4];
+#pragma unroll
         for (int h = 0; h < 2; ++h) {
             const int tm = 2 * tp + h;
-            if (tm >= gm_f) break;
-            const long long tf = (long long)tm * gn_f + kb / 2;
+            const long long tf = (long long)min(tm, gm_f - 1) * gn_f + kb / 2;
             const uint8_t* tmask = mask + tf * 2048 + (kb & 1) * 8;  // 2 words of each 16-byte row
 #pragma unroll
-            for (int r = lane; r < 128; r += 32) {
-                const uint2 w = *reinterpret_cast<const uint2*>(tmask + r * 16);
-                any |= w.x | w.y;
-            }
+            for (int q = 0; q < 4; ++q)
+                w[h][q] = tm < gm_f ? *reinterpret_cast<const uint2*>(tmask + (lane + 32 * q) * 16) : make_uint2(0, 0);
         }
+        uint32_t any = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) any |= w[h][q].x | w[h][q].y;
         any = __any_sync(FULL, any != 0);
-        if (lane == 0) s_live[kb] = any ? 1 : 0;
+        if (lane == 0) flags[kb] = any ? 1 : 0;
     }
+    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int n = 0;
-        for (int kb = 0; kb < nkb; ++kb)
-            if (s_live[kb]) kb_list[(long long)tp * nkb + n++] = kb;
-        kb_count[tp] = n;
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(&kb_count[tp], 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!s_last || warp != 0) return;
+    __threadfence();
+    // ordered in-place compaction: entry n <= kb is written after flag kb is read
+    int n = 0;
+    for (int k0 = 0; k0 < nkb; k0 += 32) {
+        const int k = k0 + lane;
+        const bool live = k < nkb && __ldcg(flags + k) != 0;
+        const unsigned b = __ballot_sync(FULL, live);
+        if (live) flags[n + __popc(b & ((1u << lane) - 1u))] = k;
+        n += __popc(b);
     }
+    if (lane == 0) kb_count[tp] = n;
 }
 
 }  // namespace
@@ -179,10 +233,13 @@ extern "C" int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, i
     if (M <= 0 || N <= 0 || !bitmask || !kb_list || !kb_count) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 7u) return SFFN_ERR_ALIGN;
     const long long gm = (M + 127) / 128, gp = (M + 255) / 256, gn_f = (N + 127) / 128, nkb = (N + 63) / 64;
-    if (nkb > 12288) return SFFN_ERR_UNSUPPORTED;  // shared-memory flag array
+    if (gp > 0x7FFFFFFF || nkb > 0x7FFFFFFF) return SFFN_ERR_ARG;
     if (int rc = bind_device_of(bitmask)) return rc;
-    live_kblocks_kernel<<<(unsigned)gp, 256, (size_t)nkb * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
-        bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list, kb_count);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    SFFN_CUDA_TRY(cudaMemsetAsync(kb_count, 0, (size_t)gp * sizeof(int32_t), st));
+    const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));
+    live_kblocks_kernel<<<grid, LIVE_WARPS * 32, 0, st>>>(bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list,
+                                                         kb_count);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

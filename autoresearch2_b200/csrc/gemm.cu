@@ -92,6 +92,7 @@ struct GemmArgs {
     long long vals_len;
     const int* row_offsets;  // DGRAD: [num_tiles][128] prefix[t] + in-tile row prefix
     const int* vals_offset;
+    float* colsum;  // DGRAD: optional fp32 [N] += column sums of dpre
     uint32_t* status;
 };
 
@@ -528,10 +529,40 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         }
                         if (vec) {
                             stage_store32(&tmC, sbuf, lane, wd, gcol0 + c * 32, row0);
+                            if (args.colsum) {
+                                // lane = column: sum the staged dpre block over its rows
+                                // (rows past M hold zeros); conflict-free swizzled reads
+                                const uint32_t sb0 = smem_u32(sbuf);
+                                const int ch = lane >> 3, sub = (lane & 7) * 2;
+                                float acc = 0.f;
+#pragma unroll 8
+                                for (int rr = 0; rr < 32; ++rr) {
+                                    uint16_t h;
+                                    asm volatile("ld.shared.u16 %0, [%1];"
+                                                 : "=h"(h)
+                                                 : "r"(sb0 + (uint32_t)(rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)) + sub)));
+                                    acc += bf16_to_f(h);
+                                }
+                                const int col = gcol0 + c * 32 + lane;
+                                if (col < args.N) atomicAdd(args.colsum + col, acc);
+                            }
                             stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
-                        } else if (row_ok) {
-                            store_row32(orow, gcol0 + c * 32, args.N, false, wd);
-                            store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
+                        } else {
+                            if (row_ok) {
+                                store_row32(orow, gcol0 + c * 32, args.N, false, wd);
+                                store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
+                            }
+                            if (args.colsum) {
+                                // column sums by shuffles (rows past M contribute zeros)
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    float v = row_ok ? bf16_to_f((uint16_t)(wd[j >> 1] >> (16 * (j & 1)))) : 0.f;
+#pragma unroll
+                                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+                                    const int col = gcol0 + c * 32 + j;
+                                    if (lane == 0 && col < args.N) atomicAdd(args.colsum + col, v);
+                                }
+                            }
                         }
                     }
                 }
@@ -756,7 +787,7 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
                               int64_t T, int64_t D, int64_t F, int act, const void* vals,
                               int64_t vals_len, const uint8_t* bitmask, const int32_t* row_offsets,
                               const int32_t* vals_offset_dev, void* dpre_out, void* act_out,
-                              int64_t ld_out, uint32_t* status_dev, void* stream) {
+                              int64_t ld_out, float* db1_sum, uint32_t* status_dev, void* stream) {
     // dA[T, F] = dout[T, D] @ W2[D, F]: B = W2 is [K=D][N=F], N contiguous (MN-major).
     int rc = check_operands(dout, ld_dout, false, w2, ldw2, true, T, F, D);
     if (rc) return rc;
@@ -774,6 +805,7 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
     a.vals_len = vals_len;
     a.row_offsets = row_offsets;
     a.vals_offset = vals_offset_dev;
+    a.colsum = db1_sum;
     a.status = status_dev;
     return dispatch<EPI_DGRAD>(false, true, dout, ld_dout, w2, ldw2, a, reinterpret_cast<cudaStream_t>(stream));
 }

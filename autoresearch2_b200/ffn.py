@@ -74,13 +74,15 @@ def _fused_backward(ctx, grad_output, act):
     kb_list, kb_count = ctx.kb
     ctx.kb = None
     grad_output = grad_output.contiguous()
-    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets)
+    # the bias gradient (column sums of dpre) is summed in the same kernel, in fp32
+    db1 = torch.zeros(W1.shape[0], dtype=torch.float32, device=x.device) if ctx.has_bias else None
+    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1)
     ctx.row_offsets = None
+    grad_b1 = submit_grad(db1.to(dpre.dtype)) if ctx.has_bias else None
     grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
     grad_W1 = submit_grad(G.mm(dpre.T, x))
-    grad_b1 = submit_grad(dpre.sum(0, dtype=torch.float32).to(dpre.dtype)) if ctx.has_bias else None
     return grad_x, grad_W1, grad_W2, None, grad_b1
 
 

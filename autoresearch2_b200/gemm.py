@@ -104,11 +104,12 @@ def tile_row_offsets(z_sparse):
     return ro
 
 
-def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None):
+def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None):
     """Fused dout @ W2 with the activation gradient; returns (dpre, act2)
     where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F].  z_sparse is a
     128x128-tile BitsparseTensor; row_offsets its per-row offsets (computed
-    here if not given)."""
+    here if not given).  db1: optional zeroed float32 [F] that receives the
+    column sums of dpre (the bias gradient)."""
     T, D = dout.shape
     F = W2.shape[1]
     dev = dout.device
@@ -120,6 +121,6 @@ def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None):
     act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     call("sffn_ffn_dgrad", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,
          ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(row_offsets),
-         ptr(z_sparse.vals_offset), ptr(dpre), ptr(act2), dpre.stride(0),
+         ptr(z_sparse.vals_offset), ptr(dpre), ptr(act2), dpre.stride(0), ptr(db1),
          ptr(_lib.status_word(dev)), stream_ptr(dev))
     return dpre, act2

@@ -244,13 +244,16 @@ int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_
  * (act = 0): dpre = bit ? g : 0 and act_out = z -- z gathered from the
  * tiled 128x128 BitsparseTensor (vals, bitmask, *vals_offset_dev) at the
  * row offsets of sffn_tile_row_offsets.
+ * If db1_sum is not NULL, the column sums of dpre (the bias gradient, over
+ * the T rows) are added into db1_sum[F] in fp32 (zero it first; the order of
+ * the additions is not fixed).
  *   replaces old/lib_sparse/sparse.py:92-102,132-145 (grad_output @ W2 with
  *   _mask_with_bitmask_kernel / _grad_relu2_kernel) and the unpack inside spAx
  *   (sparse.py:305-351). */
 int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2,
                    int64_t T, int64_t D, int64_t F, int act, const void* vals, int64_t vals_len,
                    const uint8_t* bitmask, const int32_t* row_offsets, const int32_t* vals_offset_dev,
-                   void* dpre_out, void* act_out, int64_t ld_out, uint32_t* status_dev,
+                   void* dpre_out, void* act_out, int64_t ld_out, float* db1_sum, uint32_t* status_dev,
                    void* stream);
 
 #ifdef __cplusplus

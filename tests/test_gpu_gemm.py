@@ -147,7 +147,10 @@ def test_ffn_dgrad_fused(act):
     offset = torch.zeros(1, dtype=torch.int32, device=DEV)
     _, bitmask, prefix, voff, _ = gemm.ffn_up(x, W1, b1, act, arena, offset)
     zs = sf.BitsparseTensor(arena, bitmask, prefix, voff, -(-T // 128), -(-F // 128), 128, 128, (T, F))
-    dpre, act2 = gemm.ffn_dgrad(dout, W2, act, zs)
+    db1 = torch.zeros(F, dtype=torch.float32, device=DEV)
+    dpre, act2 = gemm.ffn_dgrad(dout, W2, act, zs, db1=db1)
+    # fused bias gradient: column sums of the bf16 dpre, accumulated in fp32
+    torch.testing.assert_close(db1, dpre.float().sum(0), rtol=1e-5, atol=1e-4)
     z = zs.to_dense().float()
     g = (dout.float() @ W2.float()).to(torch.bfloat16).float()
     if act == 1:
