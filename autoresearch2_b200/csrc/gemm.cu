@@ -589,6 +589,247 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------------- 2:4 GEMM ----
+// C[M, N] = A24[M, K] * B[N, K]^T with A in the 2:4 form of sp24.cu
+// (compressed values [M, K/2] + tensor-memory-ordered metadata); B K-major
+// ([N][ldb]) or MN-major ([K][ldb]).  Pair tiles of 256 x 256 as in
+// gemm_kernel; a stage is 128 logical K (four tcgen05.mma.sp of K = 32):
+// 16 KB of compressed A + 32 KB of B per CTA, 4 stages.
+//   warps 0-5   TMA issuers, one per (operand copy A / B0 / B1, even / odd
+//               stage); the A issuers of the leader arm the stage barrier
+//   warp 6      MMA issuer (leader)
+//   warps 7-10  metadata: each copies its lane quarter's 16 bytes per stage
+//               from global memory into 4 tensor-memory columns (one per MMA)
+//   warps 11-18 epilogue: two warpgroups of 128 accumulator columns.  There is
+//               one accumulator (256 columns) because the metadata ring needs
+//               tensor memory too; the epilogue frees it fast by converting
+//               each 32-column chunk to bf16 into spare tensor-memory columns,
+//               then stores from there while the next tile accumulates.
+constexpr int S_BK = 128;
+constexpr int S_STAGES = 4;
+constexpr int S_THREADS = 19 * 32;
+constexpr int S_META_COL = 256;  // metadata ring: 4 columns per stage
+constexpr int S_PACK_COL = 272;  // bf16 staging: 64 columns per warpgroup
+
+template <bool B_MN>
+__global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
+    gemm_sp24_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, const uint4* __restrict__ meta, int M, int N, int K,
+                     uint32_t* __restrict__ status) {
+    constexpr int A_BYTES = G_BM * (S_BK / 2) * 2;  // 16 KB
+    constexpr int B_HALF = 128 * 64 * 2;             // one 16 KB box
+    constexpr int STAGE_BYTES = A_BYTES + 2 * B_HALF;
+    constexpr uint32_t IDESC = idesc_bf16_f32(G_BM * G_CTAS, 256, false, B_MN) | (1u << 2);
+    extern __shared__ __align__(1024) unsigned char g_smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    __shared__ __align__(8) uint64_t full_bar[S_STAGES], empty_bar[S_STAGES], meta_bar[S_STAGES];
+    __shared__ __align__(8) uint64_t tfull_bar, tempty_bar;
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tiles_m = M / G_BM, tiles_n = (N + 255) / 256;
+    const int tiles_mp = (tiles_m + 1) / 2;
+    const int ntiles = tiles_mp * tiles_n;
+    const int nkb = K / S_BK;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int first_tile = (int)cluster_id_x();
+    const int tile_stride = (int)cluster_count_x();
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+            mbar_init(&meta_bar[s], 4 * G_CTAS);  // the 4 metadata warps of both CTAs
+        }
+        mbar_init(&tfull_bar, 1);
+        mbar_init(&tempty_bar, 8 * G_CTAS);  // the 8 epilogue warps of both CTAs
+        s_abort = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(&s_tmem, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem;
+
+    if (warp < 6) {
+        // ------------------------------------------------------ producers --
+        const int op = warp % 3;           // 0: A, 1: B (first half), 2: B (second half)
+        const int par = warp / 3;          // even / odd stages
+        if (lane == 0) {
+            int armed[S_STAGES] = {0};
+            long long kc = 0;
+            bool stop = false;
+            for (int tile = first_tile; tile < ntiles && !stop && !s_abort; tile += tile_stride) {
+                int pm, tn;
+                raster(tile, tiles_mp, tiles_n, pm, tn);
+                const int arow = (pm * G_CTAS + (int)rank) * G_BM;
+                const int brow = tn * 256 + (int)rank * 128;
+                for (int kb = 0; kb < nkb; ++kb, ++kc) {
+                    if ((int)(kc & 1) != par) continue;
+                    const int stage = (int)(kc % S_STAGES);
+                    const uint32_t phase = (uint32_t)((kc / S_STAGES) & 1);
+                    if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
+                        atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                        s_abort = 1;
+                        stop = true;
+                        break;
+                    }
+                    unsigned char* sa = smem + (size_t)stage * STAGE_BYTES;
+                    unsigned char* sb = sa + A_BYTES;
+                    if (op == 0) {
+                        if (leader) {
+                            mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES * G_CTAS);
+                            ++armed[stage];
+                        }
+                        tma_load_2d_pair(sa, &tmA, kb * (S_BK / 2), arow, &full_bar[stage]);
+                    } else {
+                        const int h = op - 1;
+                        if constexpr (!B_MN)  // [N][K]: K offsets 0 / 64 of the stage
+                            tma_load_2d_pair(sb + h * B_HALF, &tmB, kb * S_BK + h * 64, brow, &full_bar[stage]);
+                        else  // [K][N]: N blocks 0 / 64, 128 K rows each
+                            tma_load_2d_pair(sb + h * B_HALF, &tmB, brow + h * 64, kb * S_BK, &full_bar[stage]);
+                    }
+                }
+            }
+            if (leader && op == 0)
+                for (int s = 0; s < S_STAGES; ++s)
+                    if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 6) {
+        // ----------------------------------------------------------- MMA --
+        if (lane == 0 && leader) {
+            long long kc = 0;
+            int it = 0;
+            for (int tile = first_tile; tile < ntiles && !s_abort; tile += tile_stride, ++it) {
+                if (!mbar_wait_bounded(&tempty_bar, ((uint32_t)it & 1u) ^ 1u)) {
+                    atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                bool fail = false;
+                for (int kb = 0; kb < nkb; ++kb, ++kc) {
+                    const int stage = (int)(kc % S_STAGES);
+                    const uint32_t phase = (uint32_t)((kc / S_STAGES) & 1);
+                    if (!mbar_wait_bounded(&full_bar[stage], phase) || !mbar_wait_bounded(&meta_bar[stage], phase)) {
+                        atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                        s_abort = 1;
+                        fail = true;
+                        break;
+                    }
+                    tc_fence_after();  // the metadata arrived by thread synchronisation
+                    const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
+                    const uint32_t sb = sa + A_BYTES;
+                    const uint32_t e0 = tmem_base + S_META_COL + 4 * stage;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const uint64_t ad = umma_desc_sw128(sa + 32 * j, 16, 1024);
+                        const uint64_t bd = B_MN ? umma_desc_sw128(sb + 4096 * j, B_HALF, 1024)
+                                                 : umma_desc_sw128(sb + (j >> 1) * B_HALF + 64 * (j & 1), 16, 1024);
+                        tc_mma_sp_pair(tmem_base, ad, bd, e0 + (uint32_t)(j & ~1), IDESC | (uint32_t)(j & 1),
+                                       (kb | j) != 0 ? 1u : 0u);
+                    }
+                    tc_commit_pair_multicast(&empty_bar[stage], 0x3);
+                }
+                if (fail) break;
+                tc_commit_pair_multicast(&tfull_bar, 0x3);
+            }
+        }
+        __syncwarp();
+    } else if (warp < 11) {
+        // ------------------------------------------------------ metadata --
+        const int q = warp & 3;  // lane quarter
+        const uint32_t meta_leader = leader_smem_addr(&meta_bar[0]);
+        long long kc = 0;
+        bool stop = false;
+        for (int tile = first_tile; tile < ntiles && !stop; tile += tile_stride) {
+            int pm, tn;
+            raster(tile, tiles_mp, tiles_n, pm, tn);
+            const int tm = pm * G_CTAS + (int)rank;
+            const bool tile_ok = tm < tiles_m;
+            for (int kb = 0; kb < nkb; ++kb, ++kc) {
+                const int stage = (int)(kc % S_STAGES);
+                const uint32_t phase = (uint32_t)((kc / S_STAGES) & 1);
+                const bool ok = __all_sync(FULL, mbar_wait_bounded(&empty_bar[stage], phase ^ 1u));
+                if (!ok || __any_sync(FULL, s_abort != 0)) {
+                    if (lane == 0 && !ok) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                    stop = true;
+                    break;
+                }
+                const uint4 v = tile_ok ? __ldg(meta + ((long long)tm * nkb + kb) * 128 + q * 32 + lane)
+                                        : make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
+                tc_fence_after();
+                tmem_st4(tmem_base + ((uint32_t)(q * 32) << 16) + S_META_COL + 4 * stage, v);
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(meta_leader + 8u * (uint32_t)stage);
+            }
+        }
+    } else {
+        // ------------------------------------------------------ epilogue --
+        const int ew = warp & 3;          // lane quarter: accumulator rows 32*ew ..
+        const int wg = (warp - 11) >> 2;  // columns 128*wg ..
+        unsigned char* sbuf = smem + (size_t)S_STAGES * STAGE_BYTES + (size_t)(warp - 11) * 2048;
+        const uint32_t tempty_leader = leader_smem_addr(&tempty_bar);
+        const uint32_t lane_base = tmem_base + ((uint32_t)(ew * 32) << 16);
+        int it = 0;
+        for (int tile = first_tile; tile < ntiles; tile += tile_stride, ++it) {
+            int pm, tn;
+            raster(tile, tiles_mp, tiles_n, pm, tn);
+            const int tm = pm * G_CTAS + (int)rank;
+            const bool ok = __all_sync(FULL, mbar_wait_bounded(&tfull_bar, (uint32_t)it & 1u));
+            if (!ok || __any_sync(FULL, s_abort != 0)) {
+                if (lane == 0 && !ok) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            // accumulator -> bf16 in the spare columns, then free the accumulator
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32], w[16];
+                tmem_ld32(lane_base + (uint32_t)(wg * 128 + c * 32), r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int q2 = 0; q2 < 16; ++q2)
+                    w[q2] = pack_bf16x2(__uint_as_float(r[2 * q2]), __uint_as_float(r[2 * q2 + 1]));
+                tmem_st16(lane_base + (uint32_t)(S_PACK_COL + wg * 64 + c * 16), w);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty_leader);
+            if (tm < tiles_m && tn * 256 + wg * 128 < N) {
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[16];
+                    tmem_ld16(lane_base + (uint32_t)(S_PACK_COL + wg * 64 + c * 16), w);
+                    tmem_wait_ld();
+                    stage_store32(&tmC, sbuf, lane, w, tn * 256 + wg * 128 + c * 32, tm * G_BM + ew * 32);
+                }
+            }
+        }
+        if (lane == 0) bulk_wait_group0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    cluster_sync();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, 512);
+    }
+}
+
 // ------------------------------------------------------------------ host ----
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -742,6 +983,47 @@ GemmArgs base_args(long long M, long long N, long long K, void* out, long long l
     return a;
 }
 
+template <bool B_MN>
+int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K, const void* B, long long ldb,
+                void* C, long long ldc, long long N, uint32_t* status, cudaStream_t st) {
+    CUtensorMap ta, tb, tc;
+    if (!make_tmap(&ta, vals, K / 2, M, K / 2, 64, 128)) return SFFN_ERR_CUDA;
+    const bool okB = B_MN ? make_tmap(&tb, B, N, K, ldb, 64, 128) : make_tmap(&tb, B, K, N, ldb, 64, 128);
+    if (!okB) return SFFN_ERR_CUDA;
+    if (!make_tmap(&tc, C, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return SFFN_ERR_CUDA;
+    constexpr int smem = S_STAGES * (G_BM * (S_BK / 2) * 2 + 2 * 128 * 64 * 2) + 8 * 2048 + 1024;
+    auto k = gemm_sp24_kernel<B_MN>;
+    SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    static int cached[2] = {0, 0};
+    int& maxc = cached[B_MN ? 1 : 0];
+    if (!maxc) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(G_CTAS * 64);
+        cfg.blockDim = dim3(S_THREADS);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = G_CTAS;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (void*)k, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = g_num_sms() / G_CTAS;
+        }
+        maxc = n;
+    }
+    const long long tiles_m = M / G_BM, tiles_n = (N + 255) / 256;
+    const int npairs = (int)(((tiles_m + 1) / 2) * tiles_n);
+    const int clusters = std::min(npairs, maxc);
+    k<<<clusters * G_CTAS, S_THREADS, smem, st>>>(ta, tb, tc, reinterpret_cast<const uint4*>(meta), (int)M, (int)N,
+                                                  (int)K, status);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
 }  // namespace
 }  // namespace sffn
 
@@ -808,4 +1090,20 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
     a.colsum = db1_sum;
     a.status = status_dev;
     return dispatch<EPI_DGRAD>(false, true, dout, ld_dout, w2, ldw2, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M, int64_t K, const void* B,
+                              int64_t ldb, int b_mn, void* C, int64_t ldc, int64_t N, uint32_t* status_dev,
+                              void* stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || M % 128 || K % 128) return SFFN_ERR_UNSUPPORTED;
+    if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    if (!vals || !meta || !B || !C || !status_dev) return SFFN_ERR_ARG;
+    if (!aligned16(vals) || !aligned16(meta) || !aligned16(B) || !aligned16(C) || (ldb * 2) % 16 || (ldc * 2) % 16)
+        return SFFN_ERR_ALIGN;
+    if (ldb < (b_mn ? N : K) || ldc < N) return SFFN_ERR_ARG;
+    if (int rc = bind_device_of(vals)) return rc;
+    if (!device_is_sm100()) return SFFN_ERR_DEVICE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return b_mn ? launch_sp24<true>(vals, meta, M, K, B, ldb, C, ldc, N, status_dev, st)
+                : launch_sp24<false>(vals, meta, M, K, B, ldb, C, ldc, N, status_dev, st);
 }

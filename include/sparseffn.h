@@ -256,6 +256,36 @@ int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2, int64_t ld
                    void* dpre_out, void* act_out, int64_t ld_out, float* db1_sum, uint32_t* status_dev,
                    void* stream);
 
+/* ---- 2:4 structured form for the sparse tensor-core GEMMs -------------------
+ * No counterpart in the reference, whose products are dense cuBLAS matmuls
+ * (old/lib_sparse/sparse.py:75,95-100,118,136-139); the sparse path is
+ * checked end to end against dense products.  A [M, K] (M, K multiples of
+ * 128, K <= 65536) splits into its 2:4 part -- per group of 4 consecutive K
+ * elements the first two non-zeros: vals [M, K/2] bf16 and meta
+ * [M/128][K/128][128 lanes][4] uint32, index nibbles in tensor-memory lane
+ * order (lane dp = m0 + 8*k1 + 16*m2: K-half k1 of 32-wide step j, rows
+ * 16*m2+m0 in bits 0-15 and 16*m2+m0+8 in bits 16-31) -- and its overflow,
+ * the 3rd and 4th non-zero of a group, per row r at ovf_cols/ovf_vals
+ * [r*(K/2) ...], ovf_count[r] entries (in no fixed order). */
+
+/* Compress A (trans = 0: src is A [M][ld]; trans = 1: src is X [K][ld] and
+ * A = X^T) into the 2:4 form.  16-bit dtypes. */
+int sffn_sp24_compress(const void* src, int64_t ld, int trans, int64_t M, int64_t K, void* vals,
+                       uint32_t* meta, void* ovf_cols, void* ovf_vals, int32_t* ovf_count, void* stream);
+
+/* C[M, N] (bf16, row stride ldc) = A24 @ B for the 2:4 part of A, where B is
+ * [K, N]: b_mn = 1 for B stored [K][ldb] (N contiguous), 0 for B stored
+ * [N][ldb] (K contiguous).  bf16 in, fp32 accumulation. */
+int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M, int64_t K, const void* B, int64_t ldb,
+                   int b_mn, void* C, int64_t ldc, int64_t N, uint32_t* status_dev, void* stream);
+
+/* C[r, :] += sum over row r's overflow entries (k, v) of v * Bt[k, :]
+ * (Bt = B as [K][ldb] row-major, N <= 8192, N % 8 == 0), accumulated in fp32
+ * and rounded once to bf16. */
+int sffn_sp24_overflow_add(const void* ovf_cols, const void* ovf_vals, const int32_t* ovf_count, int64_t M,
+                           int64_t K, const void* bt, int64_t ldb, int64_t N, void* C, int64_t ldc,
+                           void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -260,3 +260,84 @@ def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.floa
     if b1 is not None:
         res["db1"] = dpre.sum(axis=0)
     return res
+
+
+# ------------------------------------------------------------------ 2:4 ----
+# The 2:4 structured form used by the library's sparse tensor-core GEMMs.  It
+# has no counterpart in the reference (whose products are dense cuBLAS
+# matmuls, old/lib_sparse/sparse.py:75,95-100,118,136-139); what must match
+# the reference is the product, checked end to end against dense products.
+# Here: A [M, K] (uint16 bf16 bits), K % 128 == 0, M % 128 == 0.
+#   vals [M, K/2]: per group of 4 (k = 4q..4q+3) the first two non-zero
+#     elements by position (non-zero: magnitude bits != 0); a group with
+#     fewer keeps zero slots so that idx0 < idx1 (one non-zero at p: p and 3,
+#     or 2 and 3 when p == 3; none: 0 and 1).
+#   nib [M, K/4]: idx0 | idx1 << 2.
+#   meta [M/128, K/128, 128 lanes, 4 words]: word j of lane
+#     dp = m0 + 8*k1 + 16*m2 holds the nibbles of K-half k1 (4 groups) of the
+#     j-th 32-wide K step for row 16*m2 + m0 (bits 0-15) and row
+#     16*m2 + m0 + 8 (bits 16-31), group g at bits 4g.
+#   overflow: the 3rd and 4th non-zero of each group, (row, col, value).
+def _sp24_lut():
+    k0 = np.zeros(16, np.int64)
+    k1 = np.zeros(16, np.int64)
+    ov = np.zeros(16, np.uint8)
+    for p in range(16):
+        idx = [i for i in range(4) if (p >> i) & 1]
+        keep = idx[:2]
+        if not keep:
+            keep = [0, 1]
+        elif len(keep) == 1:
+            keep = sorted([keep[0], 3 if keep[0] != 3 else 2])
+        k0[p], k1[p] = keep
+        for i in idx[2:]:
+            ov[p] |= 1 << i
+    return k0, k1, ov
+
+
+_SP24 = _sp24_lut()
+
+
+def sp24_compress(a_bits):
+    """-> (vals [M, K/2] uint16, nib [M, K/4] uint8, ovf_rows, ovf_cols, ovf_vals)
+    with the overflow in row-major order."""
+    a_bits = np.ascontiguousarray(a_bits, dtype=np.uint16)
+    M, K = a_bits.shape
+    g = a_bits.reshape(M, K // 4, 4)
+    nzm = (g & 0x7FFF) != 0
+    pat = (nzm * (1 << np.arange(4))).sum(-1)
+    k0, k1, ov = _SP24[0][pat], _SP24[1][pat], _SP24[2][pat]
+    v0 = np.take_along_axis(g, k0[..., None], -1)[..., 0]
+    v1 = np.take_along_axis(g, k1[..., None], -1)[..., 0]
+    v0 = np.where(np.take_along_axis(nzm, k0[..., None], -1)[..., 0], v0, 0)
+    v1 = np.where(np.take_along_axis(nzm, k1[..., None], -1)[..., 0], v1, 0)
+    vals = np.stack([v0, v1], -1).reshape(M, K // 2).astype(np.uint16)
+    nib = (k0 | (k1 << 2)).astype(np.uint8)
+    ovm = ((ov[..., None] >> np.arange(4)) & 1).astype(bool).reshape(M, K)
+    rows, cols = np.nonzero(ovm)
+    return vals, nib, rows, cols, a_bits[rows, cols]
+
+
+def sp24_meta(nib):
+    """nib [M, K/4] -> uint32 [M/128, K/128, 128, 4] in tensor-memory lane order."""
+    M, G = nib.shape
+    K = 4 * G
+    n = nib.astype(np.uint32).reshape(M // 128, 128, K // 128, 4, 2, 4)  # tm, row, kb, j, k1, g
+    half = (n << (4 * np.arange(4, dtype=np.uint32))).sum(-1, dtype=np.uint32)  # tm, row, kb, j, k1
+    r = half.reshape(M // 128, 8, 2, 8, K // 128, 4, 2)  # tm, m2, m1, m0, kb, j, k1
+    w = r[:, :, 0] | (r[:, :, 1] << 16)  # tm, m2, m0, kb, j, k1
+    w = w.transpose(0, 3, 1, 5, 2, 4)  # tm, kb, m2, k1, m0, j  -> lane = m0 + 8*k1 + 16*m2
+    return np.ascontiguousarray(w.reshape(M // 128, K // 128, 128, 4), dtype=np.uint32)
+
+
+def sp24_project(vals, nib):
+    """The dense [M, K] matrix (uint16 bits) that vals/nib represent."""
+    M, half = vals.shape
+    K = 2 * half
+    out = np.zeros((M, K // 4, 4), np.uint16)
+    v = vals.reshape(M, K // 4, 2)
+    i0 = (nib & 3).astype(np.int64)
+    i1 = (nib >> 2).astype(np.int64)
+    np.put_along_axis(out, i0[..., None], v[..., 0:1], -1)
+    np.put_along_axis(out, i1[..., None], v[..., 1:2], -1)
+    return out.reshape(M, K)

@@ -107,3 +107,22 @@ def test_ffn_matches_reference(act):
         dense = g[ref + "_dense"].astype(np.float64)
         np.testing.assert_allclose(r[key], dense, rtol=1e-5, atol=1e-5 * np.abs(dense).max())
     assert int(g["nnz"][0]) == int(r["mask"].sum())
+
+
+def test_sp24_oracle_split_is_lossless():
+    """2:4 part + overflow reproduce every non-zero of A (the split the sparse
+    tensor-core path relies on), and every kept pair has idx0 < idx1."""
+    rng = np.random.default_rng(4)
+    for p_zero in (0.0, 0.5, 0.9):
+        A = rng.standard_normal((256, 512)).astype(np.float32)
+        A[rng.random(A.shape) < p_zero] = 0
+        A_bits = oracle.f32_to_bf16(A)
+        vals, nib, rows, cols, ov = oracle.sp24_compress(A_bits)
+        full = oracle.sp24_project(vals, nib)
+        full[rows, cols] = ov
+        keep = (A_bits & 0x7FFF) != 0
+        assert np.array_equal(full[keep], A_bits[keep])
+        assert not np.any(full[~keep] & 0x7FFF)
+        assert np.all((nib & 3) < (nib >> 2))
+        meta = oracle.sp24_meta(nib)
+        assert meta.shape == (2, 4, 128, 4)
