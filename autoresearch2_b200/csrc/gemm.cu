@@ -594,36 +594,41 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
 // (compressed values [M, K/2] + tensor-memory-ordered metadata); B K-major
 // ([N][ldb]) or MN-major ([K][ldb]).  Pair tiles of 256 x 256 as in
 // gemm_kernel; a stage is 128 logical K (four tcgen05.mma.sp of K = 32):
-// 16 KB of compressed A + 32 KB of B per CTA, 4 stages.
-//   warps 0-5   TMA issuers, one per (operand copy A / B0 / B1, even / odd
-//               stage); the A issuers of the leader arm the stage barrier
-//   warp 6      MMA issuer (leader)
-//   warps 7-10  metadata: each copies its lane quarter's 16 bytes per stage
-//               from global memory into 4 tensor-memory columns (one per MMA)
-//   warps 11-18 epilogue: two warpgroups of 128 accumulator columns.  There is
+// 16 KB of compressed A + 32 KB of B + 2 KB of metadata per CTA, 4 stages.
+//   warps 0-7   TMA issuers, one per (copy A / B0 / B1 / metadata, even / odd
+//               stage), since one thread's copies complete one after another;
+//               the A issuers of the leader arm the stage barrier
+//   warp 8      MMA issuer (leader): per stage one tcgen05.cp moves the
+//               stage's metadata (128 lanes x 16 bytes, in each CTA) from
+//               shared into 4 tensor-memory columns, then four tcgen05.mma.sp
+//   warps 9-16  epilogue: two warpgroups of 128 accumulator columns.  There is
 //               one accumulator (256 columns) because the metadata ring needs
 //               tensor memory too; the epilogue frees it fast by converting
 //               each 32-column chunk to bf16 into spare tensor-memory columns,
 //               then stores from there while the next tile accumulates.
 constexpr int S_BK = 128;
 constexpr int S_STAGES = 4;
-constexpr int S_THREADS = 19 * 32;
+constexpr int S_THREADS = 17 * 32;
+constexpr int S_EPI0 = 9;  // first epilogue warp
 constexpr int S_META_COL = 256;  // metadata ring: 4 columns per stage
 constexpr int S_PACK_COL = 272;  // bf16 staging: 64 columns per warpgroup
 
 template <bool B_MN>
 __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
     gemm_sp24_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const __grid_constant__ CUtensorMap tmC, const uint4* __restrict__ meta, int M, int N, int K,
+                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmE, int M, int N,
+                     int K,
                      uint32_t* __restrict__ status) {
     constexpr int A_BYTES = G_BM * (S_BK / 2) * 2;  // 16 KB
     constexpr int B_HALF = 128 * 64 * 2;             // one 16 KB box
-    constexpr int STAGE_BYTES = A_BYTES + 2 * B_HALF;
+    constexpr int META_BYTES = 128 * 16;  // 2 KB
+    constexpr int TMA_BYTES = A_BYTES + 2 * B_HALF;
+    constexpr int STAGE_BYTES = TMA_BYTES + META_BYTES;  // all of it completes on the leader's full barrier
     constexpr uint32_t IDESC = idesc_bf16_f32(G_BM * G_CTAS, 256, false, B_MN) | (1u << 2);
     extern __shared__ __align__(1024) unsigned char g_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    __shared__ __align__(8) uint64_t full_bar[S_STAGES], empty_bar[S_STAGES], meta_bar[S_STAGES];
+    __shared__ __align__(8) uint64_t full_bar[S_STAGES], empty_bar[S_STAGES];
     __shared__ __align__(8) uint64_t tfull_bar, tempty_bar;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
@@ -642,7 +647,6 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
         for (int s = 0; s < S_STAGES; ++s) {
             mbar_init(&full_bar[s], 1);
             mbar_init(&empty_bar[s], 1);
-            mbar_init(&meta_bar[s], 4 * G_CTAS);  // the 4 metadata warps of both CTAs
         }
         mbar_init(&tfull_bar, 1);
         mbar_init(&tempty_bar, 8 * G_CTAS);  // the 8 epilogue warps of both CTAs
@@ -650,6 +654,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
         fence_mbar_init();
         prefetch_tmap(&tmA);
         prefetch_tmap(&tmB);
+        prefetch_tmap(&tmE);
     }
     if (warp == 0) {
         tmem_alloc_pair(&s_tmem, 512);
@@ -660,10 +665,10 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem_base = s_tmem;
 
-    if (warp < 6) {
+    if (warp < 8) {
         // ------------------------------------------------------ producers --
-        const int op = warp % 3;           // 0: A, 1: B (first half), 2: B (second half)
-        const int par = warp / 3;          // even / odd stages
+        const int op = warp & 3;   // 0: A, 1: B (first half), 2: B (second half), 3: metadata
+        const int par = warp >> 2;  // even / odd stages
         if (lane == 0) {
             int armed[S_STAGES] = {0};
             long long kc = 0;
@@ -691,6 +696,11 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
                             ++armed[stage];
                         }
                         tma_load_2d_pair(sa, &tmA, kb * (S_BK / 2), arow, &full_bar[stage]);
+                    } else if (op == 3) {
+                        // this CTA's 128-row tile; the empty half of an odd last pair
+                        // copies the previous tile's metadata (its A rows are zero)
+                        const int tm = min(pm * G_CTAS + (int)rank, tiles_m - 1);
+                        tma_load_2d_pair(sa + TMA_BYTES, &tmE, 0, ((tm * nkb) + kb) * 128, &full_bar[stage]);
                     } else {
                         const int h = op - 1;
                         if constexpr (!B_MN)  // [N][K]: K offsets 0 / 64 of the stage
@@ -705,7 +715,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
                     if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
         }
         __syncwarp();
-    } else if (warp == 6) {
+    } else if (warp == 8) {
         // ----------------------------------------------------------- MMA --
         if (lane == 0 && leader) {
             long long kc = 0;
@@ -721,16 +731,16 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
                 for (int kb = 0; kb < nkb; ++kb, ++kc) {
                     const int stage = (int)(kc % S_STAGES);
                     const uint32_t phase = (uint32_t)((kc / S_STAGES) & 1);
-                    if (!mbar_wait_bounded(&full_bar[stage], phase) || !mbar_wait_bounded(&meta_bar[stage], phase)) {
+                    if (!mbar_wait_bounded(&full_bar[stage], phase)) {
                         atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
                         s_abort = 1;
                         fail = true;
                         break;
                     }
-                    tc_fence_after();  // the metadata arrived by thread synchronisation
                     const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
                     const uint32_t sb = sa + A_BYTES;
                     const uint32_t e0 = tmem_base + S_META_COL + 4 * stage;
+                    tc_cp_pair_128x128b(e0, smem_desc_rows16(sa + TMA_BYTES));
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
                         const uint64_t ad = umma_desc_sw128(sa + 32 * j, 16, 1024);
@@ -746,41 +756,12 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
             }
         }
         __syncwarp();
-    } else if (warp < 11) {
-        // ------------------------------------------------------ metadata --
-        const int q = warp & 3;  // lane quarter
-        const uint32_t meta_leader = leader_smem_addr(&meta_bar[0]);
-        long long kc = 0;
-        bool stop = false;
-        for (int tile = first_tile; tile < ntiles && !stop; tile += tile_stride) {
-            int pm, tn;
-            raster(tile, tiles_mp, tiles_n, pm, tn);
-            const int tm = pm * G_CTAS + (int)rank;
-            const bool tile_ok = tm < tiles_m;
-            for (int kb = 0; kb < nkb; ++kb, ++kc) {
-                const int stage = (int)(kc % S_STAGES);
-                const uint32_t phase = (uint32_t)((kc / S_STAGES) & 1);
-                const bool ok = __all_sync(FULL, mbar_wait_bounded(&empty_bar[stage], phase ^ 1u));
-                if (!ok || __any_sync(FULL, s_abort != 0)) {
-                    if (lane == 0 && !ok) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
-                    stop = true;
-                    break;
-                }
-                const uint4 v = tile_ok ? __ldg(meta + ((long long)tm * nkb + kb) * 128 + q * 32 + lane)
-                                        : make_uint4(0x44444444u, 0x44444444u, 0x44444444u, 0x44444444u);
-                tc_fence_after();
-                tmem_st4(tmem_base + ((uint32_t)(q * 32) << 16) + S_META_COL + 4 * stage, v);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cluster(meta_leader + 8u * (uint32_t)stage);
-            }
-        }
+    } else if (warp < S_EPI0) {
     } else {
         // ------------------------------------------------------ epilogue --
         const int ew = warp & 3;          // lane quarter: accumulator rows 32*ew ..
-        const int wg = (warp - 11) >> 2;  // columns 128*wg ..
-        unsigned char* sbuf = smem + (size_t)S_STAGES * STAGE_BYTES + (size_t)(warp - 11) * 2048;
+        const int wg = (warp - S_EPI0) >> 2;  // columns 128*wg ..
+        unsigned char* sbuf = smem + (size_t)S_STAGES * STAGE_BYTES + (size_t)(warp - S_EPI0) * 2048;
         const uint32_t tempty_leader = leader_smem_addr(&tempty_bar);
         const uint32_t lane_base = tmem_base + ((uint32_t)(ew * 32) << 16);
         int it = 0;
@@ -991,7 +972,24 @@ int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K
     const bool okB = B_MN ? make_tmap(&tb, B, N, K, ldb, 64, 128) : make_tmap(&tb, B, K, N, ldb, 64, 128);
     if (!okB) return SFFN_ERR_CUDA;
     if (!make_tmap(&tc, C, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return SFFN_ERR_CUDA;
-    constexpr int smem = S_STAGES * (G_BM * (S_BK / 2) * 2 + 2 * 128 * 64 * 2) + 8 * 2048 + 1024;
+    // metadata: rows of 16 bytes (4 uint32), 128-row boxes, no swizzle
+    CUtensorMap te;
+    {
+        auto fn = encode_fn();
+        if (!fn) return SFFN_ERR_CUDA;
+        cuuint64_t dims[2] = {4, (cuuint64_t)((M / 128) * (K / 128) * 128)};
+        cuuint64_t strides[1] = {16};
+        cuuint32_t box[2] = {4, 128};
+        cuuint32_t estr[2] = {1, 1};
+        const CUresult r = fn(&te, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(meta), dims, strides,
+                              box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS) {
+            set_error_text("cuTensorMapEncodeTiled failed for the 2:4 metadata");
+            return SFFN_ERR_CUDA;
+        }
+    }
+    constexpr int smem = S_STAGES * (G_BM * (S_BK / 2) * 2 + 2 * 128 * 64 * 2 + 128 * 16) + 8 * 2048 + 1024;
     auto k = gemm_sp24_kernel<B_MN>;
     SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     static int cached[2] = {0, 0};
@@ -1018,8 +1016,7 @@ int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K
     const long long tiles_m = M / G_BM, tiles_n = (N + 255) / 256;
     const int npairs = (int)(((tiles_m + 1) / 2) * tiles_n);
     const int clusters = std::min(npairs, maxc);
-    k<<<clusters * G_CTAS, S_THREADS, smem, st>>>(ta, tb, tc, reinterpret_cast<const uint4*>(meta), (int)M, (int)N,
-                                                  (int)K, status);
+    k<<<clusters * G_CTAS, S_THREADS, smem, st>>>(ta, tb, tc, te, (int)M, (int)N, (int)K, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

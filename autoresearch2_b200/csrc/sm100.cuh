@@ -320,6 +320,18 @@ __device__ __forceinline__ void tc_mma_sp_pair(uint32_t d_tmem, uint64_t adesc, 
         "l"(adesc), "l"(bdesc), "r"(e_tmem), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// Pair copy shared -> tensor memory of a 128-row x 128-bit matrix, in each
+// CTA from its own shared memory into its own tensor memory (issued by the
+// leader; ordered before the tcgen05.mma the same thread issues after it).
+__device__ __forceinline__ void tc_cp_pair_128x128b(uint32_t taddr, uint64_t sdesc) {
+    asm volatile("tcgen05.cp.cta_group::2.128x128b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Descriptor of a no-swizzle shared-memory matrix of rows of 16 bytes stored
+// back to back (8-row core matrices 128 bytes apart; both strides 128 bytes).
+__device__ __forceinline__ uint64_t smem_desc_rows16(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(128 >> 4) << 32) |
+           (1ull << 46);
+}
 // Commit the leader's pair MMAs to the barrier at the same offset in every CTA of `mask`.
 __device__ __forceinline__ void tc_commit_pair_multicast(uint64_t* bar, uint16_t mask) {
     asm volatile(
