@@ -10,7 +10,7 @@ from .bitsparse import (BitsparseTensor, TensorBuffer, bitsparse_pack, bitsparse
                         init_sparse_buffer, mask_with_bitmask_, reset_sparse_globals, spAx,
                         tile_unpack)
 from .ffn import FFNSparse, FFNSpRelu2
-from . import parallel, tiled
+from . import ffn, parallel, sp24, tiled
 
 __all__ = [
     "BitsparseTensor", "TensorBuffer", "bitsparse_pack", "bitsparse_unpack", "check_status",

@@ -127,9 +127,11 @@ __global__ void __launch_bounds__(SP_TILE) sp24_compress_kernel(
 }
 
 // C[r, :] += sum over the overflow entries (k, v) of row r of v * Bt[k, :],
-// in fp32, then rounded once more to bf16.  One CTA of 128 threads per row;
-// thread t owns columns 8t + 1024*i (16-byte vectors).
-constexpr int OV_NT = 128;
+// in fp32, then rounded once more to bf16.  One CTA of 256 threads per row;
+// thread t owns the 16 columns 16t .. 16t+15 of each 4096-column block, and
+// four entries' loads are in flight at a time.
+constexpr int OV_NT = 256;
+constexpr int OV_COLS = OV_NT * 16;  // columns per block
 __global__ void __launch_bounds__(OV_NT) sp24_overflow_kernel(
     const uint16_t* __restrict__ ovf_cols, const uint16_t* __restrict__ ovf_vals,
     const int* __restrict__ ovf_count, long long ovf_ld, const uint16_t* __restrict__ bt, long long ldb,
@@ -138,49 +140,51 @@ __global__ void __launch_bounds__(OV_NT) sp24_overflow_kernel(
     const int n = ovf_count[r];
     if (n == 0) return;
     const int t = threadIdx.x;
-    constexpr int MAXV = 8;  // up to 8 vectors of 8 columns per thread: N <= 8192
-    float acc[MAXV][8];
-#pragma unroll
-    for (int i = 0; i < MAXV; ++i)
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[i][e] = 0.f;
     const uint16_t* oc = ovf_cols + r * ovf_ld;
     const uint16_t* ov = ovf_vals + r * ovf_ld;
-    for (int e = 0; e < n; ++e) {
-        const long long k = oc[e];
-        const float v = __uint_as_float((uint32_t)ov[e] << 16);
-        const uint16_t* brow = bt + k * ldb;
+    uint16_t* crow = C + r * ldc;
+    for (int c0 = 0; c0 < N; c0 += OV_COLS) {
+        const int col = c0 + 16 * t;
+        if (col >= N) break;  // N % 16 == 0: whole 16-column groups
+        float acc[16];
 #pragma unroll
-        for (int i = 0; i < MAXV; ++i) {
-            const int col = 8 * t + 1024 * i;
-            if (col < N) {
-                const uint4 q = __ldg(reinterpret_cast<const uint4*>(brow + col));
-                const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+        for (int e0 = 0; e0 < n; e0 += 4) {
+            uint4 q[4][2];
+            float v[4];
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    acc[i][2 * h] += v * __uint_as_float(w[h] << 16);
-                    acc[i][2 * h + 1] += v * __uint_as_float(w[h] & 0xFFFF0000u);
+            for (int u = 0; u < 4; ++u) {
+                const int e = min(e0 + u, n - 1);
+                v[u] = e0 + u < n ? __uint_as_float((uint32_t)__ldg(ov + e) << 16) : 0.f;
+                const uint4* brow = reinterpret_cast<const uint4*>(bt + (long long)__ldg(oc + e) * ldb + col);
+                q[u][0] = __ldg(brow);
+                q[u][1] = __ldg(brow + 1);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t w[8] = {q[u][0].x, q[u][0].y, q[u][0].z, q[u][0].w,
+                                       q[u][1].x, q[u][1].y, q[u][1].z, q[u][1].w};
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    acc[2 * h] += v[u] * __uint_as_float(w[h] << 16);
+                    acc[2 * h + 1] += v[u] * __uint_as_float(w[h] & 0xFFFF0000u);
                 }
             }
         }
-    }
-    uint16_t* crow = C + r * ldc;
+        uint4* p = reinterpret_cast<uint4*>(crow + col);
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-        const int col = 8 * t + 1024 * i;
-        if (col < N) {
-            uint4* p = reinterpret_cast<uint4*>(crow + col);
-            const uint4 q = *p;
-            const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+        for (int hv = 0; hv < 2; ++hv) {
+            const uint4 qc = p[hv];
+            const uint32_t w[4] = {qc.x, qc.y, qc.z, qc.w};
             uint32_t o[4];
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-                const float lo = __uint_as_float(w[h] << 16) + acc[i][2 * h];
-                const float hi = __uint_as_float(w[h] & 0xFFFF0000u) + acc[i][2 * h + 1];
+                const float lo = __uint_as_float(w[h] << 16) + acc[8 * hv + 2 * h];
+                const float hi = __uint_as_float(w[h] & 0xFFFF0000u) + acc[8 * hv + 2 * h + 1];
                 o[h] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
                        ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
             }
-            *p = make_uint4(o[0], o[1], o[2], o[3]);
+            p[hv] = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
 }
@@ -216,7 +220,7 @@ extern "C" int sffn_sp24_compress(const void* src, int64_t ld, int trans, int64_
 extern "C" int sffn_sp24_overflow_add(const void* ovf_cols, const void* ovf_vals, const int32_t* ovf_count,
                                       int64_t M, int64_t K, const void* bt, int64_t ldb, int64_t N, void* C,
                                       int64_t ldc, void* stream) {
-    if (M <= 0 || N <= 0 || K <= 0 || N > 8192 || N % 8) return SFFN_ERR_UNSUPPORTED;
+    if (M <= 0 || N <= 0 || K <= 0 || N % 16) return SFFN_ERR_UNSUPPORTED;
     if (!ovf_cols || !ovf_vals || !ovf_count || !bt || !C) return SFFN_ERR_ARG;
     if (!aligned16(bt) || !aligned16(C) || (ldb * 2) % 16 || (ldc * 2) % 16 || ldb < N || ldc < N)
         return SFFN_ERR_ALIGN;

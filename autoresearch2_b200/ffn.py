@@ -31,9 +31,34 @@ from torch.autograd import Function
 
 from . import bitsparse as bs
 from . import gemm as G
+from . import sp24
 from .parallel import submit_grad
 
-__all__ = ["FFNSparse", "FFNSpRelu2"]
+__all__ = ["FFNSparse", "FFNSpRelu2", "set_sparse_mma", "sparse_mma"]
+
+# The four products with a sparse operand -- forward a @ W2^T, backward
+# dpre @ W1, dpre^T @ x and a^T @ dout -- can run on the 2:4 sparse tensor
+# cores (sp24): the 2:4 part of the activation at twice the dense rate plus
+# its overflow on the CUDA cores.  "off": dense tcgen05 GEMMs; "on": sp24
+# whenever the shapes allow it (T and F multiples of 128, up to 65536).
+_SPARSE_MMA = "off"
+
+
+def set_sparse_mma(mode: str):
+    """Choose the products' path for the fused bf16 FFN: "off" or "on"."""
+    global _SPARSE_MMA
+    if mode not in ("off", "on"):
+        raise ValueError("sparse MMA mode is 'off' or 'on'")
+    _SPARSE_MMA = mode
+
+
+def sparse_mma() -> str:
+    return _SPARSE_MMA
+
+
+def _sp24_ok(T, D, Fd):
+    return (_SPARSE_MMA == "on" and T % 128 == 0 and Fd % 128 == 0 and D % 16 == 0 and T <= 65536
+            and Fd <= 65536)
 
 
 def _fused_ok(x, W1, W2, b1, vals):
@@ -53,9 +78,18 @@ def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     T, D = x.shape
     Fd = W1.shape[0]
     a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset)
-    kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
-    out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
-    del a
+    use_sp24 = _sp24_ok(T, D, Fd)
+    if use_sp24:
+        # 2:4 part on the sparse tensor cores, overflow rows k of W2^T
+        kb_list = kb_count = None
+        a24 = sp24.compress(a)
+        del a
+        out = sp24.mm(a24, W2.T, bt=W2.T.contiguous())
+        del a24
+    else:
+        kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
+        out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
+        del a
     z_sparse = bs.BitsparseTensor(vals, bitmask, prefix, voff, -(-T // 128), -(-Fd // 128), 128, 128,
                                   (T, Fd))
     ctx.save_for_backward(x, W1, W2)
@@ -64,6 +98,7 @@ def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     ctx.row_offsets = row_offsets
     ctx.has_bias = b1 is not None
     ctx.fused = True
+    ctx.sp24 = use_sp24
     return out
 
 
@@ -79,6 +114,15 @@ def _fused_backward(ctx, grad_output, act):
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1)
     ctx.row_offsets = None
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if ctx.has_bias else None
+    if ctx.sp24:
+        # dW2 = (a^T @ dout)^T: the sparse operand a^T is compressed along the
+        # token dimension; the reduction runs on the contiguous [F, D] product
+        gW2T = submit_grad(sp24.mm(sp24.compress(a, trans=True), grad_output))
+        grad_W2 = gW2T.T
+        del a
+        grad_x = sp24.mm(sp24.compress(dpre), W1)
+        grad_W1 = submit_grad(sp24.mm(sp24.compress(dpre, trans=True), x))
+        return grad_x, grad_W1, grad_W2, None, grad_b1
     grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)

@@ -280,7 +280,7 @@ int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M, int64_t K,
                    int b_mn, void* C, int64_t ldc, int64_t N, uint32_t* status_dev, void* stream);
 
 /* C[r, :] += sum over row r's overflow entries (k, v) of v * Bt[k, :]
- * (Bt = B as [K][ldb] row-major, N <= 8192, N % 8 == 0), accumulated in fp32
+ * (Bt = B as [K][ldb] row-major, N % 16 == 0), accumulated in fp32
  * and rounded once to bf16. */
 int sffn_sp24_overflow_add(const void* ovf_cols, const void* ovf_vals, const int32_t* ovf_count, int64_t M,
                            int64_t K, const void* bt, int64_t ldb, int64_t N, void* C, int64_t ldc,

@@ -49,11 +49,25 @@ def test_ffn_fp32_golden(act):
     assert int(off.item()) == int(g["nnz"][0])
 
 
+@pytest.mark.parametrize("mma", ["off", "on"])
 @pytest.mark.parametrize("act", ["relu", "relu2"])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("T,D,F", [(256, 128, 384), (512, 256, 1024)])
-def test_ffn_against_oracle(act, dtype, T, D, F):
+def test_ffn_against_oracle(act, dtype, T, D, F, mma):
+    """mma = "on": the bf16 products with a sparse operand run on the 2:4
+    sparse tensor cores (plus the overflow); the results must not change."""
     import autoresearch2_b200 as sf
+    if mma == "on" and dtype != torch.bfloat16:
+        pytest.skip("the sparse tensor-core path is bf16-only")
+    prev = sf.ffn.sparse_mma()
+    sf.ffn.set_sparse_mma(mma)
+    try:
+        _ffn_against_oracle(sf, act, dtype, T, D, F)
+    finally:
+        sf.ffn.set_sparse_mma(prev)
+
+
+def _ffn_against_oracle(sf, act, dtype, T, D, F):
     g = torch.Generator().manual_seed(T + D + F)
     x = torch.randn(T, D, generator=g)
     W1 = torch.randn(F, D, generator=g) / D ** 0.5
