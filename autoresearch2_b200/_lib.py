@@ -33,6 +33,12 @@ SIGNATURES = {
     "sffn_sp24_compress": (_int, [_vp, _i64, _int, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _vp]),
     "sffn_gemm_sp24": (_int, [_vp, _vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _i64, _vp, _vp]),
     "sffn_sp24_overflow_add": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp]),
+    "sffn_transpose16": (_int, [_vp, _i64, _i64, _i64, _vp, _i64, _vp]),
+    "sffn_sp24_mm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _vp, _i64, _int, _i64, _vp, _vp]),
+    "sffn_ffn_up_sp24": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp,
+                                _vp, _vp]),
+    "sffn_ffn_dgrad_sp24": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp, _vp,
+                                   _vp, _vp, _vp, _vp, _vp, _vp]),
     "sffn_version": (_int, []),
     "sffn_error_string": (ctypes.c_char_p, [_int]),
     "sffn_last_cuda_error": (ctypes.c_char_p, []),
@@ -82,6 +88,7 @@ def load():
 
 # Kernels of this library each entry point launches per call.
 LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_add": 1,
+             "sffn_ffn_up_sp24": 1, "sffn_ffn_dgrad_sp24": 1, "sffn_sp24_mm": 1, "sffn_transpose16": 1,
              "sffn_flat_pack": 1, "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,

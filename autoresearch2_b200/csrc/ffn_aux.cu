@@ -183,10 +183,66 @@ __global__ void __launch_bounds__(LIVE_WARPS * 32) live_kblocks_kernel(const uin
     if (lane == 0) kb_count[tp] = n;
 }
 
+// dst[c][r] = src[r][c] for 16-bit elements: a 64 x 64 tile per CTA, read
+// and written in 16-byte rows through shared memory padded to 66 elements a
+// row (column reads of 2-byte elements then fall in distinct banks).
+constexpr int TR_T = 64;
+constexpr int TR_LD = TR_T + 2;
+__global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t* __restrict__ src, long long ld_src,
+                                                          int rows, int cols, uint16_t* __restrict__ dst,
+                                                          long long ld_dst) {
+    __shared__ uint16_t tile[TR_T][TR_LD];
+    const int r0 = blockIdx.y * TR_T, c0 = blockIdx.x * TR_T;
+    const int t = threadIdx.x;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int idx = t + 256 * i;  // 512 16-byte pieces: 64 rows x 8
+        const int rr = idx >> 3, cc = (idx & 7) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r0 + rr < rows && c0 + cc < cols)  // cols % 8 == 0: whole pieces
+            v = __ldg(reinterpret_cast<const uint4*>(src + (long long)(r0 + rr) * ld_src + c0 + cc));
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            tile[rr][cc + 2 * h] = (uint16_t)w[h];
+            tile[rr][cc + 2 * h + 1] = (uint16_t)(w[h] >> 16);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int idx = t + 256 * i;  // 64 output rows (source columns) x 8 pieces
+        const int oc = idx >> 3, orr = (idx & 7) * 8;
+        if (c0 + oc < cols && r0 + orr < rows) {  // rows % 8 == 0
+            uint32_t w[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h)
+                w[h] = (uint32_t)tile[orr + 2 * h][oc] | ((uint32_t)tile[orr + 2 * h + 1][oc] << 16);
+            *reinterpret_cast<uint4*>(dst + (long long)(c0 + oc) * ld_dst + r0 + orr) =
+                make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    }
+}
+
 }  // namespace
 }  // namespace sffn
 
 using namespace sffn;
+
+extern "C" int sffn_transpose16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst,
+                                int64_t ld_dst, void* stream) {
+    if (rows < 0 || cols < 0 || rows % 8 || cols % 8) return SFFN_ERR_ARG;
+    if (rows == 0 || cols == 0) return SFFN_OK;
+    if (!src || !dst || ld_src < cols || ld_dst < rows) return SFFN_ERR_ARG;
+    if ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) % 16 || ld_src % 8 || ld_dst % 8)
+        return SFFN_ERR_ALIGN;
+    if (rows / TR_T + 1 > 65535) return SFFN_ERR_ARG;
+    const dim3 grid((unsigned)((cols + TR_T - 1) / TR_T), (unsigned)((rows + TR_T - 1) / TR_T));
+    transpose16_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(src), ld_src, (int)rows, (int)cols, static_cast<uint16_t*>(dst), ld_dst);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
 
 extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int64_t ntiles, int32_t* prefix,
                                      int32_t* offset_dev, int32_t* vals_offset_dev, uint32_t* status_dev,

@@ -56,6 +56,7 @@
 
 #include "common.cuh"
 #include "sm100.cuh"
+#include "sp24.cuh"
 
 namespace sffn {
 namespace {
@@ -72,6 +73,17 @@ constexpr int FT_ELEMS = FT * FT;
 
 enum { EPI_STORE = 0, EPI_UP = 1, EPI_DGRAD = 2 };
 enum { ACT_RELU = 0, ACT_RELU2 = 1 };
+
+// One matrix written in the 2:4 form of sp24.cu by a fused epilogue.
+struct Sp24Out {
+    uint16_t* vals;   // [rows][vals_ld] kept values
+    uint32_t* meta;   // [rows/128][nkb][128 lanes][4]
+    uint16_t* ocols;  // [rows][vals_ld] overflow columns
+    uint16_t* ovals;  //                 and values
+    int* ocount;      // [rows]
+    long long vals_ld;  // K/2 of the matrix
+    int nkb;            // K/128
+};
 
 struct GemmArgs {
     int M, N, K;
@@ -93,6 +105,8 @@ struct GemmArgs {
     const int* row_offsets;  // DGRAD: [num_tiles][128] prefix[t] + in-tile row prefix
     const int* vals_offset;
     float* colsum;  // DGRAD: optional fp32 [N] += column sums of dpre
+    int sp_on;      // UP: a, DGRAD: dpre, dpre^T and a^T in 2:4 form instead of dense
+    Sp24Out sp[3];  // UP: [0] a; DGRAD: [0] dpre, [1] dpre^T, [2] a^T
     uint32_t* status;
 };
 
@@ -153,6 +167,68 @@ __device__ __forceinline__ void stage_store32(const CUtensorMap* tmap, unsigned 
         tma_store_2d(tmap, sbuf, col, row0);
         bulk_commit_group();
     }
+}
+
+// The warp's 32 x 32 block (lane = row) into its staging buffer, same layout
+// as stage_store32, without a store to global memory.
+__device__ __forceinline__ void stage_words(unsigned char* sbuf, int lane, const uint32_t (&w)[16]) {
+    const uint32_t rb = smem_u32(sbuf) + (uint32_t)lane * 64u;
+    const int sw = (lane >> 1) & 3;
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + 16u * (uint32_t)(ch ^ sw)),
+                     "r"(w[4 * ch]), "r"(w[4 * ch + 1]), "r"(w[4 * ch + 2]), "r"(w[4 * ch + 3])
+                     : "memory");
+}
+// Column `lane` of the staged block (rows 0..31, two per word) and its sum.
+__device__ __forceinline__ void staged_column(const unsigned char* sbuf, int lane, uint32_t (&wt)[16], float& sum) {
+    const uint32_t sb0 = smem_u32(sbuf);
+    const int ch = lane >> 3, sub = (lane & 7) * 2;
+    sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 16; ++q) {
+        uint16_t h0, h1;
+        const int r0 = 2 * q, r1 = 2 * q + 1;
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h0) : "r"(sb0 + (uint32_t)(r0 * 64 + 16 * (ch ^ ((r0 >> 1) & 3)) + sub)));
+        asm volatile("ld.shared.u16 %0, [%1];" : "=h"(h1) : "r"(sb0 + (uint32_t)(r1 * 64 + 16 * (ch ^ ((r1 >> 1) & 3)) + sub)));
+        wt[q] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+        sum += bf16_to_f(h0) + bf16_to_f(h1);
+    }
+}
+// Element e of row r of a block staged by stage_words.
+__device__ __forceinline__ uint32_t staged_elem(const unsigned char* sbuf, int r, int e) {
+    uint16_t h;
+    asm volatile("ld.shared.u16 %0, [%1];"
+                 : "=h"(h)
+                 : "r"(smem_u32(sbuf) + (uint32_t)(r * 64 + 16 * ((e >> 3) ^ ((r >> 1) & 3)) + 2 * (e & 7))));
+    return h;
+}
+// 2:4 form of row `row` (elements k0 .. k0+31 in w) of a matrix: kept values
+// and overflow to global memory; returns the tensor-memory-order metadata
+// word of this lane (warp-collective: every lane calls it).  The overflow
+// values, rare, are read back by val(e) from the staged block rather than
+// from w, which a rolled loop could only index through local memory.
+template <typename ValFn>
+__device__ __forceinline__ uint32_t sp24_emit(const Sp24Out& o, const uint32_t (&w)[16], long long row, int k0,
+                                              int lane, ValFn&& val) {
+    uint32_t cw[8], nib, ov;
+    sp24_chunk(w, cw, nib, ov);
+    uint4* dst = reinterpret_cast<uint4*>(o.vals + row * o.vals_ld + k0 / 2);
+    dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+    dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+    if (ov) {
+        int pos = atomicAdd(o.ocount + row, __popc(ov));
+        const long long base = row * o.vals_ld;
+#pragma unroll 1
+        while (ov) {
+            const int e = __ffs(ov) - 1;
+            ov &= ov - 1u;
+            o.ocols[base + pos] = (uint16_t)(k0 + e);
+            o.ovals[base + pos] = (uint16_t)val(e);
+            ++pos;
+        }
+    }
+    return sp24_lane_word(nib, lane);
 }
 
 // 128-thread exclusive scan of one count per epilogue thread (ew = warp 0..3).
@@ -421,6 +497,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     // this row's z values go to its own 128-element segment of the slot
                     uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;
                     uint32_t words[4];
+                    uint32_t mw[4] = {0, 0, 0, 0};  // 2:4 metadata words (sp_on)
                     int cnt = 0;
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
@@ -455,7 +532,11 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             w[q] = args.act == ACT_RELU2 ? bf162_bits(__hmul2(zb, zb)) : z;
                         }
                         bits &= colmask;
-                        if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                        if (args.sp_on) {
+                            stage_words(sbuf, lane, w);  // own row: read back by this lane only
+                            mw[c] = sp24_emit(args.sp[0], w, grow, gcol, lane,
+                                              [&](int e) { return staged_elem(sbuf, lane, e); });
+                        } else if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
                         else if (row_ok) store_row32(orow, gcol, args.N, false, w);
                         // this chunk's z values, in column order, to the row's slot segment
 #pragma unroll
@@ -470,6 +551,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     }
                     *reinterpret_cast<uint4*>(args.mask + tf * FT_BYTES + row * 16) =
                         make_uint4(words[0], words[1], words[2], words[3]);
+                    if (args.sp_on)  // the 128 columns are one K block of the 2:4 form
+                        reinterpret_cast<uint4*>(args.sp[0].meta)[((long long)tm * args.sp[0].nkb + gcol0 / 128) * 128 +
+                                                                  ew * 32 + lane] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
                     // per-warp partial count of the tile (summed by the scan kernel)
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
@@ -485,10 +569,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         mw = __ldg(reinterpret_cast<const uint4*>(args.mask + tf * FT_BYTES + row * 16));
                         vbase = (long long)*args.vals_offset + __ldg(args.row_offsets + tf * FT + row);
                     }
-                    const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const uint32_t bits = words[c];
+                    // chunk c (columns gcol0 + 32c ..): dpre and the activation, from
+                    // the accumulator and z gathered from the packed values
+                    auto chunk = [&](int c, uint32_t bits, uint32_t (&wd)[16], uint32_t (&wa)[16]) {
                         // gather this chunk's z first: read-only loads, free to run ahead
                         uint32_t zb[16];
 #pragma unroll
@@ -508,7 +591,6 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         uint32_t r[32];
                         tmem_ld32(tbase + c * 32, r);
                         tmem_wait_ld();
-                        uint32_t wd[16], wa[16];
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             // g = bf16(acc); z from the packed values (0 off the mask)
@@ -527,40 +609,87 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                 wa[q] = zb[q];
                             }
                         }
-                        if (vec) {
-                            stage_store32(&tmC, sbuf, lane, wd, gcol0 + c * 32, row0);
-                            if (args.colsum) {
-                                // lane = column: sum the staged dpre block over its rows
-                                // (rows past M hold zeros); conflict-free swizzled reads
-                                const uint32_t sb0 = smem_u32(sbuf);
-                                const int ch = lane >> 3, sub = (lane & 7) * 2;
-                                float acc = 0.f;
+                    };
+                    if (args.sp_on) {
+                        // dpre by rows (for dX), dpre^T and a^T by columns (for dW1,
+                        // dW2): the block's column `lane` is row f = gcol0 + 32c + lane
+                        // of the transposed matrices, 32 consecutive tokens of its K.
+                        // A rolled loop: the three compressions per chunk would not
+                        // fit the instruction cache four times over.
+                        uint32_t spw0 = 0, spw1 = 0, spw2 = 0, spw3 = 0;
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            const uint32_t bits = c == 0 ? mw.x : c == 1 ? mw.y : c == 2 ? mw.z : mw.w;
+                            uint32_t wd[16], wa[16];
+                            chunk(c, bits, wd, wa);
+                            auto own = [&](int e) { return staged_elem(sbuf, lane, e); };
+                            auto col = [&](int e) { return staged_elem(sbuf, e, lane); };
+                            stage_words(sbuf, lane, wd);
+                            const uint32_t lw = sp24_emit(args.sp[0], wd, grow, gcol0 + c * 32, lane, own);
+                            spw0 = c == 0 ? lw : spw0;
+                            spw1 = c == 1 ? lw : spw1;
+                            spw2 = c == 2 ? lw : spw2;
+                            spw3 = c == 3 ? lw : spw3;
+                            const long long f = gcol0 + c * 32 + lane;
+                            const long long tmeta =
+                                ((long long)(gcol0 / 128) * args.sp[1].nkb + tm) * 128 + c * 32 + lane;
+                            const int tk0 = tm * G_BM + ew * 32;
+                            uint32_t wt[16];
+                            float csum;
+                            __syncwarp();
+                            staged_column(sbuf, lane, wt, csum);
+                            if (args.colsum) atomicAdd(args.colsum + f, csum);
+                            args.sp[1].meta[tmeta * 4 + ew] = sp24_emit(args.sp[1], wt, f, tk0, lane, col);
+                            __syncwarp();
+                            stage_words(sbuf, lane, wa);
+                            __syncwarp();
+                            staged_column(sbuf, lane, wt, csum);
+                            args.sp[2].meta[tmeta * 4 + ew] = sp24_emit(args.sp[2], wt, f, tk0, lane, col);
+                            __syncwarp();
+                        }
+                        reinterpret_cast<uint4*>(args.sp[0].meta)[((long long)tm * args.sp[0].nkb + gcol0 / 128) * 128 +
+                                                                  ew * 32 + lane] = make_uint4(spw0, spw1, spw2, spw3);
+                    } else {
+                        const uint32_t words[4] = {mw.x, mw.y, mw.z, mw.w};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t wd[16], wa[16];
+                            chunk(c, words[c], wd, wa);
+                            if (vec) {
+                                stage_store32(&tmC, sbuf, lane, wd, gcol0 + c * 32, row0);
+                                if (args.colsum) {
+                                    // lane = column: sum the staged dpre block over its rows
+                                    // (rows past M hold zeros); conflict-free swizzled reads
+                                    const uint32_t sb0 = smem_u32(sbuf);
+                                    const int ch = lane >> 3, sub = (lane & 7) * 2;
+                                    float acc = 0.f;
 #pragma unroll 8
-                                for (int rr = 0; rr < 32; ++rr) {
-                                    uint16_t h;
-                                    asm volatile("ld.shared.u16 %0, [%1];"
-                                                 : "=h"(h)
-                                                 : "r"(sb0 + (uint32_t)(rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)) + sub)));
-                                    acc += bf16_to_f(h);
+                                    for (int rr = 0; rr < 32; ++rr) {
+                                        uint16_t h;
+                                        asm volatile("ld.shared.u16 %0, [%1];"
+                                                     : "=h"(h)
+                                                     : "r"(sb0 + (uint32_t)(rr * 64 + 16 * (ch ^ ((rr >> 1) & 3)) + sub)));
+                                        acc += bf16_to_f(h);
+                                    }
+                                    const int col = gcol0 + c * 32 + lane;
+                                    if (col < args.N) atomicAdd(args.colsum + col, acc);
                                 }
-                                const int col = gcol0 + c * 32 + lane;
-                                if (col < args.N) atomicAdd(args.colsum + col, acc);
-                            }
-                            stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
-                        } else {
-                            if (row_ok) {
-                                store_row32(orow, gcol0 + c * 32, args.N, false, wd);
-                                store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
-                            }
-                            if (args.colsum) {
-                                // column sums by shuffles (rows past M contribute zeros)
+                                stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
+                            } else {
+                                if (row_ok) {
+                                    store_row32(orow, gcol0 + c * 32, args.N, false, wd);
+                                    store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
+                                }
+                                if (args.colsum) {
+                                    // column sums by shuffles (rows past M contribute zeros)
 #pragma unroll
-                                for (int j = 0; j < 32; ++j) {
-                                    float v = row_ok ? bf16_to_f((uint16_t)(wd[j >> 1] >> (16 * (j & 1)))) : 0.f;
+                                    for (int j = 0; j < 32; ++j) {
+                                        float v = row_ok ? bf16_to_f((uint16_t)(wd[j >> 1] >> (16 * (j & 1)))) : 0.f;
 #pragma unroll
-                                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
-                                    const int col = gcol0 + c * 32 + j;
-                                    if (lane == 0 && col < args.N) atomicAdd(args.colsum + col, v);
+                                        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+                                        const int col = gcol0 + c * 32 + j;
+                                        if (lane == 0 && col < args.N) atomicAdd(args.colsum + col, v);
+                                    }
                                 }
                             }
                         }
@@ -613,12 +742,23 @@ constexpr int S_EPI0 = 9;  // first epilogue warp
 constexpr int S_META_COL = 256;  // metadata ring: 4 columns per stage
 constexpr int S_PACK_COL = 272;  // bf16 staging: 64 columns per warpgroup
 
+// The 2:4 GEMM's store phase: the overflow of A added in fp32 (rows of B
+// read from bt, B as row-major [K][ldbt]) and C stored as is or transposed.
+struct Sp24Epi {
+    const uint16_t* ocols;  // NULL: no overflow to add
+    const uint16_t* ovals;
+    const int* ocount;
+    long long ovf_ld;  // K/2
+    const uint16_t* bt;
+    long long ldbt;
+    int c_trans;  // store C^T ([N][ldc]) instead of C
+};
+
 template <bool B_MN>
 __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
     gemm_sp24_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmE, int M, int N,
-                     int K,
-                     uint32_t* __restrict__ status) {
+                     int K, const Sp24Epi epi, uint32_t* __restrict__ status) {
     constexpr int A_BYTES = G_BM * (S_BK / 2) * 2;  // 16 KB
     constexpr int B_HALF = 128 * 64 * 2;             // one 16 KB box
     constexpr int META_BYTES = 128 * 16;  // 2 KB
@@ -791,12 +931,88 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(tempty_leader);
             if (tm < tiles_m && tn * 256 + wg * 128 < N) {
+                const long long grow = (long long)tm * G_BM + ew * 32 + lane;
+                const int novf = epi.ocols ? min(max(__ldg(epi.ocount + grow), 0), (int)epi.ovf_ld) : 0;
+                const bool any_ovf = __any_sync(FULL, novf > 0);  // warp-uniform
+                const uint16_t* ocol = epi.ocols + grow * epi.ovf_ld;
+                const uint16_t* oval = epi.ovals + grow * epi.ovf_ld;
 #pragma unroll 1
                 for (int c = 0; c < 4; ++c) {
+                    const int col0 = tn * 256 + wg * 128 + c * 32;
+                    if (col0 >= N) break;  // uniform; N is a multiple of 32 with overflow
                     uint32_t w[16];
-                    tmem_ld16(lane_base + (uint32_t)(S_PACK_COL + wg * 64 + c * 16), w);
-                    tmem_wait_ld();
-                    stage_store32(&tmC, sbuf, lane, w, tn * 256 + wg * 128 + c * 32, tm * G_BM + ew * 32);
+                    if (any_ovf) {
+                        // this row's overflow entries (k, v): C[row, col0 ..] += v * B[k, col0 ..],
+                        // summed from zero in entry order, then added to the bf16 C (as
+                        // sffn_sp24_overflow_add does).  Two entries' rows of B in flight,
+                        // the next pair's (k, v) fetched alongside them.
+                        // (per-lane loop: no warp-collective instruction inside)
+                        float acc[32];
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+                        int k0 = novf > 0 ? __ldg(ocol) : 0, k1 = novf > 1 ? __ldg(ocol + 1) : k0;
+                        float v0 = novf > 0 ? bf16_to_f(__ldg(oval)) : 0.f;
+                        float v1 = novf > 1 ? bf16_to_f(__ldg(oval + 1)) : 0.f;
+#pragma unroll 1
+                        for (int i = 0; i < novf; i += 2) {
+                            const uint4* r0 = reinterpret_cast<const uint4*>(epi.bt + (long long)k0 * epi.ldbt + col0);
+                            const uint4* r1 = reinterpret_cast<const uint4*>(epi.bt + (long long)k1 * epi.ldbt + col0);
+                            uint4 b0[4], b1[4];
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                b0[u] = __ldg(r0 + u);
+                                b1[u] = __ldg(r1 + u);
+                            }
+                            const float cv0 = v0, cv1 = v1;
+                            if (i + 2 < novf) {
+                                k0 = __ldg(ocol + i + 2);
+                                v0 = bf16_to_f(__ldg(oval + i + 2));
+                                k1 = i + 3 < novf ? __ldg(ocol + i + 3) : k0;
+                                v1 = i + 3 < novf ? bf16_to_f(__ldg(oval + i + 3)) : 0.f;
+                            }
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const uint32_t bw0[4] = {b0[u].x, b0[u].y, b0[u].z, b0[u].w};
+                                const uint32_t bw1[4] = {b1[u].x, b1[u].y, b1[u].z, b1[u].w};
+#pragma unroll
+                                for (int h = 0; h < 4; ++h) {
+                                    float& lo = acc[8 * u + 2 * h];
+                                    float& hi = acc[8 * u + 2 * h + 1];
+                                    lo = fmaf(cv0, __uint_as_float(bw0[h] << 16), lo);
+                                    hi = fmaf(cv0, __uint_as_float(bw0[h] & 0xFFFF0000u), hi);
+                                    lo = fmaf(cv1, __uint_as_float(bw1[h] << 16), lo);
+                                    hi = fmaf(cv1, __uint_as_float(bw1[h] & 0xFFFF0000u), hi);
+                                }
+                            }
+                        }
+                        // the bf16 C chunk only now, to keep the loop's registers free
+                        // (tcgen05.ld is warp-collective: every lane gets here)
+                        __syncwarp();
+                        tmem_ld16(lane_base + (uint32_t)(S_PACK_COL + wg * 64 + c * 16), w);
+                        tmem_wait_ld();
+                        if (novf > 0)  // rows without overflow stay as they are (signed zeros too)
+#pragma unroll
+                            for (int q = 0; q < 16; ++q)
+                                w[q] = pack_bf16x2(__uint_as_float(w[q] << 16) + acc[2 * q],
+                                                   __uint_as_float(w[q] & 0xFFFF0000u) + acc[2 * q + 1]);
+                    } else {
+                        tmem_ld16(lane_base + (uint32_t)(S_PACK_COL + wg * 64 + c * 16), w);
+                        tmem_wait_ld();
+                    }
+                    if (!epi.c_trans) {
+                        stage_store32(&tmC, sbuf, lane, w, col0, tm * G_BM + ew * 32);
+                    } else {
+                        // transpose through the staging buffer: lane takes column `lane`
+                        // of the block, row col0 + lane of C^T
+                        if (lane == 0) bulk_wait_group_read0();
+                        __syncwarp();
+                        stage_words(sbuf, lane, w);
+                        __syncwarp();
+                        uint32_t wt[16];
+                        float unused;
+                        staged_column(sbuf, lane, wt, unused);
+                        stage_store32(&tmC, sbuf, lane, wt, tm * G_BM + ew * 32, col0);
+                    }
                 }
             }
         }
@@ -966,12 +1182,14 @@ GemmArgs base_args(long long M, long long N, long long K, void* out, long long l
 
 template <bool B_MN>
 int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K, const void* B, long long ldb,
-                void* C, long long ldc, long long N, uint32_t* status, cudaStream_t st) {
+                void* C, long long ldc, long long N, const Sp24Epi& epi, uint32_t* status, cudaStream_t st) {
     CUtensorMap ta, tb, tc;
     if (!make_tmap(&ta, vals, K / 2, M, K / 2, 64, 128)) return SFFN_ERR_CUDA;
     const bool okB = B_MN ? make_tmap(&tb, B, N, K, ldb, 64, 128) : make_tmap(&tb, B, K, N, ldb, 64, 128);
     if (!okB) return SFFN_ERR_CUDA;
-    if (!make_tmap(&tc, C, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)) return SFFN_ERR_CUDA;
+    const bool okC = epi.c_trans ? make_tmap(&tc, C, M, N, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                                 : make_tmap(&tc, C, N, M, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (!okC) return SFFN_ERR_CUDA;
     // metadata: rows of 16 bytes (4 uint32), 128-row boxes, no swizzle
     CUtensorMap te;
     {
@@ -1016,7 +1234,7 @@ int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K
     const long long tiles_m = M / G_BM, tiles_n = (N + 255) / 256;
     const int npairs = (int)(((tiles_m + 1) / 2) * tiles_n);
     const int clusters = std::min(npairs, maxc);
-    k<<<clusters * G_CTAS, S_THREADS, smem, st>>>(ta, tb, tc, te, (int)M, (int)N, (int)K, status);
+    k<<<clusters * G_CTAS, S_THREADS, smem, st>>>(ta, tb, tc, te, (int)M, (int)N, (int)K, epi, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -1089,6 +1307,80 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
     return dispatch<EPI_DGRAD>(false, true, dout, ld_dout, w2, ldw2, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// The host description of one 2:4 output, checked; rows x K of the matrix.
+int sp24_out(const sffn_sp24_mat* m, long long rows, long long K, Sp24Out& o, cudaStream_t st) {
+    if (!m || !m->vals || !m->meta || !m->ovf_cols || !m->ovf_vals || !m->ovf_count) return SFFN_ERR_ARG;
+    if (!aligned16(m->vals) || !aligned16(m->meta)) return SFFN_ERR_ALIGN;
+    o.vals = static_cast<uint16_t*>(m->vals);
+    o.meta = m->meta;
+    o.ocols = static_cast<uint16_t*>(m->ovf_cols);
+    o.ovals = static_cast<uint16_t*>(m->ovf_vals);
+    o.ocount = m->ovf_count;
+    o.vals_ld = K / 2;
+    o.nkb = (int)(K / 128);
+    return cudaMemsetAsync(m->ovf_count, 0, (size_t)rows * sizeof(int32_t), st) == cudaSuccess ? SFFN_OK
+                                                                                               : SFFN_ERR_CUDA;
+}
+bool sp24_dims_ok(long long T, long long F) {
+    return T % 128 == 0 && F % 128 == 0 && T <= 65536 && F <= 65536;
+}
+}  // namespace
+
+extern "C" int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
+                                int64_t T, int64_t D, int64_t F, int act, const sffn_sp24_mat* out,
+                                uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
+                                void* stream) {
+    int rc = check_operands(x, ldx, false, w1, ldw1, false, T, F, D);
+    if (rc) return rc;
+    if (!sp24_dims_ok(T, F)) return SFFN_ERR_UNSUPPORTED;
+    if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
+    if (!bitmask || !tile_counts || !slots || !status_dev) return SFFN_ERR_ARG;
+    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    GemmArgs a = base_args(T, F, D, nullptr, F);
+    a.vec_out = 0;
+    a.sp_on = 1;
+    if ((rc = sp24_out(out, T, F, a.sp[0], st))) return rc;
+    a.act = act;
+    a.bias = static_cast<const uint16_t*>(b1);
+    a.mask = bitmask;
+    a.tile_counts = tile_counts;
+    a.slots = static_cast<uint16_t*>(slots);
+    a.status = status_dev;
+    return dispatch<EPI_UP>(false, false, x, ldx, w1, ldw1, a, st);
+}
+
+extern "C" int sffn_ffn_dgrad_sp24(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2, int64_t T,
+                                   int64_t D, int64_t F, int act, const void* vals, int64_t vals_len,
+                                   const uint8_t* bitmask, const int32_t* row_offsets,
+                                   const int32_t* vals_offset_dev, const sffn_sp24_mat* dpre,
+                                   const sffn_sp24_mat* dpre_t, const sffn_sp24_mat* act_t, float* db1_sum,
+                                   uint32_t* status_dev, void* stream) {
+    int rc = check_operands(dout, ld_dout, false, w2, ldw2, true, T, F, D);
+    if (rc) return rc;
+    if (!sp24_dims_ok(T, F)) return SFFN_ERR_UNSUPPORTED;
+    if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
+    if (!vals || !bitmask || !row_offsets || !vals_offset_dev || !status_dev) return SFFN_ERR_ARG;
+    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    GemmArgs a = base_args(T, F, D, nullptr, F);
+    a.vec_out = 0;
+    a.sp_on = 1;
+    if ((rc = sp24_out(dpre, T, F, a.sp[0], st)) || (rc = sp24_out(dpre_t, F, T, a.sp[1], st)) ||
+        (rc = sp24_out(act_t, F, T, a.sp[2], st)))
+        return rc;
+    a.act = act;
+    a.mask = const_cast<uint8_t*>(bitmask);
+    a.vals = static_cast<const uint16_t*>(vals);
+    a.vals_len = vals_len;
+    a.row_offsets = row_offsets;
+    a.vals_offset = vals_offset_dev;
+    a.colsum = db1_sum;
+    a.status = status_dev;
+    return dispatch<EPI_DGRAD>(false, true, dout, ld_dout, w2, ldw2, a, st);
+}
+
 extern "C" int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M, int64_t K, const void* B,
                               int64_t ldb, int b_mn, void* C, int64_t ldc, int64_t N, uint32_t* status_dev,
                               void* stream) {
@@ -1101,6 +1393,34 @@ extern "C" int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M,
     if (int rc = bind_device_of(vals)) return rc;
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    return b_mn ? launch_sp24<true>(vals, meta, M, K, B, ldb, C, ldc, N, status_dev, st)
-                : launch_sp24<false>(vals, meta, M, K, B, ldb, C, ldc, N, status_dev, st);
+    Sp24Epi epi{};
+    return b_mn ? launch_sp24<true>(vals, meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st)
+                : launch_sp24<false>(vals, meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st);
+}
+
+extern "C" int sffn_sp24_mm(const sffn_sp24_mat* a, int64_t M, int64_t K, const void* B, int64_t ldb, int b_mn,
+                            const void* bt, int64_t ldbt, void* C, int64_t ldc, int c_trans, int64_t N,
+                            uint32_t* status_dev, void* stream) {
+    if (M <= 0 || N <= 0 || K <= 0 || M % 128 || K % 128 || N % 32 || K > 65536) return SFFN_ERR_UNSUPPORTED;
+    if (M > 0x7FFFFFFF || N > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    if (!a || !a->vals || !a->meta || !a->ovf_cols || !a->ovf_vals || !a->ovf_count || !B || !bt || !C ||
+        !status_dev)
+        return SFFN_ERR_ARG;
+    if (!aligned16(a->vals) || !aligned16(a->meta) || !aligned16(B) || !aligned16(bt) || !aligned16(C) ||
+        (ldb * 2) % 16 || (ldbt * 2) % 16 || (ldc * 2) % 16)
+        return SFFN_ERR_ALIGN;
+    if (ldb < (b_mn ? N : K) || ldbt < N || ldc < (c_trans ? M : N)) return SFFN_ERR_ARG;
+    if (int rc = bind_device_of(a->vals)) return rc;
+    if (!device_is_sm100()) return SFFN_ERR_DEVICE;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    Sp24Epi epi{};
+    epi.ocols = static_cast<const uint16_t*>(a->ovf_cols);
+    epi.ovals = static_cast<const uint16_t*>(a->ovf_vals);
+    epi.ocount = a->ovf_count;
+    epi.ovf_ld = K / 2;
+    epi.bt = static_cast<const uint16_t*>(bt);
+    epi.ldbt = ldbt;
+    epi.c_trans = c_trans ? 1 : 0;
+    return b_mn ? launch_sp24<true>(a->vals, a->meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st)
+                : launch_sp24<false>(a->vals, a->meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st);
 }

@@ -20,6 +20,7 @@
 // (old/lib_sparse/sparse.py:75,95-100,118,136-139); the path is checked end to
 // end against dense products.
 #include "common.cuh"
+#include "sp24.cuh"
 
 namespace sffn {
 namespace {
@@ -50,68 +51,45 @@ __global__ void __launch_bounds__(SP_TILE) sp24_compress_kernel(
     }
     __syncthreads();
     const int m = t;
-    auto elem = [&](int k) -> uint32_t {
-        if (TRANS) return s_tile[k * SP_TILE + m];
-        return s_tile[m * SP_TILE + (((k >> 3) ^ (m & 15)) << 3) + (k & 7)];
-    };
-    // Per group of 4: kept pair, its nibble, and the overflow bits.
-    uint32_t packed[32];  // kept values, two bf16 per group
-    uint32_t rowmeta[4] = {0, 0, 0, 0};
-    uint32_t ovbits[4] = {0, 0, 0, 0};  // 4 bits per group, 8 groups per word
-    int ocount = 0;
+    const long long row = (long long)tm * SP_TILE + m;
+    uint32_t rowmeta[4];
 #pragma unroll
-    for (int q = 0; q < 32; ++q) {
-        const uint32_t e0 = elem(4 * q), e1 = elem(4 * q + 1), e2 = elem(4 * q + 2), e3 = elem(4 * q + 3);
-        const uint32_t p = ((e0 & 0x7FFFu) != 0) | (((e1 & 0x7FFFu) != 0) << 1) | (((e2 & 0x7FFFu) != 0) << 2) |
-                           (((e3 & 0x7FFFu) != 0) << 3);
-        const uint32_t p2 = p & (p - 1u);   // without the first non-zero
-        const uint32_t rest = p2 & (p2 - 1u);  // beyond the second: overflow
-        int i0, i1;
-        if (p == 0) {
-            i0 = 0;
-            i1 = 1;
-        } else if (p2 == 0) {  // one non-zero at f: pair it with slot 3 (or 2)
-            const int f = __ffs(p) - 1;
-            i0 = f == 3 ? 2 : f;
-            i1 = 3;
+    for (int j = 0; j < 4; ++j) {  // 32-wide K steps of the block
+        uint32_t w[16];
+        if (TRANS) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                w[q] = (uint32_t)s_tile[(32 * j + 2 * q) * SP_TILE + m] |
+                       ((uint32_t)s_tile[(32 * j + 2 * q + 1) * SP_TILE + m] << 16);
         } else {
-            i0 = __ffs(p) - 1;
-            i1 = __ffs(p2) - 1;
-        }
-        const uint32_t ev[4] = {e0, e1, e2, e3};
-        const uint32_t v0 = (p >> i0) & 1u ? ev[i0] : 0u;
-        const uint32_t v1 = (p >> i1) & 1u ? ev[i1] : 0u;
-        packed[q] = v0 | (v1 << 16);
-        const int j = q >> 3, gq = q & 7;  // 32-wide K step, group within it
-        rowmeta[j] |= (uint32_t)(i0 | (i1 << 2)) << (4 * gq);  // k1 = gq / 4 -> bits 16k1 + 4(gq%4)
-        ovbits[q >> 3] |= rest << (4 * (q & 7));
-        ocount += __popc(rest);
-    }
-    // compressed values: 64 per row (128 bytes)
-    uint4* vdst = reinterpret_cast<uint4*>(vals + ((long long)tm * SP_TILE + m) * (K / 2) + (long long)kb * 64);
 #pragma unroll
-    for (int c = 0; c < 8; ++c)
-        vdst[c] = make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) s_rowmeta[m][j] = rowmeta[j];
-    // overflow entries of this row and block
-    if (ocount) {
-        const long long row = (long long)tm * SP_TILE + m;
-        int pos = atomicAdd(&ovf_count[row], ocount);
-        const long long base = row * (long long)(K / 2);
-#pragma unroll 1
-        for (int w = 0; w < 4; ++w) {
-            uint32_t b = ovbits[w];
-            while (b) {
-                const int bit = __ffs(b) - 1;
-                b &= b - 1u;
-                const int k = (w * 8 + (bit >> 2)) * 4 + (bit & 3);  // element within the block
-                ovf_cols[base + pos] = (uint16_t)(kb * SP_TILE + k);
-                ovf_vals[base + pos] = (uint16_t)elem(k);
-                ++pos;
+            for (int h = 0; h < 4; ++h) {
+                const int c = 4 * j + h;  // 16-byte chunk of the row
+                const uint4 v = *reinterpret_cast<const uint4*>(&s_tile[m * SP_TILE + ((c ^ (m & 15)) << 3)]);
+                w[4 * h] = v.x;
+                w[4 * h + 1] = v.y;
+                w[4 * h + 2] = v.z;
+                w[4 * h + 3] = v.w;
             }
         }
+        uint32_t cw[8], nib, ov;
+        sp24_chunk(w, cw, nib, ov);
+        rowmeta[j] = nib;
+        uint4* vdst = reinterpret_cast<uint4*>(vals + row * (K / 2) + (long long)kb * 64 + 16 * j);
+        vdst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+        vdst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+        if (ov) {
+            int pos = atomicAdd(&ovf_count[row], __popc(ov));
+            const long long base = row * (long long)(K / 2);
+            sp24_for_overflow(w, ov, [&](int e, uint32_t v) {
+                ovf_cols[base + pos] = (uint16_t)(kb * SP_TILE + 32 * j + e);
+                ovf_vals[base + pos] = (uint16_t)v;
+                ++pos;
+            });
+        }
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s_rowmeta[m][j] = rowmeta[j];
     __syncthreads();
     // tensor-memory lane order: lane dp = m0 + 8*k1 + 16*m2
     {

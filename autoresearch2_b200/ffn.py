@@ -57,7 +57,7 @@ def sparse_mma() -> str:
 
 
 def _sp24_ok(T, D, Fd):
-    return (_SPARSE_MMA == "on" and T % 128 == 0 and Fd % 128 == 0 and D % 16 == 0 and T <= 65536
+    return (_SPARSE_MMA == "on" and T % 128 == 0 and Fd % 128 == 0 and D % 32 == 0 and T <= 65536
             and Fd <= 65536)
 
 
@@ -77,15 +77,14 @@ def _fused_ok(x, W1, W2, b1, vals):
 def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     T, D = x.shape
     Fd = W1.shape[0]
-    a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset)
     use_sp24 = _sp24_ok(T, D, Fd)
+    # with sp24 the up-projection epilogue writes a in the 2:4 form directly
+    a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24)
     if use_sp24:
         # 2:4 part on the sparse tensor cores, overflow rows k of W2^T
         kb_list = kb_count = None
-        a24 = sp24.compress(a)
+        out = sp24.mm(a, W2.T, bt=sp24.transpose(W2))
         del a
-        out = sp24.mm(a24, W2.T, bt=W2.T.contiguous())
-        del a24
     else:
         kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
         out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
@@ -111,18 +110,21 @@ def _fused_backward(ctx, grad_output, act):
     grad_output = grad_output.contiguous()
     # the bias gradient (column sums of dpre) is summed in the same kernel, in fp32
     db1 = torch.zeros(W1.shape[0], dtype=torch.float32, device=x.device) if ctx.has_bias else None
+    if ctx.sp24:
+        # the epilogue writes dpre, dpre^T and a^T in the 2:4 form (the
+        # transposed ones compressed along the token dimension)
+        dpre, dpre_t, a_t = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1, sp24=True)
+        ctx.row_offsets = None
+        grad_b1 = submit_grad(db1.to(x.dtype)) if ctx.has_bias else None
+        # dW2 = (a^T @ dout)^T, stored transposed by the kernel: [D, F] row-major
+        grad_W2 = submit_grad(sp24.mm(a_t, grad_output, trans_out=True))
+        del a_t
+        grad_x = sp24.mm(dpre, W1)
+        grad_W1 = submit_grad(sp24.mm(dpre_t, x))
+        return grad_x, grad_W1, grad_W2, None, grad_b1
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1)
     ctx.row_offsets = None
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if ctx.has_bias else None
-    if ctx.sp24:
-        # dW2 = (a^T @ dout)^T: the sparse operand a^T is compressed along the
-        # token dimension; the reduction runs on the contiguous [F, D] product
-        gW2T = submit_grad(sp24.mm(sp24.compress(a, trans=True), grad_output))
-        grad_W2 = gW2T.T
-        del a
-        grad_x = sp24.mm(sp24.compress(dpre), W1)
-        grad_W1 = submit_grad(sp24.mm(sp24.compress(dpre, trans=True), x))
-        return grad_x, grad_W1, grad_W2, None, grad_b1
     grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)

@@ -4,6 +4,8 @@ mm(A, B) computes A @ B for 2-D bf16 CUDA tensors that are row-major or
 transposed views of row-major tensors (the kernel reads either major order
 directly, so no transposed copies are made).
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -68,16 +70,17 @@ def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
     return kb_list, kb_count
 
 
-def ffn_up(x, W1, b1, act, vals, offset):
+def ffn_up(x, W1, b1, act, vals, offset, sp24=False):
     """Fused x @ W1.T (+ b1) -> act(z) dense plus the tiled 128x128 sparse z.
 
-    Returns (act_dense [T, F], bitmask, prefix, vals_offset, row_offsets)."""
+    Returns (act [T, F], bitmask, prefix, vals_offset, row_offsets); act is
+    dense, or with sp24=True an ``sp24.Sp24`` (2:4 form, K = F) written by the
+    same epilogue (T, F multiples of 128)."""
     T, D = x.shape
     F = W1.shape[0]
     dev = x.device
     gm, gn = -(-T // 128), -(-F // 128)
     nt = gm * gn
-    act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
     counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
     slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
@@ -86,8 +89,16 @@ def ffn_up(x, W1, b1, act, vals, offset):
     row_offsets = torch.empty(nt * 128, dtype=torch.int32, device=dev)
     status = ptr(_lib.status_word(dev))
     st = stream_ptr(dev)
-    call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
-         ptr(act_out), act_out.stride(0), ptr(bitmask), ptr(counts), ptr(slots), status, st)
+    if sp24:
+        from .sp24 import Sp24
+        act_out = Sp24.empty(T, F, dev)
+        d = act_out.desc()
+        call("sffn_ffn_up_sp24", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
+             ctypes.addressof(d), ptr(bitmask), ptr(counts), ptr(slots), status, st)
+    else:
+        act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+        call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
+             ptr(act_out), act_out.stride(0), ptr(bitmask), ptr(counts), ptr(slots), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
     call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
@@ -104,12 +115,14 @@ def tile_row_offsets(z_sparse):
     return ro
 
 
-def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None):
+def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None, sp24=False):
     """Fused dout @ W2 with the activation gradient; returns (dpre, act2)
     where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F].  z_sparse is a
     128x128-tile BitsparseTensor; row_offsets its per-row offsets (computed
     here if not given).  db1: optional zeroed float32 [F] that receives the
-    column sums of dpre (the bias gradient)."""
+    column sums of dpre (the bias gradient).  With sp24=True the outputs are
+    ``sp24.Sp24`` matrices instead: (dpre [T, F], dpre^T [F, T], act2^T
+    [F, T]), written by the same epilogue (T, F multiples of 128)."""
     T, D = dout.shape
     F = W2.shape[1]
     dev = dout.device
@@ -117,6 +130,15 @@ def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None):
         raise ValueError("the fused activation gradient reads 128x128 tiles")
     if row_offsets is None:
         row_offsets = tile_row_offsets(z_sparse)
+    if sp24:
+        from .sp24 import Sp24
+        outs = (Sp24.empty(T, F, dev), Sp24.empty(F, T, dev), Sp24.empty(F, T, dev))
+        ds = [o.desc() for o in outs]
+        call("sffn_ffn_dgrad_sp24", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,
+             ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(row_offsets),
+             ptr(z_sparse.vals_offset), *(ctypes.addressof(d) for d in ds), ptr(db1),
+             ptr(_lib.status_word(dev)), stream_ptr(dev))
+        return outs
     dpre = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
     call("sffn_ffn_dgrad", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,

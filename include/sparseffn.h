@@ -286,6 +286,50 @@ int sffn_sp24_overflow_add(const void* ovf_cols, const void* ovf_vals, const int
                            int64_t K, const void* bt, int64_t ldb, int64_t N, void* C, int64_t ldc,
                            void* stream);
 
+/* dst[c][r] = src[r][c] for a 16-bit [rows][ld_src] matrix (rows and cols
+ * multiples of 8, 16-byte aligned rows): B^T for sffn_sp24_mm's bt when B is
+ * a transposed view. */
+int sffn_transpose16(const void* src, int64_t ld_src, int64_t rows, int64_t cols, void* dst, int64_t ld_dst,
+                     void* stream);
+
+/* One matrix in the 2:4 form above: vals [M, K/2], meta, overflow columns
+ * (uint16), values and per-row counts. */
+typedef struct sffn_sp24_mat {
+    void* vals;
+    uint32_t* meta;
+    void* ovf_cols;
+    void* ovf_vals;
+    int32_t* ovf_count;
+} sffn_sp24_mat;
+
+/* The full product of a 2:4 matrix A (a, [M, K]) with B [K, N] (B as in
+ * sffn_gemm_sp24): the 2:4 part on the sparse tensor cores and the overflow
+ * added in the same kernel from bt, B as row-major [K][ldbt] (bt may be B
+ * itself when b_mn = 1).  The 2:4 part is rounded to bf16, the overflow added
+ * in fp32 and the sum rounded to bf16.  c_trans = 0: C is [M][ldc]; 1: C^T
+ * is stored, [N][ldc].  M, K multiples of 128 (K <= 65536), N of 32. */
+int sffn_sp24_mm(const sffn_sp24_mat* a, int64_t M, int64_t K, const void* B, int64_t ldb, int b_mn,
+                 const void* bt, int64_t ldbt, void* C, int64_t ldc, int c_trans, int64_t N,
+                 uint32_t* status_dev, void* stream);
+
+/* sffn_ffn_up with the activation a written in the 2:4 form (out, K = F)
+ * instead of dense; bitmask, tile counts and slots as there.  T and F
+ * multiples of 128, F <= 65536.  The 2:4 form is bit-identical to
+ * sffn_sp24_compress of the dense a (overflow order aside). */
+int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1, int64_t T,
+                     int64_t D, int64_t F, int act, const sffn_sp24_mat* out, uint8_t* bitmask,
+                     int32_t* tile_counts, void* slots, uint32_t* status_dev, void* stream);
+
+/* sffn_ffn_dgrad with its outputs in the 2:4 form instead of dense:
+ * dpre [T, F] (K = F, for dX = dpre @ W1), dpre^T [F, T] and act^T [F, T]
+ * (K = T, for dW1 = dpre^T @ x and dW2^T = act^T @ dout); db1_sum as there.
+ * T and F multiples of 128, both <= 65536. */
+int sffn_ffn_dgrad_sp24(const void* dout, int64_t ld_dout, const void* w2, int64_t ldw2, int64_t T, int64_t D,
+                        int64_t F, int act, const void* vals, int64_t vals_len, const uint8_t* bitmask,
+                        const int32_t* row_offsets, const int32_t* vals_offset_dev, const sffn_sp24_mat* dpre,
+                        const sffn_sp24_mat* dpre_t, const sffn_sp24_mat* act_t, float* db1_sum,
+                        uint32_t* status_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

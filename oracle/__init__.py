@@ -271,7 +271,8 @@ def ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=None, code=F32, compute=np.floa
 #   vals [M, K/2]: per group of 4 (k = 4q..4q+3) the first two non-zero
 #     elements by position (non-zero: magnitude bits != 0); a group with
 #     fewer keeps zero slots so that idx0 < idx1 (one non-zero at p: p and 3,
-#     or 2 and 3 when p == 3; none: 0 and 1).
+#     or 2 and 3 when p == 3; none: 0 and 1).  A slot holds the bits of the
+#     element at its index, so a kept zero keeps its sign (+0 or -0).
 #   nib [M, K/4]: idx0 | idx1 << 2.
 #   meta [M/128, K/128, 128 lanes, 4 words]: word j of lane
 #     dp = m0 + 8*k1 + 16*m2 holds the nibbles of K-half k1 (4 groups) of the
@@ -309,8 +310,6 @@ def sp24_compress(a_bits):
     k0, k1, ov = _SP24[0][pat], _SP24[1][pat], _SP24[2][pat]
     v0 = np.take_along_axis(g, k0[..., None], -1)[..., 0]
     v1 = np.take_along_axis(g, k1[..., None], -1)[..., 0]
-    v0 = np.where(np.take_along_axis(nzm, k0[..., None], -1)[..., 0], v0, 0)
-    v1 = np.where(np.take_along_axis(nzm, k1[..., None], -1)[..., 0], v1, 0)
     vals = np.stack([v0, v1], -1).reshape(M, K // 2).astype(np.uint16)
     nib = (k0 | (k1 << 2)).astype(np.uint8)
     ovm = ((ov[..., None] >> np.arange(4)) & 1).astype(bool).reshape(M, K)

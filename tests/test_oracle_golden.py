@@ -123,6 +123,8 @@ def test_sp24_oracle_split_is_lossless():
         keep = (A_bits & 0x7FFF) != 0
         assert np.array_equal(full[keep], A_bits[keep])
         assert not np.any(full[~keep] & 0x7FFF)
+        # kept slots carry the element's own bits, signed zeros included
+        assert np.array_equal(full[full != 0], A_bits[full != 0])
         assert np.all((nib & 3) < (nib >> 2))
         meta = oracle.sp24_meta(nib)
         assert meta.shape == (2, 4, 128, 4)
