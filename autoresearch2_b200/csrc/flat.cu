@@ -4,31 +4,18 @@
 // prefix, vals kernel -- the dense tensor is read twice) and
 // old/sparse_unpack.py:6-97 (popcount, one-program serial prefix, rebuild).
 //
-// Both directions are ONE single-pass kernel over tiles of 32 KB of dense
-// data (16384 bf16/fp16 or 8192 fp32 elements), one tile per CTA of 256
-// threads.  A CTA takes the next tile number from a ticket counter, so every
-// tile's predecessors have started before it and the decoupled look-back that
-// gives the tile its offset in `vals` always ends.  The look-back reads 512
-// predecessor states per round in coalesced rows, so the resolved frontier
-// moves 16 MB of dense data per L2 round trip and does not limit the
-// bandwidth.  Every byte of the dense tensor, the mask and the values crosses
-// HBM exactly once.
+// Two implementations:
+//   * sffn_flat_pack / sffn_flat_unpack (workspace): per-tile counts, one
+//     scan block, then independent blocks that compact or expand their tile
+//     at its offset -- full occupancy, no waits between blocks (see "scan-based
+//     path" below).  Unpack reads the mask twice, pack the dense tensor.
+//   * sffn_flat_pack_noalloc (fixed 32 KB scratch): one single-pass persistent
+//     kernel over 32 KB tiles whose offsets come from a decoupled look-back
+//     (see "pack" below), so the dense tensor crosses HBM once and the scratch
+//     holds one state per tile.
 //
-//   pack:   bring the tile into shared memory with one bulk copy, write the
-//           mask words, scan the counts, publish the tile aggregate, look
-//           back, and write each thread's set elements from the staged tile
-//           to their places in `vals`.
-//   unpack: load the tile's mask, scan the counts, publish, look back, load
-//           the tile's values (16-byte loads where `vals` allows) into shared
-//           memory, expand and write the dense tile with 16-byte streaming
-//           stores.
-//
-// Thread layout: in group g thread `tid` owns the 8 consecutive elements
-// f = 8*(tid + 256*g) .. +7 of its tile, i.e. mask byte tid + 256*g of the
-// tile; lanes 4k..4k+3 form one little-endian uint32 mask word (bit f%32 of
-// word f/32 == bit f%8 of byte f/8).  Values are ordered by f: group-major,
-// then thread, then element -- the (group, warp) partial counts are scanned in
-// that order.
+// Mask layout: element f -> byte f/8, bit f%8 (a little-endian uint32 word w
+// holds elements 32w .. 32w+31).  Values are in element order.
 #include <stdio.h>
 
 #include <algorithm>
@@ -72,6 +59,7 @@ template <> struct Vec8<uint16_t> {
                            ((t2 & 0x80008000u) >> 11) | ((t3 & 0x80008000u) >> 9);
         return (x | (x >> 15)) & 0xFFu;
     }
+    __device__ void load_global(const uint16_t* p) { q = __ldg(reinterpret_cast<const uint4*>(p)); }
     __device__ void store_first16(uint16_t* p) const { *reinterpret_cast<uint4*>(p) = q; }
     __device__ void load_smem(const uint16_t* p) { q = *reinterpret_cast<const uint4*>(p); }
     __device__ void store_global_cs(uint16_t* p) const { __stcs(reinterpret_cast<uint4*>(p), q); }
@@ -94,6 +82,10 @@ template <> struct Vec8<uint32_t> {
         for (int j = 0; j < 8; ++j) r |= (uint32_t)nonzero_bits(get(j)) << j;
         return r;
     }
+    __device__ void load_global(const uint32_t* p) {
+        a = __ldg(reinterpret_cast<const uint4*>(p));
+        b = __ldg(reinterpret_cast<const uint4*>(p) + 1);
+    }
     __device__ void store_first16(uint32_t* p) const { *reinterpret_cast<uint4*>(p) = a; }
     __device__ void load_smem(const uint32_t* p) {
         a = reinterpret_cast<const uint4*>(p)[0];
@@ -106,27 +98,38 @@ template <> struct Vec8<uint32_t> {
 };
 
 // ------------------------------------------------------------------ pack ----
-// Persistent and pipelined, one CTA per SM: 16 compute warps and a look-back
-// warp, a ring of five 32 KB input buffers filled by bulk copies, and a 32 KB
-// ring of compacted values.  Iteration k of the compute warps:
-//   1. scan tile k: mask bytes, mask words to global memory, counts, CTA scan,
-//      publication of the tile aggregate for the look-back warp;
-//   2. compact tile k's set elements into the value ring (writing out older
-//      tiles first if the ring lacks room);
-//   3. start the bulk copy of tile k+5 into the input buffer just freed;
+// Persistent and pipelined, one CTA per SM: 16 compute warps, two look-back
+// warps (even and odd tiles of the CTA), and a loader warp that takes tiles
+// by ticket and fills a ring of five 32 KB input buffers by bulk copies, so
+// neither the ticket nor the look-back latency is on the compute warps' path.
+// The loader keeps four ticket requests in flight (one thread's atomics on
+// one address return in order, so its tiles still rise); one tile per ticket
+// keeps the CTAs' tiles interleaved -- a CTA holding a run of consecutive
+// tiles would make the next CTA's look-backs wait on its iterations, and so
+// on around the grid.  A 32 KB ring holds compacted values.  Iteration k of
+// the compute warps:
+//   1. scan tile k from its input buffer into registers: mask bytes to global
+//      memory, counts, CTA scan, publication of the tile aggregate for the
+//      look-back warps;
+//   2. the input buffer is free again: hand it back to the loader;
+//   3. compact tile k's set elements from registers into the value ring
+//      (writing out older tiles first if the ring lacks room);
 //   4. write to `vals` every compacted tile up to k-2, at the offset the
-//      look-back warp found for it meanwhile.
-// So the input buffers are busy only while a tile is in flight or scanned,
-// and the look-back latency stays off the compute warps' path.
-// Warp w owns the contiguous chunks (8 elements each) CPW*w .. CPW*w+CPW-1 of
-// the tile.  In the load layout lane l reads chunks l, l+32, ... (512
-// contiguous bytes of shared memory per instruction); in the count layout
-// lane l owns G consecutive chunks (one mask word) and compacts them by
-// walking the word's set bits, at the warp's base + its exclusive count.
+//      look-back warp found for it meanwhile, in 16-byte stores realigned
+//      from the ring by funnel shifts.
+// Thread layout: warp w owns the chunks (8 elements, one mask byte) CPW*w ..
+// CPW*w + CPW - 1 of the tile; lane l takes chunks l, l+32, ... (G of them),
+// so each shared-memory load of a warp reads 512 contiguous bytes and each
+// mask-byte store writes 32 contiguous bytes.  Values are ordered by chunk:
+// the warp's chunks of round u (l + 32u over the lanes) follow all chunks of
+// the rounds before.
 constexpr int FP_CW = 16;                 // compute warps
 constexpr int FP_CT = FP_CW * 32;         // compute threads
-constexpr int FP_THREADS = FP_CT + 32;    // plus the look-back warp
+constexpr int FP_LB = FP_CW;              // first of the two look-back warps
+constexpr int FP_LOADER = FP_CW + 2;      // loader warp
+constexpr int FP_THREADS = FP_CT + 96;    // plus the look-back and loader warps
 constexpr int FP_NB = 5;                  // input tile buffers
+constexpr int FP_TQ = 4;                  // ticket requests in flight
 constexpr int FP_D = 2;                   // a tile is written out D iterations after its scan
 static_assert(FP_D < FP_NB, "a tile's bookkeeping lives until its write-out");
 constexpr int FP_BAR = 1;                 // named barrier of the compute warps
@@ -152,17 +155,44 @@ struct PackCfg {
     static constexpr int CPW = CHUNKS / FP_CW;                    // chunks per warp
     static constexpr int G = CPW / 32;                            // chunks per lane
     static constexpr int EPV = 16 / (int)sizeof(B);               // elements per 16 bytes
-    static_assert(G == 4 || G == 2, "32- or 16-bit mask words per lane");
+    static_assert(G == 4 || G == 2, "four or two chunks per lane");
     static constexpr int RC = TILE;  // value ring, in elements (a power of two)
     static_assert((RC & (RC - 1)) == 0, "ring index by mask");
-    static constexpr size_t SMEM = (size_t)(FP_NB * TILE + RC) * sizeof(B) + (size_t)CHUNKS;
+    static constexpr size_t SMEM = (size_t)(FP_NB * TILE + RC) * sizeof(B);
 };
 
-// This lane's G mask bytes (count layout) from the warp's byte region.
-template <int G>
-__device__ __forceinline__ uint32_t lane_bits(const uint8_t* wmb, int lane) {
-    if constexpr (G == 4) return *reinterpret_cast<const uint32_t*>(wmb + 4 * lane);
-    else return *reinterpret_cast<const uint16_t*>(wmb + 2 * lane);
+// The 16 bytes that start D elements into the 32 bytes a:b (D < EPV).
+template <typename B, int D>
+__device__ __forceinline__ uint4 realign(const uint4 a, const uint4 b) {
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t o[4];
+    if constexpr (sizeof(B) == 2) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            o[i] = (D & 1) ? __funnelshift_r(w[D / 2 + i], w[D / 2 + i + 1], 16) : w[D / 2 + i];
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = w[D + i];
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// nvec 16-byte vectors to dst (16-byte aligned) from the ring, whose element
+// at ring position a0 + D begins them (a0 a multiple of EPV).
+template <typename B, int D>
+__device__ __forceinline__ void ring_copy_out(const B* s_ring, uint32_t a0, int nvec, B* dst, int tid) {
+    using C = PackCfg<B>;
+    for (int v = tid; v < nvec; v += FP_CT) {
+        const uint32_t ra = (a0 + (uint32_t)(C::EPV * v)) & (uint32_t)(C::RC - 1);
+        const uint4 x = *reinterpret_cast<const uint4*>(s_ring + ra);
+        uint4 o = x;
+        if constexpr (D != 0) {
+            const uint4 y =
+                *reinterpret_cast<const uint4*>(s_ring + ((ra + (uint32_t)C::EPV) & (uint32_t)(C::RC - 1)));
+            o = realign<B, D>(x, y);
+        }
+        *reinterpret_cast<uint4*>(dst + (size_t)C::EPV * v) = o;
+    }
 }
 
 // VEC: `vals` is 16-byte aligned (16-byte stores for the write-out).
@@ -174,34 +204,37 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
     using C = PackCfg<B>;
     constexpr int TILE = C::TILE, CPW = C::CPW, G = C::G, EPV = C::EPV, RC = C::RC;
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    B* s_buf = reinterpret_cast<B*>(smem_raw);                                 // [NB][TILE]
-    B* s_ring = s_buf + (size_t)FP_NB * TILE;                                  // [RC]
-    uint8_t* s_mb = reinterpret_cast<uint8_t*>(s_ring + RC);                   // [CHUNKS]
-    __shared__ __align__(8) uint64_t full[FP_NB], pub[FP_NB], exr[FP_NB];
+    B* s_buf = reinterpret_cast<B*>(smem_raw);  // [NB][TILE]
+    B* s_ring = s_buf + (size_t)FP_NB * TILE;   // [RC]
+    __shared__ __align__(8) uint64_t full[FP_NB], empty[FP_NB], pub[FP_NB], exr[FP_NB];
     __shared__ long long s_tile[FP_NB];  // tile in each input buffer
     // per scanned tile j, in slot j % NB until its write-out: tile number,
     // offset in `vals`, value count, start in the value ring
-    __shared__ long long s_wtile[FP_NB], s_ex[FP_NB], s_rst[FP_NB];
+    __shared__ long long s_wtile[FP_NB], s_ex[FP_NB];
+    __shared__ uint32_t s_rst[FP_NB];
     __shared__ int s_agg[FP_NB];
     __shared__ int s_wt[FP_CW];
     __shared__ volatile int s_abort;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const long long nbytes = (n + 7) >> 3;
     if (tid == 0) {
         for (int j = 0; j < FP_NB; ++j) {
             mbar_init(&full[j], 1);
+            mbar_init(&empty[j], 1);
             mbar_init(&pub[j], 1);
             mbar_init(&exr[j], 1);
+            s_wtile[j] = ntiles;
         }
         s_abort = 0;
         fence_mbar_init();
     }
     __syncthreads();
 
-    // ---------------------------------------------------- look-back warp ----
-    // Resolves this CTA's scanned tiles in order: tile j in slot j % NB.
-    if (warp == FP_CW) {
-        for (int j = 0;; ++j) {
+    // --------------------------------------------------- look-back warps ----
+    // Warp i resolves this CTA's scanned tiles j = i, i+2, ... in order: tile
+    // j in slot j % NB.  The two run side by side: a tile's look-back reads
+    // its predecessor's aggregate, published at its scan, not its result.
+    if (warp == FP_LB || warp == FP_LB + 1) {
+        for (int j = warp - FP_LB;; j += 2) {
             const int b = j % FP_NB;
             const bool ok = __all_sync(FULL, mbar_wait_bounded(&pub[b], (uint32_t)(j / FP_NB) & 1u));
             if (!ok || s_abort) {
@@ -224,27 +257,61 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
         return;
     }
 
+    // ------------------------------------------------------- loader warp ----
+    // Fill j goes to buffer j % NB once the compute warps freed it; the
+    // first past-the-end tile is the last fill (the compute warps stop there).
+    if (warp == FP_LOADER) {
+        if (lane == 0) {
+            unsigned int q[FP_TQ];  // tickets requested, oldest first
+#pragma unroll
+            for (int i = 0; i < FP_TQ; ++i) q[i] = atomicAdd(ticket, 1u);
+            int last[FP_NB] = {0};  // 1 + phase of each buffer's latest fill
+            for (int j = 0;; ++j) {
+                const int b = j % FP_NB;
+                const bool ok = mbar_wait_bounded(&empty[b], ((uint32_t)(j / FP_NB) & 1u) ^ 1u);
+                if (!ok || s_abort) {
+                    if (!ok) {
+                        atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
+                        s_abort = 1;
+                    }
+                    // tiles taken but not handed over: resolved, so that the
+                    // successors' look-backs end
+#pragma unroll
+                    for (int i = 0; i < FP_TQ; ++i)
+                        if ((long long)q[i] < ntiles) st_relaxed_u64(&states[q[i]], LB_INCL);
+                    break;
+                }
+                const long long t = (long long)q[0];
+#pragma unroll
+                for (int i = 0; i + 1 < FP_TQ; ++i) q[i] = q[i + 1];
+                q[FP_TQ - 1] = atomicAdd(ticket, 1u);
+                s_tile[b] = t;
+                uint32_t bytes = 0;
+                if (t < ntiles) {
+                    const long long nv = min((long long)TILE, n - t * TILE);
+                    bytes = (uint32_t)(nv * (long long)sizeof(B)) & ~15u;
+                }
+                if (bytes) {
+                    mbar_arrive_expect_tx(&full[b], bytes);
+                    bulk_g2s(s_buf + (size_t)b * TILE, dense + t * TILE, bytes, &full[b]);
+                } else {
+                    mbar_arrive(&full[b]);
+                }
+                last[b] = j / FP_NB + 1;
+                if (t >= ntiles) break;  // the queued tickets are past the end too
+            }
+            // no copy may still be writing this CTA's shared memory when it exits
+            for (int b = 0; b < FP_NB; ++b)
+                if (last[b]) (void)mbar_wait_bounded(&full[b], (uint32_t)(last[b] - 1) & 1u);
+        }
+        __syncwarp();
+        return;
+    }
+
     // ------------------------------------------------------ compute warps ----
-    // thread 0: take the next tile into buffer j and start its copy
-    auto acquire = [&](int j) {
-        const long long t = (long long)atomicAdd(ticket, 1u);
-        s_tile[j] = t;
-        uint32_t bytes = 0;
-        if (t < ntiles) {
-            const long long nv = min((long long)TILE, n - t * TILE);
-            bytes = (uint32_t)(nv * (long long)sizeof(B)) & ~15u;
-        }
-        if (bytes) {
-            mbar_arrive_expect_tx(&full[j], bytes);
-            bulk_g2s(s_buf + (size_t)j * TILE, dense + t * TILE, bytes, &full[j]);
-        } else {
-            mbar_arrive(&full[j]);
-        }
-    };
     // Give up after a wait ran out: resolve the tiles this CTA holds for the
-    // successors, wait (bounded) for the `cnt` copies in flight from iteration
-    // k0 on, and wake the look-back warp.
-    auto abort_all = [&](int k0, int cnt) {
+    // successors and wake the look-back and loader warps.
+    auto abort_all = [&]() {
         if (tid == 0) {
             atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
             s_abort = 1;
@@ -252,28 +319,25 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
                 if (s_tile[j] < ntiles) st_relaxed_u64(&states[s_tile[j]], LB_INCL);
                 if (s_wtile[j] < ntiles) st_relaxed_u64(&states[s_wtile[j]], LB_INCL);
             }
-            for (int j = 0; j < cnt; ++j)
-                (void)mbar_wait_bounded(&full[(k0 + j) % FP_NB], (uint32_t)((k0 + j) / FP_NB) & 1u);
-            for (int j = 0; j < FP_NB; ++j) mbar_arrive(&pub[j]);
+            for (int j = 0; j < FP_NB; ++j) {
+                mbar_arrive(&pub[j]);
+                mbar_arrive(&empty[j]);
+            }
         }
     };
-    if (tid == 0)
-        for (int j = 0; j < FP_NB; ++j) {
-            s_wtile[j] = ntiles;
-            acquire(j);
-        }
 
     // Every compute thread keeps the same ring and write-out counters.
-    long long head = 0, tail = 0;  // value ring: elements written / freed
-    int wnext = 0;                 // next scanned tile to write out
-    int k_end = -1;                // first iteration whose tile was past the end
+    uint32_t head = 0, tail = 0;  // value ring: elements written / freed (mod 2^32)
+    int wnext = 0;                // next scanned tile to write out
+    int k_end = -1;               // first iteration whose tile was past the end
     // Writes tile j's compacted values to `vals` (after its look-back); false
     // if the wait for the look-back ran out (the CTA then gives up).
     auto write_out = [&](int j) -> bool {
         const int bj = j % FP_NB;
         const bool okw = mbar_wait_bounded(&exr[bj], (uint32_t)(j / FP_NB) & 1u);
         if (named_bar_or(FP_BAR, FP_CT, !okw)) return false;
-        const long long ex = s_ex[bj], rs = s_rst[bj], tw = s_wtile[bj];
+        const long long ex = s_ex[bj], tw = s_wtile[bj];
+        const uint32_t rs = s_rst[bj];
         const int agg = s_agg[bj];
         // [ex, ex + agg) clipped to the capacity of `vals`
         const int lim = (int)max(0ll, min((long long)agg, cap - ex));
@@ -282,21 +346,27 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
             const int h = min(lim, (int)((EPV - ex % EPV) % EPV));  // to a 16-byte boundary
             if (tid < h) vals[ex + tid] = s_ring[(rs + tid) & (RC - 1)];
             const int nvec = (lim - h) / EPV;
-            for (int v = tid; v < nvec; v += FP_CT) {
-                const long long i0 = rs + h + v * EPV;
-                Vec8<B> o;
-#pragma unroll
-                for (int e = 0; e < EPV; ++e) o.set(e, s_ring[(i0 + e) & (RC - 1)]);
-                o.store_first16(vals + ex + h + v * EPV);
+            const uint32_t r0 = rs + (uint32_t)h;
+            const uint32_t a0 = r0 & ~(uint32_t)(EPV - 1);
+            B* dst = vals + ex + h;
+            switch ((int)(r0 & (uint32_t)(EPV - 1))) {  // uniform: one loop per tile
+                case 0: ring_copy_out<B, 0>(s_ring, a0, nvec, dst, tid); break;
+                case 1: ring_copy_out<B, 1>(s_ring, a0, nvec, dst, tid); break;
+                case 2: ring_copy_out<B, 2>(s_ring, a0, nvec, dst, tid); break;
+                case 3: ring_copy_out<B, 3>(s_ring, a0, nvec, dst, tid); break;
+                case 4: if constexpr (EPV > 4) ring_copy_out<B, (EPV > 4 ? 4 : 0)>(s_ring, a0, nvec, dst, tid); break;
+                case 5: if constexpr (EPV > 4) ring_copy_out<B, (EPV > 4 ? 5 : 0)>(s_ring, a0, nvec, dst, tid); break;
+                case 6: if constexpr (EPV > 4) ring_copy_out<B, (EPV > 4 ? 6 : 0)>(s_ring, a0, nvec, dst, tid); break;
+                default: if constexpr (EPV > 4) ring_copy_out<B, (EPV > 4 ? 7 : 0)>(s_ring, a0, nvec, dst, tid); break;
             }
             done = h + nvec * EPV;
         }
-        for (int i = done + tid; i < lim; i += FP_CT) vals[ex + i] = s_ring[(rs + i) & (RC - 1)];
+        for (int i = done + tid; i < lim; i += FP_CT) vals[ex + i] = s_ring[(rs + (uint32_t)i) & (RC - 1)];
         if (tid == 0) {
             if (ex + agg > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
             if (tw == ntiles - 1) *nnz_out = ex + agg;
         }
-        tail += agg;
+        tail += (uint32_t)agg;
         return true;
     };
 
@@ -307,61 +377,76 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
             // ---- 1. scan of tile k ----
             const bool ok = mbar_wait_bounded(&full[b], (uint32_t)(k / FP_NB) & 1u);
             if (named_bar_or(FP_BAR, FP_CT, !ok)) {
-                abort_all(k, FP_NB);
+                abort_all();
                 return;
             }
             have = s_tile[b] < ntiles;
             if (!have) {
                 k_end = k;
                 if (tid == 0) {
+                    // tell both look-back warps that the tiles ended (slot k+1
+                    // held tile k+1-NB, written out two iterations ago)
+                    const int b1 = (k + 1) % FP_NB;
                     s_wtile[b] = ntiles;
-                    mbar_arrive(&pub[b]);  // tells the look-back warp that the tiles ended
+                    s_wtile[b1] = ntiles;
+                    mbar_arrive(&pub[b]);
+                    mbar_arrive(&pub[b1]);
                 }
             }
         }
         if (have) {
             const long long t = s_tile[b];
-            const B* in = s_buf + (size_t)b * TILE;
+            B* in = s_buf + (size_t)b * TILE;
             const long long base = t * TILE;
             const int nvalid = (int)min((long long)TILE, n - base);
             const int tma_elems =
                 (int)(((long long)nvalid * (long long)sizeof(B)) & ~15ll) / (int)sizeof(B);
             if (tma_elems < nvalid) {  // the last tile's tail, not a multiple of 16 bytes
-                for (int i = tma_elems + tid; i < nvalid; i += FP_CT)
-                    const_cast<B*>(in)[i] = dense[base + i];
+                for (int i = tma_elems + tid; i < nvalid; i += FP_CT) in[i] = dense[base + i];
                 named_bar_sync(FP_BAR, FP_CT);
             }
-            uint8_t* wmb = s_mb + CPW * warp;
-            // load layout: mask byte of chunk CPW*warp + lane + 32*g
+            // this lane's chunks l + 32u of the warp: values and mask bytes
+            Vec8<B> v[G];
+            uint32_t mb[G];
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const int f = 8 * (CPW * warp + lane + 32 * g);
-                uint32_t byte = 0;
+            for (int u = 0; u < G; ++u) {
+                const int ci = CPW * warp + lane + 32 * u;  // chunk of the tile
+                const int f = 8 * ci;
+                mb[u] = 0;
+                v[u].zero();
                 if (f < nvalid) {
-                    Vec8<B> v;
-                    v.load_smem(in + f);
-                    byte = v.nonzero_byte();
+                    v[u].load_smem(in + f);
+                    uint32_t byte = v[u].nonzero_byte();
                     if (f + 8 > nvalid) byte &= (1u << (nvalid - f)) - 1u;
-                }
-                wmb[lane + 32 * g] = (uint8_t)byte;
-            }
-            __syncwarp();
-            // count layout: this lane's G chunks as one mask word
-            uint32_t m = lane_bits<G>(wmb, lane);
-            {
-                const long long byte0 = (base >> 3) + (long long)CPW * warp + (long long)G * lane;
-                if (byte0 + G <= nbytes) {
-                    if (G == 4) *reinterpret_cast<uint32_t*>(mask + byte0) = m;
-                    else *reinterpret_cast<uint16_t*>(mask + byte0) = (uint16_t)m;
-                } else {
-                    for (int e = 0; e < G; ++e)
-                        if (byte0 + e < nbytes) mask[byte0 + e] = (uint8_t)(m >> (8 * e));
+                    mb[u] = byte;
+                    mask[(base >> 3) + ci] = (uint8_t)byte;  // 32 contiguous bytes per warp
                 }
             }
-            const int cnt = __popc(m);
-            const int inc = warp_incl_scan(cnt, lane);
-            if (lane == 31) s_wt[warp] = inc;
-            named_bar_sync(FP_BAR, FP_CT);
+            // offsets of the chunks in the warp's value order: two counts per
+            // scanned word (each at most 32 * 8 = 256 over the warp)
+            int off[G], wtot;
+            if constexpr (G == 4) {
+                const int pa = __popc(mb[0]) | (__popc(mb[1]) << 16), pb = __popc(mb[2]) | (__popc(mb[3]) << 16);
+                const int ia = warp_incl_scan(pa, lane), ib = warp_incl_scan(pb, lane);
+                const int ta = __shfl_sync(FULL, ia, 31), tb = __shfl_sync(FULL, ib, 31);
+                const int ea = ia - pa, eb = ib - pb;
+                const int t0 = ta & 0xFFFF, t1 = ta >> 16, t2 = tb & 0xFFFF;
+                off[0] = ea & 0xFFFF;
+                off[1] = t0 + (ea >> 16);
+                off[2] = t0 + t1 + (eb & 0xFFFF);
+                off[3] = t0 + t1 + t2 + (eb >> 16);
+                wtot = t0 + t1 + t2 + (tb >> 16);
+            } else {
+                const int pa = __popc(mb[0]) | (__popc(mb[1]) << 16);
+                const int ia = warp_incl_scan(pa, lane);
+                const int ta = __shfl_sync(FULL, ia, 31);
+                const int ea = ia - pa;
+                off[0] = ea & 0xFFFF;
+                off[1] = (ta & 0xFFFF) + (ea >> 16);
+                wtot = (ta & 0xFFFF) + (ta >> 16);
+            }
+            if (lane == 0) s_wt[warp] = wtot;
+            named_bar_sync(FP_BAR, FP_CT);  // also: every lane has read buffer b
             const int wv = lane < FP_CW ? s_wt[lane] : 0;
             const int wi = warp_incl_scan(wv, lane);
             const int wbase = __shfl_sync(FULL, wi - wv, warp);
@@ -372,38 +457,48 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
                 s_rst[b] = head;
                 lookback_publish_relaxed(states, t, (unsigned long long)agg);
                 mbar_arrive(&pub[b]);
+                // ---- 2. the input buffer is free: back to the loader ----
+                fence_proxy_async_smem();
+                mbar_arrive(&empty[b]);
             }
-            // ---- 2. compaction into the value ring ----
-            if (RC - (head - tail) < agg) {
-                while (RC - (head - tail) < agg)
+            // ---- 3. compaction into the value ring ----
+            if (RC - (int)(head - tail) < agg) {
+                while (RC - (int)(head - tail) < agg)
                     if (!write_out(wnext++)) {
-                        abort_all(k + 1, FP_NB - 1);
+                        abort_all();
                         return;
                     }
                 named_bar_sync(FP_BAR, FP_CT);  // freed ring slots fully read
             }
-            {
-                const B* src = in + 8 * (CPW * warp + G * lane);
-                long long p = head + wbase + (inc - cnt);
-                while (m) {
-                    const int j = __ffs(m) - 1;
-                    m &= m - 1;
-                    s_ring[(p++) & (RC - 1)] = src[j];
+            const uint32_t p0 = head + (uint32_t)wbase;
+            if (4 * agg > TILE) {
+                // dense tile: every element tested, predicated stores
+#pragma unroll
+                for (int u = 0; u < G; ++u) {
+                    uint32_t p = p0 + (uint32_t)off[u];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if ((mb[u] >> j) & 1u) s_ring[(p++) & (RC - 1)] = v[u].get(j);
+                }
+            } else {
+                // sparse tile: walk the set bits
+#pragma unroll
+                for (int u = 0; u < G; ++u) {
+                    uint32_t p = p0 + (uint32_t)off[u], bb = mb[u];
+                    while (bb) {
+                        const int j = __ffs(bb) - 1;
+                        bb &= bb - 1u;
+                        s_ring[(p++) & (RC - 1)] = v[u].get(j);
+                    }
                 }
             }
-            head += agg;
-        }
-        // ---- 3. the input buffer of tile k is free: tile k+NB ----
-        named_bar_sync(FP_BAR, FP_CT);
-        if (tid == 0 && have) {
-            fence_proxy_async_smem();
-            acquire(b);
+            head += (uint32_t)agg;
         }
         // ---- 4. write-out of the tiles scanned D or more iterations ago ----
         const int upto = k_end < 0 ? k - FP_D : k_end - 1;
         while (wnext <= upto)
             if (!write_out(wnext++)) {
-                abort_all(k + 1, k_end < 0 ? FP_NB : 0);
+                abort_all();
                 return;
             }
         if (k_end >= 0) break;  // every scanned tile is written
@@ -412,229 +507,287 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
 }
 
 
-// ---------------------------------------------------------------- unpack ----
-constexpr int PK_CW = 8;                       // compute warps (unpack)
-constexpr int PK_THREADS = (PK_CW + 1) * 32;   // plus the look-back warp
-constexpr int PK_NB = 3;                       // tile buffers
-constexpr int PK_BAR = 1;                      // named barrier of the compute warps
-constexpr int PK_CT = PK_CW * 32;              // compute threads
+// ------------------------------------------------------ scan-based path ----
+// The workspace entry points run two launches over tiles of FS_TILE = 8192
+// elements (256 threads x 32), with no waits between blocks:
+//   pack:   flat_mask_count_kernel (mask bytes, tile counts) ->
+//           flat_compact_kernel (values staged in shared memory at the
+//           output's alignment, written in 16-byte stores);
+//   unpack: flat_mask_popc_kernel (tile counts from the mask) ->
+//           flat_expand_kernel (the tile's values staged by 16-byte loads,
+//           expanded into 16-byte streaming stores).
+// A counting block adds its tile count to the sum of its group of 256 tiles;
+// a second-kernel block finds its offset from at most 255 counts and nt/256
+// group sums, loaded together in one round trip (tile_offset).  Every block is independent, so the kernels run at full
+// occupancy and memory latency is hidden by other blocks.  The pack reads the
+// dense tensor twice (once per kernel); unpack re-reads only the mask.
+// Thread layout: warp w owns chunks 128w .. 128w+127 of the tile, lane l takes
+// chunks l, l+32, l+64, l+96, and values are ordered by chunk.
+//
+// Workspace (16 + 8 * nt bytes suffice): int32 tile counts, then the int64
+// sums of the 256-tile groups (zeroed on the stream before the counting
+// kernel).
+constexpr int FS_TILE = FT_MIN_TILE;  // elements per tile
+constexpr int FS_T = 256;             // threads per tile
+constexpr int FS_W = FS_T / 32;
+static_assert(FS_TILE == FS_T * 32, "32 elements per thread");
 
-// The CPT mask bytes of owner thread `o` (count layout) as one word.
-template <int CPT>
-__device__ __forceinline__ uint64_t owner_bits(const uint8_t* s_mb, int o) {
-    if constexpr (CPT == 8) return *reinterpret_cast<const uint64_t*>(s_mb + 8 * o);
-    else return *reinterpret_cast<const uint32_t*>(s_mb + 4 * o);
-}
-
-// Same pipeline as pack.  In iteration k the compute warps count tile k (its
-// mask words were loaded into registers during iteration k-1) and expand tile
-// k-1; the look-back warp resolves tile k and then starts the bulk copy of its
-// values into the tile's buffer, so the values are in shared memory when the
-// compute warps expand it in iteration k+1.  The dense tile is written with
-// 16-byte streaming stores, 512 contiguous bytes per warp instruction.
-template <typename B>
-struct UnpackCfg {
-    static constexpr int TILE = FT_TILE_BYTES / (int)sizeof(B);
-    static constexpr int CHUNKS = TILE / 8;
-    static constexpr int G = CHUNKS / PK_CT;
-    static constexpr int EPV = 16 / (int)sizeof(B);  // elements per 16-byte vector
-    static constexpr int VCAP = TILE + 2 * EPV;      // staged values, with alignment slack
-    static_assert(G == 8 || G == 4, "64- or 32-bit words in the count layout");
-    static constexpr size_t SMEM =
-        (size_t)PK_NB * VCAP * sizeof(B) + (size_t)PK_NB * CHUNKS + (size_t)PK_NB * PK_CT * 4;
+struct TileSums {
+    int* counts;              // [nt]
+    unsigned long long* g1;   // [ceil(nt / 256)]
 };
 
-// VEC: `vals` is 16-byte aligned, so the look-back warp bulk-copies values.
-template <typename B, bool VEC>
-__global__ void __launch_bounds__(PK_THREADS, 2) flat_unpack_kernel(
-    const B* __restrict__ vals, long long vals_len, const uint8_t* __restrict__ mask, long long n,
-    B* __restrict__ out, unsigned long long* __restrict__ states, unsigned int* __restrict__ ticket,
-    uint32_t* __restrict__ status, long long ntiles) {
-    using C = UnpackCfg<B>;
-    constexpr int TILE = C::TILE, CHUNKS = C::CHUNKS, G = C::G, EPV = C::EPV, VCAP = C::VCAP;
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    B* s_vals = reinterpret_cast<B*>(smem_raw);                                // [NB][VCAP]
-    uint8_t* s_mb = smem_raw + (size_t)PK_NB * VCAP * sizeof(B);               // [NB][CHUNKS]
-    int* s_off = reinterpret_cast<int*>(s_mb + (size_t)PK_NB * CHUNKS);        // [NB][CT]
-    __shared__ __align__(8) uint64_t pub[PK_NB], vfull[PK_NB];
-    __shared__ long long s_tile[PK_NB], s_ex[PK_NB], s_va0[PK_NB], s_vend[PK_NB];
-    __shared__ int s_wt[PK_NB][PK_CW], s_wb[PK_NB][PK_CW], s_agg[PK_NB];
-    __shared__ volatile int s_abort;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const long long nbytes = (n + 7) >> 3;
-    if (tid == 0) {
-        for (int j = 0; j < PK_NB; ++j) {
-            mbar_init(&pub[j], 1);
-            mbar_init(&vfull[j], 1);
+inline TileSums tile_sums(void* ws, long long nt) {
+    char* p = static_cast<char*>(ws);
+    TileSums t;
+    t.counts = reinterpret_cast<int*>(p);
+    t.g1 = reinterpret_cast<unsigned long long*>(p + ((nt * 4 + 7) & ~7ll));
+    return t;
+}
+inline size_t tile_sums_zero_bytes(long long nt) { return (size_t)((nt + 255) / 256) * 8; }
+
+// Tile t's count into the tables (one thread).
+__device__ __forceinline__ void tile_sums_add(const TileSums& ts, long long t, int cnt) {
+    ts.counts[t] = cnt;
+    if (cnt) atomicAdd(ts.g1 + (t >> 8), (unsigned long long)cnt);
+}
+
+// Elements before tile t: the counts of the earlier tiles of its 256-group
+// and the sums of the earlier 256-groups.  Block-collective (FS_T threads).
+__device__ __forceinline__ long long tile_offset(const TileSums& ts, long long t, long long* s_red) {
+    const int i = threadIdx.x, lane = i & 31, warp = i >> 5;
+    const long long a = t & ~255ll, b1 = t >> 8;
+    long long s = 0;
+    if (a + i < t) s += __ldg(ts.counts + a + i);
+    for (long long k = i; k < b1; k += FS_T) s += (long long)__ldg(ts.g1 + k);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(FULL, s, o);
+    if (lane == 0) s_red[warp] = s;
+    __syncthreads();
+    long long r = 0;
+#pragma unroll
+    for (int w = 0; w < FS_W; ++w) r += s_red[w];
+    return r;
+}
+
+// Chunk-order offsets of this lane's four chunks inside the block (counts c[u]
+// at most 8, so two counts share one scanned word), and the block total.
+__device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[4], int (&off)[4], int& total,
+                                                    int* s_wt, int warp, int lane) {
+    const int pa = __popc(mb[0]) | (__popc(mb[1]) << 16), pb = __popc(mb[2]) | (__popc(mb[3]) << 16);
+    const int ia = warp_incl_scan(pa, lane), ib = warp_incl_scan(pb, lane);
+    const int ta = __shfl_sync(FULL, ia, 31), tb = __shfl_sync(FULL, ib, 31);
+    const int ea = ia - pa, eb = ib - pb;
+    const int t0 = ta & 0xFFFF, t1 = ta >> 16, t2 = tb & 0xFFFF;
+    if (lane == 0) s_wt[warp] = t0 + t1 + t2 + (tb >> 16);
+    __syncthreads();
+    int wbase = 0;
+    total = 0;
+#pragma unroll
+    for (int w = 0; w < FS_W; ++w) {
+        const int x = s_wt[w];
+        wbase += w < warp ? x : 0;
+        total += x;
+    }
+    off[0] = wbase + (ea & 0xFFFF);
+    off[1] = wbase + t0 + (ea >> 16);
+    off[2] = wbase + t0 + t1 + (eb & 0xFFFF);
+    off[3] = wbase + t0 + t1 + t2 + (eb >> 16);
+}
+
+// This lane's four mask bytes (chunks l + 32u of its warp), bits past n clear.
+__device__ __forceinline__ void lane_mask_bytes(const uint8_t* __restrict__ mask, long long base, long long n,
+                                                int warp, int lane, uint32_t (&mb)[4]) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+        uint32_t b = 0;
+        if (f < n) {
+            b = __ldg(mask + (f >> 3));
+            if (f + 8 > n) b &= (1u << (n - f)) - 1u;
         }
-        s_abort = 0;
-        fence_mbar_init();
+        mb[u] = b;
+    }
+}
+
+template <typename B>
+__global__ void __launch_bounds__(FS_T) flat_mask_count_kernel(const B* __restrict__ dense, long long n,
+                                                               uint8_t* __restrict__ mask, TileSums ts) {
+    const long long t = blockIdx.x, base = t * FS_TILE;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ int s_w[FS_W];
+    Vec8<B> v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {  // all loads first
+        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+        v[u].zero();
+        if (f + 8 <= n) v[u].load_global(dense + f);
+        else
+            for (int j = 0; j < 8; ++j)
+                if (f + j < n) v[u].set(j, dense[f + j]);
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+        if (f < n) {
+            const uint32_t b = v[u].nonzero_byte();  // zero-filled past n
+            mask[f >> 3] = (uint8_t)b;
+            cnt += __popc(b);
+        }
+    }
+    cnt = __reduce_add_sync(FULL, cnt);
+    if (lane == 0) s_w[warp] = cnt;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int s = 0;
+#pragma unroll
+        for (int w = 0; w < FS_W; ++w) s += s_w[w];
+        tile_sums_add(ts, t, s);
+    }
+}
+
+// Eight tiles per block: each warp counts one tile's 1024 mask bytes (16 B per
+// lane, two rounds).
+constexpr int FP_TPB = FS_W;
+__global__ void __launch_bounds__(FS_T) flat_mask_popc_kernel(const uint8_t* __restrict__ mask, long long n,
+                                                              long long nt, TileSums ts) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long t = (long long)blockIdx.x * FP_TPB + warp;
+    if (t >= nt) return;
+    const long long base = t * FS_TILE;
+    int cnt = 0;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const long long f = base + 128LL * (lane + 32 * r);  // 16 mask bytes
+        if (f + 128 <= n) {
+            const uint8_t* m = mask + (f >> 3);
+            if ((reinterpret_cast<uintptr_t>(mask) & 15u) == 0) {
+                const uint4 w = __ldg(reinterpret_cast<const uint4*>(m));
+                cnt += __popc(w.x) + __popc(w.y) + __popc(w.z) + __popc(w.w);
+            } else {  // the mask is only 4-byte aligned
+#pragma unroll
+                for (int k = 0; k < 4; ++k) cnt += __popc(__ldg(reinterpret_cast<const uint32_t*>(m) + k));
+            }
+        } else if (f < n) {
+            for (int k = 0; k < 16; ++k) {
+                const long long g = f + 8 * k;
+                if (g < n) {
+                    uint32_t b = __ldg(mask + (g >> 3));
+                    if (g + 8 > n) b &= (1u << (n - g)) - 1u;
+                    cnt += __popc(b);
+                }
+            }
+        }
+    }
+    cnt = __reduce_add_sync(FULL, cnt);
+    if (lane == 0) tile_sums_add(ts, t, cnt);
+}
+
+template <typename B, bool VEC>
+__global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict__ dense, long long n,
+                                                            const uint8_t* __restrict__ mask, TileSums ts,
+                                                            B* __restrict__ vals, long long cap,
+                                                            long long* __restrict__ nnz_out,
+                                                            uint32_t* __restrict__ status) {
+    constexpr int EPV = 16 / (int)sizeof(B);
+    __shared__ __align__(16) B s_val[FS_TILE + EPV];
+    __shared__ int s_wt[FS_W];
+    __shared__ long long s_red[FS_W];
+    const long long t = blockIdx.x, base = t * FS_TILE;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    uint32_t mb[4];
+    lane_mask_bytes(mask, base, n, warp, lane, mb);
+    Vec8<B> v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {  // only chunks with set bits are read
+        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+        v[u].zero();
+        if (mb[u]) {
+            if (f + 8 <= n) v[u].load_global(dense + f);
+            else
+                for (int j = 0; j < 8; ++j)
+                    if (f + j < n) v[u].set(j, dense[f + j]);
+        }
+    }
+    const long long ex = tile_offset(ts, t, s_red);
+    int off[4], total;
+    block_chunk_offsets(mb, off, total, s_wt, warp, lane);
+    if (tid == 0 && t == gridDim.x - 1) *nnz_out = ex + total;
+    // staging index of output element ex + i is sh + i: 16-byte aligned together
+    const int sh = (int)(ex % EPV);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        int p = sh + off[u];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if ((mb[u] >> j) & 1u) s_val[p++] = v[u].get(j);
     }
     __syncthreads();
-
-    // ---------------------------------------------------- look-back warp ----
-    if (warp == PK_CW) {
-        for (int k = 0;; ++k) {
-            const int b = k % PK_NB;
-            const bool ok = __all_sync(FULL, mbar_wait_bounded(&pub[b], (uint32_t)(k / PK_NB) & 1u));
-            if (!ok || s_abort) {
-                if (!ok && lane == 0) {
-                    atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
-                    s_abort = 1;
-                }
-                break;
-            }
-            const long long t = s_tile[b];
-            if (t >= ntiles) break;
-            const int agg = s_agg[b];
-            const long long ex =
-                (long long)lookback_rows<FT_LBW>(states, t, (unsigned long long)agg, status, lane);
-            if (lane == 0) {
-                // values [ex, ex+agg): the 16-byte-aligned part that lies inside
-                // vals_len by one bulk copy, the rest by the compute warps
-                long long a0 = ex, a1 = ex;
-                if (VEC) {
-                    a0 = ex & ~(long long)(EPV - 1);
-                    a1 = min((ex + agg + EPV - 1) & ~(long long)(EPV - 1),
-                             vals_len & ~(long long)(EPV - 1));
-                    if (a1 < a0) a1 = a0;
-                }
-                s_ex[b] = ex;
-                s_va0[b] = a0;
-                s_vend[b] = a1;
-                if (a1 > a0) {
-                    fence_proxy_async_smem();
-                    const uint32_t bytes = (uint32_t)((a1 - a0) * (long long)sizeof(B));
-                    mbar_arrive_expect_tx(&vfull[b], bytes);
-                    bulk_g2s(s_vals + (size_t)b * VCAP, vals + a0, bytes, &vfull[b]);
-                } else {
-                    mbar_arrive(&vfull[b]);
-                }
-            }
-            __syncwarp();
-        }
-        return;
+    const int lim = (int)max(0ll, min((long long)total, cap - ex));
+    if (tid == 0 && ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+    int done = 0;
+    if (VEC) {
+        const int h = min(lim, (EPV - sh) % EPV);  // to the first 16-byte boundary
+        if (tid < h) vals[ex + tid] = s_val[sh + tid];
+        const int nvec = (lim - h) / EPV;
+        for (int q = tid; q < nvec; q += FS_T)
+            *reinterpret_cast<uint4*>(vals + ex + h + (long long)EPV * q) =
+                *reinterpret_cast<const uint4*>(s_val + sh + h + EPV * q);
+        done = h + nvec * EPV;
     }
+    for (int i = done + tid; i < lim; i += FS_T) vals[ex + i] = s_val[sh + i];
+}
 
-    // ------------------------------------------------------ compute warps ----
-    // this thread's G mask bytes (count layout) of tile t, bits past n cleared
-    auto load_bits = [&](long long t) -> uint64_t {
-        if (t >= ntiles) return 0;
-        const long long base = t * TILE;
-        const long long byte0 = (base >> 3) + (long long)G * tid;
-        uint64_t m = 0;
-        if (byte0 + G <= nbytes) {
-            const uint32_t* src = reinterpret_cast<const uint32_t*>(mask + byte0);
-            m = __ldcs(src);
-            if (G == 8) m |= (uint64_t)__ldcs(src + 1) << 32;
-        } else {
-            for (int e = 0; e < G; ++e)
-                if (byte0 + e < nbytes) m |= (uint64_t)mask[byte0 + e] << (8 * e);
-        }
-        const long long e0 = base + 8LL * G * tid;  // element of bit 0
-        if (e0 + 8 * G > n) {
-            const long long keep = n - e0;
-            m = keep <= 0 ? 0 : (m & ((1ull << keep) - 1ull));
-        }
-        return m;
-    };
-    if (tid == 0) s_tile[0] = (long long)atomicAdd(ticket, 1u);
-    named_bar_sync(PK_BAR, PK_CT);
-    uint64_t m_cur = load_bits(s_tile[0]);
-
-    for (int k = 0;; ++k) {
-        const int b = k % PK_NB, bn = (k + 1) % PK_NB;
-        if (tid == 0) s_tile[bn] = (long long)atomicAdd(ticket, 1u);
-        named_bar_sync(PK_BAR, PK_CT);
-        const uint64_t m_next = load_bits(s_tile[bn]);  // consumed next iteration
-        // ---- counts of tile k ----
-        const long long t = s_tile[b];
-        const bool have = t < ntiles;
-        if (have) {
-            uint8_t* mb = s_mb + (size_t)b * CHUNKS;
-            if (G == 8) *reinterpret_cast<uint64_t*>(mb + 8 * tid) = m_cur;
-            else *reinterpret_cast<uint32_t*>(mb + 4 * tid) = (uint32_t)m_cur;
-            const int cnt = __popcll(m_cur);
-            const int inc = warp_incl_scan(cnt, lane);
-            s_off[(size_t)b * PK_CT + tid] = inc - cnt;
-            if (lane == 31) s_wt[b][warp] = inc;
-            named_bar_sync(PK_BAR, PK_CT);
-            if (warp == 0) {
-                const int w = lane < PK_CW ? s_wt[b][lane] : 0;
-                const int wi = warp_incl_scan(w, lane);
-                if (lane < PK_CW) s_wb[b][lane] = wi - w;
-                const int agg = __shfl_sync(FULL, wi, PK_CW - 1);
-                if (lane == 0) {
-                    s_agg[b] = agg;
-                    lookback_publish_relaxed(states, t, (unsigned long long)agg);
-                    mbar_arrive(&pub[b]);
-                }
-            }
-        } else if (tid == 0) {
-            mbar_arrive(&pub[b]);  // tells the look-back warp that the tiles ended
-        }
-
-        // ---- expansion of tile k-1 ----
-        if (k >= 1) {
-            const int bp = (k - 1) % PK_NB;
-            const long long tp = s_tile[bp];
-            if (tp < ntiles) {
-                const bool okp = mbar_wait_bounded(&vfull[bp], (uint32_t)((k - 1) / PK_NB) & 1u);
-                if (named_bar_or(PK_BAR, PK_CT, !okp)) {
-                    if (tid == 0) {
-                        atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
-                        s_abort = 1;
-                        for (int j = 0; j < PK_NB; ++j)
-                            if (s_tile[j] < ntiles) st_relaxed_u64(&states[s_tile[j]], LB_INCL);
-                        (void)mbar_wait_bounded(&vfull[bp], (uint32_t)((k - 1) / PK_NB) & 1u);
-                        for (int j = 0; j < PK_NB; ++j) mbar_arrive(&pub[j]);
-                    }
-                    return;
-                }
-                const long long ex = s_ex[bp], a0 = s_va0[bp], vend = s_vend[bp];
-                const int agg = s_agg[bp];
-                B* sv = s_vals + (size_t)bp * VCAP;
-                if (tid == 0 && ex + agg > vals_len) atomicOr(status, SFFN_STATUS_VALS_SHORT);
-                // values not covered by the bulk copy (none, except at the end of
-                // `vals` or when `vals` is not 16-byte aligned); past vals_len -> 0
-                const long long r0 = max(ex, vend), r1 = ex + agg;
-                if (r0 < r1) {
-                    for (long long i = r0 + tid; i < r1; i += PK_CT) sv[i - a0] = i < vals_len ? vals[i] : B(0);
-                    named_bar_sync(PK_BAR, PK_CT);
-                }
-                const uint8_t* mbp = s_mb + (size_t)bp * CHUNKS;
-                const int* offp = s_off + (size_t)bp * PK_CT;
-                const long long base = tp * TILE;
-                const int nvalid = (int)min((long long)TILE, n - base);
-                const int shift = (int)(ex - a0);
+template <typename B, bool VEC>
+__global__ void __launch_bounds__(FS_T) flat_expand_kernel(const B* __restrict__ vals, long long vals_len,
+                                                           const uint8_t* __restrict__ mask, TileSums ts,
+                                                           long long n, B* __restrict__ out,
+                                                           uint32_t* __restrict__ status) {
+    constexpr int EPV = 16 / (int)sizeof(B);
+    __shared__ __align__(16) B s_val[FS_TILE + 2 * EPV];
+    __shared__ int s_wt[FS_W];
+    __shared__ long long s_red[FS_W];
+    const long long t = blockIdx.x, base = t * FS_TILE;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    uint32_t mb[4];
+    lane_mask_bytes(mask, base, n, warp, lane, mb);  // in flight with the offset's loads
+    const long long ex = tile_offset(ts, t, s_red);
+    int off[4], total;
+    block_chunk_offsets(mb, off, total, s_wt, warp, lane);
+    if (tid == 0 && ex + total > vals_len) atomicOr(status, SFFN_STATUS_VALS_SHORT);
+    // stage vals[ex, ex + total) at staging index sh + i; past vals_len -> 0
+    const int sh = (int)(ex % EPV);
+    const long long a0 = ex - sh;  // 16-byte aligned in `vals` when VEC
+    const int span = sh + total;
+    if (VEC) {
+        for (int q = tid; EPV * q < span; q += FS_T) {
+            const long long g = a0 + (long long)EPV * q;
+            if (g + EPV <= vals_len) {
+                *reinterpret_cast<uint4*>(s_val + EPV * q) = __ldg(reinterpret_cast<const uint4*>(vals + g));
+            } else {
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const int c = tid + PK_CT * g, f = 8 * c;
-                    if (f >= nvalid) continue;
-                    const uint32_t byte = mbp[c];
-                    Vec8<B> o;
-                    o.zero();
-                    if (byte) {
-                        const int ow = c / G, sub = c % G;
-                        const uint64_t mo = owner_bits<G>(mbp, ow);
-                        int r = shift + s_wb[bp][ow >> 5] + offp[ow] +
-                                __popcll(mo & ((1ull << (8 * sub)) - 1ull));
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            if ((byte >> j) & 1u) o.set(j, sv[r++]);
-                    }
-                    if (f + 8 <= nvalid) {
-                        o.store_global_cs(out + base + f);
-                    } else {
-                        for (int j = 0; j < 8; ++j)
-                            if (f + j < nvalid) out[base + f + j] = o.get(j);
-                    }
-                }
+                for (int e = 0; e < EPV; ++e) s_val[EPV * q + e] = g + e < vals_len ? vals[g + e] : B(0);
             }
         }
-        if (!have) break;
-        named_bar_sync(PK_BAR, PK_CT);  // buffers of tile k-1 fully read
-        m_cur = m_next;
+    } else {
+        for (int i = tid; i < span; i += FS_T) s_val[i] = a0 + i < vals_len ? vals[a0 + i] : B(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+        if (f >= n) continue;
+        Vec8<B> o;
+        o.zero();
+        int p = sh + off[u];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if ((mb[u] >> j) & 1u) o.set(j, s_val[p++]);
+        if (f + 8 <= n) o.store_global_cs(out + f);
+        else
+            for (int j = 0; j < 8; ++j)
+                if (f + j < n) out[f + j] = o.get(j);
     }
 }
 
@@ -672,9 +825,12 @@ int launch_pack_v(const B* dense, long long n, uint8_t* mask, B* vals, long long
     return SFFN_OK;
 }
 
+// The single-pass look-back pack, for sffn_flat_pack_noalloc: `scratch` is
+// [0, 16) the tile ticket, then one 8-byte look-back state per 32 KB tile;
+// both are cleared on the stream before the kernel runs.
 template <typename B>
-int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long long cap,
-                int64_t* nnz_dev, void* scratch, uint32_t* status, cudaStream_t st) {
+int launch_pack_lookback(const void* dense, long long n, uint8_t* mask, void* vals, long long cap,
+                         int64_t* nnz_dev, void* scratch, uint32_t* status, cudaStream_t st) {
     const long long nt = flat_tiles<B>(n);
     auto* ticket = static_cast<unsigned int*>(scratch);
     auto* states = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + 16);
@@ -687,36 +843,41 @@ int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long 
     return launch_pack_v<B, false>(d, n, mask, v, cap, nz, states, ticket, status, nt, st);
 }
 
-template <typename B, bool VEC>
-int launch_unpack_v(const B* vals, long long vals_len, const uint8_t* mask, long long n, B* out,
-                    unsigned long long* states, unsigned int* ticket, uint32_t* status,
-                    long long nt, cudaStream_t st) {
-    auto k = flat_unpack_kernel<B, VEC>;
-    const int smem = (int)UnpackCfg<B>::SMEM;
-    SFFN_CUDA_TRY(allow_smem(k, smem));
-    int per_sm = 0;
-    SFFN_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, PK_THREADS, smem));
-    if (per_sm < 1) return SFFN_ERR_CUDA;
-    const long long grid = std::min<long long>(nt, (long long)per_sm * num_sms());
-    k<<<(unsigned)grid, PK_THREADS, smem, st>>>(vals, vals_len, mask, n, out, states, ticket,
-                                                 status, nt);
+template <typename B>
+int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long long cap,
+                int64_t* nnz_dev, void* ws, uint32_t* status, cudaStream_t st) {
+    const long long nt = (n + FS_TILE - 1) / FS_TILE;
+    const TileSums ts = tile_sums(ws, nt);
+    SFFN_CUDA_TRY(cudaMemsetAsync(ts.g1, 0, tile_sums_zero_bytes(nt), st));
+    const B* d = static_cast<const B*>(dense);
+    flat_mask_count_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts);
+    SFFN_CHECK_LAUNCH();
+    B* v = static_cast<B*>(vals);
+    long long* nz = reinterpret_cast<long long*>(nnz_dev);
+    if (aligned16(vals))
+        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, v, cap, nz, status);
+    else
+        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, v, cap, nz, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
 
 template <typename B>
 int launch_unpack(const void* vals, long long vals_len, const uint8_t* mask, long long n, void* out,
-                  void* scratch, uint32_t* status, cudaStream_t st) {
-    const long long nt = flat_tiles<B>(n);
-    auto* ticket = static_cast<unsigned int*>(scratch);
-    auto* states = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) + 16);
-    SFFN_CUDA_TRY(cudaMemsetAsync(scratch, 0, 16 + (size_t)nt * 8, st));
+                  void* ws, uint32_t* status, cudaStream_t st) {
+    const long long nt = (n + FS_TILE - 1) / FS_TILE;
+    const TileSums ts = tile_sums(ws, nt);
+    SFFN_CUDA_TRY(cudaMemsetAsync(ts.g1, 0, tile_sums_zero_bytes(nt), st));
+    flat_mask_popc_kernel<<<(unsigned)((nt + FP_TPB - 1) / FP_TPB), FS_T, 0, st>>>(mask, n, nt, ts);
+    SFFN_CHECK_LAUNCH();
     const B* v = static_cast<const B*>(vals);
+    B* o = static_cast<B*>(out);
     if (aligned16(vals))
-        return launch_unpack_v<B, true>(v, vals_len, mask, n, static_cast<B*>(out), states, ticket,
-                                        status, nt, st);
-    return launch_unpack_v<B, false>(v, vals_len, mask, n, static_cast<B*>(out), states, ticket,
-                                     status, nt, st);
+        flat_expand_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
+    else
+        flat_expand_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
 }
 
 }  // namespace
@@ -854,11 +1015,11 @@ extern "C" int sffn_flat_pack_noalloc(const void* dense, int dtype, int64_t n, u
     }
     void* scratch = nullptr;
     if (int rc = noalloc_scratch(attr.device, &scratch)) return rc;
-    // launch_pack clears the ticket and the states this call uses (the
-    // previous call left its own in the array) before the kernel runs.
+    // launch_pack_lookback clears the ticket and the states this call uses
+    // (the previous call left its own in the array) before the kernel runs.
     if (esize_of(dtype) == 4)
-        return launch_pack<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, scratch,
-                                     status_dev, st);
-    return launch_pack<uint16_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, scratch,
-                                 status_dev, st);
+        return launch_pack_lookback<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, scratch,
+                                              status_dev, st);
+    return launch_pack_lookback<uint16_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, scratch,
+                                          status_dev, st);
 }
