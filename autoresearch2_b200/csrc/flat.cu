@@ -570,16 +570,31 @@ __device__ __forceinline__ long long tile_offset(const TileSums& ts, long long t
     return r;
 }
 
-// Chunk-order offsets of this lane's four chunks inside the block (counts c[u]
-// at most 8, so two counts share one scanned word), and the block total.
-__device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[4], int (&off)[4], int& total,
+// Chunk-order offsets of this lane's G chunks (l + 32u of its warp) inside
+// the block, and the block total.  Two counts (each at most 8, at most 256
+// over the warp) share one scanned word.
+template <int G>
+__device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[G], int (&off)[G], int& total,
                                                     int* s_wt, int warp, int lane) {
-    const int pa = __popc(mb[0]) | (__popc(mb[1]) << 16), pb = __popc(mb[2]) | (__popc(mb[3]) << 16);
-    const int ia = warp_incl_scan(pa, lane), ib = warp_incl_scan(pb, lane);
-    const int ta = __shfl_sync(FULL, ia, 31), tb = __shfl_sync(FULL, ib, 31);
-    const int ea = ia - pa, eb = ib - pb;
-    const int t0 = ta & 0xFFFF, t1 = ta >> 16, t2 = tb & 0xFFFF;
-    if (lane == 0) s_wt[warp] = t0 + t1 + t2 + (tb >> 16);
+    int ex[G], tot[G];
+#pragma unroll
+    for (int h = 0; h < G / 2; ++h) {
+        const int pv = __popc(mb[2 * h]) | (__popc(mb[2 * h + 1]) << 16);
+        const int iv = warp_incl_scan(pv, lane);
+        const int tv = __shfl_sync(FULL, iv, 31);
+        const int ev = iv - pv;
+        ex[2 * h] = ev & 0xFFFF;
+        ex[2 * h + 1] = ev >> 16;
+        tot[2 * h] = tv & 0xFFFF;
+        tot[2 * h + 1] = tv >> 16;
+    }
+    int wsum = 0;
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+        off[u] = wsum + ex[u];
+        wsum += tot[u];
+    }
+    if (lane == 0) s_wt[warp] = wsum;
     __syncthreads();
     int wbase = 0;
     total = 0;
@@ -589,18 +604,18 @@ __device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[4], int
         wbase += w < warp ? x : 0;
         total += x;
     }
-    off[0] = wbase + (ea & 0xFFFF);
-    off[1] = wbase + t0 + (ea >> 16);
-    off[2] = wbase + t0 + t1 + (eb & 0xFFFF);
-    off[3] = wbase + t0 + t1 + t2 + (eb >> 16);
+#pragma unroll
+    for (int u = 0; u < G; ++u) off[u] += wbase;
 }
 
-// This lane's four mask bytes (chunks l + 32u of its warp), bits past n clear.
+// This lane's G mask bytes (chunks l + 32u of its warp; a warp owns 32G
+// chunks from `base`), bits past n clear.
+template <int G>
 __device__ __forceinline__ void lane_mask_bytes(const uint8_t* __restrict__ mask, long long base, long long n,
-                                                int warp, int lane, uint32_t (&mb)[4]) {
+                                                int warp, int lane, uint32_t (&mb)[G]) {
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+    for (int u = 0; u < G; ++u) {
+        const long long f = base + 8LL * (32 * G * warp + lane + 32 * u);
         uint32_t b = 0;
         if (f < n) {
             b = __ldg(mask + (f >> 3));
@@ -610,10 +625,18 @@ __device__ __forceinline__ void lane_mask_bytes(const uint8_t* __restrict__ mask
     }
 }
 
+// Tiles per block of the expand kernel: two for 16-bit types (32 KB of dense
+// output per block), one for 32-bit types.  The compact kernel holds its
+// values in registers and keeps one tile per block (two would halve its
+// occupancy).
+template <typename B>
+constexpr int fs_tpb() { return sizeof(B) == 2 ? 2 : 1; }
+
 template <typename B>
 __global__ void __launch_bounds__(FS_T) flat_mask_count_kernel(const B* __restrict__ dense, long long n,
-                                                               uint8_t* __restrict__ mask, TileSums ts) {
-    const long long t = blockIdx.x, base = t * FS_TILE;
+                                                               uint8_t* __restrict__ mask, TileSums ts,
+                                                               long long t0) {
+    const long long t = t0 + blockIdx.x, base = t * FS_TILE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ int s_w[FS_W];
     Vec8<B> v[4];
@@ -684,59 +707,115 @@ __global__ void __launch_bounds__(FS_T) flat_mask_popc_kernel(const uint8_t* __r
     if (lane == 0) tile_sums_add(ts, t, cnt);
 }
 
+// The chunk's set elements to consecutive places from `dp` (returned advanced).
+template <typename B>
+__device__ __forceinline__ B* put_set(const Vec8<B>& v, uint32_t bits, B* dp) {
+    if constexpr (sizeof(B) == 2) {
+        const uint32_t w[4] = {v.q.x, v.q.y, v.q.z, v.q.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t b0 = (bits >> (2 * q)) & 1u, b1 = (bits >> (2 * q + 1)) & 1u;
+            if (b0) *dp = (B)w[q];
+            dp += b0;
+            if (b1) *dp = (B)(w[q] >> 16);
+            dp += b1;
+        }
+    } else {
+        const uint32_t w[8] = {v.a.x, v.a.y, v.a.z, v.a.w, v.b.x, v.b.y, v.b.z, v.b.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t bj = (bits >> j) & 1u;
+            if (bj) *dp = w[j];
+            dp += bj;
+        }
+    }
+    return dp;
+}
+
+// The chunk rebuilt from consecutive values at `sp` (returned advanced): set
+// elements take the next value, the others zero.
+template <typename B>
+__device__ __forceinline__ const B* take_set(Vec8<B>& o, uint32_t bits, const B* sp) {
+    if constexpr (sizeof(B) == 2) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const uint32_t b0 = (bits >> (2 * q)) & 1u, b1 = (bits >> (2 * q + 1)) & 1u;
+            const uint32_t lo = b0 ? (uint32_t)*sp : 0u;
+            sp += b0;
+            const uint32_t hi = b1 ? (uint32_t)*sp : 0u;
+            sp += b1;
+            w[q] = lo | (hi << 16);
+        }
+        o.q = make_uint4(w[0], w[1], w[2], w[3]);
+    } else {
+        uint32_t w[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t bj = (bits >> j) & 1u;
+            w[j] = bj ? *sp : 0u;
+            sp += bj;
+        }
+        o.a = make_uint4(w[0], w[1], w[2], w[3]);
+        o.b = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    return sp;
+}
+
+// Pack, second kernel: the tile is read again and its set elements
+// (recomputed from the values, so no mask read) are staged in shared memory
+// and written to `vals` at the tile's offset.  VEC: `vals` 16-byte aligned.
+// Indices inside the tile are 32-bit; `rem` elements of it exist.
 template <typename B, bool VEC>
 __global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict__ dense, long long n,
-                                                            const uint8_t* __restrict__ mask, TileSums ts,
+                                                            TileSums ts, long long nt, long long t0,
                                                             B* __restrict__ vals, long long cap,
                                                             long long* __restrict__ nnz_out,
                                                             uint32_t* __restrict__ status) {
     constexpr int EPV = 16 / (int)sizeof(B);
+    constexpr int G = 4;
     __shared__ __align__(16) B s_val[FS_TILE + EPV];
     __shared__ int s_wt[FS_W];
     __shared__ long long s_red[FS_W];
-    const long long t = blockIdx.x, base = t * FS_TILE;
+    const long long t = t0 + (long long)blockIdx.x, base = t * FS_TILE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    uint32_t mb[4];
-    lane_mask_bytes(mask, base, n, warp, lane, mb);
-    Vec8<B> v[4];
+    const int rem = (int)min(n - base, (long long)FS_TILE);
+    const B* db = dense + base;
+    Vec8<B> v[G];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {  // only chunks with set bits are read
-        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
+    for (int u = 0; u < G; ++u) {
+        const int f = 8 * (32 * G * warp + lane + 32 * u);
         v[u].zero();
-        if (mb[u]) {
-            if (f + 8 <= n) v[u].load_global(dense + f);
-            else
-                for (int j = 0; j < 8; ++j)
-                    if (f + j < n) v[u].set(j, dense[f + j]);
-        }
+        if (f + 8 <= rem) v[u].load_global(db + f);
+        else
+            for (int j = 0; j < 8; ++j)
+                if (f + j < rem) v[u].set(j, db[f + j]);
     }
-    const long long ex = tile_offset(ts, t, s_red);
-    int off[4], total;
-    block_chunk_offsets(mb, off, total, s_wt, warp, lane);
-    if (tid == 0 && t == gridDim.x - 1) *nnz_out = ex + total;
+    const long long ex = tile_offset(ts, t, s_red);  // its loads in flight with the values'
+    uint32_t mb[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) mb[u] = v[u].nonzero_byte();  // zero-filled past n
+    int off[G], total;
+    block_chunk_offsets<G>(mb, off, total, s_wt, warp, lane);
+    if (tid == 0 && t + 1 >= nt) *nnz_out = ex + total;
     // staging index of output element ex + i is sh + i: 16-byte aligned together
     const int sh = (int)(ex % EPV);
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        int p = sh + off[u];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if ((mb[u] >> j) & 1u) s_val[p++] = v[u].get(j);
-    }
+    for (int u = 0; u < G; ++u) put_set<B>(v[u], mb[u], s_val + sh + off[u]);
     __syncthreads();
     const int lim = (int)max(0ll, min((long long)total, cap - ex));
     if (tid == 0 && ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+    B* vo = vals + ex;
     int done = 0;
     if (VEC) {
         const int h = min(lim, (EPV - sh) % EPV);  // to the first 16-byte boundary
-        if (tid < h) vals[ex + tid] = s_val[sh + tid];
+        if (tid < h) vo[tid] = s_val[sh + tid];
         const int nvec = (lim - h) / EPV;
         for (int q = tid; q < nvec; q += FS_T)
-            *reinterpret_cast<uint4*>(vals + ex + h + (long long)EPV * q) =
-                *reinterpret_cast<const uint4*>(s_val + sh + h + EPV * q);
+            *reinterpret_cast<uint4*>(vo + h + EPV * q) = *reinterpret_cast<const uint4*>(s_val + sh + h + EPV * q);
         done = h + nvec * EPV;
     }
-    for (int i = done + tid; i < lim; i += FS_T) vals[ex + i] = s_val[sh + i];
+    for (int i = done + tid; i < lim; i += FS_T) vo[i] = s_val[sh + i];
 }
 
 template <typename B, bool VEC>
@@ -745,49 +824,61 @@ __global__ void __launch_bounds__(FS_T) flat_expand_kernel(const B* __restrict__
                                                            long long n, B* __restrict__ out,
                                                            uint32_t* __restrict__ status) {
     constexpr int EPV = 16 / (int)sizeof(B);
-    __shared__ __align__(16) B s_val[FS_TILE + 2 * EPV];
+    constexpr int TPB = fs_tpb<B>(), G = 4 * TPB;
+    __shared__ __align__(16) B s_val[TPB * FS_TILE + 2 * EPV];
     __shared__ int s_wt[FS_W];
     __shared__ long long s_red[FS_W];
-    const long long t = blockIdx.x, base = t * FS_TILE;
+    const long long t = (long long)blockIdx.x * TPB, base = t * FS_TILE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-    uint32_t mb[4];
-    lane_mask_bytes(mask, base, n, warp, lane, mb);  // in flight with the offset's loads
-    const long long ex = tile_offset(ts, t, s_red);
-    int off[4], total;
-    block_chunk_offsets(mb, off, total, s_wt, warp, lane);
+    const int rem = (int)min(n - base, (long long)(TPB * FS_TILE));
+    uint32_t mb[G];
+    {  // mask bytes of chunks l + 32u of the warp, bits past n clear
+        const uint8_t* mbase = mask + (base >> 3);
+#pragma unroll
+        for (int u = 0; u < G; ++u) {
+            const int f = 8 * (32 * G * warp + lane + 32 * u);
+            uint32_t b = 0;
+            if (f < rem) {
+                b = __ldg(mbase + (f >> 3));
+                if (f + 8 > rem) b &= (1u << (rem - f)) - 1u;
+            }
+            mb[u] = b;
+        }
+    }
+    const long long ex = tile_offset(ts, t, s_red);  // its loads in flight with the mask's
+    int off[G], total;
+    block_chunk_offsets<G>(mb, off, total, s_wt, warp, lane);
     if (tid == 0 && ex + total > vals_len) atomicOr(status, SFFN_STATUS_VALS_SHORT);
     // stage vals[ex, ex + total) at staging index sh + i; past vals_len -> 0
     const int sh = (int)(ex % EPV);
     const long long a0 = ex - sh;  // 16-byte aligned in `vals` when VEC
     const int span = sh + total;
+    const long long avail = vals_len - a0;  // values from a0 that exist
+    const B* va = vals + a0;
     if (VEC) {
         for (int q = tid; EPV * q < span; q += FS_T) {
-            const long long g = a0 + (long long)EPV * q;
-            if (g + EPV <= vals_len) {
-                *reinterpret_cast<uint4*>(s_val + EPV * q) = __ldg(reinterpret_cast<const uint4*>(vals + g));
+            if (EPV * q + EPV <= avail) {
+                *reinterpret_cast<uint4*>(s_val + EPV * q) = __ldg(reinterpret_cast<const uint4*>(va + EPV * q));
             } else {
 #pragma unroll
-                for (int e = 0; e < EPV; ++e) s_val[EPV * q + e] = g + e < vals_len ? vals[g + e] : B(0);
+                for (int e = 0; e < EPV; ++e) s_val[EPV * q + e] = EPV * q + e < avail ? va[EPV * q + e] : B(0);
             }
         }
     } else {
-        for (int i = tid; i < span; i += FS_T) s_val[i] = a0 + i < vals_len ? vals[a0 + i] : B(0);
+        for (int i = tid; i < span; i += FS_T) s_val[i] = i < avail ? va[i] : B(0);
     }
     __syncthreads();
+    B* ob = out + base;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
-        if (f >= n) continue;
+    for (int u = 0; u < G; ++u) {
+        const int f = 8 * (32 * G * warp + lane + 32 * u);
+        if (f >= rem) continue;
         Vec8<B> o;
-        o.zero();
-        int p = sh + off[u];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if ((mb[u] >> j) & 1u) o.set(j, s_val[p++]);
-        if (f + 8 <= n) o.store_global_cs(out + f);
+        take_set<B>(o, mb[u], s_val + sh + off[u]);
+        if (f + 8 <= rem) o.store_global_cs(ob + f);
         else
             for (int j = 0; j < 8; ++j)
-                if (f + j < n) out[f + j] = o.get(j);
+                if (f + j < rem) ob[f + j] = o.get(j);
     }
 }
 
@@ -850,14 +941,14 @@ int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long 
     const TileSums ts = tile_sums(ws, nt);
     SFFN_CUDA_TRY(cudaMemsetAsync(ts.g1, 0, tile_sums_zero_bytes(nt), st));
     const B* d = static_cast<const B*>(dense);
-    flat_mask_count_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts);
+    flat_mask_count_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, 0);
     SFFN_CHECK_LAUNCH();
     B* v = static_cast<B*>(vals);
     long long* nz = reinterpret_cast<long long*>(nnz_dev);
     if (aligned16(vals))
-        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, v, cap, nz, status);
+        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, ts, nt, 0, v, cap, nz, status);
     else
-        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, v, cap, nz, status);
+        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, ts, nt, 0, v, cap, nz, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -872,10 +963,11 @@ int launch_unpack(const void* vals, long long vals_len, const uint8_t* mask, lon
     SFFN_CHECK_LAUNCH();
     const B* v = static_cast<const B*>(vals);
     B* o = static_cast<B*>(out);
+    const unsigned nb = (unsigned)((nt + fs_tpb<B>() - 1) / fs_tpb<B>());
     if (aligned16(vals))
-        flat_expand_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
+        flat_expand_kernel<B, true><<<nb, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
     else
-        flat_expand_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
+        flat_expand_kernel<B, false><<<nb, FS_T, 0, st>>>(v, vals_len, mask, ts, n, o, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
