@@ -9,12 +9,12 @@ from .bitsparse import (BitsparseTensor, TensorBuffer, bitsparse_pack, bitsparse
                         check_status, dense_to_tilesparse, get_globals, grad_relu2_,
                         init_sparse_buffer, mask_with_bitmask_, reset_sparse_globals, spAx,
                         tile_unpack)
-from .ffn import FFNSparse, FFNSpRelu2
+from .ffn import FFNSparse, FFNSpRelu2, set_sparse_mma, sparse_mma
 from . import ffn, parallel, sp24, tiled
 
 __all__ = [
     "BitsparseTensor", "TensorBuffer", "bitsparse_pack", "bitsparse_unpack", "check_status",
     "dense_to_tilesparse", "get_globals", "grad_relu2_", "init_sparse_buffer",
     "mask_with_bitmask_", "reset_sparse_globals", "spAx", "tile_unpack", "FFNSparse",
-    "FFNSpRelu2", "parallel", "tiled",
+    "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "parallel", "sp24", "tiled",
 ]
