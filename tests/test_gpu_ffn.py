@@ -98,3 +98,33 @@ def _ffn_against_oracle(sf, act, dtype, T, D, F):
     close(W1g.grad, r["dW1"], tol)
     close(W2g.grad, r["dW2"], tol)
     close(b1g.grad, r["db1"], tol)
+
+
+@pytest.mark.parametrize("shift,expect", [(-3.2, "sp24"), (-0.5, "dense")])
+def test_auto_mode_follows_observed_sparsity(shift, expect):
+    """Auto mode: the first step runs dense and records the activation's
+    non-zero count without waiting; later steps take the 2:4 products when
+    that step had >= AUTO_MIN_SPARSITY zeros.  Both paths give the same result
+    within the bf16 bar."""
+    import autoresearch2_b200 as sf
+    prev = sf.ffn.sparse_mma()
+    sf.ffn.set_sparse_mma("auto")
+    try:
+        T, D, F = 512, 256, 512
+        g = torch.Generator(device="cuda").manual_seed(31)
+        x = torch.randn(T, D, device="cuda", generator=g).to(torch.bfloat16)
+        W1 = (torch.randn(F, D, device="cuda", generator=g) * D ** -0.5).to(torch.bfloat16)
+        W2 = (torch.randn(D, F, device="cuda", generator=g) * F ** -0.5).to(torch.bfloat16)
+        b1 = torch.full((F,), shift, device="cuda", dtype=torch.bfloat16)
+        outs, paths = [], []
+        for _ in range(3):
+            arena = (torch.empty(T * F, device="cuda", dtype=torch.bfloat16),
+                     torch.zeros(1, dtype=torch.int32, device="cuda"))
+            outs.append(sf.FFNSpRelu2.apply(x, W1, W2, arena, b1).float())
+            paths.append(sf.ffn.last_path())
+            torch.cuda.synchronize()
+        assert paths[0] == "dense" and paths[-1] == expect, paths
+        scale = outs[0].abs().max().item() + 1e-6
+        assert (outs[-1] - outs[0]).abs().max().item() <= 2e-2 * scale
+    finally:
+        sf.ffn.set_sparse_mma(prev)
