@@ -289,9 +289,12 @@ def cpu_baseline(sample_tokens):
 
 
 # -------------------------------------------------------------- roofline ----
-# DRAM traffic per launch of the roofline kernel (dram__bytes_read.sum +
-# dram__bytes_write.sum of one ncu capture, summarised under profiles/).
-TRAFFIC_BYTES = {}
+# DRAM traffic per launch of the roofline kernels at T=16384: dram__bytes_read.sum
+# + dram__bytes_write.sum of one ncu capture at T=4096 (up 299.9 + 126.5 MB,
+# activation gradient 331.8 + 200.9 MB; profiles/gemm_kernel_up_down_dgrad_t4096.md)
+# times 4 -- activations, masks and the weight re-reads per row tile all grow
+# with the tokens.
+TRAFFIC_BYTES = {"sffn_ffn_up": 4 * (299.9e6 + 126.5e6), "sffn_ffn_dgrad": 4 * (331.8e6 + 200.9e6)}
 
 
 def kernel_breakdown(timer, steps_recorded, step_ms):
