@@ -707,43 +707,57 @@ __global__ void __launch_bounds__(FS_T) flat_mask_popc_kernel(const uint8_t* __r
     if (lane == 0) tile_sums_add(ts, t, cnt);
 }
 
-// The chunk's set elements to consecutive places from `dp` (returned advanced).
+// Shared-memory store of a 16- or 32-bit value under a predicate (no branch).
+__device__ __forceinline__ void st_shared_if(uint32_t addr, uint16_t v, uint32_t p) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.shared.u16 [%0], %1;\n\t}" ::"r"(addr),
+                 "h"(v), "r"(p)
+                 : "memory");
+}
+__device__ __forceinline__ void st_shared_if(uint32_t addr, uint32_t v, uint32_t p) {
+    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.shared.u32 [%0], %1;\n\t}" ::"r"(addr),
+                 "r"(v), "r"(p)
+                 : "memory");
+}
+
+// The chunk's set elements to consecutive places from shared address `da`
+// (returned advanced): predicated stores, the address stepped by each bit.
 template <typename B>
-__device__ __forceinline__ B* put_set(const Vec8<B>& v, uint32_t bits, B* dp) {
+__device__ __forceinline__ uint32_t put_set(const Vec8<B>& v, uint32_t bits, uint32_t da) {
     if constexpr (sizeof(B) == 2) {
         const uint32_t w[4] = {v.q.x, v.q.y, v.q.z, v.q.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const uint32_t b0 = (bits >> (2 * q)) & 1u, b1 = (bits >> (2 * q + 1)) & 1u;
-            if (b0) *dp = (B)w[q];
-            dp += b0;
-            if (b1) *dp = (B)(w[q] >> 16);
-            dp += b1;
+            st_shared_if(da, (uint16_t)w[q], b0);
+            da += 2 * b0;
+            st_shared_if(da, (uint16_t)(w[q] >> 16), b1);
+            da += 2 * b1;
         }
     } else {
         const uint32_t w[8] = {v.a.x, v.a.y, v.a.z, v.a.w, v.b.x, v.b.y, v.b.z, v.b.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t bj = (bits >> j) & 1u;
-            if (bj) *dp = w[j];
-            dp += bj;
+            st_shared_if(da, w[j], bj);
+            da += 4 * bj;
         }
     }
-    return dp;
+    return da;
 }
 
-// The chunk rebuilt from consecutive values at `sp` (returned advanced): set
-// elements take the next value, the others zero.
+// The chunk rebuilt from consecutive values at `sp`: set elements take the
+// next value, the others zero.  Every slot is read (the read past the last
+// value stays inside the staging buffer) and masked, so there is no branch.
 template <typename B>
-__device__ __forceinline__ const B* take_set(Vec8<B>& o, uint32_t bits, const B* sp) {
+__device__ __forceinline__ void take_set(Vec8<B>& o, uint32_t bits, const B* sp) {
     if constexpr (sizeof(B) == 2) {
         uint32_t w[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
             const uint32_t b0 = (bits >> (2 * q)) & 1u, b1 = (bits >> (2 * q + 1)) & 1u;
-            const uint32_t lo = b0 ? (uint32_t)*sp : 0u;
+            const uint32_t lo = (uint32_t)*sp & (0u - b0);
             sp += b0;
-            const uint32_t hi = b1 ? (uint32_t)*sp : 0u;
+            const uint32_t hi = (uint32_t)*sp & (0u - b1);
             sp += b1;
             w[q] = lo | (hi << 16);
         }
@@ -753,13 +767,12 @@ __device__ __forceinline__ const B* take_set(Vec8<B>& o, uint32_t bits, const B*
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const uint32_t bj = (bits >> j) & 1u;
-            w[j] = bj ? *sp : 0u;
+            w[j] = *sp & (0u - bj);
             sp += bj;
         }
         o.a = make_uint4(w[0], w[1], w[2], w[3]);
         o.b = make_uint4(w[4], w[5], w[6], w[7]);
     }
-    return sp;
 }
 
 // Pack, second kernel: the tile is read again and its set elements
@@ -800,8 +813,9 @@ __global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict_
     if (tid == 0 && t + 1 >= nt) *nnz_out = ex + total;
     // staging index of output element ex + i is sh + i: 16-byte aligned together
     const int sh = (int)(ex % EPV);
+    const uint32_t sbase = smem_u32(s_val) + (uint32_t)(sh * (int)sizeof(B));
 #pragma unroll
-    for (int u = 0; u < G; ++u) put_set<B>(v[u], mb[u], s_val + sh + off[u]);
+    for (int u = 0; u < G; ++u) put_set<B>(v[u], mb[u], sbase + (uint32_t)(off[u] * (int)sizeof(B)));
     __syncthreads();
     const int lim = (int)max(0ll, min((long long)total, cap - ex));
     if (tid == 0 && ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
