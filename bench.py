@@ -257,10 +257,11 @@ def bench_pack(device, p=PACK_P, reps=20):
 
 
 # ---------------------------------------------------------- CPU baseline ----
-def cpu_baseline(sample_tokens):
+def cpu_baseline(sample_tokens, steps=1, warmup=0):
     """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
-    the C restatement of its pack) on the host cores, on `sample_tokens`
-    tokens of the headline workload.  Returns tokens/s."""
+    the C restatement of its pack) on the host cores: `warmup` untimed and
+    `steps` timed samples of `sample_tokens` tokens of the headline workload.
+    Returns tokens/s over the timed samples."""
     import numpy as np
     import oracle
     try:
@@ -276,16 +277,32 @@ def cpu_baseline(sample_tokens):
     dout = rng.standard_normal((T, D), dtype=np.float32)
     pre = x @ W1.T
     b1 = np.full(F, -np.quantile(pre[:256], SPARSITY), dtype=np.float32)
+    arena = np.empty(T * F, dtype=np.float32)
+
+    def sample():
+        r = oracle.ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=b1, code=oracle.F32,
+                               compute=np.float32)
+        oracle.tile_pack(r["z"].astype(np.float32), 128, 128, arena, 0)
+
+    for _ in range(warmup):
+        sample()
     t0 = time.perf_counter()
-    r = oracle.ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=b1, code=oracle.F32,
-                           compute=np.float32)
-    z = r["z"].astype(np.float32)
-    arena = np.empty(z.size, dtype=np.float32)
-    oracle.tile_pack(z, 128, 128, arena, 0)
+    for _ in range(steps):
+        sample()
     dt = time.perf_counter() - t0
-    return {"value": round(T / dt, 1), "unit": "tokens/s", "cores": int(cores), "kind": "port",
-            "sample": f"{T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
-                      f"+ tiled pack of z; {dt:.1f} s"}
+    return {"value": round(steps * T / dt, 1), "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "sample": f"{steps} x {T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
+                      f"+ tiled pack of z, after {warmup} untimed; {dt:.1f} s"}
+
+
+def workload_config(tpg, world, tokens, s_meas=None):
+    """The `config` of both arms' lines."""
+    c = {"workload": f"relu2_ffn_fwd_bwd_d4096_f14336_t{tpg}_s0.9", "tokens_per_gpu": tpg,
+         "global_tokens": tokens, "d_model": D_MODEL, "d_ff": D_FF, "target_sparsity": SPARSITY,
+         "parallelism": f"dp{world}", "l2": "inputs larger than L2"}
+    if s_meas is not None:
+        c["measured_sparsity"] = round(s_meas, 4)
+    return c
 
 
 # -------------------------------------------------------------- roofline ----
@@ -356,12 +373,13 @@ def main():
 
     if args.impl == "reference":
         if rank == 0:
-            cb = cpu_baseline(args.cpu_tokens)
+            # each step: one bounded sample (args.cpu_tokens tokens) of the workload
+            cb = cpu_baseline(args.cpu_tokens, steps=args.steps, warmup=args.warmup)
             line = {"impl": "reference", "metric": METRIC, "value": cb["value"],
-                    "unit": "tokens/s", "n_gpus": args.gpus, "steps": 1, "warmup": 0,
-                    "higher_is_better": True, "dtype": "f32", "data": "synthetic",
-                    "config": {"workload": "relu2_ffn_fwd_bwd_d4096_f14336_s0.9 (CPU sample)",
-                               "tokens_per_gpu": T_PER_GPU},
+                    "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+                    "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
+                    "data": "synthetic (seeded)",
+                    "config": workload_config(tpg, world, tpg * world),
                     "cpu_baseline": cb,
                     "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                             "d2h_bytes_per_step": 0}}
@@ -463,18 +481,15 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
-            "config": {"workload": f"relu2_ffn_fwd_bwd_d4096_f14336_t{tpg}_s0.9",
-                       "tokens_per_gpu": tpg, "global_tokens": tokens, "d_model": D_MODEL,
-                       "d_ff": D_FF, "target_sparsity": SPARSITY,
-                       "measured_sparsity": round(s_meas, 4), "parallelism": f"dp{world}",
-                       "l2": "inputs larger than L2"},
+            "config": workload_config(tpg, world, tokens, s_meas),
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)
         if world == 1 and not args.quick:
             try:
-                line["cpu_baseline"] = cpu_baseline(args.cpu_tokens)
+                # about 10 s of host work: 8 samples after one untimed
+                line["cpu_baseline"] = cpu_baseline(args.cpu_tokens, steps=8, warmup=1)
             except Exception as e:  # noqa: BLE001
                 line["cpu_baseline"] = {"error": repr(e)}
         print(json.dumps(line), flush=True)
