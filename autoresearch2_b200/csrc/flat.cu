@@ -775,12 +775,14 @@ __device__ __forceinline__ void take_set(Vec8<B>& o, uint32_t bits, const B* sp)
     }
 }
 
-// Pack, second kernel: the tile is read again and its set elements
-// (recomputed from the values, so no mask read) are staged in shared memory
-// and written to `vals` at the tile's offset.  VEC: `vals` 16-byte aligned.
+// Pack, second kernel: the tile is read again together with its mask bytes
+// (written by the first kernel; loaded alongside the values, so no extra
+// round trip), its set elements are staged in shared memory and written to
+// `vals` at the tile's offset.  VEC: `vals` 16-byte aligned.
 // Indices inside the tile are 32-bit; `rem` elements of it exist.
 template <typename B, bool VEC>
 __global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict__ dense, long long n,
+                                                            const uint8_t* __restrict__ mask,
                                                             TileSums ts, long long nt, long long t0,
                                                             B* __restrict__ vals, long long cap,
                                                             long long* __restrict__ nnz_out,
@@ -794,20 +796,20 @@ __global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict_
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int rem = (int)min(n - base, (long long)FS_TILE);
     const B* db = dense + base;
+    const uint8_t* mbase = mask + (base >> 3);
     Vec8<B> v[G];
+    uint32_t mb[G];  // the first kernel cleared the bits past n
 #pragma unroll
     for (int u = 0; u < G; ++u) {
         const int f = 8 * (32 * G * warp + lane + 32 * u);
         v[u].zero();
+        mb[u] = f < rem ? (uint32_t)__ldg(mbase + (f >> 3)) : 0u;
         if (f + 8 <= rem) v[u].load_global(db + f);
         else
             for (int j = 0; j < 8; ++j)
                 if (f + j < rem) v[u].set(j, db[f + j]);
     }
     const long long ex = tile_offset(ts, t, s_red);  // its loads in flight with the values'
-    uint32_t mb[G];
-#pragma unroll
-    for (int u = 0; u < G; ++u) mb[u] = v[u].nonzero_byte();  // zero-filled past n
     int off[G], total;
     block_chunk_offsets<G>(mb, off, total, s_wt, warp, lane);
     if (tid == 0 && t + 1 >= nt) *nnz_out = ex + total;
@@ -960,9 +962,9 @@ int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long 
     B* v = static_cast<B*>(vals);
     long long* nz = reinterpret_cast<long long*>(nnz_dev);
     if (aligned16(vals))
-        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, ts, nt, 0, v, cap, nz, status);
+        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, nt, 0, v, cap, nz, status);
     else
-        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, ts, nt, 0, v, cap, nz, status);
+        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, nt, 0, v, cap, nz, status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
