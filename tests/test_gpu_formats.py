@@ -109,6 +109,80 @@ def test_flat_full_size_round_trip(p):
     assert torch.equal(vals, d.view(-1)[keep.view(-1)])
 
 
+def _flat_capi(dtype, n, p, seed):
+    from autoresearch2_b200 import _lib
+    d = flat_case(1, n, p, dtype, seed=seed).view(-1)
+    ov, om = oracle.flat_pack(to_np(d))
+    L = _lib.load()
+    ws = _lib.workspace(L.sffn_flat_workspace_bytes(n), DEV)
+    return _lib, d.to(DEV), ov, om, ws
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_flat_capi_unaligned_vals_and_short_capacity(dtype):
+    """Through the C ABI: `vals` 2 or 4 bytes past a 16-byte boundary (the
+    element-wise write-out) gives the oracle's values; a capacity below nnz
+    writes exactly the first `cap` values, nothing past them, sets
+    SFFN_STATUS_VALS_OVERFLOW and still reports the full nnz."""
+    n = 3 * 8192 + 13
+    _lib, d, ov, om, ws = _flat_capi(dtype, n, 0.3, seed=41)
+    code = _lib.dtype_code(d)
+    nnz = len(ov)
+    st = _lib.stream_ptr(DEV)
+    status = _lib.status_word(DEV)
+    mask = torch.empty((n + 7) // 8, dtype=torch.uint8, device=DEV)
+    nnz_d = torch.zeros(1, dtype=torch.int64, device=DEV)
+    buf = torch.full((nnz + 16,), 7, dtype=dtype, device=DEV)
+    vals = buf[1:]  # one element past the allocation's (16-byte aligned) start
+    _lib.call("sffn_flat_pack", _lib.ptr(d), code, n, _lib.ptr(mask), _lib.ptr(vals), nnz, _lib.ptr(nnz_d),
+              _lib.ptr(ws), ws.numel(), _lib.ptr(status), st)
+    assert _lib.check_status(DEV, raise_on_error=False) == 0
+    bits_equal(to_np(mask), om)
+    bits_equal(to_np(vals[:nnz]), ov)
+    assert int(nnz_d.item()) == nnz
+    cap = nnz // 2 + 3
+    buf.fill_(7)
+    _lib.call("sffn_flat_pack", _lib.ptr(d), code, n, _lib.ptr(mask), _lib.ptr(vals), cap, _lib.ptr(nnz_d),
+              _lib.ptr(ws), ws.numel(), _lib.ptr(status), st)
+    assert _lib.check_status(DEV, raise_on_error=False) == 1  # SFFN_STATUS_VALS_OVERFLOW
+    bits_equal(to_np(vals[:cap]), ov[:cap])
+    assert torch.all(vals[cap:] == 7) and float(buf[0]) == 7
+    assert int(nnz_d.item()) == nnz
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_flat_capi_unpack_unaligned_and_short_vals(dtype):
+    """Through the C ABI: unpack from `vals` off a 16-byte boundary with a mask
+    only 4-byte aligned equals the oracle; with vals_len < nnz the elements
+    whose values are missing come out as zero and SFFN_STATUS_VALS_SHORT is
+    set."""
+    n = 5 * 8192 + 77
+    _lib, d, ov, om, ws = _flat_capi(dtype, n, 0.2, seed=43)
+    code = _lib.dtype_code(d)
+    nnz = len(ov)
+    st = _lib.stream_ptr(DEV)
+    status = _lib.status_word(DEV)
+    vbuf = torch.zeros(nnz + 8, dtype=dtype, device=DEV)
+    vals = vbuf[3:3 + nnz]
+    vals.copy_(to_t(ov))
+    mbuf = torch.zeros(len(om) + 16, dtype=torch.uint8, device=DEV)
+    mask = mbuf[4:4 + len(om)]  # 4-byte but not 16-byte aligned
+    mask.copy_(torch.from_numpy(om).to(DEV))
+    out = torch.full((n,), 5, dtype=dtype, device=DEV)
+    _lib.call("sffn_flat_unpack", _lib.ptr(vals), nnz, _lib.ptr(mask), code, n, _lib.ptr(out), _lib.ptr(ws),
+              ws.numel(), _lib.ptr(status), st)
+    assert _lib.check_status(DEV, raise_on_error=False) == 0
+    want = oracle.flat_unpack(ov, om, (n,))
+    bits_equal(to_np(out), want)
+    short = nnz - 100
+    _lib.call("sffn_flat_unpack", _lib.ptr(vals), short, _lib.ptr(mask), code, n, _lib.ptr(out), _lib.ptr(ws),
+              ws.numel(), _lib.ptr(status), st)
+    assert _lib.check_status(DEV, raise_on_error=False) == 8  # SFFN_STATUS_VALS_SHORT
+    ov_short = ov.copy()
+    ov_short[short:] = 0
+    bits_equal(to_np(out), oracle.flat_unpack(ov_short, om, (n,)))
+
+
 # ----------------------------------------------------------------- tiled ----
 @pytest.mark.parametrize("name", golden_names("tiled_"))
 def test_tile_pack_golden(name):
