@@ -264,8 +264,12 @@ def cpu_baseline(sample_tokens, steps=1, warmup=0):
     Returns tokens/s over the timed samples."""
     import numpy as np
     import oracle
+    # every host core for the BLAS pool, whatever OMP_NUM_THREADS a launcher set
+    # (torchrun sets it to 1 per process)
+    limiter = None
     try:
-        from threadpoolctl import threadpool_info
+        from threadpoolctl import threadpool_info, threadpool_limits
+        limiter = threadpool_limits(limits=os.cpu_count() or 1)
         cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
     except Exception:  # noqa: BLE001
         cores = os.cpu_count() or 1
@@ -290,6 +294,8 @@ def cpu_baseline(sample_tokens, steps=1, warmup=0):
     for _ in range(steps):
         sample()
     dt = time.perf_counter() - t0
+    if limiter is not None:
+        limiter.restore_original_limits()
     return {"value": round(steps * T / dt, 1), "unit": "tokens/s", "cores": int(cores), "kind": "port",
             "sample": f"{steps} x {T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
                       f"+ tiled pack of z, after {warmup} untimed; {dt:.1f} s"}
