@@ -608,23 +608,6 @@ __device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[G], int
     for (int u = 0; u < G; ++u) off[u] += wbase;
 }
 
-// This lane's G mask bytes (chunks l + 32u of its warp; a warp owns 32G
-// chunks from `base`), bits past n clear.
-template <int G>
-__device__ __forceinline__ void lane_mask_bytes(const uint8_t* __restrict__ mask, long long base, long long n,
-                                                int warp, int lane, uint32_t (&mb)[G]) {
-#pragma unroll
-    for (int u = 0; u < G; ++u) {
-        const long long f = base + 8LL * (32 * G * warp + lane + 32 * u);
-        uint32_t b = 0;
-        if (f < n) {
-            b = __ldg(mask + (f >> 3));
-            if (f + 8 > n) b &= (1u << (n - f)) - 1u;
-        }
-        mb[u] = b;
-    }
-}
-
 // Tiles per block of the expand kernel: two for 16-bit types (32 KB of dense
 // output per block), one for 32-bit types.  The compact kernel holds its
 // values in registers and keeps one tile per block (two would halve its
@@ -906,8 +889,6 @@ cudaError_t allow_smem(K kernel, int bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-// `scratch`: [0,16) tile ticket, then one 8-byte look-back state per tile;
-// both are cleared on the stream before the kernel runs.
 int num_sms() {
     int dev = 0, sms = 148;
     if (cudaGetDevice(&dev) == cudaSuccess)
