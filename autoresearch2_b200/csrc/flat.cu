@@ -758,6 +758,48 @@ __device__ __forceinline__ void take_set(Vec8<B>& o, uint32_t bits, const B* sp)
     }
 }
 
+// Expansion of 16-bit elements, four (one mask nibble n) at a time: from the
+// next four staged values packed as x (values 0, 1) and y (values 2, 3),
+// output halfwords 0-1 are __byte_perm(x, 0, low half of nib_take_sel(n)) --
+// bytes 4-5 of the zero word where unset -- and halfwords 2-3 are
+// __byte_perm(x, y, high half) masked by nib_take_mask(n).  (A matching
+// compaction by permutes needs 16 more registers in the compact kernel and
+// measured slower there than the predicated stores.)
+__host__ __device__ constexpr uint32_t nib_take_sel(int n) {
+    uint32_t s = 0;
+    int r = 0;
+    for (int e = 0; e < 4; ++e) {
+        uint32_t pair = e < 2 ? (4u | (5u << 4)) : (0u | (1u << 4));
+        if ((n >> e) & 1) {
+            pair = (uint32_t)((2 * r) | ((2 * r + 1) << 4));
+            ++r;
+        }
+        s |= pair << (8 * e);
+    }
+    return s;
+}
+__host__ __device__ constexpr uint32_t nib_take_mask(int n) {
+    return (((n >> 2) & 1) ? 0x0000FFFFu : 0u) | (((n >> 3) & 1) ? 0xFFFF0000u : 0u);
+}
+static_assert(nib_take_sel(0b1001) == 0x32105410u && nib_take_mask(0b1001) == 0xFFFF0000u, "take table");
+
+// The chunk rebuilt from the consecutive staged values at `sp`.  Reads up to
+// three values past the chunk's last one (inside the staging buffer).
+__device__ __forceinline__ uint4 take_set16(uint32_t bits, const uint16_t* sp, const uint2* s_take) {
+    uint32_t w[4];
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        const uint32_t n = (bits >> (4 * g)) & 15u;
+        const uint32_t x = (uint32_t)sp[0] | ((uint32_t)sp[1] << 16);
+        const uint32_t y = (uint32_t)sp[2] | ((uint32_t)sp[3] << 16);
+        const uint2 t = s_take[n];
+        w[2 * g] = __byte_perm(x, 0u, t.x & 0xFFFFu);
+        w[2 * g + 1] = __byte_perm(x, y, t.x >> 16) & t.y;
+        sp += __popc(n);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 // Pack, second kernel: the tile is read again together with its mask bytes
 // (written by the first kernel; loaded alongside the values, so no extra
 // round trip), its set elements are staged in shared memory and written to
@@ -827,6 +869,9 @@ __global__ void __launch_bounds__(FS_T) flat_expand_kernel(const B* __restrict__
     __shared__ __align__(16) B s_val[TPB * FS_TILE + 2 * EPV];
     __shared__ int s_wt[FS_W];
     __shared__ long long s_red[FS_W];
+    __shared__ uint2 s_take[16];
+    if (threadIdx.x < 16)  // read after the next barrier
+        s_take[threadIdx.x] = make_uint2(nib_take_sel((int)threadIdx.x), nib_take_mask((int)threadIdx.x));
     const long long t = (long long)blockIdx.x * TPB, base = t * FS_TILE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int rem = (int)min(n - base, (long long)(TPB * FS_TILE));
@@ -873,7 +918,8 @@ __global__ void __launch_bounds__(FS_T) flat_expand_kernel(const B* __restrict__
         const int f = 8 * (32 * G * warp + lane + 32 * u);
         if (f >= rem) continue;
         Vec8<B> o;
-        take_set<B>(o, mb[u], s_val + sh + off[u]);
+        if constexpr (sizeof(B) == 2) o.q = take_set16(mb[u], s_val + sh + off[u], s_take);
+        else take_set<B>(o, mb[u], s_val + sh + off[u]);
         if (f + 8 <= rem) o.store_global_cs(ob + f);
         else
             for (int j = 0; j < 8; ++j)
