@@ -370,6 +370,9 @@ def main():
                     help="time the sparse step only: no dense, sweep, e2e, pack or CPU legs")
     ap.add_argument("--pack-only", action="store_true",
                     help="only the flat pack/unpack sweep over p (one JSON line per p)")
+    ap.add_argument("--sparse-mma", default="auto", choices=["auto", "on", "off"],
+                    help="path of the products with a sparse operand: 2:4 sparse tensor cores "
+                         "chosen by the observed sparsity (auto), always, or never")
     args = ap.parse_args()
     tpg = args.tokens
 
@@ -394,6 +397,8 @@ def main():
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    import autoresearch2_b200 as _sf
+    _sf.set_sparse_mma(args.sparse_mma)
     if args.pack_only:
         pk = peaks()
         for p in PACK_SWEEP:
@@ -510,7 +515,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
-            "config": workload_config(tpg, world, tokens, s_meas),
+            "config": workload_config(tpg, world, tokens, s_meas), "sparse_mma": args.sparse_mma,
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
             "gpu_launches": launches_per_step * args.steps,
         }
