@@ -3,18 +3,19 @@
 Reference: Maccy-Z/autoresearch2 (old/lib_sparse/sparse.py, old/sparse_pack.py,
 old/sparse_unpack.py, old/full_matmul/sparse_pack.py).  All compute runs in
 libsparseffn.so (hand-written CUDA for sm_100a behind a C ABI,
-include/sparseffn.h); there is no CPU or fallback path.
+include/sparseffn.h); there is no CPU or fallback path.  The operations are also
+registered as torch.library ops (sparseffn::*, library.py) for torch.compile.
 """
 from .bitsparse import (BitsparseTensor, TensorBuffer, bitsparse_pack, bitsparse_unpack,
                         check_status, dense_to_tilesparse, get_globals, grad_relu2_,
                         init_sparse_buffer, mask_with_bitmask_, reset_sparse_globals, spAx,
                         tile_unpack)
 from .ffn import FFNSparse, FFNSpRelu2, set_sparse_mma, sparse_mma
-from . import ffn, parallel, sp24, tiled
+from . import ffn, library, parallel, sp24, tiled  # library registers the sparseffn:: ops
 
 __all__ = [
     "BitsparseTensor", "TensorBuffer", "bitsparse_pack", "bitsparse_unpack", "check_status",
     "dense_to_tilesparse", "get_globals", "grad_relu2_", "init_sparse_buffer",
     "mask_with_bitmask_", "reset_sparse_globals", "spAx", "tile_unpack", "FFNSparse",
-    "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "parallel", "sp24", "tiled",
+    "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "library", "parallel", "sp24", "tiled",
 ]

@@ -16,14 +16,16 @@ that are zero in a whole 128-row tile; the backward's dout @ W2 epilogue
 applies the mask / 2z gradient from the packed z and emits the activation
 for dW2, so no dense z is kept between forward and backward.  float32 and
 float16 inputs run cuBLAS matmuls with this library's pack/mask kernels
-(64x64 tiles, as in the reference).
+(64x64 tiles, as in the reference).  Forward and backward each run as one
+torch.library op (sparseffn::ffn_fwd, sparseffn::ffn_bwd, registered in
+library.py), so torch.compile traces these Functions without a graph break.
 
 Differences (documented, not inherited defects): FFNSpRelu2 accepts the vals
 arena (the reference's forward omits it and raises TypeError,
 sparse.py:120), both accept an optional up-projection bias b1 [F] as a
-trailing argument (the reference has none), and the fused bf16 backward
-leaves the stored z values unchanged (the reference squares them in place,
-sparse.py:136-144).
+trailing argument (the reference has none), and the backward leaves the
+stored z values unchanged (the reference squares them in place,
+sparse.py:136-144; here z^2 is formed where it is read).
 """
 import torch
 import torch.nn.functional as F
@@ -123,7 +125,10 @@ def _fused_ok(x, W1, W2, b1, vals):
     return D % 8 == 0 and Fd % 8 == 0 and x.shape[0] * Fd < 2 ** 31
 
 
-def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
+def _fused_forward(x, W1, W2, vals, offset, b1, act):
+    """bf16 forward on the tcgen05 kernels.  Returns (out, bitmask, prefix,
+    vals_offset, row_offsets, kb_list, kb_count): the tiled 128x128 z, its
+    per-row value offsets and the live 64-wide K blocks of each 256-row tile."""
     T, D = x.shape
     Fd = W1.shape[0]
     global _last_path
@@ -132,56 +137,77 @@ def _fused_forward(ctx, x, W1, W2, vals, offset, b1, act):
     # with sp24 the up-projection epilogue writes a in the 2:4 form directly
     a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24)
     _observe(W1, prefix, T, D, Fd)
+    # the K-block lists also serve dX when the backward takes the dense path
+    kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
     if use_sp24:
         # 2:4 part on the sparse tensor cores, overflow rows k of W2^T
-        kb_list = kb_count = None
         out = sp24.mm(a, W2.T, bt=sp24.transpose(W2))
-        del a
     else:
-        kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
         out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
-        del a
-    z_sparse = bs.BitsparseTensor(vals, bitmask, prefix, voff, -(-T // 128), -(-Fd // 128), 128, 128,
-                                  (T, Fd))
-    ctx.save_for_backward(x, W1, W2)
-    ctx.z_sparse = z_sparse
-    ctx.kb = (kb_list, kb_count)
-    ctx.row_offsets = row_offsets
-    ctx.has_bias = b1 is not None
-    ctx.fused = True
-    ctx.sp24 = use_sp24
-    return out
+    del a
+    return out, bitmask, prefix, voff, row_offsets, kb_list, kb_count
 
 
-def _fused_backward(ctx, grad_output, act):
-    x, W1, W2 = ctx.saved_tensors
-    z_sparse = ctx.z_sparse
-    ctx.z_sparse = None
-    kb_list, kb_count = ctx.kb
-    ctx.kb = None
+def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_count, has_bias, act):
+    """bf16 backward -> (grad_x, grad_W1, grad_W2, grad_b1 or None).  The
+    products' path is chosen again here, by the same rule as the forward's."""
+    T, D = x.shape
+    Fd = W1.shape[0]
     grad_output = grad_output.contiguous()
     # the bias gradient (column sums of dpre) is summed in the same kernel, in fp32
-    db1 = torch.zeros(W1.shape[0], dtype=torch.float32, device=x.device) if ctx.has_bias else None
-    if ctx.sp24:
+    db1 = torch.zeros(Fd, dtype=torch.float32, device=x.device) if has_bias else None
+    if _sp24_ok(T, D, Fd, W1):
         # the epilogue writes dpre, dpre^T and a^T in the 2:4 form (the
         # transposed ones compressed along the token dimension)
-        dpre, dpre_t, a_t = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1, sp24=True)
-        ctx.row_offsets = None
-        grad_b1 = submit_grad(db1.to(x.dtype)) if ctx.has_bias else None
+        dpre, dpre_t, a_t = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1, sp24=True)
+        del row_offsets
+        grad_b1 = submit_grad(db1.to(x.dtype)) if has_bias else None
         # dW2 = (a^T @ dout)^T, stored transposed by the kernel: [D, F] row-major
         grad_W2 = submit_grad(sp24.mm(a_t, grad_output, trans_out=True))
         del a_t
         grad_x = sp24.mm(dpre, W1)
         grad_W1 = submit_grad(sp24.mm(dpre_t, x))
-        return grad_x, grad_W1, grad_W2, None, grad_b1
-    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, ctx.row_offsets, db1=db1)
-    ctx.row_offsets = None
-    grad_b1 = submit_grad(db1.to(dpre.dtype)) if ctx.has_bias else None
+        return grad_x, grad_W1, grad_W2, grad_b1
+    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
+    del row_offsets
+    grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
     grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
     del a
     grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
     grad_W1 = submit_grad(G.mm(dpre.T, x))
-    return grad_x, grad_W1, grad_W2, None, grad_b1
+    return grad_x, grad_W1, grad_W2, grad_b1
+
+
+def _unfused_forward(x, W1, W2, vals, offset, b1, act):
+    """float32 / float16 (or unaligned) forward: cuBLAS matmuls and this
+    library's 64x64-tile pack.  Returns (out, z_sparse)."""
+    preact = x @ W1.T
+    if b1 is not None:
+        preact += b1
+    z = F.relu(preact)
+    output = (z * z if act == G.ACT_RELU2 else z) @ W2.T
+    z_sparse = bs.dense_to_tilesparse(z, vals, offset)
+    return output, z_sparse
+
+
+def _unfused_backward(grad_output, x, W1, W2, z_sparse, has_bias, act):
+    """-> (grad_x, grad_W1, grad_W2, grad_b1 or None), old/lib_sparse/sparse.py:84-109
+    (ReLU) and :129-151 (ReLU^2)."""
+    grad_output = grad_output.contiguous()
+    grad_z = grad_output @ W2
+    if act == G.ACT_RELU2:
+        # grad_pre = grad_z * 2z; dW2 takes z^2, which the reference stores over
+        # z in place (sparse.py:136-147) -- here it is formed while unpacking, the
+        # same rounding, so the stored z stay unchanged
+        bs.grad_relu2_(grad_z, z_sparse, square=False)
+        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T, square=True))
+    else:
+        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T))
+        bs.mask_with_bitmask_(grad_z, z_sparse)
+    grad_x = grad_z @ W1
+    grad_W1 = submit_grad(grad_z.T @ x)
+    grad_b1 = submit_grad(grad_z.sum(0)) if has_bias else None
+    return grad_x, grad_W1, grad_W2, grad_b1
 
 
 def _arena(sparse_data, numel, like):
@@ -192,42 +218,46 @@ def _arena(sparse_data, numel, like):
     return vals, off
 
 
+def _forward(ctx, x, W1, W2, sparse_data, b1, act):
+    vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
+    fused = _fused_ok(x, W1, W2, b1, vals)
+    # one sparseffn:: op (torch.library), so torch.compile traces through it
+    out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = torch.ops.sparseffn.ffn_fwd(
+        x, W1, W2, b1, vals, offset, act)
+    T, Fd = x.shape[0], W1.shape[0]
+    bm = 128 if fused else 64
+    ctx.save_for_backward(x, W1, W2)
+    # the arena is not saved with save_for_backward: later layers write other
+    # parts of it in place, which would fail autograd's version check
+    ctx.z_sparse = bs.BitsparseTensor(vals, bitmask, prefix, voff, -(-T // bm), -(-Fd // bm), bm, bm,
+                                      (T, Fd))
+    ctx.aux = (row_offsets, kb_list, kb_count)
+    ctx.fused, ctx.has_bias, ctx.act = fused, b1 is not None, act
+    return out
+
+
+def _backward(ctx, grad_output):
+    x, W1, W2 = ctx.saved_tensors
+    z = ctx.z_sparse
+    ctx.z_sparse = None
+    row_offsets, kb_list, kb_count = ctx.aux
+    ctx.aux = None
+    grad_x, grad_W1, grad_W2, grad_b1 = torch.ops.sparseffn.ffn_bwd(
+        grad_output, x, W1, W2, z.vals, z.bitmask, z.prefix, z.vals_offset, row_offsets, kb_list,
+        kb_count, ctx.fused, ctx.has_bias, ctx.act)
+    return grad_x, grad_W1, grad_W2, None, (grad_b1 if ctx.has_bias else None)
+
+
 class FFNSparse(Function):
     """ReLU FFN whose backward rebuilds the ReLU mask from the bitmask."""
 
     @staticmethod
     def forward(ctx, x, W1, W2, sparse_data, b1=None):
-        vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
-        if _fused_ok(x, W1, W2, b1, vals):
-            return _fused_forward(ctx, x, W1, W2, vals, offset, b1, G.ACT_RELU)
-        ctx.fused = False
-        preact = x @ W1.T
-        if b1 is not None:
-            preact += b1
-        z = F.relu(preact)
-        output = z @ W2.T
-        z_sparse = bs.dense_to_tilesparse(z, vals, offset)
-        del z, preact
-        ctx.save_for_backward(x, W1, W2)
-        ctx.z_sparse = z_sparse
-        ctx.has_bias = b1 is not None
-        return output
+        return _forward(ctx, x, W1, W2, sparse_data, b1, G.ACT_RELU)
 
     @staticmethod
     def backward(ctx, grad_output):
-        if ctx.fused:
-            return _fused_backward(ctx, grad_output, G.ACT_RELU)
-        x, W1, W2 = ctx.saved_tensors
-        z_sparse = ctx.z_sparse
-        ctx.z_sparse = None
-        grad_output = grad_output.contiguous()
-        grad_z = grad_output @ W2
-        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T))
-        bs.mask_with_bitmask_(grad_z, z_sparse)
-        grad_x = grad_z @ W1
-        grad_W1 = submit_grad(grad_z.T @ x)
-        grad_b1 = submit_grad(grad_z.sum(0)) if ctx.has_bias else None
-        return grad_x, grad_W1, grad_W2, None, grad_b1
+        return _backward(ctx, grad_output)
 
 
 class FFNSpRelu2(Function):
@@ -235,35 +265,8 @@ class FFNSpRelu2(Function):
 
     @staticmethod
     def forward(ctx, x, W1, W2, sparse_data=None, b1=None):
-        vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
-        if _fused_ok(x, W1, W2, b1, vals):
-            return _fused_forward(ctx, x, W1, W2, vals, offset, b1, G.ACT_RELU2)
-        ctx.fused = False
-        preact = x @ W1.T
-        if b1 is not None:
-            preact += b1
-        z = F.relu(preact)
-        output = (z * z) @ W2.T
-        z_sparse = bs.dense_to_tilesparse(z, vals, offset)
-        del z, preact
-        ctx.save_for_backward(x, W1, W2)
-        ctx.z_sparse = z_sparse
-        ctx.has_bias = b1 is not None
-        return output
+        return _forward(ctx, x, W1, W2, sparse_data, b1, G.ACT_RELU2)
 
     @staticmethod
     def backward(ctx, grad_output):
-        if ctx.fused:
-            return _fused_backward(ctx, grad_output, G.ACT_RELU2)
-        x, W1, W2 = ctx.saved_tensors
-        z_sparse = ctx.z_sparse
-        ctx.z_sparse = None
-        grad_output = grad_output.contiguous()
-        grad_z = grad_output @ W2
-        # grad_pre = grad_z * 2z; the stored z become z^2 for dW2 (sparse.py:136-147)
-        bs.grad_relu2_(grad_z, z_sparse, square=True)
-        grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T, square=False))
-        grad_x = grad_z @ W1
-        grad_W1 = submit_grad(grad_z.T @ x)
-        grad_b1 = submit_grad(grad_z.sum(0)) if ctx.has_bias else None
-        return grad_x, grad_W1, grad_W2, None, grad_b1
+        return _backward(ctx, grad_output)
