@@ -24,6 +24,9 @@ outputs' shapes and dtypes, so tracing needs no device.
         which call them; act is 0 (ReLU) or 1 (ReLU^2).  The ops that write the
         arena carry no autograd formula (torch.library allows none on a
         mutating op): the autograd.Function classes in ffn.py hold that.
+    sparseffn::codec15_compress(data) -> stream
+    sparseffn::codec15_uncompress(stream, shape, dtype) -> data
+        the 15-bit sign-strip codec, bitshifting/code.py:129-177
 
 The fused bf16 path (ffn._fused_ok, decided from dtypes, contiguity and
 shapes alone) keeps z in 128x128 tiles and returns per-row value offsets and
@@ -35,12 +38,14 @@ from typing import Optional
 import torch
 from torch import Tensor
 
+from . import bitshift
 from . import bitsparse as bs
 from . import ffn
 
 __all__ = ["OPS"]
 
-OPS = ("bitsparse_pack", "bitsparse_unpack", "tile_pack", "tile_unpack", "ffn_fwd", "ffn_bwd")
+OPS = ("bitsparse_pack", "bitsparse_unpack", "tile_pack", "tile_unpack", "ffn_fwd", "ffn_bwd",
+       "codec15_compress", "codec15_uncompress")
 
 
 def _cdiv(a, b):
@@ -158,3 +163,26 @@ def _(grad_output, x, W1, W2, vals, bitmask, prefix, vals_offset, row_offsets, k
       fused, has_bias, act):
     return (x.new_empty(x.shape), W1.new_empty(W1.shape), W2.new_empty(W2.shape),
             x.new_empty(W1.shape[0] if has_bias else 0))
+
+
+# ---------------------------------------------------------------------------
+# 15-bit sign-strip codec
+# ---------------------------------------------------------------------------
+@torch.library.custom_op("sparseffn::codec15_compress", mutates_args=())
+def codec15_compress(data: Tensor) -> Tensor:
+    return bitshift.compress_fn(data)
+
+
+@codec15_compress.register_fake
+def _(data):
+    return data.new_empty(bitshift.padded_bytes(data.numel()), dtype=torch.uint8)
+
+
+@torch.library.custom_op("sparseffn::codec15_uncompress", mutates_args=())
+def codec15_uncompress(compressed: Tensor, shape: list[int], dtype: torch.dtype) -> Tensor:
+    return bitshift.uncompress_fn(compressed, shape, dtype)
+
+
+@codec15_uncompress.register_fake
+def _(compressed, shape, dtype):
+    return compressed.new_empty(shape, dtype=dtype)

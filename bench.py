@@ -12,7 +12,9 @@ weak scaling); the only exchange is the NCCL all-reduce of dW1/dW2.
 
 Also reported in the same JSON line: the dense cuBLAS bf16 FFN at the same
 config, the sparsity sweep, standalone pack/unpack GB/s on [65536, 4096]
-bf16 (p = 0.1), the roofline of the dominant kernel, and a CPU baseline.
+bf16 (p = 0.1), the 15-bit sign-strip codec (compress / uncompress GB/s at
+3^16 bf16 values, and the reference harness's round-trip total over
+n = 3^12..3^16), the roofline of the dominant kernel, and a CPU baseline.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -36,6 +38,7 @@ SPARSITY = 0.9
 SWEEP = (0.5, 0.8, 0.95, 0.99)
 PACK_SHAPE, PACK_P = (65536, 4096), 0.1
 PACK_SWEEP = (0.5, 0.2, 0.1, 0.05, 0.01)
+CODEC_SIZES = tuple(3 ** i for i in range(12, 17))  # bitshifting/prepare.py:26
 METRIC = "sparse FFN fwd+bwd tokens/s vs cuBLAS dense @80-95% sparsity; pack GB/s"
 
 
@@ -254,6 +257,71 @@ def bench_pack(device, p=PACK_P, reps=20):
     return {"shape": list(PACK_SHAPE), "p": p, "dtype": "bf16", "algo_bytes": algo,
             "pack_gbs": round(res["pack"]["gbs"], 1), "unpack_gbs": round(res["unpack"]["gbs"], 1),
             "pack_ms": round(res["pack"]["ms"], 4), "unpack_ms": round(res["unpack"]["ms"], 4)}
+
+
+# ----------------------------------------------------------- codec15 ----
+def bench_codec15(device, reps=20, iters=100):
+    """The 15-bit sign-strip codec on |N(0,1)| bf16 data (bitshifting/prepare.py:8-10).
+
+    Kernels: compress and uncompress of 3^16 values through the C ABI with
+    preallocated buffers; median over `reps` calls of CUDA-event time on the
+    launching stream, L2 flushed (a 256 MB buffer zeroed) before each call,
+    since the 86 MB of data fit in L2.  GB/s = (2 n + ceil(15 n / 8)) / time.
+    Harness: the reference's figure -- for each n in 3^12..3^16, the mean of
+    `iters` compress_fn + uncompress_fn round trips through the public API
+    after 5 warm-up ones (prepare.py:29-49), summed over the sizes; checked
+    exact like prepare.py:45."""
+    from autoresearch2_b200 import _lib, bitshift
+    g = torch.Generator(device=device).manual_seed(0)
+    n = CODEC_SIZES[-1]
+    x = torch.randn(n, generator=g, device=device).to(torch.bfloat16).abs()
+    nb = bitshift.compressed_bytes(n)
+    stream = torch.empty(bitshift.padded_bytes(n), dtype=torch.uint8, device=device)
+    back = torch.empty_like(x)
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=device)
+    st = _lib.stream_ptr(device)
+
+    def compress():
+        _lib.call("sffn_codec15_compress", _lib.ptr(x), n, _lib.ptr(stream), stream.numel(), st)
+
+    def uncompress():
+        _lib.call("sffn_codec15_uncompress", _lib.ptr(stream), stream.numel(), n, _lib.ptr(back), st)
+
+    algo = 2 * n + nb
+    res = {"n": n, "algo_bytes": algo}
+    for name, fn in (("compress", compress), ("uncompress", uncompress)):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b))
+        ms = statistics.median(ts)
+        res[f"{name}_gbs"] = round(algo / ms / 1e6, 1)
+        res[f"{name}_ms"] = round(ms, 4)
+    assert torch.equal(back, x)
+    del flush
+    total = 0.0
+    for m in CODEC_SIZES:
+        d = torch.randn(m, generator=g, device=device).to(torch.bfloat16).abs()
+        for _ in range(5):
+            bitshift.uncompress_fn(bitshift.compress_fn(d), d.shape, torch.bfloat16)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            out = bitshift.uncompress_fn(bitshift.compress_fn(d), d.shape, torch.bfloat16)
+        b.record()
+        b.synchronize()
+        assert torch.equal(out, d)
+        total += a.elapsed_time(b) / iters
+    res["harness_total_ms"] = round(total, 4)
+    res["harness_sizes"] = list(CODEC_SIZES)
+    return res
 
 
 # ---------------------------------------------------------- CPU baseline ----
@@ -497,7 +565,7 @@ def main():
 
     pk = peaks()
     roof = roofline(kernels, tpg, pk)
-    pack = None
+    pack = codec = None
     if rank == 0 and not args.quick:
         pack = bench_pack(device)
         pack["pack_frac_of_measured_hbm"] = round(pack["pack_gbs"] / pk["hbm_gbs"], 3)
@@ -508,6 +576,9 @@ def main():
                 r = bench_pack(device, p, reps=10)
                 sweep_p[str(p)] = {"pack_gbs": r["pack_gbs"], "unpack_gbs": r["unpack_gbs"]}
         pack["sweep_p"] = sweep_p
+        codec = bench_codec15(device)
+        for k in ("compress", "uncompress"):
+            codec[f"{k}_frac_of_measured_hbm"] = round(codec[f"{k}_gbs"] / pk["hbm_gbs"], 3)
 
     if rank == 0:
         line = {
@@ -517,6 +588,7 @@ def main():
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
             "config": workload_config(tpg, world, tokens, s_meas), "sparse_mma": args.sparse_mma,
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
+            "codec15": codec,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)

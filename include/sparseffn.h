@@ -330,6 +330,28 @@ int sffn_ffn_dgrad_sp24(const void* dout, int64_t ld_dout, const void* w2, int64
                         const sffn_sp24_mat* dpre_t, const sffn_sp24_mat* act_t, float* db1_sum,
                         uint32_t* status_dev, void* stream);
 
+/* ---- 15-bit sign-strip codec --------------------------------------------
+ * n 16-bit words (bf16 / fp16 bit patterns of non-negative values) <-> a byte
+ * stream of ceil(15 n / 8) bytes, value i at stream bits [15 i, 15 i + 15),
+ * little-endian.  The bytes are the reference's for every input: a set sign
+ * bit of word i is OR-ed into stream bit 15 (i + 1) unless i % 8 == 7, as
+ * its byte formula does (bitshifting/code.py:39-69).  Word and byte buffers
+ * must not overlap; words are 2-byte aligned.  Sizes up to 2^40 words.
+ */
+
+/* ceil(15 n / 8): packed bytes of n words (bitshifting/code.py:135); -1 for n < 0. */
+int64_t sffn_codec15_bytes(int64_t n);
+
+/* compress_fn(data) (bitshifting/code.py:129-160): writes exactly
+ * sffn_codec15_bytes(n) bytes of dst (dst_bytes may be larger; the rest is
+ * left as it is -- the reference leaves its 8-9 padding bytes unset too). */
+int sffn_codec15_compress(const void* src, int64_t n, uint8_t* dst, int64_t dst_bytes, void* stream);
+
+/* uncompress_fn(compressed, shape, dtype) (bitshifting/code.py:163-177):
+ * dst[i] = field i (sign bit 0).  Reads only the first sffn_codec15_bytes(n)
+ * of src's src_bytes. */
+int sffn_codec15_uncompress(const uint8_t* src, int64_t src_bytes, int64_t n, void* dst, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -340,3 +340,40 @@ def sp24_project(vals, nib):
     np.put_along_axis(out, i0[..., None], v[..., 0:1], -1)
     np.put_along_axis(out, i1[..., None], v[..., 1:2], -1)
     return out.reshape(M, K)
+
+
+# ---------------------------------------------------------------------------
+# 15-bit sign-strip codec (bitshifting/code.py)
+# ---------------------------------------------------------------------------
+def codec15_bytes(n):
+    """Length of the packed stream of n values: ceil(15 n / 8) bytes (code.py:135)."""
+    return (15 * n + 7) // 8
+
+
+def codec15_compress(bits):
+    """Pack 16-bit words into a stream of 15-bit fields, value i at stream bits
+    [15 i, 15 i + 15), bytes little-endian.  Follows the reference's byte
+    formula (code.py:39-69): byte b starts at stream bit 8 b, inside value
+    i = 8 b // 15 at offset o = 8 b % 15, and is ((v[i] >> o) | (v[i+1] << (15 - o)))
+    & 0xFF with v[n] = 0.  The full 16-bit words enter that formula, so a set
+    sign bit of v[i] lands on stream bit 15 (i + 1) whenever the byte holding
+    that bit starts inside v[i] (15 (i + 1) % 8 != 0); for non-negative data,
+    the codec's intended input, the stream is exactly the 15-bit fields."""
+    v = np.asarray(bits, dtype=np.uint16).reshape(-1).astype(np.uint32)
+    n = v.size
+    b = np.arange(codec15_bytes(n), dtype=np.int64)
+    i = (8 * b) // 15
+    o = ((8 * b) % 15).astype(np.uint32)
+    vp = np.concatenate([v, np.zeros(1, np.uint32)])
+    return (((vp[i] >> o) | (vp[i + 1] << (15 - o))) & 0xFF).astype(np.uint8)
+
+
+def codec15_uncompress(stream, n):
+    """Value i = stream bits [15 i, 15 i + 15), sign bit 0 (code.py:98-122)."""
+    s = np.zeros(codec15_bytes(n) + 4, np.uint8)
+    s[:codec15_bytes(n)] = np.asarray(stream, dtype=np.uint8).reshape(-1)[:codec15_bytes(n)]
+    k = 15 * np.arange(n, dtype=np.int64)
+    byte, sh = k // 8, (k % 8).astype(np.uint32)
+    w = (s[byte].astype(np.uint32) | (s[byte + 1].astype(np.uint32) << 8)
+         | (s[byte + 2].astype(np.uint32) << 16))
+    return ((w >> sh) & 0x7FFF).astype(np.uint16)

@@ -280,6 +280,52 @@ def gen_ffn(mods, out):
                             dW2_dense=_np(W2d.grad), nnz=_np(off))
 
 
+def _import_codec15(ref):
+    """bitshifting/code.py, loaded by path (its module name would shadow the
+    standard library's ``code``)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("ref_codec15", os.path.join(ref, "bitshifting", "code.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def gen_codec15(ref, out):
+    """The 15-bit sign-strip codec (bitshifting/code.py:129-177).  Its kernels
+    are autotuned, and the autotuner needs a driver, so each is launched
+    through the autotuner's own function with one of its configurations
+    (BLOCK_SIZE 256) and the grid its public function computes; the output
+    buffer is the one compress_fn allocates, zero-filled so that its padding
+    is defined.  Data as bitshifting/prepare.py:8-10 (|randn| bf16), plus raw
+    16-bit patterns with the sign bit set, which the reference does not strip
+    cleanly (its byte formula ORs the sign into the next value's bit 0)."""
+    import math
+    import triton
+    m = _import_codec15(ref)
+    g = torch.Generator().manual_seed(3)
+    cases = [("bf16_n1", 1, "abs"), ("bf16_n7", 7, "abs"), ("bf16_n16", 16, "abs"),
+             ("bf16_n17", 17, "abs"), ("bf16_n1000", 1000, "abs"), ("f16_n333", 333, "abs16"),
+             ("raw_n2187", 2187, "raw")]
+    for name, n, kind in cases:
+        if kind == "raw":
+            bits = torch.randint(0, 1 << 16, (n,), generator=g, dtype=torch.int32).to(torch.int16)
+            bits = bits.view(torch.uint16)
+        else:
+            dt = torch.float16 if kind == "abs16" else torch.bfloat16
+            bits = torch.randn(n, generator=g).to(dt).abs().view(torch.uint16)
+        cb = (n * 15 + 7) // 8
+        padded = cb + 8
+        padded += padded & 1
+        comp = torch.zeros(padded, dtype=torch.uint8)
+        m._compress_15bit_kernel.fn[(triton.cdiv(cb, 256),)](bits, comp, n, cb, BLOCK_SIZE=256)
+        restored = torch.empty(n, dtype=torch.uint16)
+        m._uncompress_15bit_kernel.fn[(triton.cdiv(n, 256),)](comp.view(torch.uint16), restored, n, cb,
+                                                              BLOCK_SIZE=256)
+        out[f"codec15_{name}"] = dict(bits=bits.numpy(), compressed=comp[:cb].numpy(),
+                                      restored=restored.numpy())
+        assert math.prod(restored.shape) == n
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default="/root/reference")
@@ -290,6 +336,7 @@ def main():
     gen_flat(mods, out)
     gen_tiled(mods, out)
     gen_ffn(mods, out)
+    gen_codec15(args.ref, out)
     for name, rec in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
         print(name, {k: v.shape for k, v in rec.items()})

@@ -78,6 +78,23 @@ def test_host_side_rejections(lib):
                                 1, 64, None) == 1
 
 
+def test_codec15_host_checks(lib):
+    vp = ctypes.c_void_p
+    lib.sffn_codec15_bytes.restype = ctypes.c_int64
+    lib.sffn_codec15_bytes.argtypes = [ctypes.c_int64]
+    assert [lib.sffn_codec15_bytes(n) for n in (0, 1, 8, 16, 17, -1)] == [0, 2, 15, 30, 32, -1]
+    words, stream = vp(1 << 20), vp(1 << 24)  # never dereferenced
+    assert lib.sffn_codec15_compress(None, 0, None, 0, None) == 0  # empty: nothing to do
+    assert lib.sffn_codec15_compress(words, -1, stream, 10, None) == 1
+    assert lib.sffn_codec15_compress(None, 5, stream, 10, None) == 1
+    assert lib.sffn_codec15_compress(words, 16, stream, 29, None) == 1  # stream needs 30 bytes
+    assert lib.sffn_codec15_compress(vp((1 << 20) + 1), 16, stream, 30, None) == 3
+    assert lib.sffn_codec15_compress(words, 16, vp((1 << 20) + 31), 30, None) == 1  # overlap
+    assert lib.sffn_codec15_uncompress(stream, 31, 17, words, None) == 1  # stream needs 32 bytes
+    assert lib.sffn_codec15_uncompress(stream, 30, 16, vp((1 << 24) - 2), None) == 1  # overlap
+    assert lib.sffn_codec15_uncompress(stream, 30, 1 << 41, words, None) == 1  # beyond 2^40 words
+
+
 def test_python_api_refuses_cpu_tensors():
     import torch
     import autoresearch2_b200 as sf

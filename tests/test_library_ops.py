@@ -37,6 +37,16 @@ def test_flat_fake_kernels():
         assert out.shape == (37, 53) and out.dtype == torch.bfloat16 and out.is_cuda
 
 
+def test_codec15_fake_kernels():
+    with fake_mode():
+        d = torch.empty(9, 37, device="cuda", dtype=torch.bfloat16)
+        stream = ops.codec15_compress(d)
+        nb = (9 * 37 * 15 + 7) // 8 + 8
+        assert stream.shape == (nb + nb % 2,) and stream.dtype == torch.uint8
+        out = ops.codec15_uncompress(stream, [9, 37], torch.float16)
+        assert out.shape == (9, 37) and out.dtype == torch.float16 and out.is_cuda
+
+
 @pytest.mark.parametrize("bm,bn", [(64, 64), (128, 128), (64, 128)])
 def test_tile_fake_kernels(bm, bn):
     with fake_mode():

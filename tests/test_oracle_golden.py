@@ -128,3 +128,27 @@ def test_sp24_oracle_split_is_lossless():
         assert np.all((nib & 3) < (nib >> 2))
         meta = oracle.sp24_meta(nib)
         assert meta.shape == (2, 4, 128, 4)
+
+
+@pytest.mark.parametrize("name", golden_names("codec15_"))
+def test_codec15_matches_reference(name):
+    g = golden(name)
+    n = g["bits"].size
+    comp = oracle.codec15_compress(g["bits"])
+    np.testing.assert_array_equal(comp, g["compressed"])
+    np.testing.assert_array_equal(oracle.codec15_uncompress(comp, n), g["restored"])
+    if not name.startswith("codec15_raw"):  # non-negative data round-trips exactly
+        np.testing.assert_array_equal(g["restored"], g["bits"])
+
+
+def test_codec15_sign_lands_on_the_next_field():
+    """A set sign bit of value i reaches bit 0 of value i + 1 exactly when the
+    byte that holds stream bit 15 (i + 1) starts inside value i."""
+    for i in range(16):
+        bits = np.zeros(17, np.uint16)
+        bits[i] = 0x8000
+        got = oracle.codec15_uncompress(oracle.codec15_compress(bits), 17)
+        want = np.zeros(17, np.uint16)
+        if (15 * (i + 1)) % 8:
+            want[i + 1] = 1
+        np.testing.assert_array_equal(got, want)
