@@ -324,6 +324,24 @@ def bench_codec15(device, reps=20, iters=100):
     return res
 
 
+# -------------------------------------------------------------- deep ----
+def bench_deep(device):
+    """The reference's multi-layer harness (old/lib_sparse/prepare.py:115-148):
+    4 residual ReLU FFN layers, width 4096, hidden 21504, 10000 tokens, bf16,
+    Xavier weights; dense baseline (dense ReLU output kept per layer) against
+    the sparse stack over one arena of 0.55 x the dense activation size.
+    Peak MB from torch's allocator, ms per step by host clock around
+    synchronised steps (as the harness); eager, no torch.compile."""
+    from autoresearch2_b200 import deep
+    g = torch.Generator(device=device).manual_seed(0)
+    x = torch.randn(10000, 4096, generator=g, device=device, dtype=torch.bfloat16)
+    model = deep.DeepFFN(torch.bfloat16, layers=4, hidm=4096, device=device)
+    r = deep.memory_report(x, model)
+    del model, x
+    torch.cuda.empty_cache()
+    return r
+
+
 # ---------------------------------------------------------- CPU baseline ----
 def cpu_baseline(sample_tokens, steps=1, warmup=0):
     """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
@@ -565,7 +583,7 @@ def main():
 
     pk = peaks()
     roof = roofline(kernels, tpg, pk)
-    pack = codec = None
+    pack = codec = deep_ffn = None
     if rank == 0 and not args.quick:
         pack = bench_pack(device)
         pack["pack_frac_of_measured_hbm"] = round(pack["pack_gbs"] / pk["hbm_gbs"], 3)
@@ -577,6 +595,7 @@ def main():
                 sweep_p[str(p)] = {"pack_gbs": r["pack_gbs"], "unpack_gbs": r["unpack_gbs"]}
         pack["sweep_p"] = sweep_p
         codec = bench_codec15(device)
+        deep_ffn = bench_deep(device)
         for k in ("compress", "uncompress"):
             codec[f"{k}_frac_of_measured_hbm"] = round(codec[f"{k}_gbs"] / pk["hbm_gbs"], 3)
 
@@ -588,7 +607,7 @@ def main():
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
             "config": workload_config(tpg, world, tokens, s_meas), "sparse_mma": args.sparse_mma,
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
-            "codec15": codec,
+            "codec15": codec, "deep_ffn": deep_ffn,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)
