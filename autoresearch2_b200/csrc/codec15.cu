@@ -12,9 +12,12 @@
 //
 // Work unit: a group of 16 values = 240 bits = 30 bytes, self-contained
 // (15 * 16 % 8 == 0, and value 16g + 15 has i % 8 == 7).  One thread per
-// group, 256 groups (4096 values, 7680 bytes) per CTA; the 30-byte records
+// group, 256 groups (4096 values, 7680 bytes) per tile; the 30-byte records
 // are staged in shared memory so that global reads and writes of the packed
 // side are 16-byte vectors at 16-byte aligned offsets (7680 = 480 * 16).
+// Compress: one tile per CTA, values loaded straight into registers.
+// Uncompress: persistent CTAs, the next tile's stream bytes copied into a
+// second shared buffer (cp.async) while the current tile is decoded.
 // Both kernels are HBM-bound: 2 n + ceil(15 n / 8) bytes per call.
 #include "common.cuh"
 
@@ -86,45 +89,71 @@ __global__ void __launch_bounds__(C15_T) codec15_compress_kernel(const uint16_t*
     }
 }
 
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+// Stream bytes of tile t into a shared buffer: whole 16-byte-aligned tiles by
+// asynchronous 16-byte copies, the last (partial) tile or an unaligned
+// stream by plain byte loads with zero fill.  Always closes one copy group.
+__device__ __forceinline__ void c15_fetch(const uint8_t* __restrict__ src, long long nbytes, long long t,
+                                          long long tiles, bool vec_in, uint8_t* buf) {
+    if (t < tiles) {
+        const long long b0 = t * C15_BLOCK_BYTES;
+        const long long left = nbytes - b0;
+        if (vec_in && left >= C15_BLOCK_BYTES) {
+            for (int q = threadIdx.x; q < C15_BLOCK_BYTES / 16; q += C15_T) cp_async16(buf + 16 * q, src + b0 + 16 * q);
+        } else {
+            for (int q = threadIdx.x; q < C15_BLOCK_BYTES; q += C15_T) buf[q] = q < left ? __ldg(src + b0 + q) : 0;
+        }
+    }
+    cp_async_commit();
+}
+
+// Persistent over tiles (stride gridDim.x), two shared buffers: the next
+// tile's bytes are in flight while the current one is decoded and stored.
 __global__ void __launch_bounds__(C15_T) codec15_uncompress_kernel(const uint8_t* __restrict__ src,
                                                                    long long nbytes, long long n,
                                                                    uint16_t* __restrict__ dst, bool vec_in,
                                                                    bool vec_out) {
-    __shared__ __align__(16) uint8_t sbuf[C15_BLOCK_BYTES];
-    const long long blk_b = (long long)blockIdx.x * C15_BLOCK_BYTES;
-    const long long left = nbytes - blk_b;
-    const int bytes = left < C15_BLOCK_BYTES ? (int)left : C15_BLOCK_BYTES;
-    if (vec_in && bytes == C15_BLOCK_BYTES) {
-        const uint4* s = reinterpret_cast<const uint4*>(src + blk_b);
-        uint4* d = reinterpret_cast<uint4*>(sbuf);
-        for (int q = threadIdx.x; q < C15_BLOCK_BYTES / 16; q += C15_T) d[q] = __ldg(s + q);
-    } else {
-        for (int q = threadIdx.x; q < C15_BLOCK_BYTES; q += C15_T) sbuf[q] = q < bytes ? __ldg(src + blk_b + q) : 0;
-    }
-    __syncthreads();
-    const uint16_t* s16 = reinterpret_cast<const uint16_t*>(sbuf + C15_GROUP_BYTES * threadIdx.x);
-    uint32_t w[8];
+    __shared__ __align__(16) uint8_t sbuf[2][C15_BLOCK_BYTES];
+    const long long tiles = (n + C15_BLOCK_VALS - 1) / C15_BLOCK_VALS;
+    int stage = 0;
+    c15_fetch(src, nbytes, blockIdx.x, tiles, vec_in, sbuf[0]);
+    for (long long t = blockIdx.x; t < tiles; t += gridDim.x) {
+        c15_fetch(src, nbytes, t + gridDim.x, tiles, vec_in, sbuf[stage ^ 1]);
+        cp_async_wait_one();  // this thread's copies of tile t have landed
+        __syncthreads();      // ... and every thread's
+        const uint16_t* s16 = reinterpret_cast<const uint16_t*>(sbuf[stage] + C15_GROUP_BYTES * threadIdx.x);
+        uint32_t w[8];
 #pragma unroll
-    for (int j = 0; j < 7; ++j) w[j] = c15_join(s16[2 * j], s16[2 * j + 1]);
-    w[7] = s16[14];
-    uint32_t v[16];
+        for (int j = 0; j < 7; ++j) w[j] = c15_join(s16[2 * j], s16[2 * j + 1]);
+        w[7] = s16[14];
+        uint32_t v[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int p = 15 * i;
-        uint32_t x = w[p >> 5] >> (p & 31);
-        if ((p & 31) > 17) x |= w[(p >> 5) + 1] << (32 - (p & 31));
-        v[i] = x & 0x7FFFu;
-    }
-    const long long v0 = (long long)blockIdx.x * C15_BLOCK_VALS + 16 * threadIdx.x;
-    if (vec_out && v0 + 16 <= n) {
-        uint4* d = reinterpret_cast<uint4*>(dst + v0);
-        d[0] = make_uint4(c15_join(v[0], v[1]), c15_join(v[2], v[3]), c15_join(v[4], v[5]), c15_join(v[6], v[7]));
-        d[1] = make_uint4(c15_join(v[8], v[9]), c15_join(v[10], v[11]), c15_join(v[12], v[13]),
-                          c15_join(v[14], v[15]));
-    } else {
+        for (int i = 0; i < 16; ++i) {
+            const int p = 15 * i;
+            uint32_t x = w[p >> 5] >> (p & 31);
+            if ((p & 31) > 17) x |= w[(p >> 5) + 1] << (32 - (p & 31));
+            v[i] = x & 0x7FFFu;
+        }
+        const long long v0 = t * C15_BLOCK_VALS + 16 * threadIdx.x;
+        if (vec_out && v0 + 16 <= n) {
+            uint4* d = reinterpret_cast<uint4*>(dst + v0);
+            d[0] = make_uint4(c15_join(v[0], v[1]), c15_join(v[2], v[3]), c15_join(v[4], v[5]),
+                              c15_join(v[6], v[7]));
+            d[1] = make_uint4(c15_join(v[8], v[9]), c15_join(v[10], v[11]), c15_join(v[12], v[13]),
+                              c15_join(v[14], v[15]));
+        } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-            if (v0 + i < n) dst[v0 + i] = (uint16_t)v[i];
+            for (int i = 0; i < 16; ++i)
+                if (v0 + i < n) dst[v0 + i] = (uint16_t)v[i];
+        }
+        __syncthreads();  // sbuf[stage] is refilled two tiles from now
+        stage ^= 1;
     }
 }
 
@@ -169,7 +198,11 @@ extern "C" int sffn_codec15_uncompress(const uint8_t* src, int64_t src_bytes, in
     if (int rc = bind_device_of(src)) return rc;
     const bool vec_in = reinterpret_cast<uintptr_t>(src) % 16 == 0;
     const bool vec_out = reinterpret_cast<uintptr_t>(dst) % 16 == 0;
-    codec15_uncompress_kernel<<<blocks, C15_T, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+    // persistent: 8 CTAs (2048 threads) per SM at most
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const unsigned cap = 8u * (unsigned)(sms > 0 ? sms : 148);
+    codec15_uncompress_kernel<<<blocks < cap ? blocks : cap, C15_T, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         src, sffn_codec15_bytes(n), n, static_cast<uint16_t*>(dst), vec_in, vec_out);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;

@@ -129,20 +129,21 @@ def run_step(x, model, sparse, steps=1):
 
 
 def memory_report(x, model, fill=0.55, steps=2):
-    """Dense and sparse steps of the same model on the same input (the
-    reference's evaluate(), prepare.py:115-148, with its asserts restated as
-    measurements): peak MB and ms per step of each, also as MB above what
-    was resident before the steps (weights, input, other live tensors; the
-    arena counts in the sparse step's), the arena's capacity and the
-    fraction of it the last sparse step used, and the largest relative
-    difference of loss and of gradient std between the two."""
+    """Dense and sparse steps of the same model on the same input, each after
+    one warm-up step (the reference's evaluate(), prepare.py:115-148, with its
+    asserts restated as measurements): peak MB and ms per step of each, also
+    as MB above what was resident before the steps (weights, input, other
+    live tensors; the arena counts in the sparse step's), the arena's
+    capacity and the fraction of it the last sparse step used, and the
+    largest relative difference of loss and of gradient std between the two."""
     layers = len(model.W1s)
     hidm = x.shape[-1]
     bs.init_sparse_buffer(0, x.device, x.dtype)  # no arena while the dense step is measured
     model.zero_grad()
     gc.collect()
     resident = torch.cuda.memory_allocated(x.device) / 1024 ** 2  # weights, input, anything else live
-    loss_d, gs_d, peak_d, ms_d = run_step(x, model, sparse=False, steps=1)
+    run_step(x, model, sparse=False, steps=1)  # warm-up
+    loss_d, gs_d, peak_d, ms_d = run_step(x, model, sparse=False, steps=steps)
     cap = arena_elements(x.shape[0], hidm, layers, fill, model.W1s[0].shape[0] / hidm)
     buf = bs.init_sparse_buffer(cap, x.device, x.dtype)
     run_step(x, model, sparse=True, steps=steps)  # warm-up

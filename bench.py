@@ -572,11 +572,21 @@ def main():
         for s in SWEEP:
             xs, W1s, W2s, b1s, dos = make_ffn_inputs(tpg, D_MODEL, D_FF, s, device)
             st = Step(xs, W1s, W2s, b1s, dos)
-            sm = time_steps(st, max(3, args.steps // 2), 2, device)
-            dm = time_steps(DenseStep(xs, W1s, W2s, b1s, dos), max(3, args.steps // 2), 2, device)
+            k = max(3, args.steps // 2)
+            # 4 warm-up steps: the auto mode reads the sparsity the first step observed
+            sm = time_steps(st, k, 4, device)
+            used = st.buf.used()
+            forced = {}
+            for mode in ("off", "on"):  # the two product paths the auto mode chooses between
+                sf.set_sparse_mma(mode)
+                forced[mode] = time_steps(st, k, 2, device)
+            sf.set_sparse_mma(args.sparse_mma)
+            dm = time_steps(DenseStep(xs, W1s, W2s, b1s, dos), k, 2, device)
             sweep[str(s)] = {"tokens_per_s": round(tpg / (sm / 1e3), 1),
+                             "dense_products_tokens_per_s": round(tpg / (forced["off"] / 1e3), 1),
+                             "sp24_products_tokens_per_s": round(tpg / (forced["on"] / 1e3), 1),
                              "dense_tokens_per_s": round(tpg / (dm / 1e3), 1),
-                             "measured_sparsity": round(1.0 - st.buf.used() / (tpg * D_FF), 4)}
+                             "measured_sparsity": round(1.0 - used / (tpg * D_FF), 4)}
             del st, xs, W1s, W2s, b1s, dos
             torch.cuda.empty_cache()
         extras["sweep"] = sweep
