@@ -342,6 +342,43 @@ def bench_deep(device):
     return r
 
 
+# --------------------------------------------------------------- gpt ----
+def bench_gpt(device, pk, steps=5, warmup=3):
+    """GPT-style training step with the sparse ReLU^2 MLPs against the same
+    model with dense torch MLPs: 12 layers, width 768, 12 heads, hidden 3072,
+    vocab 50304, 1024-token sequences, batch 32 (32768 tokens per step),
+    bf16, N(0, 0.02) weights, uniform random token ids (seed 0), fused AdamW.
+    tokens/s from CUDA events over `steps` steps after `warmup`; MFU against
+    the measured sustained bf16 figure; peak MB from torch's allocator."""
+    from autoresearch2_b200 import gpt
+    cfg = gpt.GPTConfig()
+    batch = 32
+    idx, tgt = gpt.synthetic_batch(cfg, batch, device)
+    res = {"config": {"n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_head": cfg.n_head,
+                      "ffn_hidden": cfg.ffn_hidden, "vocab": cfg.vocab, "seq_len": cfg.seq_len,
+                      "batch": batch, "mlp": "relu2"},
+           "flops_per_token": gpt.flops_per_token(cfg)}
+    for name, sparse in (("sparse", True), ("dense", False)):
+        model = gpt.GPT(cfg, sparse=sparse, device=device)
+        step = gpt.TrainStep(model, idx, tgt)
+        torch.cuda.reset_peak_memory_stats(device)
+        ms = time_steps(step, steps, warmup, device)
+        loss = float(step())
+        tps = batch * cfg.seq_len / (ms / 1e3)
+        res[name] = {"tokens_per_s": round(tps, 1), "ms_per_step": round(ms, 3),
+                     "mfu_of_measured_sustained": round(gpt.mfu(tps, cfg, pk["bf16_tflops_sustained"]), 3),
+                     "peak_mb": round(torch.cuda.max_memory_allocated(device) / 2 ** 20, 1),
+                     "loss_after": round(loss, 4)}
+        if sparse:
+            res[name]["activation_zeros"] = round(
+                1 - model.arena.used() / (batch * cfg.seq_len * cfg.ffn_hidden * cfg.n_layer), 4)
+        del step, model
+        torch.cuda.empty_cache()
+    import autoresearch2_b200 as sf
+    sf.check_status(device)
+    return res
+
+
 # ---------------------------------------------------------- CPU baseline ----
 def cpu_baseline(sample_tokens, steps=1, warmup=0):
     """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
@@ -593,7 +630,7 @@ def main():
 
     pk = peaks()
     roof = roofline(kernels, tpg, pk)
-    pack = codec = deep_ffn = None
+    pack = codec = deep_ffn = gpt_step = None
     if rank == 0 and not args.quick:
         pack = bench_pack(device)
         pack["pack_frac_of_measured_hbm"] = round(pack["pack_gbs"] / pk["hbm_gbs"], 3)
@@ -605,7 +642,9 @@ def main():
                 sweep_p[str(p)] = {"pack_gbs": r["pack_gbs"], "unpack_gbs": r["unpack_gbs"]}
         pack["sweep_p"] = sweep_p
         codec = bench_codec15(device)
-        deep_ffn = bench_deep(device)
+        if world == 1:  # single-GPU harnesses; at N > 1 the other ranks would wait on them
+            deep_ffn = bench_deep(device)
+            gpt_step = bench_gpt(device, peaks())
         for k in ("compress", "uncompress"):
             codec[f"{k}_frac_of_measured_hbm"] = round(codec[f"{k}_gbs"] / pk["hbm_gbs"], 3)
 
@@ -617,7 +656,7 @@ def main():
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
             "config": workload_config(tpg, world, tokens, s_meas), "sparse_mma": args.sparse_mma,
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
-            "codec15": codec, "deep_ffn": deep_ffn,
+            "codec15": codec, "deep_ffn": deep_ffn, "gpt": gpt_step,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)
