@@ -132,4 +132,3 @@ def synthetic_batch(cfg: GPTConfig, batch, device, seed=0):
 def mfu(tokens_per_s, cfg, peak_tflops):
     """Model FLOPs utilisation against a peak in TFLOP/s."""
     return tokens_per_s * flops_per_token(cfg) / (peak_tflops * 1e12)
-

@@ -44,3 +44,21 @@ def test_training_steps_lower_the_loss():
     assert all(math.isfinite(v) for v in losses) and losses[-1] < losses[0] - 0.1, losses
     used, cap = m.arena.used(), m.arena.n
     assert 0 < used <= cap
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_data_parallel_ranks_stay_identical():
+    """Two ranks (torchrun, NCCL, DistributedDataParallel), different batches:
+    after the steps every parameter is bit-identical across the ranks."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29531", "-m",
+           "autoresearch2_b200.train_gpt", "--check", "--layers=2", "--width=256", "--heads=4", "--hidden=1024",
+           "--vocab=1024", "--seq=128", "--batch=4", "--steps=3", "--warmup=1"]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", PYTHONPATH=root)
+    r = subprocess.run(cmd, cwd=root, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    assert '"params_identical": true' in r.stdout, r.stdout
