@@ -478,6 +478,40 @@ def roofline(kernels, tokens, pk):
             "ms_per_launch": ms, "peak_source": f"{pk['source']} (sustained bf16)"}
 
 
+def step_flops(step, ms, s, pk):
+    """The step's FLOPs three ways, per GPU: dense-equivalent 12 T D F; the
+    algorithmic sparse count 2 T D F (1 + 5 (1 - s)) (the up-projection dense,
+    the down-projection, dgrad's live entries, dW2, dX and dW1 scaling with
+    the nonzeros); and what the kernels execute, 2 T D F (4 + 2 l) with l the
+    fraction of 64-wide K blocks that are live in a 256-row tile (the
+    down-projection and dX skip the others; the up-projection, the
+    activation-gradient GEMM, dW1 and dW2 run dense).  l is read from one
+    more forward's K-block lists; rates use the step time `ms`."""
+    import autoresearch2_b200 as sf
+    T, D = step.x.shape
+    F = step.W1.shape[0]
+    step.buf.reset_buffer()
+    out = sf.FFNSpRelu2.apply(step.x, step.W1, step.W2, step.buf.as_sparse_data(), step.b1)
+    kb_count = out.grad_fn.aux[2]
+    nkb = -(-F // 64)
+    live = float(kb_count.sum()) / (kb_count.numel() * nkb) if kb_count.numel() else None
+    path = sf.ffn.last_path()
+    del out
+    base = 2.0 * T * D * F
+    dense_eq, alg = 6 * base, base * (1 + 5 * (1 - s))
+    exe = base * (4 + 2 * live) if live is not None else None
+    rate = lambda f: round(f / (ms * 1e-3) / 1e12, 1)  # noqa: E731
+    r = {"dense_equivalent_per_step": dense_eq, "algorithmic_per_step": alg,
+         "live_kblock_fraction": None if live is None else round(live, 4), "products_path": path,
+         "dense_equivalent_tflops": rate(dense_eq), "algorithmic_tflops": rate(alg),
+         "peak_tflops": pk["bf16_tflops_sustained"]}
+    if exe is not None:
+        r["executed_per_step"] = exe
+        r["executed_tflops"] = rate(exe)
+        r["executed_frac_of_measured_sustained"] = round(exe / (ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 3)
+    return r
+
+
 # ------------------------------------------------------------------ main ----
 def main():
     ap = argparse.ArgumentParser()
@@ -630,6 +664,7 @@ def main():
 
     pk = peaks()
     roof = roofline(kernels, tpg, pk)
+    flops = step_flops(step, ms, s_meas, pk) if rank == 0 else None
     pack = codec = deep_ffn = gpt_step = None
     if rank == 0 and not args.quick:
         pack = bench_pack(device)
@@ -656,7 +691,7 @@ def main():
             "data": "synthetic (seeded; inputs larger than L2, no flush)",
             "config": workload_config(tpg, world, tokens, s_meas), "sparse_mma": args.sparse_mma,
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
-            "codec15": codec, "deep_ffn": deep_ffn, "gpt": gpt_step,
+            "codec15": codec, "deep_ffn": deep_ffn, "gpt": gpt_step, "flops": flops,
             "gpu_launches": launches_per_step * args.steps,
         }
         line.update(extras)
