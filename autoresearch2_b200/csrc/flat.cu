@@ -1020,8 +1020,11 @@ int launch_unpack(const void* vals, long long vals_len, const uint8_t* mask, lon
 
 using namespace sffn;
 
-// Workspace: [0,16) tile ticket, then one 8-byte look-back state per tile of
-// 32 KB of dense data, counted for the widest type (8192 elements per tile).
+// Workspace: 16 bytes plus 8 per tile of 8192 elements.  The two-kernel pack
+// and unpack keep int32 tile counts followed by the int64 sums of 256-tile
+// groups there (tile_sums).  The persistent look-back pack of the no-alloc
+// entry point keeps a 16-byte ticket and one state word per 32 KB tile of
+// dense data in its static array instead.
 extern "C" size_t sffn_flat_workspace_bytes(int64_t n) {
     if (n < 0) return 0;
     return 16 + (size_t)((n + FT_MIN_TILE - 1) / FT_MIN_TILE) * 8;
