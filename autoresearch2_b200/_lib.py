@@ -67,6 +67,7 @@ SIGNATURES = {
     "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
                               _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "sffn_wait_probe": (_int, [_int, _i64, _vp, _vp, _vp, _vp]),
 }
 
 _lib = None
@@ -96,7 +97,8 @@ LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_a
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
              "sffn_tile_gather_slots": 1, "sffn_tile_row_offsets": 1, "sffn_live_kblocks": 1,
-             "sffn_ffn_dgrad": 1, "sffn_codec15_compress": 1, "sffn_codec15_uncompress": 1}
+             "sffn_ffn_dgrad": 1, "sffn_codec15_compress": 1, "sffn_codec15_uncompress": 1,
+             "sffn_wait_probe": 1}
 launch_count = 0
 
 # Per-entry-point CUDA event pairs, recorded while a KernelTimer is active.

@@ -38,8 +38,8 @@ def bitsparse_pack(dense: torch.Tensor, block: int = 2048, vals_out: torch.Tenso
 
     Follows old/sparse_pack.py:66-106: packed_mask is uint8[ceil(N/8)] with
     element f at byte f//8, bit f%8 (set iff x != 0); vals holds the nonzeros
-    in row-major order.  One kernel pass; like the reference, the call waits
-    for the device to learn len(vals).  `vals_out` (optional, 1-D, same dtype,
+    in row-major order.  Two kernels (mask and counts, then the values);
+    like the reference, the call waits for the device to learn len(vals).  `vals_out` (optional, 1-D, same dtype,
     >= nnz elements) receives the values instead of a fresh buffer."""
     require_cuda(dense)
     code = dtype_code(dense)

@@ -181,7 +181,7 @@ extern "C" int sffn_codec15_compress(const void* src, int64_t n, uint8_t* dst, i
     unsigned blocks = 0;
     if (int rc = c15_check(src, n, dst, dst_bytes, blocks)) return rc;
     if (n == 0) return SFFN_OK;
-    if (int rc = bind_device_of(src)) return rc;
+    SFFN_BIND(dev_scope, src);
     const bool vec_in = reinterpret_cast<uintptr_t>(src) % 16 == 0;
     const bool vec_out = reinterpret_cast<uintptr_t>(dst) % 16 == 0;
     codec15_compress_kernel<<<blocks, C15_T, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
@@ -195,7 +195,7 @@ extern "C" int sffn_codec15_uncompress(const uint8_t* src, int64_t src_bytes, in
     unsigned blocks = 0;
     if (int rc = c15_check(dst, n, src, src_bytes, blocks)) return rc;
     if (n == 0) return SFFN_OK;
-    if (int rc = bind_device_of(src)) return rc;
+    SFFN_BIND(dev_scope, src);
     const bool vec_in = reinterpret_cast<uintptr_t>(src) % 16 == 0;
     const bool vec_out = reinterpret_cast<uintptr_t>(dst) % 16 == 0;
     // persistent: 8 CTAs (2048 threads) per SM at most

@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <initializer_list>
 #include <type_traits>
 
 #include "../../include/sparseffn.h"
@@ -38,26 +39,41 @@ void set_error_text(const char* msg);
         }                                                    \
     } while (0)
 
-// Make the device that owns `p` current for this thread (and its primary
-// context current, which driver calls such as cuTensorMapEncodeTiled need).
-// Callers may arrive on any host thread -- e.g. an autograd worker -- on which
-// this library's runtime has not selected a device yet.
-inline int bind_device_of(const void* p) {
-    cudaPointerAttributes a;
-    if (p && cudaPointerGetAttributes(&a, p) == cudaSuccess &&
-        (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged)) {
-        int cur = -1;
-        if (cudaGetDevice(&cur) != cudaSuccess || cur != a.device) {
-            if (cudaSetDevice(a.device) != cudaSuccess) return SFFN_ERR_CUDA;
-        }
-        // cudaSetDevice does not bind the context when the device is already
-        // current; cudaFree(0) initialises and binds it.
-        if (cudaFree(nullptr) != cudaSuccess) return SFFN_ERR_CUDA;
-        return SFFN_OK;
-    }
-    cudaGetLastError();  // clear a failed pointer query
-    return SFFN_ERR_ARG;
-}
+// Device of a device (or managed) pointer, or -1 (the failed query cleared).
+int device_of(const void* p);
+// Unique id of the thread's current CUDA context (ids are never reused, also
+// not after a device reset creates a new primary context), or 0 if unknown.
+unsigned long long current_context_id();
+
+// For the length of one entry-point call: makes the device that owns a
+// pointer current on the calling thread, with its primary context bound
+// (driver calls such as cuTensorMapEncodeTiled need one), and on every return
+// path puts back the context that was current when the call began -- which
+// may be another device's, or none.  Callers arrive on any host thread (an
+// autograd worker, a plug-in host's thread) and keep their own device.
+class DeviceScope {
+  public:
+    DeviceScope() = default;
+    DeviceScope(const DeviceScope&) = delete;
+    DeviceScope& operator=(const DeviceScope&) = delete;
+    ~DeviceScope();
+    // SFFN_OK, SFFN_ERR_ARG (not device memory) or SFFN_ERR_CUDA.
+    int bind(const void* p);
+    // Also SFFN_ERR_ARG unless every non-null pointer of `others` lives on the bound device.
+    int bind_same(const void* p, std::initializer_list<const void*> others);
+    int device() const { return dev_; }
+
+  private:
+    void* saved_ = nullptr;  // CUcontext current at bind()
+    bool restore_ = false;
+    int dev_ = -1;
+};
+
+// One-line form for the entry points: `SFFN_BIND(scope, ptr)` declares a
+// DeviceScope named `scope` bound to ptr's device, returning on failure.
+#define SFFN_BIND(scope, p)                              \
+    ::sffn::DeviceScope scope;                           \
+    if (int _rc = scope.bind(p)) return _rc
 
 inline int esize_of(int dtype) { return dtype == SFFN_F32 ? 4 : 2; }
 inline bool dtype_ok(int dtype) { return dtype == SFFN_F32 || dtype == SFFN_BF16 || dtype == SFFN_F16; }
@@ -175,7 +191,8 @@ __device__ __forceinline__ void lookback_publish(unsigned long long* states, lon
 template <int W>
 __device__ __forceinline__ unsigned long long lookback(unsigned long long* states, long long part,
                                                       unsigned long long agg, uint32_t* status,
-                                                      int lane) {
+                                                      int lane,
+                                                      unsigned long long limit_ns = kLookbackLimitNs) {
     if (part == 0) return 0;
     unsigned long long excl = 0;
     long long pred = part - 1;
@@ -205,7 +222,7 @@ __device__ __forceinline__ unsigned long long lookback(unsigned long long* state
             asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
             if (t0 == 0) t0 = now;
             // lane 0's clock decides for the whole warp
-            if (__shfl_sync(FULL, now - t0 > kLookbackLimitNs ? 1 : 0, 0)) {
+            if (__shfl_sync(FULL, now - t0 > limit_ns ? 1 : 0, 0)) {
                 if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
                 break;
             }
@@ -246,7 +263,8 @@ __device__ __forceinline__ void lookback_publish_relaxed(unsigned long long* sta
 template <int W>
 __device__ __forceinline__ unsigned long long lookback_rows(unsigned long long* states, long long part,
                                                            unsigned long long agg, uint32_t* status,
-                                                           int lane) {
+                                                           int lane,
+                                                           unsigned long long limit_ns = kLookbackLimitNs) {
     if (part == 0) return 0;
     unsigned long long excl = 0;
     long long pred = part - 1;
@@ -283,7 +301,7 @@ __device__ __forceinline__ unsigned long long lookback_rows(unsigned long long* 
             asm volatile("mov.u64 %0, %globaltimer;" : "=l"(now));
             if (t0 == 0) t0 = now;
             // lane 0's clock decides for the whole warp
-            if (__shfl_sync(FULL, now - t0 > kLookbackLimitNs ? 1 : 0, 0)) {
+            if (__shfl_sync(FULL, now - t0 > limit_ns ? 1 : 0, 0)) {
                 if (lane == 0) atomicOr(status, SFFN_STATUS_WAIT_TIMEOUT);
                 break;
             }

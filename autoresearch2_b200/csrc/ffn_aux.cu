@@ -250,7 +250,7 @@ extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int6
     if (ntiles <= 0 || parts <= 0 || !tile_counts || !prefix || !offset_dev || !vals_offset_dev || !status_dev)
         return SFFN_ERR_ARG;
     if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
-    if (int rc = bind_device_of(tile_counts)) return rc;
+    SFFN_BIND(dev_scope, tile_counts);
     tile_scan_kernel<<<1, SCAN_NT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         tile_counts, parts, ntiles, prefix, offset_dev, vals_offset_dev, status_dev);
     SFFN_CHECK_LAUNCH();
@@ -265,7 +265,7 @@ extern "C" int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask,
     if (ntiles <= 0 || !slots || !bitmask || !prefix || !vals_offset_dev || !vals || !status_dev)
         return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(vals)) return rc;
+    SFFN_BIND(dev_scope, vals);
     tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         bitmask, prefix, row_offsets, static_cast<const uint16_t*>(slots), vals_offset_dev,
         static_cast<uint16_t*>(vals), vals_capacity, status_dev);
@@ -277,7 +277,7 @@ extern "C" int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* pref
                                      int32_t* row_offsets, void* stream) {
     if (ntiles <= 0 || !bitmask || !prefix || !row_offsets) return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(row_offsets)) return rc;
+    SFFN_BIND(dev_scope, row_offsets);
     tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         bitmask, prefix, row_offsets, nullptr, nullptr, nullptr, 0, nullptr);
     SFFN_CHECK_LAUNCH();
@@ -290,7 +290,7 @@ extern "C" int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, i
     if (reinterpret_cast<uintptr_t>(bitmask) & 7u) return SFFN_ERR_ALIGN;
     const long long gm = (M + 127) / 128, gp = (M + 255) / 256, gn_f = (N + 127) / 128, nkb = (N + 63) / 64;
     if (gp > 0x7FFFFFFF || nkb > 0x7FFFFFFF) return SFFN_ERR_ARG;
-    if (int rc = bind_device_of(bitmask)) return rc;
+    SFFN_BIND(dev_scope, bitmask);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     SFFN_CUDA_TRY(cudaMemsetAsync(kb_count, 0, (size_t)gp * sizeof(int32_t), st));
     const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));

@@ -1037,7 +1037,7 @@ extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* 
     if (n < 0 || vals_capacity < 0 || !nnz_dev || !status_dev) return SFFN_ERR_ARG;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (n == 0) {
-        if (int rc = bind_device_of(nnz_dev)) return rc;
+        SFFN_BIND(dev_scope, nnz_dev);
         SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
         return SFFN_OK;
     }
@@ -1045,7 +1045,7 @@ extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* 
     if (!aligned16(dense) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u)) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
     if ((n + FT_MIN_TILE - 1) / FT_MIN_TILE > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // grid limit
-    if (int rc = bind_device_of(dense)) return rc;
+    SFFN_BIND(dev_scope, dense);
     if (esize_of(dtype) == 4)
         return launch_pack<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, workspace,
                                      status_dev, st);
@@ -1063,7 +1063,7 @@ extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_
     if (!aligned16(out) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u)) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
     if ((n + FT_MIN_TILE - 1) / FT_MIN_TILE > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // grid limit
-    if (int rc = bind_device_of(out)) return rc;
+    SFFN_BIND(dev_scope, out);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (esize_of(dtype) == 4)
         return launch_unpack<uint32_t>(vals, vals_len, packed_mask, n, out, workspace, status_dev, st);
@@ -1081,12 +1081,17 @@ extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_
 // look-back state lives in the fixed array below, which every GPU that loads
 // this library holds until the process exits.
 //
-// Set-up: the first call on a device looks up that device's address of the
-// array with cudaGetSymbolAddress (with the device current) and caches it;
-// make that first call before any stream capture.  Every call shares the
-// array and finds the previous call's contents in it, so each call clears the
-// part it uses before its kernel runs; calls that overlap on the GPU (other
-// streams, other host threads) race on it and must be serialised by the caller.
+// Set-up: the first call on a device (more precisely, in a CUDA context: a
+// device reset makes a new primary context, in which the array may sit
+// elsewhere) looks up that device's address of the array with
+// cudaGetSymbolAddress, with the device current, and caches it keyed by the
+// context's unique id; make that first call before any stream capture.  Every
+// call shares the array and finds the previous call's contents in it, so each
+// call clears the part it uses before its kernel runs; calls that overlap on
+// the GPU (other streams, other host threads) race on it and must be
+// serialised by the caller.  The call binds the device of `dense` and puts
+// back the caller's current device (context) before it returns; every pointer
+// argument must live on that device.
 // ---------------------------------------------------------------------------
 namespace sffn {
 namespace {
@@ -1096,22 +1101,29 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[16 + kNoAllocMa
 
 constexpr int kMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kMaxDevices] = {};
+struct ScratchAddr {
+    unsigned long long ctx_id;  // context the address belongs to (0: none cached)
+    void* addr;
+};
+ScratchAddr g_noalloc_addr[kMaxDevices] = {};
 
-// Device address of the scratch array on `dev` (which must be current).
+// Device address of the scratch array on `dev`, whose context is current.
 int noalloc_scratch(int dev, void** out) {
     if (dev < 0 || dev >= kMaxDevices) return SFFN_ERR_ARG;
+    const unsigned long long ctx = current_context_id();
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (!g_noalloc_addr[dev]) {
+    ScratchAddr& c = g_noalloc_addr[dev];
+    if (ctx == 0 || c.ctx_id != ctx || !c.addr) {
         void* p = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) {
             set_cuda_error(e);
             return SFFN_ERR_CUDA;
         }
-        g_noalloc_addr[dev] = p;
+        c.ctx_id = ctx;  // 0 (id unknown): looked up again on the next call
+        c.addr = p;
     }
-    *out = g_noalloc_addr[dev];
+    *out = c.addr;
     return SFFN_OK;
 }
 
@@ -1137,22 +1149,21 @@ extern "C" int sffn_flat_pack_noalloc(const void* dense, int dtype, int64_t n, u
     }
     if (n > 0 && (!dense || !packed_mask || (!vals && vals_capacity > 0))) return SFFN_ERR_ARG;
     if (n > 0 && (!aligned16(dense) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u))) return SFFN_ERR_ALIGN;
-    // Select the device that owns the output (cudaSetDevice initialises its
-    // context); nothing on this path allocates or frees device memory.
-    cudaPointerAttributes attr;
-    if (cudaPointerGetAttributes(&attr, nnz_dev) != cudaSuccess ||
-        (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)) {
-        cudaGetLastError();
-        return SFFN_ERR_ARG;
-    }
-    SFFN_CUDA_TRY(cudaSetDevice(attr.device));
+    // The device that owns the input (the count, for an empty input); every
+    // other buffer must be on it.  Nothing on this path allocates or frees
+    // device memory.
+    DeviceScope dev_scope;
+    if (int rc = dev_scope.bind_same(n > 0 ? dense : nnz_dev,
+                                     {nnz_dev, status_dev, n > 0 ? packed_mask : nullptr,
+                                      n > 0 && vals_capacity > 0 ? vals : nullptr}))
+        return rc;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (n == 0) {
         SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
         return SFFN_OK;
     }
     void* scratch = nullptr;
-    if (int rc = noalloc_scratch(attr.device, &scratch)) return rc;
+    if (int rc = noalloc_scratch(dev_scope.device(), &scratch)) return rc;
     // launch_pack_lookback clears the ticket and the states this call uses
     // (the previous call left its own in the array) before the kernel runs.
     if (esize_of(dtype) == 4)

@@ -1155,14 +1155,14 @@ int dispatch(bool a_mn, bool b_mn, const void* A, long long lda, const void* B, 
 
 // Common argument checks.  TMA needs 16-byte aligned bases and row strides,
 // and every inner coordinate we issue is a multiple of 64 elements.
-int check_operands(const void* A, long long lda, bool a_mn, const void* B, long long ldb, bool b_mn,
-                   long long M, long long N, long long K) {
+int check_operands(DeviceScope& scope, const void* A, long long lda, bool a_mn, const void* B, long long ldb,
+                   bool b_mn, long long M, long long N, long long K) {
     if (M <= 0 || N <= 0 || K <= 0) return SFFN_ERR_ARG;
     if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return SFFN_ERR_ARG;
     if (!A || !B) return SFFN_ERR_ARG;
     if (!aligned16(A) || !aligned16(B) || (lda * 2) % 16 || (ldb * 2) % 16) return SFFN_ERR_ALIGN;
     if (lda < (a_mn ? M : K) || ldb < (b_mn ? N : K)) return SFFN_ERR_ARG;
-    if (int rc = bind_device_of(A)) return rc;
+    if (int rc = scope.bind_same(A, {B})) return rc;
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     return SFFN_OK;
 }
@@ -1248,7 +1248,8 @@ extern "C" int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
                               void* C, int64_t ldc, int64_t M, int64_t N, int64_t K,
                               const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
                               uint32_t* status_dev, void* stream) {
-    int rc = check_operands(A, lda, a_mn, B, ldb, b_mn, M, N, K);
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
     if (rc) return rc;
     if (!C || ldc < N || !status_dev) return SFFN_ERR_ARG;
     if ((kb_list == nullptr) != (kb_count == nullptr)) return SFFN_ERR_ARG;
@@ -1264,7 +1265,8 @@ extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t l
                            int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
                            uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
                            void* stream) {
-    int rc = check_operands(x, ldx, false, w1, ldw1, false, T, F, D);
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
     if (!act_out || ld_act < F || !bitmask || !tile_counts || !slots || !status_dev) return SFFN_ERR_ARG;
@@ -1286,7 +1288,8 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
                               const int32_t* vals_offset_dev, void* dpre_out, void* act_out,
                               int64_t ld_out, float* db1_sum, uint32_t* status_dev, void* stream) {
     // dA[T, F] = dout[T, D] @ W2[D, F]: B = W2 is [K=D][N=F], N contiguous (MN-major).
-    int rc = check_operands(dout, ld_dout, false, w2, ldw2, true, T, F, D);
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, dout, ld_dout, false, w2, ldw2, true, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
     if (!vals || !bitmask || !row_offsets || !vals_offset_dev || !dpre_out || !act_out || ld_out < F ||
@@ -1331,7 +1334,8 @@ extern "C" int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int6
                                 int64_t T, int64_t D, int64_t F, int act, const sffn_sp24_mat* out,
                                 uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
                                 void* stream) {
-    int rc = check_operands(x, ldx, false, w1, ldw1, false, T, F, D);
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
     if (!sp24_dims_ok(T, F)) return SFFN_ERR_UNSUPPORTED;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
@@ -1357,7 +1361,8 @@ extern "C" int sffn_ffn_dgrad_sp24(const void* dout, int64_t ld_dout, const void
                                    const int32_t* vals_offset_dev, const sffn_sp24_mat* dpre,
                                    const sffn_sp24_mat* dpre_t, const sffn_sp24_mat* act_t, float* db1_sum,
                                    uint32_t* status_dev, void* stream) {
-    int rc = check_operands(dout, ld_dout, false, w2, ldw2, true, T, F, D);
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, dout, ld_dout, false, w2, ldw2, true, T, F, D);
     if (rc) return rc;
     if (!sp24_dims_ok(T, F)) return SFFN_ERR_UNSUPPORTED;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
@@ -1390,7 +1395,7 @@ extern "C" int sffn_gemm_sp24(const void* vals, const uint32_t* meta, int64_t M,
     if (!aligned16(vals) || !aligned16(meta) || !aligned16(B) || !aligned16(C) || (ldb * 2) % 16 || (ldc * 2) % 16)
         return SFFN_ERR_ALIGN;
     if (ldb < (b_mn ? N : K) || ldc < N) return SFFN_ERR_ARG;
-    if (int rc = bind_device_of(vals)) return rc;
+    SFFN_BIND(dev_scope, vals);
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     Sp24Epi epi{};
@@ -1410,7 +1415,7 @@ extern "C" int sffn_sp24_mm(const sffn_sp24_mat* a, int64_t M, int64_t K, const 
         (ldb * 2) % 16 || (ldbt * 2) % 16 || (ldc * 2) % 16)
         return SFFN_ERR_ALIGN;
     if (ldb < (b_mn ? N : K) || ldbt < N || ldc < (c_trans ? M : N)) return SFFN_ERR_ARG;
-    if (int rc = bind_device_of(a->vals)) return rc;
+    SFFN_BIND(dev_scope, a->vals);
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     Sp24Epi epi{};

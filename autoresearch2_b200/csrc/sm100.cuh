@@ -62,13 +62,15 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
 // Wait for the phase with the given parity, giving up after kWaitLimitNs of
 // wall time (far longer than any legitimate wait in these kernels -- one
 // output tile or one chunk -- far shorter than a hang); false if it gave up.
+// (sffn_wait_probe passes a shorter limit, so that a test can make a wait
+// run out.)
 constexpr uint64_t kWaitLimitNs = 500ull * 1000 * 1000;
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
         if (mbar_try_wait_hint(bar, parity, 2000)) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
 

@@ -179,7 +179,7 @@ extern "C" int sffn_sp24_compress(const void* src, int64_t ld, int trans, int64_
     if (!src || !vals || !meta || !ovf_cols || !ovf_vals || !ovf_count) return SFFN_ERR_ARG;
     if (ld < (trans ? M : K) || (ld * 2) % 16 || !aligned16(src) || !aligned16(vals) || !aligned16(meta))
         return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(src)) return rc;
+    SFFN_BIND(dev_scope, src);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     SFFN_CUDA_TRY(cudaMemsetAsync(ovf_count, 0, (size_t)M * sizeof(int32_t), st));
     const dim3 grid((unsigned)(M / SP_TILE), (unsigned)(K / SP_TILE));
@@ -202,7 +202,7 @@ extern "C" int sffn_sp24_overflow_add(const void* ovf_cols, const void* ovf_vals
     if (!ovf_cols || !ovf_vals || !ovf_count || !bt || !C) return SFFN_ERR_ARG;
     if (!aligned16(bt) || !aligned16(C) || (ldb * 2) % 16 || (ldc * 2) % 16 || ldb < N || ldc < N)
         return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(C)) return rc;
+    SFFN_BIND(dev_scope, C);
     sp24_overflow_kernel<<<(unsigned)M, OV_NT, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<const uint16_t*>(ovf_cols), static_cast<const uint16_t*>(ovf_vals), ovf_count, K / 2,
         static_cast<const uint16_t*>(bt), ldb, static_cast<uint16_t*>(C), ldc, (int)N);

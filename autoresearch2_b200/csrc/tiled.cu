@@ -460,7 +460,7 @@ extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N
     if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_tile_workspace_bytes(M, N, BM, BN)) return SFFN_ERR_WORKSPACE;
-    if (int rc = bind_device_of(dense)) return rc;
+    SFFN_BIND(dev_scope, dense);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     TileWs w;
     w.ticket = reinterpret_cast<unsigned*>(workspace);
@@ -498,7 +498,7 @@ extern "C" int sffn_tile_unpack(const void* vals, int64_t vals_len, const uint8_
     if (tile_rows == 0) return SFFN_OK;
     if (!vals || !bitmask || !prefix || !vals_offset_dev || !out) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(out)) return rc;
+    SFFN_BIND(dev_scope, out);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const bool of = (out_dtype == SFFN_F32) && (dtype != SFFN_F32);
     const int vec = vec_ok(out, ld_out, esize_of(out_dtype)) ? 1 : 0;
@@ -533,7 +533,7 @@ extern "C" int sffn_tile_mask_grad(void* grad, int dtype, int64_t M, int64_t N, 
     if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
     if (M <= 0 || N <= 0 || ld < N || !grad || !bitmask) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(grad)) return rc;
+    SFFN_BIND(dev_scope, grad);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int esz = esize_of(dtype);
     const int vec = vec_ok(grad, ld, esz) ? 1 : 0;
@@ -556,7 +556,7 @@ extern "C" int sffn_tile_grad_relu2(void* grad, int dtype, int64_t M, int64_t N,
     if (M <= 0 || N <= 0 || ld < N || !grad || !vals || !bitmask || !prefix || !vals_offset_dev)
         return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
-    if (int rc = bind_device_of(grad)) return rc;
+    SFFN_BIND(dev_scope, grad);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int vec = vec_ok(grad, ld, esize_of(dtype)) ? 1 : 0;
 #define SFFN_RELU2_CASE(a, b)                                                                     \

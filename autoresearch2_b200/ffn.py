@@ -165,16 +165,19 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
         # dW2 = (a^T @ dout)^T, stored transposed by the kernel: [D, F] row-major
         grad_W2 = submit_grad(sp24.mm(a_t, grad_output, trans_out=True))
         del a_t
-        grad_x = sp24.mm(dpre, W1)
+        # dW1 before dX: under data parallelism its all-reduce then overlaps dX
         grad_W1 = submit_grad(sp24.mm(dpre_t, x))
+        grad_x = sp24.mm(dpre, W1)
         return grad_x, grad_W1, grad_W2, grad_b1
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
     del row_offsets
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
-    grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dX/dW1 run
+    grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dW1/dX run
     del a
-    grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
+    # dW1 before dX: under data parallelism its all-reduce then overlaps dX, and
+    # no weight-gradient reduction is left without compute to hide behind
     grad_W1 = submit_grad(G.mm(dpre.T, x))
+    grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
     return grad_x, grad_W1, grad_W2, grad_b1
 
 
@@ -204,9 +207,9 @@ def _unfused_backward(grad_output, x, W1, W2, z_sparse, has_bias, act):
     else:
         grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T))
         bs.mask_with_bitmask_(grad_z, z_sparse)
-    grad_x = grad_z @ W1
-    grad_W1 = submit_grad(grad_z.T @ x)
     grad_b1 = submit_grad(grad_z.sum(0)) if has_bias else None
+    grad_W1 = submit_grad(grad_z.T @ x)
+    grad_x = grad_z @ W1
     return grad_x, grad_W1, grad_W2, grad_b1
 
 

@@ -9,8 +9,9 @@ no multi-GPU code; its harness runs one GPU, program.md:27.)
 GradAllReduce overlaps that sum with the rest of the backward: inside
 ``with comm.attached():`` the fused FFN backward hands each weight gradient to
 the communicator as soon as it is computed -- dW2 comes out of the first
-backward GEMM, so its all_reduce runs on a side stream while dX and dW1 are
-still being computed.  ``comm.wait()`` makes the current stream wait for all
+backward GEMM and dW1 out of the next, so their all_reduces run on a side
+stream while dW1 and then dX are still being computed; dX, computed last,
+needs no reduction.  ``comm.wait()`` makes the current stream wait for all
 reductions.  On CPU tensors (the gloo backend) the reduction is synchronous.
 """
 import contextlib

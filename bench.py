@@ -145,18 +145,19 @@ class Step:
         self.buf = sf.TensorBuffer(T * F, x.device, x.dtype).init_buffer()
         self.group = group
 
-    def __call__(self, x=None):
+    def __call__(self, x=None, dout=None):
         x = self.x if x is None else x
+        dout = self.dout if dout is None else dout
         self.buf.reset_buffer()
         for p in (self.W1, self.W2, self.b1):
             p.grad = None
         out = self.sf.FFNSpRelu2.apply(x, self.W1, self.W2, self.buf.as_sparse_data(), self.b1)
         if self.comm is None:
-            out.backward(self.dout)
+            out.backward(dout)
         else:
             # dW sums over the token shards overlap the rest of the backward
             with self.comm.attached():
-                out.backward(self.dout)
+                out.backward(dout)
             self.comm.wait()
         return out
 
@@ -380,48 +381,131 @@ def bench_gpt(device, pk, steps=5, warmup=3):
 
 
 # ---------------------------------------------------------- CPU baseline ----
-def cpu_baseline(sample_tokens, steps=1, warmup=0):
-    """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
-    the C restatement of its pack) on the host cores: `warmup` untimed and
-    `steps` timed samples of `sample_tokens` tokens of the headline workload.
-    Returns tokens/s over the timed samples."""
+class _HostThreads:
+    """Every host core for torch's and BLAS's thread pools while a CPU leg
+    runs, whatever OMP_NUM_THREADS a launcher set (torchrun sets 1)."""
+
+    def __enter__(self):
+        self.cores = os.cpu_count() or 1
+        self.prev = torch.get_num_threads()
+        torch.set_num_threads(self.cores)
+        self.limiter = None
+        try:
+            from threadpoolctl import threadpool_limits
+            self.limiter = threadpool_limits(limits=self.cores)
+        except Exception:  # noqa: BLE001
+            pass
+        return self
+
+    def __exit__(self, *exc):
+        torch.set_num_threads(self.prev)
+        if self.limiter is not None:
+            self.limiter.restore_original_limits()
+
+
+def _cpu_flat_round_trip(z):
+    """The flat pack and unpack of z on the host (the C restatement of the
+    reference's bit order, old/bitpack/prepare.py:6-23), checked exact."""
     import numpy as np
     import oracle
-    # every host core for the BLAS pool, whatever OMP_NUM_THREADS a launcher set
-    # (torchrun sets it to 1 per process)
-    limiter = None
-    try:
-        from threadpoolctl import threadpool_info, threadpool_limits
-        limiter = threadpool_limits(limits=os.cpu_count() or 1)
-        cores = max((i.get("num_threads", 1) for i in threadpool_info()), default=1)
-    except Exception:  # noqa: BLE001
-        cores = os.cpu_count() or 1
-    rng = np.random.default_rng(0)
-    T, D, F = sample_tokens, D_MODEL, D_FF
-    x = rng.standard_normal((T, D), dtype=np.float32)
-    W1 = (rng.standard_normal((F, D), dtype=np.float32) / np.sqrt(D)).astype(np.float32)
-    W2 = (rng.standard_normal((D, F), dtype=np.float32) / np.sqrt(F)).astype(np.float32)
-    dout = rng.standard_normal((T, D), dtype=np.float32)
-    pre = x @ W1.T
-    b1 = np.full(F, -np.quantile(pre[:256], SPARSITY), dtype=np.float32)
-    arena = np.empty(T * F, dtype=np.float32)
+    zn = z.detach().contiguous().numpy()
+    vals, mask = oracle.flat_pack(zn, nthreads=os.cpu_count() or 1)
+    back = oracle.flat_unpack(vals, mask, zn.shape, nthreads=os.cpu_count() or 1)
+    assert np.array_equal(back.view(np.uint32), zn.view(np.uint32))
+    return vals.size
 
-    def sample():
-        r = oracle.ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=b1, code=oracle.F32,
-                               compute=np.float32)
-        oracle.tile_pack(r["z"].astype(np.float32), 128, 128, arena, 0)
 
-    for _ in range(warmup):
-        sample()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        sample()
-    dt = time.perf_counter() - t0
-    if limiter is not None:
-        limiter.restore_original_limits()
-    return {"value": round(steps * T / dt, 1), "unit": "tokens/s", "cores": int(cores), "kind": "port",
-            "sample": f"{steps} x {T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
-                      f"+ tiled pack of z, after {warmup} untimed; {dt:.1f} s"}
+def cpu_reference_ffn(T, D, F, steps, warmup, sparsity=None, bias=None, seed=0):
+    """The reference's dense torch ReLU^2 FFN on the host cores: FFNrelu2
+    (old/lib_sparse/prepare_layer.py:12-29: relu(x @ W1.T)^2 @ W2.T, here with
+    the up-projection bias) forward and torch autograd backward in float32,
+    then the flat pack/unpack round trip of z, `warmup` untimed and `steps`
+    timed steps.  x ~ N(0,1), W1 ~ N(0,1/D), W2 ~ N(0,1/F), dout ~ N(0,1),
+    seeded; the bias is `bias`, or the quantile giving `sparsity` zeros."""
+    with _HostThreads() as ht:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(T, D, generator=g)
+        W1 = (torch.randn(F, D, generator=g) / D ** 0.5).requires_grad_()
+        W2 = (torch.randn(D, F, generator=g) / F ** 0.5).requires_grad_()
+        dout = torch.randn(T, D, generator=g)
+        if bias is None:
+            with torch.no_grad():
+                pre = (x[:256] @ W1.T).flatten()
+                bias = float(-torch.quantile(pre[:: max(1, pre.numel() // 8_000_000)], sparsity))
+        b1 = torch.full((F,), float(bias)).requires_grad_()
+        nnz = [0]
+
+        def step():
+            for p in (W1, W2, b1):
+                p.grad = None
+            z = torch.relu(x @ W1.T + b1)
+            out = (z ** 2) @ W2.T
+            out.backward(dout)
+            nnz[0] = _cpu_flat_round_trip(z)
+
+        for _ in range(warmup):
+            step()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        dt = time.perf_counter() - t0
+        return {"value": round(steps * T / dt, 1), "unit": "tokens/s", "cores": ht.cores,
+                "torch_threads": torch.get_num_threads(), "nproc": os.cpu_count(),
+                "ms_per_step": round(dt / steps * 1e3, 2), "bias": round(float(bias), 5),
+                "measured_sparsity": round(1 - nnz[0] / (T * F), 4), "kind": "port",
+                "sample": f"{steps} x {T} tokens of the D={D}, F={F} ReLU^2 FFN fwd+bwd (torch float32, "
+                          f"FFNrelu2 + autograd) + flat pack/unpack round trip of z, after {warmup} "
+                          f"untimed; {dt:.1f} s"}
+
+
+def cpu_oracle_port(sample_tokens, steps=1, warmup=0):
+    """The oracle (numpy restatement of the reference's dense ReLU^2 FFN and
+    the C restatement of its tiled pack) on the host cores: `warmup` untimed
+    and `steps` timed samples of `sample_tokens` tokens of the headline
+    workload.  Returns tokens/s over the timed samples."""
+    import numpy as np
+    import oracle
+    with _HostThreads() as ht:
+        rng = np.random.default_rng(0)
+        T, D, F = sample_tokens, D_MODEL, D_FF
+        x = rng.standard_normal((T, D), dtype=np.float32)
+        W1 = (rng.standard_normal((F, D), dtype=np.float32) / np.sqrt(D)).astype(np.float32)
+        W2 = (rng.standard_normal((D, F), dtype=np.float32) / np.sqrt(F)).astype(np.float32)
+        dout = rng.standard_normal((T, D), dtype=np.float32)
+        pre = x @ W1.T
+        b1 = np.full(F, -np.quantile(pre[:256], SPARSITY), dtype=np.float32)
+        arena = np.empty(T * F, dtype=np.float32)
+
+        def sample():
+            r = oracle.ffn_fwd_bwd(x, W1, W2, dout, act="relu2", b1=b1, code=oracle.F32,
+                                   compute=np.float32)
+            oracle.tile_pack(r["z"].astype(np.float32), 128, 128, arena, 0)
+
+        for _ in range(warmup):
+            sample()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            sample()
+        dt = time.perf_counter() - t0
+        return {"value": round(steps * T / dt, 1), "unit": "tokens/s", "cores": ht.cores, "kind": "port",
+                "sample": f"{steps} x {T} tokens of the d=4096/14336 ReLU^2 FFN fwd+bwd (float32 numpy) "
+                          f"+ tiled pack of z, after {warmup} untimed; {dt:.1f} s"}
+
+
+# configs[0]-style single layer on the CPU: T=8192 (8 x 1024), D=768, F=3072,
+# float32, up-projection bias -1.3 (about 90% zeros)
+CFG1 = {"T": 8192, "D": 768, "F": 3072, "bias": -1.3}
+
+
+def cpu_baselines(sample_tokens, steps, warmup):
+    """The CPU figures of the bench line: the reference's dense torch path at
+    the headline shape on a token sample (the baseline proper), at the exact
+    single-layer CPU configuration, and the numpy/C oracle port."""
+    base = cpu_reference_ffn(sample_tokens, D_MODEL, D_FF, steps, warmup, sparsity=SPARSITY)
+    base["cfg1"] = cpu_reference_ffn(CFG1["T"], CFG1["D"], CFG1["F"], 3, 1, bias=CFG1["bias"])
+    base["cfg1"]["config"] = dict(CFG1, dtype="f32")
+    base["oracle_port"] = cpu_oracle_port(sample_tokens, steps=4, warmup=1)
+    return base
 
 
 def workload_config(tpg, world, tokens, s_meas=None):
@@ -436,8 +520,8 @@ def workload_config(tpg, world, tokens, s_meas=None):
 
 # -------------------------------------------------------------- roofline ----
 # DRAM traffic per launch of the roofline kernels at T=16384: dram__bytes_read.sum
-# + dram__bytes_write.sum of one ncu capture at T=4096 (up 299.9 + 126.5 MB,
-# activation gradient 331.8 + 200.9 MB; profiles/gemm_kernel_up_down_dgrad_t4096.md)
+# + dram__bytes_write.sum of one ncu capture of the kernels at T=4096 (up 299.9 + 126.5 MB,
+# activation gradient 331.8 + 200.9 MB)
 # times 4 -- activations, masks and the weight re-reads per row tile all grow
 # with the tokens.
 TRAFFIC_BYTES = {"sffn_ffn_up": 4 * (299.9e6 + 126.5e6), "sffn_ffn_dgrad": 4 * (331.8e6 + 200.9e6)}
@@ -455,27 +539,33 @@ def kernel_breakdown(timer, steps_recorded, step_ms):
     return out
 
 
-def roofline(kernels, tokens, pk):
+def roofline(kernels, tokens, pk, s=SPARSITY):
     """Tensor-core roofline of the largest single launch of the step.
 
     The fused up-projection (x @ W1^T with the ReLU^2/bitmask epilogue) and the
     fused activation-gradient GEMM (dout @ W2 with the ReLU^2 derivative) each
-    do 2*T*D*F flops, dense: nothing of either can be skipped, since the
-    sparsity is only known after the up-projection and dout is dense.  The
-    denominator is the sustained cuBLAS bf16 figure, as both kernels run
-    inside a long step at the power cap."""
+    execute 2*T*D*F flops.  Their algorithmic work differs: the up-projection
+    is dense (the sparsity is only known after it), while the activation
+    gradient is only needed at the live entries of z, 2*T*D*F*(1 - s).
+    `achieved` and `frac` count the algorithmic flops; `executed_*` count the
+    flops the kernel runs.  The denominator is the sustained cuBLAS bf16
+    figure, as both kernels run inside a long step at the power cap."""
     cands = [k for k in ("sffn_ffn_dgrad", "sffn_ffn_up") if k in kernels]
     if not cands:
         return None
     name = max(cands, key=lambda k: kernels[k]["mean_ms"])
-    flops = 2.0 * tokens * D_MODEL * D_FF
+    executed = 2.0 * tokens * D_MODEL * D_FF
+    algo = executed if name == "sffn_ffn_up" else executed * (1.0 - s)
     ms = kernels[name]["mean_ms"]
-    tf = flops / (ms * 1e-3) / 1e12
+    tf = algo / (ms * 1e-3) / 1e12
+    etf = executed / (ms * 1e-3) / 1e12
     peak = pk["bf16_tflops_sustained"]
     return {"bound": "tensor", "kernel": name, "achieved": round(tf, 1), "peak": peak,
-            "unit": "TFLOP/s", "frac": round(tf / peak, 3),
-            "traffic": TRAFFIC_BYTES.get(name), "flops_per_launch": flops,
-            "ms_per_launch": ms, "peak_source": f"{pk['source']} (sustained bf16)"}
+            "unit": "TFLOP/s", "frac": round(tf / peak, 4), "traffic": TRAFFIC_BYTES.get(name),
+            "algorithmic_flops_per_launch": algo, "executed_flops_per_launch": executed,
+            "executed_achieved": round(etf, 1), "executed_frac": round(etf / peak, 3),
+            "sparsity": round(s, 4), "ms_per_launch": ms,
+            "peak_source": f"{pk['source']} (sustained bf16)"}
 
 
 def step_flops(step, ms, s, pk):
@@ -504,6 +594,7 @@ def step_flops(step, ms, s, pk):
     r = {"dense_equivalent_per_step": dense_eq, "algorithmic_per_step": alg,
          "live_kblock_fraction": None if live is None else round(live, 4), "products_path": path,
          "dense_equivalent_tflops": rate(dense_eq), "algorithmic_tflops": rate(alg),
+         "algorithmic_frac_of_measured_sustained": round(alg / (ms * 1e-3) / 1e12 / pk["bf16_tflops_sustained"], 4),
          "peak_tflops": pk["bf16_tflops_sustained"]}
     if exe is not None:
         r["executed_per_step"] = exe
@@ -540,7 +631,8 @@ def main():
     if args.impl == "reference":
         if rank == 0:
             # each step: one bounded sample (args.cpu_tokens tokens) of the workload
-            cb = cpu_baseline(args.cpu_tokens, steps=args.steps, warmup=args.warmup)
+            cb = cpu_reference_ffn(args.cpu_tokens, D_MODEL, D_FF, args.steps, args.warmup,
+                                   sparsity=SPARSITY)
             line = {"impl": "reference", "metric": METRIC, "value": cb["value"],
                     "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
                     "warmup": args.warmup, "higher_is_better": True, "dtype": "f32",
@@ -587,26 +679,31 @@ def main():
     with ClockSampler(local) as clk, _lib.KernelTimer() as ktimer:
         ms = time_steps(step, args.steps, args.warmup, device)
     clocks = clk.summary()
+    # a bounded device wait that ran out inside the timed steps would show here
+    status_after = sf.check_status(device, raise_on_error=False)
     tokens = tpg * world
     value = tokens / (ms / 1e3)
     kernels = kernel_breakdown(ktimer, args.steps + args.warmup, ms)
 
-    # end to end: every step copies a step's input from pinned host memory and
-    # reads its loss back.  As a training loop's input pipeline would, the copy
-    # of the next step's input runs on a second stream into the other of two
-    # device buffers while this step computes (PCIe and the SMs work side by
-    # side); each step waits for its own input's copy.
+    # end to end: every step copies that step's inputs -- the activations x and
+    # the upstream gradient dout -- from pinned host memory and reads its loss
+    # back.  As a training loop's input pipeline would, the copies of the next
+    # step's inputs run on a second stream into the other of two device buffer
+    # pairs while this step computes (PCIe and the SMs work side by side); each
+    # step waits for its own inputs' copies.
     x_host = x.cpu().pin_memory()
+    dout_host = dout.cpu().pin_memory()
     copy_stream = torch.cuda.Stream(device)
-    bufs = [torch.empty_like(x), torch.empty_like(x)]
+    bufs = [(torch.empty_like(x), torch.empty_like(dout)) for _ in range(2)]
     ready = [torch.cuda.Event(), torch.cuda.Event()]
     free = [torch.cuda.Event(), torch.cuda.Event()]
     pipe = {"i": 0, "primed": False}
 
     def issue_copy(k):
         with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(free[k])  # the buffer's previous step is done with it
-            bufs[k].copy_(x_host, non_blocking=True)
+            copy_stream.wait_event(free[k])  # the buffers' previous step is done with them
+            bufs[k][0].copy_(x_host, non_blocking=True)
+            bufs[k][1].copy_(dout_host, non_blocking=True)
             ready[k].record(copy_stream)
 
     loss_holder = {}
@@ -617,8 +714,8 @@ def main():
             issue_copy(k)
             pipe["primed"] = True
         torch.cuda.current_stream(device).wait_event(ready[k])
-        issue_copy(1 - k)  # the next step's input, during this step
-        out = step(bufs[k])
+        issue_copy(1 - k)  # the next step's inputs, during this step
+        out = step(*bufs[k])
         free[k].record(torch.cuda.current_stream(device))
         loss_holder["l"] = float(out.float().pow(2).mean().item())
         pipe["i"] += 1
@@ -627,7 +724,8 @@ def main():
     if not args.quick:
         e2e_ms = time_steps(e2e_step, max(3, args.steps // 2), 3, device)
         e2e = {"value": round(tokens / (e2e_ms / 1e3), 1), "unit": "tokens/s",
-               "h2d_bytes_per_step": x.numel() * x.element_size(), "d2h_bytes_per_step": 4}
+               "h2d_bytes_per_step": x.numel() * x.element_size() + dout.numel() * dout.element_size(),
+               "d2h_bytes_per_step": 4}
 
     extras = {}
     if rank == 0 and not args.quick:
@@ -663,7 +761,7 @@ def main():
         extras["sweep"] = sweep
 
     pk = peaks()
-    roof = roofline(kernels, tpg, pk)
+    roof = roofline(kernels, tpg, pk, s_meas)
     flops = step_flops(step, ms, s_meas, pk) if rank == 0 else None
     pack = codec = deep_ffn = gpt_step = None
     if rank == 0 and not args.quick:
@@ -693,18 +791,21 @@ def main():
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
             "codec15": codec, "deep_ffn": deep_ffn, "gpt": gpt_step, "flops": flops,
             "gpu_launches": launches_per_step * args.steps,
+            "device_status_after_timed": status_after,
         }
         line.update(extras)
         if world == 1 and not args.quick:
             try:
                 # about 10 s of host work: 8 samples after one untimed
-                line["cpu_baseline"] = cpu_baseline(args.cpu_tokens, steps=8, warmup=1)
+                line["cpu_baseline"] = cpu_baselines(args.cpu_tokens, steps=6, warmup=1)
             except Exception as e:  # noqa: BLE001
                 line["cpu_baseline"] = {"error": repr(e)}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    if status_after:
+        sys.exit(f"device status 0x{status_after:x} after the timed steps: the run is not valid")
 
 
 if __name__ == "__main__":

@@ -80,7 +80,10 @@ size_t sffn_flat_workspace_bytes(int64_t n);
 /* bitsparse_pack(dense, block) -> (vals, packed_mask)
  *   replaces old/sparse_pack.py:66-106 (kernels :6-63) and
  *   old/bitpack/train.py:65-103 (compress_dense).
- * One pass over dense.  Writes ceil(n/8) bytes to packed_mask, the nonzeros
+ * Two kernels: the first reads dense once for the mask bytes and per-tile
+ * counts, the second reads it again to compact the nonzeros (see
+ * sffn_flat_pack_noalloc for a single-read form).  Writes ceil(n/8) bytes to
+ * packed_mask, the nonzeros
  * to vals[0, nnz) (at most vals_capacity are written; more sets
  * SFFN_STATUS_VALS_OVERFLOW), and nnz to *nnz_dev (device int64).
  * dense must be 16-byte aligned, packed_mask 4-byte aligned. */
@@ -109,9 +112,12 @@ int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_t* packed_m
  * loads the library until exit).  Allocates and frees nothing.  n is at most
  * 67,108,864 (bf16, fp16) or 33,554,432 (fp32); larger n returns
  * SFFN_ERR_TOO_LARGE with the limit in sffn_last_cuda_error().  The
- * first call on a device looks up the array's address (make it before any
- * stream capture); calls share the array, so calls that overlap on the GPU
- * race and must be serialised by the caller. */
+ * first call on a device (in each CUDA context of it) looks up the array's
+ * address (make it before any stream capture); calls share the array, so
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * The device is the one that owns dense (nnz_dev's for n == 0); every other
+ * pointer must live on it (else SFFN_ERR_ARG).  The caller's current device
+ * (context) is the same on return as on entry. */
 int sffn_flat_pack_noalloc(const void* dense, int dtype, int64_t n,
                            uint8_t* packed_mask, void* vals, int64_t vals_capacity,
                            int64_t* nnz_dev, uint32_t* status_dev, void* stream);
@@ -351,6 +357,20 @@ int sffn_codec15_compress(const void* src, int64_t n, uint8_t* dst, int64_t dst_
  * dst[i] = field i (sign bit 0).  Reads only the first sffn_codec15_bytes(n)
  * of src's src_bytes. */
 int sffn_codec15_uncompress(const uint8_t* src, int64_t src_bytes, int64_t n, void* dst, void* stream);
+
+/* ---- bounded waits ------------------------------------------------------ */
+
+/* Test hook, no counterpart in the reference.  Runs one of this library's
+ * bounded device waits on a condition that never comes true, giving up after
+ * limit_ns (0 < limit_ns <= 100 ms) instead of the 500 ms the kernels use:
+ * kind 0 waits on an mbarrier that nothing arrives on (the GEMM and pack
+ * pipelines' wait), kind 1 is a decoupled look-back over predecessors that
+ * never publish (the tiled and flat packs' wait) and needs 64 uint64 of
+ * device memory in `states` (cleared by the call).  The wait records
+ * SFFN_STATUS_WAIT_TIMEOUT in *status_dev and the kernel returns; when
+ * elapsed_ns_dev is non-null it receives the wait's duration (%globaltimer). */
+int sffn_wait_probe(int kind, int64_t limit_ns, uint64_t* states, uint64_t* elapsed_ns_dev,
+                    uint32_t* status_dev, void* stream);
 
 #ifdef __cplusplus
 }

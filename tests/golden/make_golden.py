@@ -2,8 +2,8 @@
 
 The reference (Maccy-Z/autoresearch2) is Python + Triton.  Its kernels run on
 the CPU under Triton's interpreter (``TRITON_INTERPRET=1``), so this script
-imports the reference modules from a checkout given by ``--ref`` (default:
-``/root/reference``), calls its public functions and raw kernels on small,
+imports the reference modules from the checkout named by ``--ref`` (required),
+calls its public functions and raw kernels on small,
 seeded inputs, and stores inputs and outputs as ``.npz`` files next to this
 script.  The fixtures are committed; nothing at test time reads the reference.
 
@@ -20,7 +20,7 @@ arithmetic):
     arena arguments (TypeError in the reference) -> forward is re-run with the
     arena passed; ``backward`` is the reference's own.
 
-Usage:  python tests/golden/make_golden.py [--ref /path/to/reference]
+Usage:  python tests/golden/make_golden.py --ref /path/to/reference
 """
 import argparse
 import builtins
@@ -328,7 +328,7 @@ def gen_codec15(ref, out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="path of a checkout of the reference")
     args = ap.parse_args()
     torch.manual_seed(0)
     mods = _import_ref(args.ref)
