@@ -86,15 +86,34 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
                                                         const uint16_t* __restrict__ slots,
                                                         const int* __restrict__ vals_offset,
                                                         uint16_t* __restrict__ vals, long long cap,
-                                                        uint32_t* __restrict__ status) {
+                                                        uint32_t* __restrict__ status,
+                                                        uint4* __restrict__ colmask) {
     __shared__ int s_warp[4];
+    __shared__ uint4 s_or[4];
     const long long t = blockIdx.x;
     const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
     const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
     const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
     const int inc = warp_incl_scan(cnt, lane);
     if (lane == 31) s_warp[warp] = inc;
+    if (colmask) {
+        // the tile's live columns: OR of its 128 rows' mask words
+        const uint4 o = make_uint4(__reduce_or_sync(FULL, mw.x), __reduce_or_sync(FULL, mw.y),
+                                   __reduce_or_sync(FULL, mw.z), __reduce_or_sync(FULL, mw.w));
+        if (lane == 0) s_or[warp] = o;
+    }
     __syncthreads();
+    if (colmask && r == 0) {
+        uint4 o = s_or[0];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            o.x |= s_or[w].x;
+            o.y |= s_or[w].y;
+            o.z |= s_or[w].z;
+            o.w |= s_or[w].w;
+        }
+        colmask[t] = o;
+    }
     int before = 0;
     for (int w = 0; w < warp; ++w) before += s_warp[w];
     const int roff = prefix[t] + before + inc - cnt;
@@ -224,6 +243,194 @@ __global__ void __launch_bounds__(256) transpose16_kernel(const uint16_t* __rest
     }
 }
 
+// ---------------------------------------------------------------------------
+// Compacted-K operands of the bitmask-sparse down-projection (and dX).
+//
+// For each 128-row tile tm of a [T, F] activation in the 128x128 tiled
+// format, the live columns are those holding a set bit in any of the tile's
+// rows (the OR of the rows' mask words, `colmask`, one uint4 per format tile,
+// written by tile_rows_kernel).  The contraction over F then runs over the
+// tile's live columns only: the activation's live columns, compacted, times
+// the rows of the other operand gathered at the same column indices.
+// ---------------------------------------------------------------------------
+constexpr int CK_LIST_T = 128;
+
+// One CTA per row tile: counts per 128-column block, their exclusive prefix
+// (colpref[tm][n], by warp prefix sums), the ascending live-column list
+// idx[tm][0, K) and its padding up to a multiple of 64 with a dead column of
+// the tile (whose entries are zero in every row of it), and kcount[tm] = K.
+__global__ void __launch_bounds__(CK_LIST_T) ck_lists_kernel(const uint4* __restrict__ colmask, int gn, int F,
+                                                            int* __restrict__ idx, long long ld_idx,
+                                                            int* __restrict__ kcount, int* __restrict__ colpref) {
+    extern __shared__ int s_cnt[];  // [gn] counts, then exclusive prefixes
+    __shared__ int s_warp[CK_LIST_T / 32];
+    __shared__ int s_dead;
+    const int tm = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint4* cm = colmask + (long long)tm * gn;
+    if (tid == 0) s_dead = 0x7FFFFFFF;
+    __syncthreads();
+    // per-thread run of blocks, counts and the first dead column below F
+    const int per = (gn + CK_LIST_T - 1) / CK_LIST_T;
+    const int lo = min(tid * per, gn), hi = min(lo + per, gn);
+    int run = 0, dead = 0x7FFFFFFF;
+    for (int n = lo; n < hi; ++n) {
+        const uint4 L = __ldg(cm + n);
+        const int c = __popc(L.x) + __popc(L.y) + __popc(L.z) + __popc(L.w);
+        s_cnt[n] = c;
+        run += c;
+        if (dead == 0x7FFFFFFF && c < 128) {
+            const uint32_t w[4] = {L.x, L.y, L.z, L.w};
+            for (int q = 0; q < 4 && dead == 0x7FFFFFFF; ++q)
+                if (~w[q]) {
+                    const int col = n * 128 + 32 * q + __ffs(~w[q]) - 1;
+                    if (col < F) dead = col;
+                }
+        }
+    }
+    if (dead != 0x7FFFFFFF) atomicMin(&s_dead, dead);
+    const int inc = warp_incl_scan(run, lane);
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int w = 0; w < CK_LIST_T / 32; ++w) {
+        if (w < warp) before += s_warp[w];
+        total += s_warp[w];
+    }
+    if (!idx) {  // counts only
+        if (tid == 0) kcount[tm] = total;
+        return;
+    }
+    int p = before + inc - run;
+    for (int n = lo; n < hi; ++n) {
+        const int c = s_cnt[n];
+        s_cnt[n] = p;
+        if (colpref) colpref[(long long)tm * gn + n] = p;
+        p += c;
+    }
+    __syncthreads();
+    int* list = idx + (long long)tm * ld_idx;
+    // thread = column of a block: coalesced writes of each block's live columns
+    for (int n = 0; n < gn; ++n) {
+        const uint4 L = __ldg(cm + n);
+        const uint32_t w[4] = {L.x, L.y, L.z, L.w};
+        const int q = tid >> 5, b = tid & 31;
+        if ((w[q] >> b) & 1u) {
+            int rank = __popc(w[q] & ((1u << b) - 1u));
+            for (int k = 0; k < q; ++k) rank += __popc(w[k]);
+            list[s_cnt[n] + rank] = n * 128 + tid;
+        }
+    }
+    const int padded = (total + 63) & ~63;
+    for (int j = total + tid; j < padded; j += CK_LIST_T) list[j] = s_dead;  // total < padded <= F: a dead column exists
+    if (tid == 0) kcount[tm] = total;
+}
+
+// One CTA (128 threads, thread = row) per format tile (tm, n): the tile's
+// values of z from the packed form (bitmask, per-row offsets into vals),
+// act(z) (z*z rounded to bf16 for ReLU^2, z for ReLU) at the tile's live
+// columns, zeros where the row's bit is clear, written as row segments of
+// ac[row][colpref[tm][n] ...] through shared memory.
+constexpr int CK_SROW = 130;  // staged row stride in elements (65 words: conflict-free by row)
+constexpr int CK_GATHER_SMEM = (16384 + 128 * CK_SROW) * 2;
+__global__ void __launch_bounds__(128) ck_gather_packed_kernel(const uint16_t* __restrict__ vals, long long vals_len,
+                                                               const uint8_t* __restrict__ mask,
+                                                               const int* __restrict__ prefix,
+                                                               const int* __restrict__ row_offsets,
+                                                               const int* __restrict__ vals_offset,
+                                                               const uint4* __restrict__ colmask,
+                                                               const int* __restrict__ colpref,
+                                                               const int* __restrict__ kcount, int gn, int act,
+                                                               uint16_t* __restrict__ ac, long long ld_ac,
+                                                               uint32_t* __restrict__ status) {
+    // the tile's values (contiguous in vals, read coalesced), then the staged
+    // output rows
+    extern __shared__ __align__(16) uint16_t s_dyn[];
+    uint16_t* s_vals = s_dyn;
+    uint16_t* s_tile = s_dyn + 16384;
+    const int tm = blockIdx.x, n = blockIdx.y;
+    const long long t = (long long)tm * gn + n;
+    const int r = threadIdx.x;
+    if (n == 0) {
+        // the list's padding columns [K, K rounded up to 64) are zero
+        const int K = __ldg(kcount + tm), Kp = (K + 63) & ~63;
+        uint16_t* row = ac + ((long long)tm * 128 + r) * ld_ac;
+        for (int j = K; j < Kp; ++j) row[j] = 0;
+    }
+    const uint4 L = __ldg(colmask + t);
+    const uint32_t lw[4] = {L.x, L.y, L.z, L.w};
+    const int cnt = __popc(L.x) + __popc(L.y) + __popc(L.z) + __popc(L.w);
+    if (cnt == 0) return;  // uniform over the CTA
+    const uint4 b4 = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
+    const uint32_t bw[4] = {b4.x, b4.y, b4.z, b4.w};
+    const int p0 = __ldg(prefix + t), tcnt = min(__ldg(prefix + t + 1) - p0, 16384);
+    const long long vb = (long long)*vals_offset + p0;
+    bool short_vals = false;
+    for (int i = r; i < tcnt; i += 128) {
+        uint16_t v = 0;
+        if (vb + i < vals_len) {
+            v = __ldg(vals + vb + i);
+            if (act == 1) v = __bfloat16_as_ushort(__hmul(__ushort_as_bfloat16(v), __ushort_as_bfloat16(v)));
+        } else {
+            short_vals = true;
+        }
+        s_vals[i] = v;
+    }
+    if (short_vals) atomicOr(status, SFFN_STATUS_VALS_SHORT);
+    __syncthreads();
+    int p = __ldg(row_offsets + t * 128 + r) - p0;  // this row's first value in s_vals
+    uint16_t* srow = s_tile + r * CK_SROW;
+    int k = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t live = lw[q];  // the same for every thread: uniform loop
+        while (live) {
+            const int c = __ffs(live) - 1;
+            live &= live - 1u;
+            const uint32_t hit = (bw[q] >> c) & 1u;
+            srow[k++] = hit && p < tcnt ? s_vals[p] : (uint16_t)0;
+            p += (int)hit;
+        }
+    }
+    __syncthreads();
+    // warp w writes rows w, w + 4, ...: each row's cnt values are contiguous
+    const int warp = r >> 5, lane = r & 31;
+    const long long col0 = __ldg(colpref + t);
+    for (int rr = warp; rr < 128; rr += 4) {
+        uint16_t* dst = ac + ((long long)tm * 128 + rr) * ld_ac + col0;
+        const uint16_t* src = s_tile + rr * CK_SROW;
+        for (int j = lane; j < cnt; j += 32) dst[j] = src[j];
+    }
+}
+
+// In place, one warp per row of x [T, ld]: x[row][j] = x[row][idx[tm][j]]
+// for j < K, 32 at a time in ascending j, then zeros up to the padded count.
+// Since idx ascends with idx[j] >= j, a read never sees a position an earlier
+// round wrote, and each round's reads finish before its writes (__syncwarp).
+// Rows of tiles whose every column is live are left as they are.
+__global__ void __launch_bounds__(256) ck_compact_rows_kernel(uint16_t* __restrict__ x, long long ld, int F,
+                                                             long long T, const int* __restrict__ idx,
+                                                             long long ld_idx, const int* __restrict__ kcount) {
+    const long long row = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (row >= T) return;
+    const int lane = threadIdx.x & 31;
+    const int tm = (int)(row >> 7);
+    const int K = __ldg(kcount + tm);
+    if (K >= F) return;
+    const int Kp = (K + 63) & ~63;
+    const int* list = idx + (long long)tm * ld_idx;
+    uint16_t* xr = x + row * ld;
+    for (int j0 = 0; j0 < K; j0 += 32) {
+        const int j = j0 + lane;
+        uint16_t v = 0;
+        if (j < K) v = xr[__ldg(list + j)];
+        __syncwarp();
+        if (j < K) xr[j] = v;
+        __syncwarp();
+    }
+    for (int j = K + lane; j < Kp; j += 32) xr[j] = 0;
+}
+
 }  // namespace
 }  // namespace sffn
 
@@ -260,26 +467,26 @@ extern "C" int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int6
 extern "C" int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int32_t* prefix,
                                       const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
                                       int64_t vals_capacity, int dtype, int32_t* row_offsets,
-                                      uint32_t* status_dev, void* stream) {
+                                      uint32_t* colmask, uint32_t* status_dev, void* stream) {
     if (dtype != SFFN_BF16 && dtype != SFFN_F16) return SFFN_ERR_DTYPE;
     if (ntiles <= 0 || !slots || !bitmask || !prefix || !vals_offset_dev || !vals || !status_dev)
         return SFFN_ERR_ARG;
-    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
+    if (!aligned16(bitmask) || !aligned16(colmask)) return SFFN_ERR_ALIGN;
     SFFN_BIND(dev_scope, vals);
     tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         bitmask, prefix, row_offsets, static_cast<const uint16_t*>(slots), vals_offset_dev,
-        static_cast<uint16_t*>(vals), vals_capacity, status_dev);
+        static_cast<uint16_t*>(vals), vals_capacity, status_dev, reinterpret_cast<uint4*>(colmask));
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
 
 extern "C" int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t ntiles,
-                                     int32_t* row_offsets, void* stream) {
-    if (ntiles <= 0 || !bitmask || !prefix || !row_offsets) return SFFN_ERR_ARG;
-    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
-    SFFN_BIND(dev_scope, row_offsets);
+                                     int32_t* row_offsets, uint32_t* colmask, void* stream) {
+    if (ntiles <= 0 || !bitmask || !prefix || (!row_offsets && !colmask)) return SFFN_ERR_ARG;
+    if (!aligned16(bitmask) || !aligned16(colmask)) return SFFN_ERR_ALIGN;
+    SFFN_BIND(dev_scope, bitmask);
     tile_rows_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        bitmask, prefix, row_offsets, nullptr, nullptr, nullptr, 0, nullptr);
+        bitmask, prefix, row_offsets, nullptr, nullptr, nullptr, 0, nullptr, reinterpret_cast<uint4*>(colmask));
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -296,6 +503,58 @@ extern "C" int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, i
     const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));
     live_kblocks_kernel<<<grid, LIVE_WARPS * 32, 0, st>>>(bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list,
                                                          kb_count);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Compacted-K operands (see the kernels above).
+// ---------------------------------------------------------------------------
+extern "C" int sffn_ck_lists(const uint32_t* colmask, int64_t T, int64_t F, int32_t* idx, int64_t ld_idx,
+                             int32_t* kcount, int32_t* colpref, void* stream) {
+    if (T <= 0 || F <= 0 || T % 128 || F % 64 || !colmask || !kcount || (!idx && colpref)) return SFFN_ERR_ARG;
+    if (ld_idx < F || F > 65536 || !aligned16(colmask)) return SFFN_ERR_ARG;
+    const long long gm = T / 128, gn = (F + 127) / 128;
+    if (gm > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    SFFN_BIND(dev_scope, colmask);
+    ck_lists_kernel<<<(unsigned)gm, CK_LIST_T, (size_t)gn * sizeof(int), reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint4*>(colmask), (int)gn, (int)F, idx, ld_idx, kcount, colpref);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_ck_gather_packed(const void* vals, int64_t vals_len, const uint8_t* bitmask,
+                                     const int32_t* prefix, const int32_t* row_offsets,
+                                     const int32_t* vals_offset_dev,
+                                     const uint32_t* colmask, const int32_t* colpref, const int32_t* kcount,
+                                     int64_t T, int64_t F, int act, void* ac, int64_t ld_ac, uint32_t* status_dev,
+                                     void* stream) {
+    if (T <= 0 || F <= 0 || T % 128 || F % 64 || (act != 0 && act != 1)) return SFFN_ERR_ARG;
+    if (!vals || !bitmask || !prefix || !row_offsets || !vals_offset_dev || !colmask || !colpref || !kcount || !ac ||
+        !status_dev)
+        return SFFN_ERR_ARG;
+    if (ld_ac < F || !aligned16(bitmask) || !aligned16(colmask)) return SFFN_ERR_ARG;
+    const long long gm = T / 128, gn = (F + 127) / 128;
+    if (gm > 0x7FFFFFFF || gn > 65535) return SFFN_ERR_ARG;
+    SFFN_BIND(dev_scope, ac);
+    SFFN_CUDA_TRY(cudaFuncSetAttribute(ck_gather_packed_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       CK_GATHER_SMEM));
+    ck_gather_packed_kernel<<<dim3((unsigned)gm, (unsigned)gn), 128, CK_GATHER_SMEM,
+                              reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(vals), vals_len, bitmask, prefix, row_offsets, vals_offset_dev,
+        reinterpret_cast<const uint4*>(colmask), colpref, kcount, (int)gn, act, static_cast<uint16_t*>(ac), ld_ac,
+        status_dev);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_ck_compact_rows(void* x, int64_t ld, int64_t T, int64_t F, const int32_t* idx, int64_t ld_idx,
+                                    const int32_t* kcount, void* stream) {
+    if (T <= 0 || F <= 0 || T % 128 || F % 64 || !x || !idx || !kcount || ld < F || ld_idx < F) return SFFN_ERR_ARG;
+    if (F > 65536) return SFFN_ERR_ARG;
+    SFFN_BIND(dev_scope, x);
+    ck_compact_rows_kernel<<<(unsigned)((T + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint16_t*>(x), ld, (int)F, (long long)T, idx, ld_idx, kcount);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

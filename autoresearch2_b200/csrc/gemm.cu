@@ -536,8 +536,10 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             stage_words(sbuf, lane, w);  // own row: read back by this lane only
                             mw[c] = sp24_emit(args.sp[0], w, grow, gcol, lane,
                                               [&](int e) { return staged_elem(sbuf, lane, e); });
-                        } else if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
-                        else if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                        } else if (args.out) {  // no dense activation when the caller passed none
+                            if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                            else if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                        }
                         // this chunk's z values, in column order, to the row's slot segment
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
@@ -1027,6 +1029,279 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(S_THREADS, 1)
     }
 }
 
+// ------------------------------------------------------- compacted-K GEMM ----
+// C[M, N] = sum over j < K(tm) of Ac[row, j] * B[idx[tm][j], :] for the rows
+// of each 128-row tile tm: the contraction of the bitmask-sparse
+// down-projection (and of dX) over the tile's live columns only.  Ac is the
+// activation with those columns compacted (K-major, [M][lda]); B is the other
+// operand with rows = the contraction index ([K rows][ldb], N contiguous), of
+// which each stage gathers the 64 rows the list names by TMA tile::gather4 (a
+// one-row box, four rows per copy, this GPU's memory only).  The list of tile
+// tm is padded to a multiple of 64 with a column that is zero in every row of
+// the tile, so the padding adds nothing.
+//
+// One CTA per SM, single-CTA (cta_group::1) tcgen05.mma of M = 128, N = 256,
+// K = 16 (a pair of SMs would need one list for 256 rows, whose union of live
+// columns is larger).  Tiles of 128 x 256 are visited in groups of
+// CK_GROUP_M row tiles, row tile fastest, so that the CTAs in flight share
+// Ac tiles and the gathered rows of B (which together exceed L2) across a
+// group.
+//   warp 0       A producer: arms the stage (A and B bytes) and loads the
+//                128 x 64 Ac block (128-byte swizzle).
+//   warp 3       B producer: lane l holds four list entries (K rows 4(l%16)
+//                .., loaded a stage ahead).  When the stage's 64 rows are
+//                consecutive (whole live column runs, as clustered sparsity
+//                gives) lane 0 loads them as four tiled 64 x 64 boxes;
+//                otherwise each lane gathers its four rows for two of the
+//                four 64-column N blocks.
+//   warp 1       MMA issuer (one thread), two accumulators of 256 columns.
+//   warp 2       allocates / frees the 512 tensor-memory columns.
+//   warps 4..11  epilogue, two warpgroups of 128 columns (thread = row).
+constexpr int CK_STAGES = 4;
+constexpr int CK_BN = 256;
+constexpr int CK_THREADS = 12 * 32;
+constexpr int CK_A_BYTES = G_BM * G_BK * 2;      // 16 KB
+constexpr int CK_B_BYTES = CK_BN * G_BK * 2;     // 32 KB: four MN blocks of 64 K rows x 128 B
+constexpr int CK_STAGE_BYTES = CK_A_BYTES + CK_B_BYTES;
+constexpr int CK_SMEM = CK_STAGES * CK_STAGE_BYTES + 8 * 2048 + 1024;
+constexpr int CK_GROUP_M = 16;
+
+__device__ __forceinline__ void ck_raster(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+    const int per_group = CK_GROUP_M * tiles_n;
+    const int group = tile / per_group;
+    const int first_m = group * CK_GROUP_M;
+    const int gsize = min(tiles_m - first_m, CK_GROUP_M);
+    const int r = tile - group * per_group;
+    tm = first_m + r % gsize;
+    tn = r / gsize;
+}
+
+struct CkArgs {
+    int M, N;
+    int tiles_m, tiles_n;
+    const int* idx;     // [tiles_m][ld_idx] row of B for each compacted column
+    long long ld_idx;
+    const int* kcount;  // [tiles_m] live columns of the tile (its list is padded to 64)
+    int vec_out;
+    uint16_t* out;
+    long long ldc;
+    uint32_t* status;
+};
+
+__global__ void __launch_bounds__(CK_THREADS, 1)
+    gemm_ck_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmBt, const __grid_constant__ CUtensorMap tmC,
+                   const CkArgs args) {
+    constexpr uint32_t IDESC = idesc_bf16_f32(G_BM, CK_BN, false, true);
+    constexpr uint32_t MN_LBO = G_BK * 128;
+    extern __shared__ __align__(1024) unsigned char g_smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    __shared__ __align__(8) uint64_t full_bar[CK_STAGES];
+    __shared__ __align__(8) uint64_t empty_bar[CK_STAGES];
+    __shared__ __align__(8) uint64_t tfull_bar[2];
+    __shared__ __align__(8) uint64_t tempty_bar[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = args.tiles_m * args.tiles_n;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < CK_STAGES; ++s) {
+            mbar_init(&full_bar[s], 1);   // the A producer's arrive.expect_tx
+            mbar_init(&empty_bar[s], 1);  // one commit per use
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 8);  // every epilogue warp
+        }
+        s_abort = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB);
+        prefetch_tmap(&tmBt);
+    }
+    if (warp == 2) {
+        tmem_alloc(&s_tmem, 2 * CK_BN);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem;
+
+    auto nkb_of = [&](int tm) { return (__ldg(args.kcount + tm) + G_BK - 1) / G_BK; };
+
+    if (warp == 0 || warp == 3) {
+        // ----------------------------------------------------- producers --
+        const bool loads_a = warp == 0;
+        if (loads_a ? lane == 0 : true) {
+            int armed[CK_STAGES] = {0};
+            long long kc = 0;
+            bool stop = false;
+            const int g = lane & 15, h = lane >> 4;  // B: K rows 4g .. 4g+3, N blocks 2h, 2h+1
+            for (int tile = blockIdx.x; tile < ntiles && !stop; tile += gridDim.x) {
+                bool ab = s_abort != 0;
+                if (!loads_a) ab = __any_sync(FULL, ab);  // the B warp's lanes stay converged
+                if (ab) break;
+                int tm, tn;
+                ck_raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+                const int nkb = nkb_of(tm);
+                const int* list = args.idx + (long long)tm * args.ld_idx;
+                int4 r4 = make_int4(0, 0, 0, 0);
+                if (!loads_a && nkb > 0) r4 = __ldg(reinterpret_cast<const int4*>(list + 4 * g));
+                for (int i = 0; i < nkb; ++i, ++kc) {
+                    const int stage = (int)(kc % CK_STAGES);
+                    const uint32_t phase = (uint32_t)((kc / CK_STAGES) & 1);
+                    // the B warp decides together: its lanes shuffle and vote below
+                    const bool freed = loads_a ? mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)
+                                               : __all_sync(FULL, mbar_wait_bounded(&empty_bar[stage], phase ^ 1u));
+                    if (!freed) {
+                        atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
+                        s_abort = 1;
+                        stop = true;
+                        break;
+                    }
+                    unsigned char* sa = smem + (size_t)stage * CK_STAGE_BYTES;
+                    unsigned char* sb = sa + CK_A_BYTES;
+                    ++armed[stage];
+                    if (loads_a) {
+                        mbar_arrive_expect_tx(&full_bar[stage], CK_STAGE_BYTES);
+                        tma_load_2d(sa, &tmA, i * G_BK, tm * G_BM, &full_bar[stage]);
+                    } else {
+                        const int4 cur = r4;
+                        if (i + 1 < nkb)  // the next stage's entries, in flight while this one is issued
+                            r4 = __ldg(reinterpret_cast<const int4*>(list + (i + 1) * G_BK + 4 * g));
+                        const int base = __shfl_sync(FULL, cur.x, 0);
+                        const bool run = cur.x == base + 4 * g && cur.y == base + 4 * g + 1 &&
+                                         cur.z == base + 4 * g + 2 && cur.w == base + 4 * g + 3;
+                        if (__all_sync(FULL, run)) {
+                            // 64 consecutive rows of B: four tiled 64 x 64 boxes
+                            if (lane == 0)
+#pragma unroll
+                                for (int blk = 0; blk < 4; ++blk)
+                                    tma_load_2d(sb + blk * MN_LBO, &tmBt, tn * CK_BN + blk * 64, base, &full_bar[stage]);
+                        } else {
+#pragma unroll
+                            for (int b = 0; b < 2; ++b) {
+                                const int blk = 2 * h + b;
+                                tma_gather4(sb + blk * MN_LBO + g * 512, &tmB, tn * CK_BN + blk * 64, cur.x, cur.y,
+                                            cur.z, cur.w, &full_bar[stage]);
+                            }
+                        }
+                    }
+                }
+            }
+            // the full barriers count both operands' bytes: once the last phase
+            // this thread loaded into completes, none of its copies is landing
+            for (int s = 0; s < CK_STAGES; ++s)
+                if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ----------------------------------------------------------- MMA --
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            int acc = 0;
+            uint32_t acc_phase = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !s_abort; tile += gridDim.x) {
+                int tm, tn;
+                ck_raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+                const int nkb = nkb_of(tm);
+                if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u)) {
+                    atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
+                    s_abort = 1;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * CK_BN);
+                bool ready = nkb > 0 && mbar_try_wait(&full_bar[stage], phase);
+                bool fail = false;
+                for (int i = 0; i < nkb; ++i) {
+                    if (!ready && !mbar_wait_bounded(&full_bar[stage], phase)) {
+                        atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
+                        s_abort = 1;
+                        fail = true;
+                        break;
+                    }
+                    const uint32_t sa = smem_u32(smem + (size_t)stage * CK_STAGE_BYTES);
+                    const uint32_t sb = sa + CK_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < G_BK / 16; ++k)
+                        tc_mma_f16(d, umma_desc_sw128(sa + k * 32, 16, 1024), umma_desc_sw128(sb + k * 2048, MN_LBO, 1024),
+                                   IDESC, (i | k) != 0 ? 1u : 0u);
+                    tc_commit(&empty_bar[stage]);
+                    if (++stage == CK_STAGES) {
+                        stage = 0;
+                        phase ^= 1u;
+                    }
+                    ready = i + 1 < nkb && mbar_try_wait(&full_bar[stage], phase);
+                }
+                if (fail) break;
+                tc_commit(&tfull_bar[acc]);
+                if (++acc == 2) {
+                    acc = 0;
+                    acc_phase ^= 1u;
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp >= 4) {
+        // ------------------------------------------------------ epilogue --
+        const int wg = (warp - 4) >> 2;
+        const int ew = warp & 3;
+        unsigned char* sbuf = smem + (size_t)CK_STAGES * CK_STAGE_BYTES + (size_t)(warp - 4) * 2048;
+        int acc = 0;
+        uint32_t acc_phase = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+            int tm, tn;
+            ck_raster(tile, args.tiles_m, args.tiles_n, tm, tn);
+            const int nkb = nkb_of(tm);
+            const bool ok = __all_sync(FULL, mbar_wait_bounded(&tfull_bar[acc], acc_phase));
+            if (!ok || __any_sync(FULL, s_abort != 0)) {
+                if (lane == 0) atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t tbase = tmem_base + ((uint32_t)(ew * 32) << 16) + (uint32_t)(acc * CK_BN + wg * 128);
+            const int row0 = tm * G_BM + ew * 32;
+            const int grow = row0 + lane;
+            const int gcol0 = tn * CK_BN + wg * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld32(tbase + c * 32, r);
+                tmem_wait_ld();
+                uint32_t w[16];
+#pragma unroll
+                for (int q = 0; q < 16; ++q)
+                    w[q] = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])) : 0u;
+                if (args.vec_out) {
+                    stage_store32(&tmC, sbuf, lane, w, gcol0 + c * 32, row0);
+                } else if (grow < args.M) {
+                    store_row32(args.out + (size_t)grow * args.ldc, gcol0 + c * 32, args.N, false, w);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+            if (++acc == 2) {
+                acc = 0;
+                acc_phase ^= 1u;
+            }
+        }
+        if (lane == 0) bulk_wait_group0();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 2) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, 2 * CK_BN);
+    }
+}
+
 // ------------------------------------------------------------------ host ----
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1239,6 +1514,26 @@ int launch_sp24(const void* vals, const uint32_t* meta, long long M, long long K
     return SFFN_OK;
 }
 
+// The compacted-K GEMM: tensor maps (Ac tiles, one-row gather boxes of B, C
+// store boxes) and a persistent grid of one CTA per SM.
+int launch_gemm_ck(const void* A, long long lda, long long kmax, const void* B, long long ldb, long long krows,
+                   CkArgs args, cudaStream_t st) {
+    CUtensorMap ta, tb, tbt, tc;
+    if (!make_tmap(&ta, A, kmax, args.M, lda, G_BK, G_BM)) return SFFN_ERR_CUDA;
+    if (!make_tmap(&tb, B, args.N, krows, ldb, 64, 1)) return SFFN_ERR_CUDA;     // one-row gather boxes
+    if (!make_tmap(&tbt, B, args.N, krows, ldb, 64, G_BK)) return SFFN_ERR_CUDA;  // runs of 64 rows
+    memset(&tc, 0, sizeof(tc));
+    if (args.vec_out && !make_tmap(&tc, args.out, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+        return SFFN_ERR_CUDA;
+    SFFN_CUDA_TRY(cudaFuncSetAttribute(gemm_ck_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, CK_SMEM));
+    const int ntiles = args.tiles_m * args.tiles_n;
+    const int grid = std::min(ntiles, g_num_sms());
+    if (grid <= 0) return SFFN_OK;
+    gemm_ck_kernel<<<grid, CK_THREADS, CK_SMEM, st>>>(ta, tb, tbt, tc, args);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
 }  // namespace
 }  // namespace sffn
 
@@ -1269,10 +1564,11 @@ extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t l
     int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
-    if (!act_out || ld_act < F || !bitmask || !tile_counts || !slots || !status_dev) return SFFN_ERR_ARG;
+    if ((act_out && ld_act < F) || !bitmask || !tile_counts || !slots || !status_dev) return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
     if (T * F > 0x7FFFFFFFll) return SFFN_ERR_ARG;
-    GemmArgs a = base_args(T, F, D, act_out, ld_act);
+    GemmArgs a = base_args(T, F, D, act_out, act_out ? ld_act : F);
+    if (!act_out) a.vec_out = 0;
     a.act = act;
     a.bias = static_cast<const uint16_t*>(b1);
     a.mask = bitmask;
@@ -1428,4 +1724,32 @@ extern "C" int sffn_sp24_mm(const sffn_sp24_mat* a, int64_t M, int64_t K, const 
     epi.c_trans = c_trans ? 1 : 0;
     return b_mn ? launch_sp24<true>(a->vals, a->meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st)
                 : launch_sp24<false>(a->vals, a->meta, M, K, B, ldb, C, ldc, N, epi, status_dev, st);
+}
+
+extern "C" int sffn_gemm_ck(const void* A, int64_t lda, int64_t kmax, const void* B, int64_t ldb, int64_t krows,
+                            const int32_t* idx, int64_t ld_idx, const int32_t* kcount, void* C, int64_t ldc,
+                            int64_t M, int64_t N, uint32_t* status_dev, void* stream) {
+    // C[M, N] = Ac[M, :K(tm)] * B[idx[tm][:K(tm)], :] per 128-row tile tm.
+    if (M <= 0 || N <= 0 || kmax <= 0 || krows <= 0 || M % 128 || N % CK_BN || kmax % 64) return SFFN_ERR_UNSUPPORTED;
+    if (M > 0x7FFFFFFF || N > 0x7FFFFFFF || kmax > 0x7FFFFFFF || krows > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    if (!A || !B || !C || !idx || !kcount || !status_dev || lda < kmax || ldb < N || ldc < N || ld_idx < kmax)
+        return SFFN_ERR_ARG;
+    if (!aligned16(A) || !aligned16(B) || !aligned16(idx) || (lda * 2) % 16 || (ldb * 2) % 16 || ld_idx % 4)
+        return SFFN_ERR_ALIGN;
+    DeviceScope dev_scope;
+    if (int rc = dev_scope.bind_same(A, {B, C, idx, kcount, status_dev})) return rc;
+    if (!device_is_sm100()) return SFFN_ERR_DEVICE;
+    CkArgs a{};
+    a.M = (int)M;
+    a.N = (int)N;
+    a.tiles_m = (int)(M / 128);
+    a.tiles_n = (int)(N / CK_BN);
+    a.idx = idx;
+    a.ld_idx = ld_idx;
+    a.kcount = kcount;
+    a.out = static_cast<uint16_t*>(C);
+    a.ldc = ldc;
+    a.vec_out = aligned16(C) && (ldc * 2) % 16 == 0;
+    a.status = status_dev;
+    return launch_gemm_ck(A, lda, kmax, B, ldb, krows, a, reinterpret_cast<cudaStream_t>(stream));
 }

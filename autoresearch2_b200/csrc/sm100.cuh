@@ -118,6 +118,21 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const void* tmap, int c0,
         : "memory");
 }
 
+// 2-D TMA gather of four rows (tile::gather4): rows r0..r3 of the tensor
+// map's 2-D tensor, the map's box width of elements from column c0 each, land
+// as four consecutive box rows in shared memory (swizzled by the map's mode,
+// by shared-memory address), completing on `bar`.  The map's box must be one
+// row high; c0 * element size must be a multiple of 16 bytes.  The source is
+// this GPU's own memory; no multicast.
+__device__ __forceinline__ void tma_gather4(void* dst, const void* tmap, int c0, int r0, int r1, int r2, int r3,
+                                            uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
+        : "memory");
+}
+
 // 2-D tiled bulk-tensor store shared -> global, tracked by bulk async-groups.
 // Rows and columns outside the tensor map's extent are not written.
 __device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int c0, int c1) {

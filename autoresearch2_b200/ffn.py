@@ -36,7 +36,8 @@ from . import gemm as G
 from . import sp24
 from .parallel import submit_grad
 
-__all__ = ["FFNSparse", "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "last_path"]
+__all__ = ["FFNSparse", "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "set_compact_k", "compact_k",
+           "last_path", "down_proj", "packed_backward"]
 
 # The four products with a sparse operand -- forward a @ W2^T, backward
 # dpre @ W1, dpre^T @ x and a^T @ dout -- can run on the 2:4 sparse tensor
@@ -52,8 +53,26 @@ __all__ = ["FFNSparse", "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "last_path
 # not, and the sparse products draw less power per step.
 _SPARSE_MMA = "auto"
 AUTO_MIN_SPARSITY = 0.945
-# per layer (keyed by W1's storage and the shapes): pinned count, its copy's
-# event, the element count it refers to, the last sparsity read
+# The down-projection and dX contract over F.  With the compacted-K path
+# ("ck") each 128-row tile of tokens contracts over its live columns only --
+# the columns of z holding a non-zero in any of the tile's rows -- with the
+# activation compacted from the packed z and the rows of W2^T (W1 for dX)
+# gathered by TMA.  Its GEMM runs on one SM per 128-row tile, which needs
+# 1.5x the operand bytes per flop of the two-SM kernel of the dense path and
+# measured at half its rate at the same K (4.81 vs 2.35 ms at 8192 x 8192 x
+# 28672, 2.29 vs 1.32 ms at 16384 x 4096 x 14336 on a B200).  The dense path
+# skips 64-wide K blocks that are zero across a 256-row tile.  So the
+# compacted path pays only where its live fraction is below about half the
+# dense path's: on the clustered workload (live 0.50 per 128 rows, 0.74 per
+# 256 rows) it does not, at 99% random zeros (0.72 against 1.0) it does not,
+# at 99.9% (0.12 against 1.0) it does.  "off" / "on" / "auto" (default): "ck"
+# when the same layer's previous step had at most CK_AUTO_MAX_LIVE of its
+# (128-row tile, column) pairs live.
+_COMPACT_K = "auto"
+CK_AUTO_MAX_LIVE = 0.35
+# per layer (keyed by W1's storage and the shapes): pinned [activation count,
+# live (tile, column) count], its copy's event, the element count, the last
+# sparsity and live fraction read
 _observed = {}
 _last_path = None
 
@@ -73,9 +92,39 @@ def sparse_mma() -> str:
     return _SPARSE_MMA
 
 
+def set_compact_k(mode: str):
+    """Choose the contraction of the bf16 down-projection and dX: "off" (dense
+    K, 64-wide zero blocks skipped), "on" (compacted live columns of each
+    128-row tile) or "auto".  Also forgets the observed statistics."""
+    global _COMPACT_K
+    if mode not in ("off", "on", "auto"):
+        raise ValueError("compact-K mode is 'off', 'on' or 'auto'")
+    _COMPACT_K = mode
+    _observed.clear()
+
+
+def compact_k() -> str:
+    return _COMPACT_K
+
+
 def last_path():
-    """The products' path of the last fused forward: "sp24", "dense" or None."""
+    """The products' path of the last fused forward: "sp24", "ck" (compacted
+    K), "dense" or None."""
     return _last_path
+
+
+def _stats(T, D, Fd, W1):
+    """The layer's last observed (sparsity, live fraction), each None if not
+    seen yet; reads a landed copy without waiting."""
+    ent = _observed.get((W1.data_ptr(), T, D, Fd))
+    if ent is None:
+        return None, None
+    if ent["event"] is not None and ent["event"].query():  # the counts have landed: no wait
+        c = ent["counts"].tolist()
+        ent["sparsity"] = 1.0 - c[0] / ent["elems"]
+        ent["live"] = c[1] / ent["elems"] if c[1] >= 0 else None
+        ent["event"] = None
+    return ent["sparsity"], ent["live"]
 
 
 def _sp24_ok(T, D, Fd, W1):
@@ -84,29 +133,40 @@ def _sp24_ok(T, D, Fd, W1):
         return False
     if _SPARSE_MMA == "on":
         return True
-    ent = _observed.get((W1.data_ptr(), T, D, Fd))
-    if ent is None:
+    s, _ = _stats(T, D, Fd, W1)
+    return s is not None and s >= AUTO_MIN_SPARSITY
+
+
+def _ck_ok(T, D, Fd, W1):
+    if _COMPACT_K == "off" or not G.ck_supported(T, D, Fd):
         return False
-    if ent["event"] is not None and ent["event"].query():  # the count has landed: no wait
-        ent["sparsity"] = 1.0 - int(ent["count"].item()) / ent["elems"]
-        ent["event"] = None
-    return ent["sparsity"] is not None and ent["sparsity"] >= AUTO_MIN_SPARSITY
+    if _COMPACT_K == "on":
+        return True
+    _, live = _stats(T, D, Fd, W1)
+    return live is not None and live <= CK_AUTO_MAX_LIVE
 
 
-def _observe(W1, prefix, T, D, Fd):
-    """Auto mode: copy this step's activation count (prefix[-1]) to pinned host
-    memory without waiting; a later step reads it once its event completed."""
-    if _SPARSE_MMA != "auto":
+def _auto():
+    return _SPARSE_MMA == "auto" or _COMPACT_K == "auto"
+
+
+def _observe(W1, prefix, kcount, T, D, Fd):
+    """Auto modes: copy this step's activation count (prefix[-1]) and live
+    (tile, column) count (the sum of kcount, or -1) to pinned host memory
+    without waiting; a later step reads them once the copy's event completed."""
+    if not _auto():
         return
     key = (W1.data_ptr(), T, D, Fd)
     ent = _observed.get(key)
     if ent is None:
         ent = _observed[key] = {
-            "count": torch.empty(1, dtype=torch.int32, pin_memory=True), "event": None,
-            "elems": 1, "sparsity": None}
+            "counts": torch.empty(2, dtype=torch.int64, pin_memory=True), "event": None,
+            "elems": 1, "sparsity": None, "live": None}
     if ent["event"] is not None:  # the previous copy is still unread
         return
-    ent["count"].copy_(prefix[-1:], non_blocking=True)
+    live = kcount.sum(dtype=torch.int64).view(1) * 128 if kcount is not None else prefix.new_full((1,), -1,
+                                                                                                 dtype=torch.int64)
+    ent["counts"].copy_(torch.cat([prefix[-1:].to(torch.int64), live]), non_blocking=True)
     ent["elems"] = T * Fd
     ent["event"] = torch.cuda.Event()
     ent["event"].record()
@@ -133,22 +193,42 @@ def _fused_forward(x, W1, W2, vals, offset, b1, act):
     Fd = W1.shape[0]
     global _last_path
     use_sp24 = _sp24_ok(T, D, Fd, W1)
-    _last_path = "sp24" if use_sp24 else "dense"
-    # with sp24 the up-projection epilogue writes a in the 2:4 form directly
-    a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24)
-    _observe(W1, prefix, T, D, Fd)
+    use_ck = not use_sp24 and _ck_ok(T, D, Fd, W1)
+    _last_path = "sp24" if use_sp24 else "ck" if use_ck else "dense"
+    want_live = use_ck or (_COMPACT_K == "auto" and G.ck_supported(T, D, Fd))
+    colmask = torch.empty(-(-T // 128) * -(-Fd // 128) * 4, dtype=torch.int32, device=x.device) \
+        if want_live else None
+    # with sp24 the up-projection epilogue writes a in the 2:4 form directly;
+    # with ck it writes no dense activation at all
+    a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24,
+                                                     write_act=not use_ck, colmask=colmask)
+    if use_ck:
+        idx, kcount, colpref = G.ck_lists(colmask, T, Fd)
+    elif want_live:
+        _, kcount, _ = G.ck_lists(colmask, T, Fd, counts_only=True)
+    else:
+        kcount = None
+    _observe(W1, prefix, kcount, T, D, Fd)
     # the K-block lists also serve dX when the backward takes the dense path
     kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
     if use_sp24:
         # 2:4 part on the sparse tensor cores, overflow rows k of W2^T
         out = sp24.mm(a, W2.T, bt=sp24.transpose(W2))
+    elif use_ck:
+        # the activation compacted to each tile's live columns from the packed
+        # z, times the rows of W2^T gathered at the same columns
+        zs = bs.BitsparseTensor(vals, bitmask, prefix, voff, T // 128, Fd // 128, 128, 128, (T, Fd))
+        ac = G.ck_gather_packed(zs, row_offsets, colmask, colpref, kcount, act)
+        out = G.ck_mm(ac, sp24.transpose(W2), idx, kcount)
+        del ac
     else:
         out = G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
     del a
     return out, bitmask, prefix, voff, row_offsets, kb_list, kb_count
 
 
-def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_count, has_bias, act):
+def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_count, has_bias, act,
+                    stats_key=None):
     """bf16 backward -> (grad_x, grad_W1, grad_W2, grad_b1 or None).  The
     products' path is chosen again here, by the same rule as the forward's."""
     T, D = x.shape
@@ -169,6 +249,7 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
         grad_W1 = submit_grad(sp24.mm(dpre_t, x))
         grad_x = sp24.mm(dpre, W1)
         return grad_x, grad_W1, grad_W2, grad_b1
+    use_ck = _ck_ok(T, D, Fd, W1 if stats_key is None else stats_key)
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
     del row_offsets
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
@@ -177,8 +258,57 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
     # dW1 before dX: under data parallelism its all-reduce then overlaps dX, and
     # no weight-gradient reduction is left without compute to hide behind
     grad_W1 = submit_grad(G.mm(dpre.T, x))
-    grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
+    if use_ck:
+        # dpre is zero wherever z is: compact it in place to the live columns
+        # and gather the matching rows of W1
+        idx, kcount, _ = G.ck_lists(G.tile_colmask(z_sparse), T, Fd)
+        grad_x = G.ck_mm(G.ck_compact_rows_(dpre, idx, kcount), W1, idx, kcount)
+    else:
+        grad_x = G.mm(dpre, W1, kb_list=kb_list, kb_count=kb_count)
     return grad_x, grad_W1, grad_W2, grad_b1
+
+
+def down_proj(z_sparse, W2, act=G.ACT_RELU2):
+    """The bitmask-sparse down-projection from a packed activation:
+    out [T, D] = act(z) @ W2^T, act(z) = z*z rounded to bf16 (ReLU^2) or z
+    (ReLU), for z a bf16 128x128-tile BitsparseTensor [T, F] -- the forward
+    product of FFNSpRelu2 / FFNSparse (old/lib_sparse/sparse.py:75,118) and
+    the contraction spAx computes by unpacking (sparse.py:305-351), here
+    without a dense z: on the compacted-K path (set_compact_k) each 128-row
+    tile contracts over its live columns, otherwise the unpacked activation
+    runs through the dense tcgen05 GEMM with zero 64-wide blocks skipped."""
+    T, Fd = z_sparse.shape
+    D = W2.shape[0]
+    if z_sparse.BLOCK_M != 128 or z_sparse.BLOCK_N != 128 or W2.dtype != torch.bfloat16:
+        raise ValueError("down_proj takes a bf16 128x128-tile activation and bf16 weights")
+    global _last_path
+    use_ck = _ck_ok(T, D, Fd, W2)
+    if use_ck or (_COMPACT_K == "auto" and G.ck_supported(T, D, Fd)):
+        # statistics for the auto rule are kept under W2 here
+        colmask = G.tile_colmask(z_sparse)
+        idx, kcount, colpref = G.ck_lists(colmask, T, Fd, counts_only=not use_ck)
+        _observe(W2, z_sparse.prefix, kcount, T, D, Fd)
+    if use_ck:
+        _last_path = "ck"
+        ac = G.ck_gather_packed(z_sparse, G.tile_row_offsets(z_sparse), colmask, colpref, kcount, act)
+        return G.ck_mm(ac, sp24.transpose(W2), idx, kcount)
+    _last_path = "dense"
+    a = bs.tile_unpack(z_sparse, square=act == G.ACT_RELU2)
+    kb_list, kb_count = G.live_kblocks(z_sparse.bitmask, T, Fd)
+    return G.mm(a, W2.T, kb_list=kb_list, kb_count=kb_count)
+
+
+def packed_backward(grad_output, x, W1, W2, z_sparse, act=G.ACT_RELU2):
+    """The backward of out = act(z) @ W2^T with z = relu(x @ W1^T) kept packed
+    (a bf16 128x128-tile BitsparseTensor): (grad_x, grad_W1, grad_W2), the
+    reference's FFNSpRelu2 / FFNSparse backward (old/lib_sparse/sparse.py:
+    83-109,129-151) on this library's kernels, weight gradients handed to an
+    attached GradAllReduce as they are produced."""
+    T, Fd = z_sparse.shape
+    kb_list, kb_count = G.live_kblocks(z_sparse.bitmask, T, Fd)
+    gx, gW1, gW2, _ = _fused_backward(grad_output, x, W1, W2, z_sparse, G.tile_row_offsets(z_sparse), kb_list,
+                                      kb_count, False, act, stats_key=W2)
+    return gx, gW1, gW2
 
 
 def _unfused_forward(x, W1, W2, vals, offset, b1, act):

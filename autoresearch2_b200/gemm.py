@@ -70,12 +70,14 @@ def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
     return kb_list, kb_count
 
 
-def ffn_up(x, W1, b1, act, vals, offset, sp24=False):
+def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=None):
     """Fused x @ W1.T (+ b1) -> act(z) dense plus the tiled 128x128 sparse z.
 
     Returns (act [T, F], bitmask, prefix, vals_offset, row_offsets); act is
     dense, or with sp24=True an ``sp24.Sp24`` (2:4 form, K = F) written by the
-    same epilogue (T, F multiples of 128)."""
+    same epilogue (T, F multiples of 128), or None with write_act=False.
+    colmask (optional int32 [tiles * 4]) receives each format tile's live
+    columns (the OR of its rows' mask words)."""
     T, D = x.shape
     F = W1.shape[0]
     dev = x.device
@@ -96,13 +98,13 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False):
         call("sffn_ffn_up_sp24", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
              ctypes.addressof(d), ptr(bitmask), ptr(counts), ptr(slots), status, st)
     else:
-        act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+        act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev) if write_act else None
         call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
-             ptr(act_out), act_out.stride(0), ptr(bitmask), ptr(counts), ptr(slots), status, st)
+             ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
     call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
-         ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), status, st)
+         ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)
     return act_out, bitmask, prefix, vals_offset, row_offsets
 
 
@@ -110,9 +112,84 @@ def tile_row_offsets(z_sparse):
     """Per-row value offsets of a 128x128-tile BitsparseTensor (int32 [tiles*128])."""
     nt = z_sparse.grid_m * z_sparse.grid_n
     ro = torch.empty(nt * 128, dtype=torch.int32, device=z_sparse.bitmask.device)
-    call("sffn_tile_row_offsets", ptr(z_sparse.bitmask), ptr(z_sparse.prefix), nt, ptr(ro),
+    call("sffn_tile_row_offsets", ptr(z_sparse.bitmask), ptr(z_sparse.prefix), nt, ptr(ro), None,
          stream_ptr(ro.device))
     return ro
+
+
+def tile_colmask(z_sparse):
+    """Live columns of each format tile of a 128x128-tile BitsparseTensor: the
+    OR of the tile's 128 rows of mask words (int32 [tiles * 4])."""
+    nt = z_sparse.grid_m * z_sparse.grid_n
+    cm = torch.empty(nt * 4, dtype=torch.int32, device=z_sparse.bitmask.device)
+    call("sffn_tile_row_offsets", ptr(z_sparse.bitmask), ptr(z_sparse.prefix), nt, None, ptr(cm),
+         stream_ptr(cm.device))
+    return cm
+
+
+# ---------------------------------------------------------------------------
+# Compacted-K down-projection (and dX): the contraction over F runs over each
+# 128-row tile's live columns only.
+# ---------------------------------------------------------------------------
+def ck_supported(T, D, F):
+    """Shapes the compacted-K kernels take."""
+    return T % 128 == 0 and F % 128 == 0 and D % 256 == 0 and 0 < F <= 65536 and T * F < 2 ** 31
+
+
+def ck_lists(colmask, T, F, counts_only=False):
+    """(idx [T/128, F] int32, kcount [T/128] int32, colpref [T/128, ceil(F/128)]
+    int32): per 128-row tile the ascending live columns (padded to a multiple
+    of 64 with a column that is zero in the whole tile), their count, and where
+    each 128-column block's live columns start.  counts_only: kcount alone."""
+    dev = colmask.device
+    gm, gn = T // 128, -(-F // 128)
+    kcount = torch.empty(gm, dtype=torch.int32, device=dev)
+    if counts_only:
+        call("sffn_ck_lists", ptr(colmask), T, F, None, F, ptr(kcount), None, stream_ptr(dev))
+        return None, kcount, None
+    idx = torch.empty(gm, F, dtype=torch.int32, device=dev)
+    colpref = torch.empty(gm, gn, dtype=torch.int32, device=dev)
+    call("sffn_ck_lists", ptr(colmask), T, F, ptr(idx), F, ptr(kcount), ptr(colpref), stream_ptr(dev))
+    return idx, kcount, colpref
+
+
+def ck_gather_packed(z_sparse, row_offsets, colmask, colpref, kcount, act):
+    """The compacted activation [T, F] (columns past each tile's padded count
+    unused): act(z) at the tile's live columns, built from the packed z."""
+    T, F = z_sparse.shape
+    dev = z_sparse.vals.device
+    ac = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+    call("sffn_ck_gather_packed", ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask),
+         ptr(z_sparse.prefix), ptr(row_offsets), ptr(z_sparse.vals_offset), ptr(colmask), ptr(colpref), ptr(kcount), T, F, act,
+         ptr(ac), F, ptr(_lib.status_word(dev)), stream_ptr(dev))
+    return ac
+
+
+def ck_compact_rows_(x, idx, kcount):
+    """In place: each row of x [T, F] (bf16, row-major) compacted to its tile's
+    live columns (x's zeros must follow the activation's, as dpre's do)."""
+    T, F = x.shape
+    if x.stride(1) != 1 or x.dtype != torch.bfloat16:
+        raise ValueError("ck_compact_rows_ takes a row-major bf16 matrix")
+    call("sffn_ck_compact_rows", ptr(x), x.stride(0), T, F, ptr(idx), idx.stride(0), ptr(kcount),
+         stream_ptr(x.device))
+    return x
+
+
+def ck_mm(ac, B_rows, idx, kcount, out=None):
+    """C [T, N] = per 128-row tile tm, ac[rows, :Kp] @ B_rows[idx[tm, :Kp], :]
+    (Kp = kcount[tm] rounded up to 64): ac the compacted activation, B_rows
+    [F, N] row-major with rows = the contraction index, gathered by TMA."""
+    _lib.require_cuda(ac, B_rows)
+    T, F = ac.shape
+    Fb, N = B_rows.shape
+    if ac.stride(1) != 1 or B_rows.stride(1) != 1:
+        raise ValueError("ck_mm takes row-major operands")
+    if out is None:
+        out = torch.empty(T, N, dtype=torch.bfloat16, device=ac.device)
+    call("sffn_gemm_ck", ptr(ac), ac.stride(0), F, ptr(B_rows), B_rows.stride(0), Fb, ptr(idx), idx.stride(0),
+         ptr(kcount), ptr(out), out.stride(0), T, N, ptr(_lib.status_word(ac.device)), stream_ptr(ac.device))
+    return out
 
 
 def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None, sp24=False):

@@ -130,6 +130,131 @@ def bias_for_sparsity(x, W1, s):
     return float(-torch.quantile(pre[:: max(1, pre.numel() // 8_000_000)], s))
 
 
+# ------------------------------------------------ clustered sparsity ----
+# The large ReLU^2 FFN sharded by tokens: d_model=8192, d_ff=28672, 8192
+# tokens per GPU (65536 over 8), bf16.  Per 128-row token tile and 128-column
+# cluster of d_ff the activation is entirely zero with p=0.5; elsewhere each
+# entry is zero with p=0.8; non-zeros are |N(0,1)|.  The activation is
+# injected (generated directly) and the step runs the layer's sparse part:
+# the pack of z, the down-projection and the full backward.
+CL_TOKENS, CL_D, CL_F = 8192, 8192, 28672
+
+
+def clustered_activation(T, F, device, seed=0, p_cluster=0.5, p_zero=0.8):
+    """bf16 [T, F]: 128x128 (token tile, column cluster) blocks zero with
+    p_cluster, other entries zero with p_zero, non-zeros |N(0,1)| (an exact
+    zero draw becomes the smallest normal, so the mask is the drawn one)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    dead = torch.rand(-(-T // 128), -(-F // 128), device=device, generator=g) < p_cluster
+    dead = dead.repeat_interleave(128, 0)[:T].repeat_interleave(128, 1)[:, :F]
+    keep = (torch.rand(T, F, device=device, generator=g) >= p_zero) & ~dead
+    del dead
+    v = torch.randn(T, F, device=device, generator=g).abs_().clamp_min_(torch.finfo(torch.bfloat16).tiny)
+    return torch.where(keep, v, 0.0).to(torch.bfloat16)
+
+
+def make_clustered_inputs(T, D, F, device, seed=0):
+    """x ~ N(0,1) [T, D], W1 ~ N(0,1/D) [F, D], W2 ~ N(0,1/F) [D, F], the
+    clustered activation z [T, F] and dout ~ N(0,1) [T, D], all bf16."""
+    g = torch.Generator(device=device).manual_seed(seed + 1000)
+    x = torch.randn(T, D, device=device, generator=g).to(torch.bfloat16)
+    W1 = (torch.randn(F, D, device=device, generator=g) / D ** 0.5).to(torch.bfloat16)
+    W2 = (torch.randn(D, F, device=device, generator=g) / F ** 0.5).to(torch.bfloat16)
+    dout = torch.randn(T, D, device=device, generator=g).to(torch.bfloat16)
+    return x, W1, W2, clustered_activation(T, F, device, seed), dout
+
+
+class ClusteredStep:
+    """The sparse part of one ReLU^2 FFN layer on an injected activation:
+    dense_to_tilesparse(z) into the arena, the down-projection from the packed
+    z and the backward (dX, dW1, dW2; weight gradients all-reduced under data
+    parallelism), through the public API."""
+
+    def __init__(self, x, W1, W2, z, dout, group=None):
+        import autoresearch2_b200 as sf
+        self.sf = sf
+        self.x, self.W1, self.W2, self.z, self.dout = x, W1, W2, z, dout
+        self.comm = sf.parallel.GradAllReduce(group) if group is not None else None
+        T, F = z.shape
+        self.buf = sf.TensorBuffer(T * F // 2, z.device, z.dtype).init_buffer()
+
+    def packed(self):
+        self.buf.reset_buffer()
+        vals, off = self.buf.as_sparse_data()
+        return self.sf.dense_to_tilesparse(self.z, vals, off, 128, 128)
+
+    def __call__(self):
+        zs = self.packed()
+        out = self.sf.ffn.down_proj(zs, self.W2)
+        if self.comm is None:
+            grads = self.sf.ffn.packed_backward(self.dout, self.x, self.W1, self.W2, zs)
+        else:
+            with self.comm.attached():
+                grads = self.sf.ffn.packed_backward(self.dout, self.x, self.W1, self.W2, zs)
+            self.comm.wait()
+        return out, grads
+
+
+class ClusteredDenseStep:
+    """The same products dense on cuBLAS bf16: out = bf16(z^2) @ W2^T and the
+    backward of FFNrelu2 from dZ (old/lib_sparse/prepare_layer.py:12-29)."""
+
+    def __init__(self, x, W1, W2, z, dout):
+        self.x, self.W1, self.W2, self.z, self.dout = x, W1, W2, z, dout
+
+    def __call__(self):
+        a = self.z * self.z
+        out = a @ self.W2.T
+        dW2 = self.dout.T @ a
+        dpre = (self.dout @ self.W2) * 2 * self.z
+        dW1 = dpre.T @ self.x
+        dx = dpre @ self.W1
+        return out, (dx, dW1, dW2)
+
+
+def bench_clustered(device, group, world, steps, warmup, pk, rank):
+    """The clustered-sparsity leg: tokens/s of ClusteredStep (8192 tokens per
+    GPU, weak scaling) on the auto-chosen path, the two paths forced, the live
+    fraction of (tile, column) pairs, and on one GPU the dense cuBLAS step."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm as G
+    T, D, F = CL_TOKENS, CL_D, CL_F
+    x, W1, W2, z, dout = make_clustered_inputs(T, D, F, device, seed=rank)
+    step = ClusteredStep(x, W1, W2, z, dout, group)
+    res = {"workload": f"relu2_ffn_clustered_d{D}_f{F}_t{T}", "tokens_per_gpu": T, "global_tokens": T * world,
+           "d_model": D, "d_ff": F}
+    zs = step.packed()
+    kc = G.ck_lists(G.tile_colmask(zs), T, F, counts_only=True)[1]
+    kp = ((kc.long() + 63) // 64 * 64).sum().item()
+    live = kc.sum().item() / (T // 128 * F)
+    res["zeros"] = round(1 - int(zs.prefix[-1].item()) / (T * F), 4)
+    res["live_column_fraction"] = round(live, 4)
+    res["executed_k_fraction"] = round(kp / (T // 128 * F), 4)
+    mode = sf.compact_k()
+    for name, m in (("auto", mode), ("dense_k", "off"), ("compacted_k", "on")):
+        sf.set_compact_k(m)
+        ms = time_steps(step, steps, max(warmup, 3), device)
+        res[name] = {"tokens_per_s": round(T * world / (ms / 1e3), 1), "ms_per_step": round(ms, 3),
+                     "path": sf.ffn.last_path()}
+    sf.set_compact_k(mode)
+    base = 2.0 * T * D * F
+    ms = res["auto"]["ms_per_step"]
+    res["flops"] = {"dense_equivalent_per_step": 5 * base, "executed_compacted_per_step":
+                    base * (3 + 2 * kp / (T // 128 * F)),
+                    "algorithmic_per_step": 5 * base * (1 - res["zeros"]),
+                    "dense_equivalent_tflops": round(5 * base / (ms * 1e-3) / 1e12, 1)}
+    if world == 1:
+        dense = ClusteredDenseStep(x, W1, W2, z, dout)
+        dms = time_steps(dense, steps, max(warmup, 3), device)
+        res["dense_cublas"] = {"tokens_per_s": round(T / (dms / 1e3), 1), "ms_per_step": round(dms, 3)}
+        res["speedup_vs_dense"] = round(dms / ms, 3)
+        del dense
+    del step, x, W1, W2, z, dout, zs
+    torch.cuda.empty_cache()
+    sf.check_status(device)
+    return res
+
+
 class Step:
     """One forward + backward of the sparse ReLU^2 FFN through the public API."""
 
@@ -612,6 +737,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-tokens", type=int, default=1024)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-clustered", action="store_true",
+                    help="skip the clustered-sparsity large-FFN leg (d=8192/28672)")
     ap.add_argument("--tokens", type=int, default=T_PER_GPU,
                     help="tokens per GPU (smaller cases are for profiling)")
     ap.add_argument("--quick", action="store_true",
@@ -762,6 +889,10 @@ def main():
 
     pk = peaks()
     roof = roofline(kernels, tpg, pk, s_meas)
+    clustered = None
+    if not args.quick and not args.no_clustered:
+        # every rank runs it (its weight gradients are all-reduced)
+        clustered = bench_clustered(device, group, world, max(3, args.steps // 4), args.warmup, pk, rank)
     flops = step_flops(step, ms, s_meas, pk) if rank == 0 else None
     pack = codec = deep_ffn = gpt_step = None
     if rank == 0 and not args.quick:
@@ -791,7 +922,7 @@ def main():
             "e2e": e2e, "clocks": clocks, "roofline": roof, "kernels": kernels, "pack": pack,
             "codec15": codec, "deep_ffn": deep_ffn, "gpt": gpt_step, "flops": flops,
             "gpu_launches": launches_per_step * args.steps,
-            "device_status_after_timed": status_after,
+            "device_status_after_timed": status_after, "clustered": clustered,
         }
         line.update(extras)
         if world == 1 and not args.quick:

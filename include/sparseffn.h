@@ -198,7 +198,8 @@ int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    uint32_t* status_dev, void* stream);
 
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
- * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely, the
+ * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
+ * (unless act_out is NULL: the compacted-K down-projection needs none), the
  * tiled 128x128 bitmask of z > 0 (ceil(T/128)*ceil(F/128) tiles of 2048 B),
  * four partial counts per tile (tile_counts[t*4 .. t*4+3]) and, for tile t,
  * row r's z values in order at slots[t*16384 + r*128 ...].  Follow with
@@ -223,19 +224,22 @@ int sffn_tile_scan_counts(const int32_t* tile_counts, int parts, int64_t ntiles,
  * (count = popcount of the row's mask) to
  * vals[*vals_offset_dev + prefix[t] + values in rows < r ...] (16-bit
  * dtypes; never past vals_capacity) and, if row_offsets is not NULL, writes
- * row_offsets[t*128 + r] = prefix[t] + values in rows < r.
+ * row_offsets[t*128 + r] = prefix[t] + values in rows < r.  If colmask is
+ * not NULL (16-byte aligned, 4 uint32 per tile), colmask[t*4 .. t*4+3] =
+ * the OR of tile t's 128 rows of mask words: its live columns.
  *   replaces old/lib_sparse/sparse_pack.py:65-92 (_compact_vals_kernel). */
 int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int32_t* prefix,
                            const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
                            int64_t vals_capacity, int dtype, int32_t* row_offsets,
-                           uint32_t* status_dev, void* stream);
+                           uint32_t* colmask, uint32_t* status_dev, void* stream);
 
 /* row_offsets[t*128 + r] = prefix[t] + number of values in rows < r of tile t,
  * for a tiled 128x128 bitmask (the per-row index sffn_ffn_dgrad reads; the
  * reference recomputes ranks with tl.cumsum in every kernel,
- * old/lib_sparse/sparse_unpack.py:142,237). */
+ * old/lib_sparse/sparse_unpack.py:142,237); colmask (optional) as in
+ * sffn_tile_gather_slots.  Either output may be NULL, not both. */
 int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t ntiles,
-                          int32_t* row_offsets, void* stream);
+                          int32_t* row_offsets, uint32_t* colmask, void* stream);
 
 /* For a tiled 128x128 bitmask of an [M, N] matrix: kb_count[m] and the
  * ascending list kb_list[m*ceil(N/64) ...] of 64-column blocks of 256-row
@@ -244,6 +248,52 @@ int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t
  * down-projection is dense, sparse.py:75,118). */
 int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
                       int32_t* kb_count, void* stream);
+
+/* ---- compacted-K down-projection -----------------------------------------
+ * The bitmask-sparse down-projection out = act(z) @ W2^T (and dX = dpre @ W1)
+ * over each 128-row tile's live columns only.  The reference's forward is a
+ * dense z @ W2.T (old/lib_sparse/sparse.py:75,118) and its sparse-operand
+ * product unpacks to dense first (spAx, sparse.py:305-351); these replace
+ * both with a contraction over the compacted K.  T % 128 == 0, F % 64 == 0,
+ * F <= 65536; the live columns of format tile t come from the colmask of
+ * sffn_tile_gather_slots / sffn_tile_row_offsets. */
+
+/* Per 128-row tile tm of a [T, F] 128x128-tiled activation: kcount[tm] =
+ * live columns K, idx[tm*ld_idx + j] (j < K) = the live columns in ascending
+ * order, padded up to a multiple of 64 with a column that is zero in every
+ * row of the tile, and colpref[tm*ceil(F/128) + n] = live columns of the
+ * tile's blocks before block n (where block n's live columns start in the
+ * list).  With idx NULL only kcount is written (colpref must then be NULL). */
+int sffn_ck_lists(const uint32_t* colmask, int64_t T, int64_t F, int32_t* idx, int64_t ld_idx,
+                  int32_t* kcount, int32_t* colpref, void* stream);
+
+/* The compacted activation from the packed z (tiled 128x128 vals, bitmask,
+ * prefix, row_offsets, *vals_offset_dev): ac[row*ld_ac + j] = act(z[row][idx[tm][j]])
+ * for j < kcount[tm] (act = 1: bf16(z*z), ReLU^2; act = 0: z) -- zero where
+ * the row's bit is clear -- and zeros from kcount[tm] up to the padded
+ * count.  No dense activation is formed. */
+int sffn_ck_gather_packed(const void* vals, int64_t vals_len, const uint8_t* bitmask,
+                          const int32_t* prefix, const int32_t* row_offsets, const int32_t* vals_offset_dev,
+                          const uint32_t* colmask, const int32_t* colpref, const int32_t* kcount,
+                          int64_t T, int64_t F, int act, void* ac, int64_t ld_ac, uint32_t* status_dev,
+                          void* stream);
+
+/* In place: x[row][j] = x[row][idx[tm][j]] for j below tile tm's padded
+ * count (16-bit elements, [T, ld]); rows of tiles with every column live are
+ * left as they are.  Compacts a dense activation gradient whose zeros follow
+ * the activation's (dpre of the ReLU / ReLU^2 backward). */
+int sffn_ck_compact_rows(void* x, int64_t ld, int64_t T, int64_t F, const int32_t* idx, int64_t ld_idx,
+                         const int32_t* kcount, void* stream);
+
+/* C[M, N] (bf16, fp32 accumulation) = for each 128-row tile tm,
+ * A[rows, 0:Kp] @ B[idx[tm][0:Kp], :], Kp = kcount[tm] rounded up to 64:
+ * A [M][lda] K-major (the compacted activation, kmax >= every Kp columns
+ * addressable), B [krows][ldb] with rows = the contraction index (W2^T for
+ * the down-projection, W1 for dX), gathered by TMA.  M % 128 == 0,
+ * N % 256 == 0, kmax % 64 == 0. */
+int sffn_gemm_ck(const void* A, int64_t lda, int64_t kmax, const void* B, int64_t ldb, int64_t krows,
+                 const int32_t* idx, int64_t ld_idx, const int32_t* kcount, void* C, int64_t ldc,
+                 int64_t M, int64_t N, uint32_t* status_dev, void* stream);
 
 /* Fused activation gradient: g = bf16(dout @ W2) ([T, F]; W2 is [D, F]).
  * ReLU^2 (act = 1): dpre = bf16((g*2) * z) and act_out = bf16(z*z); ReLU

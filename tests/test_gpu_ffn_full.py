@@ -12,8 +12,9 @@
 * The single-layer CPU configuration (8192 tokens, d_model=768, d_ff=3072,
   float32, bias -1.3) on the GPU against the oracle at 1e-5.
 
-Every case runs with the dense products and with the 2:4 sparse
-tensor-core products, at 80%, 90% and 99% zeros.  Tolerances (elementwise,
+Every case runs with the dense products, with the 2:4 sparse tensor-core
+products and with the compacted-K down-projection and dX, at 80%, 90% and
+99% zeros.  Tolerances (elementwise,
 absolute floor scaled to the tensor's largest magnitude): bf16 2e-2,
 float32 1e-5."""
 import numpy as np
@@ -50,12 +51,16 @@ def _fp32_exact_and_status():
 
 
 @pytest.fixture
-def mma_mode(request):
+def path(request):
+    """The products' path: dense tcgen05 GEMMs, 2:4 sparse tensor cores, or
+    the compacted-K down-projection and dX."""
     import autoresearch2_b200 as sf
-    prev = sf.ffn.sparse_mma()
-    sf.ffn.set_sparse_mma(request.param)
+    prev = sf.sparse_mma(), sf.compact_k()
+    sf.set_sparse_mma("on" if request.param == "sp24" else "off")
+    sf.set_compact_k("on" if request.param == "ck" else "off")
     yield request.param
-    sf.ffn.set_sparse_mma(prev)
+    sf.set_sparse_mma(prev[0])
+    sf.set_compact_k(prev[1])
 
 
 def _inputs(T, s, seed):
@@ -88,12 +93,14 @@ def _run(x, W1, W2, b1, dout):
     return out, z, snap, (xg.grad, W1g.grad, W2g.grad, b1g.grad)
 
 
-@pytest.mark.parametrize("mma_mode", ["off", "on"], indirect=True)
+@pytest.mark.parametrize("path", ["dense", "sp24", "ck"], indirect=True)
 @pytest.mark.parametrize("s", [0.8, 0.9, 0.99])
-def test_headline_shape_against_oracle(s, mma_mode):
+def test_headline_shape_against_oracle(s, path):
     """1024 tokens of the d=4096/14336 layer against the float64 oracle."""
+    import autoresearch2_b200 as sf
     x, W1, W2, b1, dout = _inputs(1024, s, seed=int(s * 100))
     out, z, _, (dx, dW1, dW2, db1) = _run(x, W1, W2, b1, dout)
+    assert sf.ffn.last_path() == path
     mask = (z > 0).cpu().numpy()
     assert abs(1 - mask.mean() - s) < 0.02
     bits = [oracle.f32_to_bf16(t.float().cpu().numpy()) for t in (x, W1, W2, dout, b1)]
@@ -113,14 +120,15 @@ def test_headline_shape_against_oracle(s, mma_mode):
     close(db1, r["db1"], BF16_TOL, "db1")
 
 
-@pytest.mark.parametrize("mma_mode", ["off", "on"], indirect=True)
+@pytest.mark.parametrize("path", ["dense", "sp24", "ck"], indirect=True)
 @pytest.mark.parametrize("s", [0.8, 0.9, 0.99])
-def test_headline_workload_full_tokens(s, mma_mode):
+def test_headline_workload_full_tokens(s, path):
     """All 16384 tokens: the tiled format bit for bit, values against torch."""
     import autoresearch2_b200 as sf
     T = 16384
     x, W1, W2, b1, dout = _inputs(T, s, seed=7 + int(s * 100))
     out, z, snap, (dx, dW1, dW2, db1) = _run(x, W1, W2, b1, dout)
+    assert sf.ffn.last_path() == path
 
     # the forward's format equals dense_to_tilesparse of its own z (128 x 128
     # tiles, the arena written from the same cursor)
