@@ -46,6 +46,9 @@ SIGNATURES = {
     "sffn_error_string": (ctypes.c_char_p, [_int]),
     "sffn_last_cuda_error": (ctypes.c_char_p, []),
     "sffn_flat_workspace_bytes": (_sz, [_i64]),
+    "sffn_flat_pack_workspace_bytes": (_sz, [_i64, _int]),
+    "sffn_flat_pack_count": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _sz, _vp]),
+    "sffn_flat_pack_values": (_int, [_int, _i64, _vp, _i64, _vp, _vp, _sz, _vp, _vp]),
     "sffn_flat_pack": (_int, [_vp, _int, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp, _vp]),
     "sffn_flat_unpack": (_int, [_vp, _i64, _vp, _int, _i64, _vp, _vp, _sz, _vp, _vp]),
     "sffn_flat_pack_noalloc": (_int, [_vp, _int, _i64, _vp, _vp, _i64, _vp, _vp, _vp]),
@@ -71,6 +74,9 @@ SIGNATURES = {
     "sffn_gemm_ck": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp,
                             _vp]),
     "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "sffn_live_kblocks_t": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "sffn_gemm_bf16_ct": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp,
+                                 _vp, _int, _vp, _vp]),
     "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
                               _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
     "sffn_wait_probe": (_int, [_int, _i64, _vp, _vp, _vp, _vp]),
@@ -99,13 +105,14 @@ def load():
 # Kernels of this library each entry point launches per call.
 LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_add": 1,
              "sffn_ffn_up_sp24": 1, "sffn_ffn_dgrad_sp24": 1, "sffn_sp24_mm": 1, "sffn_transpose16": 1,
-             "sffn_flat_pack": 1, "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
+             "sffn_flat_pack": 2, "sffn_flat_pack_count": 2, "sffn_flat_pack_values": 1,
+             "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
              "sffn_tile_gather_slots": 1, "sffn_tile_row_offsets": 1, "sffn_live_kblocks": 1,
              "sffn_ffn_dgrad": 1, "sffn_codec15_compress": 1, "sffn_codec15_uncompress": 1,
              "sffn_wait_probe": 1, "sffn_ck_lists": 1, "sffn_ck_gather_packed": 1,
-             "sffn_ck_compact_rows": 1, "sffn_gemm_ck": 1}
+             "sffn_ck_compact_rows": 1, "sffn_gemm_ck": 1, "sffn_live_kblocks_t": 1, "sffn_gemm_bf16_ct": 1}
 launch_count = 0
 
 # Per-entry-point CUDA event pairs, recorded while a KernelTimer is active.

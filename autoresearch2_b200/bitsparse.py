@@ -22,7 +22,7 @@ from . import _lib
 from ._lib import call, dtype_code, ptr, require_cuda, stream_ptr
 
 __all__ = [
-    "bitsparse_pack", "bitsparse_unpack", "BitsparseTensor", "dense_to_tilesparse", "tile_unpack",
+    "bitsparse_pack", "bitsparse_pack_async", "bitsparse_unpack", "BitsparseTensor", "dense_to_tilesparse", "tile_unpack",
     "spAx", "mask_with_bitmask_", "grad_relu2_", "init_sparse_buffer", "reset_sparse_globals",
     "get_globals", "TensorBuffer", "check_status",
 ]
@@ -38,28 +38,55 @@ def bitsparse_pack(dense: torch.Tensor, block: int = 2048, vals_out: torch.Tenso
 
     Follows old/sparse_pack.py:66-106: packed_mask is uint8[ceil(N/8)] with
     element f at byte f//8, bit f%8 (set iff x != 0); vals holds the nonzeros
-    in row-major order.  Two kernels (mask and counts, then the values);
-    like the reference, the call waits for the device to learn len(vals).  `vals_out` (optional, 1-D, same dtype,
-    >= nnz elements) receives the values instead of a fresh buffer."""
+    in row-major order.  Two kernels (mask, counts and the values staged per
+    tile, then the values moved to their offsets); between them the call
+    waits for the count, as the reference does to size vals
+    (old/sparse_pack.py:98), so that vals holds exactly nnz elements.
+    `vals_out` (optional, 1-D, same dtype, >= nnz elements) receives the
+    values instead of a fresh buffer (a view of its first nnz is returned);
+    bitsparse_pack_async skips the wait."""
     require_cuda(dense)
     code = dtype_code(dense)
     flat = dense.contiguous().view(-1)
     n = flat.numel()
     dev = dense.device
+    L = _lib.load()
     mask = torch.empty((n + 7) // 8, dtype=torch.uint8, device=dev)
-    vals = vals_out if vals_out is not None else torch.empty(n, dtype=dense.dtype, device=dev)
-    if vals.dtype != dense.dtype or not vals.is_contiguous():
-        raise ValueError("vals_out must be a contiguous tensor of the input's dtype")
     out = torch.zeros(2, dtype=torch.int64, device=dev)  # [nnz, status]
-    ws = _lib.workspace(_lib.load().sffn_flat_workspace_bytes(n), dev)
-    out_ptr = out.data_ptr()
-    call("sffn_flat_pack", ptr(flat), code, n, ptr(mask), ptr(vals), vals.numel(),
-         _lib.ctypes.c_void_p(out_ptr), ptr(ws), ws.numel(), _lib.ctypes.c_void_p(out_ptr + 8),
-         stream_ptr(dev))
-    nnz, status = out.tolist()
-    if status:
-        raise _lib.SparseFFNError(f"bitsparse_pack device status 0x{status:x}")
+    ws = _lib.workspace(L.sffn_flat_pack_workspace_bytes(n, code), dev)
+    nnz_p, status_p = _lib.ctypes.c_void_p(out.data_ptr()), _lib.ctypes.c_void_p(out.data_ptr() + 8)
+    st = stream_ptr(dev)
+    call("sffn_flat_pack_count", ptr(flat), code, n, ptr(mask), nnz_p, ptr(ws), ws.numel(), st)
+    nnz = int(out[0].item())
+    if vals_out is not None:
+        if vals_out.dtype != dense.dtype or not vals_out.is_contiguous() or vals_out.numel() < nnz:
+            raise ValueError("vals_out must be a contiguous tensor of the input's dtype with >= nnz elements")
+        vals = vals_out
+    else:
+        vals = torch.empty(nnz, dtype=dense.dtype, device=dev)
+    call("sffn_flat_pack_values", code, n, ptr(vals), vals.numel(), nnz_p, ptr(ws), ws.numel(), status_p, st)
     return vals[:nnz], mask
+
+
+def bitsparse_pack_async(dense: torch.Tensor, vals_out: torch.Tensor):
+    """bitsparse_pack without a host wait: the values go to `vals_out` (a
+    caller-sized upper bound, e.g. an arena), and the count stays on the
+    device.  Returns (vals_out, packed_mask, nnz) with nnz an int64 [1] CUDA
+    tensor; more nonzeros than vals_out holds are clipped and flag
+    SFFN_STATUS_VALS_OVERFLOW in the device status word (check_status)."""
+    require_cuda(dense, vals_out)
+    code = dtype_code(dense)
+    if vals_out.dtype != dense.dtype or not vals_out.is_contiguous():
+        raise ValueError("vals_out must be a contiguous tensor of the input's dtype")
+    flat = dense.contiguous().view(-1)
+    n = flat.numel()
+    dev = dense.device
+    mask = torch.empty((n + 7) // 8, dtype=torch.uint8, device=dev)
+    nnz = torch.zeros(1, dtype=torch.int64, device=dev)
+    ws = _lib.workspace(_lib.load().sffn_flat_pack_workspace_bytes(n, code), dev)
+    call("sffn_flat_pack", ptr(flat), code, n, ptr(mask), ptr(vals_out), vals_out.numel(), ptr(nnz),
+         ptr(ws), ws.numel(), ptr(_lib.status_word(dev)), stream_ptr(dev))
+    return vals_out, mask, nnz
 
 
 def bitsparse_unpack(vals: torch.Tensor, packed_mask: torch.Tensor, shape, block: int = 8192):

@@ -202,6 +202,57 @@ __global__ void __launch_bounds__(LIVE_WARPS * 32) live_kblocks_kernel(const uin
     if (lane == 0) kb_count[tp] = n;
 }
 
+// The same lists for the weight-gradient GEMMs, whose contraction runs over
+// tokens: for each 256-column tile p of the activation (two columns of
+// 128x128 format tiles; the M tile of dpre^T @ x and a^T @ dout), the
+// ascending list of 64-row token blocks holding any set bit.  Warp w of a CTA
+// tests token block 8*group + w over the two format tiles' 64 rows.
+__global__ void __launch_bounds__(LIVE_WARPS * 32) live_kblocks_t_kernel(const uint8_t* __restrict__ mask,
+                                                                        int gm_f, int gn_f, int nkb,
+                                                                        int* __restrict__ kb_list,
+                                                                        int* __restrict__ kb_count) {
+    const int tp = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int kb = blockIdx.y * LIVE_WARPS + warp;
+    int* flags = kb_list + (long long)tp * nkb;
+    if (kb < nkb) {
+        const int tm = kb >> 1;
+        uint4 w[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int tn = 2 * tp + h;
+            const bool ok = tn < gn_f && tm < gm_f;
+            const uint8_t* tmask = mask + ((long long)tm * gn_f + min(tn, gn_f - 1)) * 2048 + (kb & 1) * 64 * 16;
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+                w[h][q] = ok ? *reinterpret_cast<const uint4*>(tmask + (lane + 32 * q) * 16) : make_uint4(0, 0, 0, 0);
+        }
+        uint32_t any = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int q = 0; q < 2; ++q) any |= w[h][q].x | w[h][q].y | w[h][q].z | w[h][q].w;
+        any = __any_sync(FULL, any != 0);
+        if (lane == 0) flags[kb] = any ? 1 : 0;
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ bool s_last;
+    if (threadIdx.x == 0) s_last = atomicAdd(&kb_count[tp], 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!s_last || warp != 0) return;
+    __threadfence();
+    int n = 0;
+    for (int k0 = 0; k0 < nkb; k0 += 32) {
+        const int k = k0 + lane;
+        const bool live = k < nkb && __ldcg(flags + k) != 0;
+        const unsigned b = __ballot_sync(FULL, live);
+        if (live) flags[n + __popc(b & ((1u << lane) - 1u))] = k;
+        n += __popc(b);
+    }
+    if (lane == 0) kb_count[tp] = n;
+}
+
 // dst[c][r] = src[r][c] for 16-bit elements: a 64 x 64 tile per CTA, read
 // and written in 16-byte rows through shared memory padded to 66 elements a
 // row (column reads of 2-byte elements then fall in distinct banks).
@@ -555,6 +606,21 @@ extern "C" int sffn_ck_compact_rows(void* x, int64_t ld, int64_t T, int64_t F, c
     SFFN_BIND(dev_scope, x);
     ck_compact_rows_kernel<<<(unsigned)((T + 7) / 8), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
         static_cast<uint16_t*>(x), ld, (int)F, (long long)T, idx, ld_idx, kcount);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_live_kblocks_t(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
+                                   int32_t* kb_count, void* stream) {
+    if (M <= 0 || N <= 0 || !bitmask || !kb_list || !kb_count) return SFFN_ERR_ARG;
+    if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
+    const long long gm = (M + 127) / 128, gn_f = (N + 127) / 128, gp = (N + 255) / 256, nkb = (M + 63) / 64;
+    if (gp > 0x7FFFFFFF || nkb > 0x7FFFFFFF || gm > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    SFFN_BIND(dev_scope, bitmask);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    SFFN_CUDA_TRY(cudaMemsetAsync(kb_count, 0, (size_t)gp * sizeof(int32_t), st));
+    const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));
+    live_kblocks_t_kernel<<<grid, LIVE_WARPS * 32, 0, st>>>(bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list, kb_count);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

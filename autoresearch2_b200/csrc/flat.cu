@@ -510,23 +510,27 @@ __global__ void __launch_bounds__(FP_THREADS, 1) flat_pack_kernel(
 // ------------------------------------------------------ scan-based path ----
 // The workspace entry points run two launches over tiles of FS_TILE = 8192
 // elements (256 threads x 32), with no waits between blocks:
-//   pack:   flat_mask_count_kernel (mask bytes, tile counts) ->
-//           flat_compact_kernel (values staged in shared memory at the
-//           output's alignment, written in 16-byte stores);
+//   pack:   flat_pack_stage_kernel (one read of the dense tensor: mask bytes,
+//           tile counts, and the tile's set elements compacted in shared
+//           memory and written to the tile's own 16-byte aligned segment of
+//           a staging area) -> flat_pack_move_kernel (each tile's values
+//           from the staging area to their offset in vals);
 //   unpack: flat_mask_popc_kernel (tile counts from the mask) ->
 //           flat_expand_kernel (the tile's values staged by 16-byte loads,
 //           expanded into 16-byte streaming stores).
 // A counting block adds its tile count to the sum of its group of 256 tiles;
 // a second-kernel block finds its offset from at most 255 counts and nt/256
-// group sums, loaded together in one round trip (tile_offset).  Every block is independent, so the kernels run at full
-// occupancy and memory latency is hidden by other blocks.  The pack reads the
-// dense tensor twice (once per kernel); unpack re-reads only the mask.
+// group sums, loaded together in one round trip (tile_offset).  Every block
+// is independent, so the kernels run at full occupancy and memory latency is
+// hidden by other blocks.  The pack reads the dense tensor once and moves
+// the values twice (2 n + n/8 + 6 nnz bytes against the 2 n + n/8 + 2 nnz it
+// must move); unpack re-reads only the mask.
 // Thread layout: warp w owns chunks 128w .. 128w+127 of the tile, lane l takes
 // chunks l, l+32, l+64, l+96, and values are ordered by chunk.
 //
-// Workspace (16 + 8 * nt bytes suffice): int32 tile counts, then the int64
-// sums of the 256-tile groups (zeroed on the stream before the counting
-// kernel).
+// Workspace: int32 tile counts, then the int64 sums of the 256-tile groups
+// (zeroed on the stream before the counting kernel), then (pack only) the
+// staging area of FS_TILE elements per tile, 16-byte aligned.
 constexpr int FS_TILE = FT_MIN_TILE;  // elements per tile
 constexpr int FS_T = 256;             // threads per tile
 constexpr int FS_W = FS_T / 32;
@@ -614,44 +618,6 @@ __device__ __forceinline__ void block_chunk_offsets(const uint32_t (&mb)[G], int
 // occupancy).
 template <typename B>
 constexpr int fs_tpb() { return sizeof(B) == 2 ? 2 : 1; }
-
-template <typename B>
-__global__ void __launch_bounds__(FS_T) flat_mask_count_kernel(const B* __restrict__ dense, long long n,
-                                                               uint8_t* __restrict__ mask, TileSums ts,
-                                                               long long t0) {
-    const long long t = t0 + blockIdx.x, base = t * FS_TILE;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    __shared__ int s_w[FS_W];
-    Vec8<B> v[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {  // all loads first
-        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
-        v[u].zero();
-        if (f + 8 <= n) v[u].load_global(dense + f);
-        else
-            for (int j = 0; j < 8; ++j)
-                if (f + j < n) v[u].set(j, dense[f + j]);
-    }
-    int cnt = 0;
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-        const long long f = base + 8LL * (128 * warp + lane + 32 * u);
-        if (f < n) {
-            const uint32_t b = v[u].nonzero_byte();  // zero-filled past n
-            mask[f >> 3] = (uint8_t)b;
-            cnt += __popc(b);
-        }
-    }
-    cnt = __reduce_add_sync(FULL, cnt);
-    if (lane == 0) s_w[warp] = cnt;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int s = 0;
-#pragma unroll
-        for (int w = 0; w < FS_W; ++w) s += s_w[w];
-        tile_sums_add(ts, t, s);
-    }
-}
 
 // Eight tiles per block: each warp counts one tile's 1024 mask bytes (16 B per
 // lane, two rounds).
@@ -800,63 +766,83 @@ __device__ __forceinline__ uint4 take_set16(uint32_t bits, const uint16_t* sp, c
     return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// Pack, second kernel: the tile is read again together with its mask bytes
-// (written by the first kernel; loaded alongside the values, so no extra
-// round trip), its set elements are staged in shared memory and written to
-// `vals` at the tile's offset.  VEC: `vals` 16-byte aligned.
-// Indices inside the tile are 32-bit; `rem` elements of it exist.
-template <typename B, bool VEC>
-__global__ void __launch_bounds__(FS_T) flat_compact_kernel(const B* __restrict__ dense, long long n,
-                                                            const uint8_t* __restrict__ mask,
-                                                            TileSums ts, long long nt, long long t0,
-                                                            B* __restrict__ vals, long long cap,
-                                                            long long* __restrict__ nnz_out,
-                                                            uint32_t* __restrict__ status) {
+// Pack, first kernel: one read of the tile, its mask bytes and count, and
+// its set elements compacted in shared memory and written, with 16-byte
+// stores, to the tile's own segment stage[t * FS_TILE ...] (16-byte aligned:
+// no realignment here).  Indices inside the tile are 32-bit.
+template <typename B>
+__global__ void __launch_bounds__(FS_T) flat_pack_stage_kernel(const B* __restrict__ dense, long long n,
+                                                               uint8_t* __restrict__ mask, TileSums ts,
+                                                               B* __restrict__ stage) {
     constexpr int EPV = 16 / (int)sizeof(B);
     constexpr int G = 4;
-    __shared__ __align__(16) B s_val[FS_TILE + EPV];
+    __shared__ __align__(16) B s_val[FS_TILE];
     __shared__ int s_wt[FS_W];
-    __shared__ long long s_red[FS_W];
-    const long long t = t0 + (long long)blockIdx.x, base = t * FS_TILE;
+    const long long t = (long long)blockIdx.x, base = t * FS_TILE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
     const int rem = (int)min(n - base, (long long)FS_TILE);
     const B* db = dense + base;
-    const uint8_t* mbase = mask + (base >> 3);
     Vec8<B> v[G];
-    uint32_t mb[G];  // the first kernel cleared the bits past n
 #pragma unroll
-    for (int u = 0; u < G; ++u) {
+    for (int u = 0; u < G; ++u) {  // every load issued before any use
         const int f = 8 * (32 * G * warp + lane + 32 * u);
         v[u].zero();
-        mb[u] = f < rem ? (uint32_t)__ldg(mbase + (f >> 3)) : 0u;
         if (f + 8 <= rem) v[u].load_global(db + f);
         else
             for (int j = 0; j < 8; ++j)
                 if (f + j < rem) v[u].set(j, db[f + j]);
     }
-    const long long ex = tile_offset(ts, t, s_red);  // its loads in flight with the values'
+    uint32_t mb[G];
+#pragma unroll
+    for (int u = 0; u < G; ++u) {
+        const int f = 8 * (32 * G * warp + lane + 32 * u);
+        mb[u] = v[u].nonzero_byte();  // zero-filled past n
+        if (f < rem) mask[(base + f) >> 3] = (uint8_t)mb[u];
+    }
     int off[G], total;
     block_chunk_offsets<G>(mb, off, total, s_wt, warp, lane);
-    if (tid == 0 && t + 1 >= nt) *nnz_out = ex + total;
-    // staging index of output element ex + i is sh + i: 16-byte aligned together
-    const int sh = (int)(ex % EPV);
-    const uint32_t sbase = smem_u32(s_val) + (uint32_t)(sh * (int)sizeof(B));
+    const uint32_t sbase = smem_u32(s_val);
 #pragma unroll
     for (int u = 0; u < G; ++u) put_set<B>(v[u], mb[u], sbase + (uint32_t)(off[u] * (int)sizeof(B)));
+    if (tid == 0) tile_sums_add(ts, t, total);
     __syncthreads();
-    const int lim = (int)max(0ll, min((long long)total, cap - ex));
-    if (tid == 0 && ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
-    B* vo = vals + ex;
-    int done = 0;
-    if (VEC) {
-        const int h = min(lim, (EPV - sh) % EPV);  // to the first 16-byte boundary
-        if (tid < h) vo[tid] = s_val[sh + tid];
-        const int nvec = (lim - h) / EPV;
-        for (int q = tid; q < nvec; q += FS_T)
-            *reinterpret_cast<uint4*>(vo + h + EPV * q) = *reinterpret_cast<const uint4*>(s_val + sh + h + EPV * q);
-        done = h + nvec * EPV;
+    B* so = stage + base;
+    const int nvec = total / EPV;
+    for (int q = tid; q < nvec; q += FS_T)
+        *reinterpret_cast<uint4*>(so + EPV * q) = *reinterpret_cast<const uint4*>(s_val + EPV * q);
+    for (int i = EPV * nvec + tid; i < total; i += FS_T) so[i] = s_val[i];
+}
+
+// Pack, second kernel: each tile's values from its staging segment to
+// vals[offset ...] (never past cap), the offset from the tile counts and
+// group sums; the last tile writes the total count.
+template <typename B>
+__global__ void __launch_bounds__(FS_T) flat_pack_move_kernel(const B* __restrict__ stage, TileSums ts, long long nt,
+                                                              B* __restrict__ vals, long long cap,
+                                                              long long* __restrict__ nnz_out,
+                                                              uint32_t* __restrict__ status) {
+    __shared__ long long s_red[FS_W];
+    const long long t = (long long)blockIdx.x;
+    const int tid = threadIdx.x;
+    const int total = __ldg(ts.counts + t);
+    const long long ex = tile_offset(ts, t, s_red);
+    if (tid == 0) {
+        if (t + 1 >= nt) *nnz_out = ex + total;
+        if (ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
     }
-    for (int i = done + tid; i < lim; i += FS_T) vo[i] = s_val[sh + i];
+    const int lim = (int)max(0ll, min((long long)total, cap - ex));
+    const B* si = stage + t * FS_TILE;
+    B* vo = vals + ex;
+    for (int i = tid; i < lim; i += FS_T) vo[i] = __ldcs(si + i);
+}
+
+// The total count (sum of the group sums) into *nnz_out: one warp.
+__global__ void flat_total_kernel(const unsigned long long* __restrict__ g1, long long ng,
+                                  long long* __restrict__ nnz_out) {
+    unsigned long long s = 0;
+    for (long long i = threadIdx.x; i < ng; i += 32) s += g1[i];
+    s = warp_sum_u64(s);
+    if (threadIdx.x == 0) *nnz_out = (long long)s;
 }
 
 template <typename B, bool VEC>
@@ -977,21 +963,30 @@ int launch_pack_lookback(const void* dense, long long n, uint8_t* mask, void* va
     return launch_pack_v<B, false>(d, n, mask, v, cap, nz, states, ticket, status, nt, st);
 }
 
+// Byte offset of the pack's staging area in the workspace (16-byte aligned).
+inline size_t pack_stage_offset(long long nt) {
+    return ((size_t)((nt * 4 + 7) & ~7ll) + (size_t)((nt + 255) / 256) * 8 + 15) & ~(size_t)15;
+}
+
 template <typename B>
-int launch_pack(const void* dense, long long n, uint8_t* mask, void* vals, long long cap,
-                int64_t* nnz_dev, void* ws, uint32_t* status, cudaStream_t st) {
+int launch_pack_count(const void* dense, long long n, uint8_t* mask, void* ws, cudaStream_t st) {
     const long long nt = (n + FS_TILE - 1) / FS_TILE;
     const TileSums ts = tile_sums(ws, nt);
     SFFN_CUDA_TRY(cudaMemsetAsync(ts.g1, 0, tile_sums_zero_bytes(nt), st));
-    const B* d = static_cast<const B*>(dense);
-    flat_mask_count_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, 0);
+    B* stage = reinterpret_cast<B*>(static_cast<char*>(ws) + pack_stage_offset(nt));
+    flat_pack_stage_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(static_cast<const B*>(dense), n, mask, ts, stage);
     SFFN_CHECK_LAUNCH();
-    B* v = static_cast<B*>(vals);
-    long long* nz = reinterpret_cast<long long*>(nnz_dev);
-    if (aligned16(vals))
-        flat_compact_kernel<B, true><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, nt, 0, v, cap, nz, status);
-    else
-        flat_compact_kernel<B, false><<<(unsigned)nt, FS_T, 0, st>>>(d, n, mask, ts, nt, 0, v, cap, nz, status);
+    return SFFN_OK;
+}
+
+template <typename B>
+int launch_pack_values(long long n, void* vals, long long cap, int64_t* nnz_dev, void* ws, uint32_t* status,
+                       cudaStream_t st) {
+    const long long nt = (n + FS_TILE - 1) / FS_TILE;
+    const TileSums ts = tile_sums(ws, nt);
+    const B* stage = reinterpret_cast<const B*>(static_cast<const char*>(ws) + pack_stage_offset(nt));
+    flat_pack_move_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(stage, ts, nt, static_cast<B*>(vals), cap,
+                                                            reinterpret_cast<long long*>(nnz_dev), status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -1020,14 +1015,73 @@ int launch_unpack(const void* vals, long long vals_len, const uint8_t* mask, lon
 
 using namespace sffn;
 
-// Workspace: 16 bytes plus 8 per tile of 8192 elements.  The two-kernel pack
-// and unpack keep int32 tile counts followed by the int64 sums of 256-tile
-// groups there (tile_sums).  The persistent look-back pack of the no-alloc
-// entry point keeps a 16-byte ticket and one state word per 32 KB tile of
-// dense data in its static array instead.
+// Workspace of the unpack: 16 bytes plus 8 per tile of 8192 elements (int32
+// tile counts followed by the int64 sums of 256-tile groups).  The pack needs
+// the same tables plus a staging area of one 8192-element segment per tile
+// (sffn_flat_pack_workspace_bytes).  The persistent look-back pack of the
+// no-alloc entry point keeps a 16-byte ticket and one state word per 32 KB
+// tile of dense data in its static array instead.
 extern "C" size_t sffn_flat_workspace_bytes(int64_t n) {
     if (n < 0) return 0;
     return 16 + (size_t)((n + FT_MIN_TILE - 1) / FT_MIN_TILE) * 8;
+}
+
+extern "C" size_t sffn_flat_pack_workspace_bytes(int64_t n, int dtype) {
+    if (n < 0 || !dtype_ok(dtype)) return 0;
+    const long long nt = (n + FS_TILE - 1) / FS_TILE;
+    return pack_stage_offset(nt) + (size_t)nt * FS_TILE * esize_of(dtype);
+}
+
+namespace {
+// Shared checks of the pack entry points (n > 0).
+int pack_args_ok(const void* dense, int dtype, int64_t n, const uint8_t* mask, size_t ws_bytes, const void* ws) {
+    if (!dense || !mask || !ws) return SFFN_ERR_ARG;
+    if (!aligned16(dense) || (reinterpret_cast<uintptr_t>(mask) & 3u) || !aligned16(ws)) return SFFN_ERR_ALIGN;
+    if (ws_bytes < sffn_flat_pack_workspace_bytes(n, dtype)) return SFFN_ERR_WORKSPACE;
+    if ((n + FT_MIN_TILE - 1) / FT_MIN_TILE > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // grid limit
+    return SFFN_OK;
+}
+}  // namespace
+
+extern "C" int sffn_flat_pack_count(const void* dense, int dtype, int64_t n, uint8_t* packed_mask, int64_t* nnz_dev,
+                                    void* workspace, size_t workspace_bytes, void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (n < 0 || !nnz_dev) return SFFN_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n == 0) {
+        SFFN_BIND(dev_scope, nnz_dev);
+        SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
+        return SFFN_OK;
+    }
+    if (int rc = pack_args_ok(dense, dtype, n, packed_mask, workspace_bytes, workspace)) return rc;
+    SFFN_BIND(dev_scope, dense);
+    const int rc = esize_of(dtype) == 4 ? launch_pack_count<uint32_t>(dense, n, packed_mask, workspace, st)
+                                        : launch_pack_count<uint16_t>(dense, n, packed_mask, workspace, st);
+    if (rc) return rc;
+    const long long nt = (n + FS_TILE - 1) / FS_TILE;
+    flat_total_kernel<<<1, 32, 0, st>>>(tile_sums(workspace, nt).g1, (nt + 255) / 256,
+                                        reinterpret_cast<long long*>(nnz_dev));
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_flat_pack_values(int dtype, int64_t n, void* vals, int64_t vals_capacity, int64_t* nnz_dev,
+                                     void* workspace, size_t workspace_bytes, uint32_t* status_dev, void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (n < 0 || vals_capacity < 0 || !nnz_dev || !status_dev) return SFFN_ERR_ARG;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n == 0) {
+        SFFN_BIND(dev_scope, nnz_dev);
+        SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
+        return SFFN_OK;
+    }
+    if ((!vals && vals_capacity > 0) || !workspace) return SFFN_ERR_ARG;
+    if (!aligned16(workspace)) return SFFN_ERR_ALIGN;
+    if (workspace_bytes < sffn_flat_pack_workspace_bytes(n, dtype)) return SFFN_ERR_WORKSPACE;
+    SFFN_BIND(dev_scope, workspace);
+    return esize_of(dtype) == 4
+               ? launch_pack_values<uint32_t>(n, vals, vals_capacity, nnz_dev, workspace, status_dev, st)
+               : launch_pack_values<uint16_t>(n, vals, vals_capacity, nnz_dev, workspace, status_dev, st);
 }
 
 extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* packed_mask,
@@ -1041,16 +1095,15 @@ extern "C" int sffn_flat_pack(const void* dense, int dtype, int64_t n, uint8_t* 
         SFFN_CUDA_TRY(cudaMemsetAsync(nnz_dev, 0, sizeof(int64_t), st));
         return SFFN_OK;
     }
-    if (!dense || !packed_mask || (!vals && vals_capacity > 0) || !workspace) return SFFN_ERR_ARG;
-    if (!aligned16(dense) || (reinterpret_cast<uintptr_t>(packed_mask) & 3u)) return SFFN_ERR_ALIGN;
-    if (workspace_bytes < sffn_flat_workspace_bytes(n)) return SFFN_ERR_WORKSPACE;
-    if ((n + FT_MIN_TILE - 1) / FT_MIN_TILE > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // grid limit
+    if (!vals && vals_capacity > 0) return SFFN_ERR_ARG;
+    if (int rc = pack_args_ok(dense, dtype, n, packed_mask, workspace_bytes, workspace)) return rc;
     SFFN_BIND(dev_scope, dense);
-    if (esize_of(dtype) == 4)
-        return launch_pack<uint32_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, workspace,
-                                     status_dev, st);
-    return launch_pack<uint16_t>(dense, n, packed_mask, vals, vals_capacity, nnz_dev, workspace,
-                                 status_dev, st);
+    if (esize_of(dtype) == 4) {
+        if (int rc = launch_pack_count<uint32_t>(dense, n, packed_mask, workspace, st)) return rc;
+        return launch_pack_values<uint32_t>(n, vals, vals_capacity, nnz_dev, workspace, status_dev, st);
+    }
+    if (int rc = launch_pack_count<uint16_t>(dense, n, packed_mask, workspace, st)) return rc;
+    return launch_pack_values<uint16_t>(n, vals, vals_capacity, nnz_dev, workspace, status_dev, st);
 }
 
 extern "C" int sffn_flat_unpack(const void* vals, int64_t vals_len, const uint8_t* packed_mask,

@@ -105,6 +105,7 @@ struct GemmArgs {
     const int* row_offsets;  // DGRAD: [num_tiles][128] prefix[t] + in-tile row prefix
     const int* vals_offset;
     float* colsum;  // DGRAD: optional fp32 [N] += column sums of dpre
+    int c_trans;    // STORE: write C^T ([N][ldc]) instead of C
     int sp_on;      // UP: a, DGRAD: dpre, dpre^T and a^T in 2:4 form instead of dense
     Sp24Out sp[3];  // UP: [0] a; DGRAD: [0] dpre, [1] dpre^T, [2] a^T
     uint32_t* status;
@@ -480,7 +481,20 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         w[q] = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])) : 0u;
-                    if (vec) {
+                    if (args.c_trans) {
+                        // the 32 x 32 block transposed through the staging buffer:
+                        // lane takes column `lane`, row gcol0 + 32c + lane of C^T
+                        if (tile_ok) {
+                            if (lane == 0) bulk_wait_group_read0();
+                            __syncwarp();
+                            stage_words(sbuf, lane, w);
+                            __syncwarp();
+                            uint32_t wt[16];
+                            float unused;
+                            staged_column(sbuf, lane, wt, unused);
+                            stage_store32(&tmC, sbuf, lane, wt, row0, gcol0 + c * 32);
+                        }
+                    } else if (vec) {
                         if (tile_ok) stage_store32(&tmC, sbuf, lane, w, gcol0 + c * 32, row0);
                     } else if (row_ok) {
                         store_row32(orow, gcol0 + c * 32, args.N, false, w);
@@ -1399,7 +1413,10 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     CUtensorMap tc, tc2;
     memset(&tc, 0, sizeof(tc));
     memset(&tc2, 0, sizeof(tc2));
-    if (args.vec_out) {
+    if (args.c_trans) {
+        if (!make_tmap(&tc, args.out, args.M, args.N, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+            return SFFN_ERR_CUDA;
+    } else if (args.vec_out) {
         if (!make_tmap(&tc, args.out, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return SFFN_ERR_CUDA;
         if (EPI == EPI_DGRAD &&
@@ -1549,6 +1566,26 @@ extern "C" int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
     if (!C || ldc < N || !status_dev) return SFFN_ERR_ARG;
     if ((kb_list == nullptr) != (kb_count == nullptr)) return SFFN_ERR_ARG;
     GemmArgs a = base_args(M, N, K, C, ldc);
+    a.kb_list = kb_list;
+    a.kb_count = kb_count;
+    a.kb_stride = kb_stride;
+    a.status = status_dev;
+    return dispatch<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                                 void* Ct, int64_t ldct, int64_t M, int64_t N, int64_t K, const int32_t* kb_list,
+                                 const int32_t* kb_count, int kb_stride, uint32_t* status_dev, void* stream) {
+    // C = A @ B computed as sffn_gemm_bf16 does, stored transposed: Ct[n][m].
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
+    if (rc) return rc;
+    if (!Ct || ldct < M || !status_dev) return SFFN_ERR_ARG;
+    if (!aligned16(Ct) || (ldct * 2) % 16) return SFFN_ERR_ALIGN;
+    if ((kb_list == nullptr) != (kb_count == nullptr)) return SFFN_ERR_ARG;
+    GemmArgs a = base_args(M, N, K, Ct, ldct);
+    a.c_trans = 1;
+    a.vec_out = 0;
     a.kb_list = kb_list;
     a.kb_count = kb_count;
     a.kb_stride = kb_stride;

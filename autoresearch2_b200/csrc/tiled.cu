@@ -4,16 +4,20 @@
 // Reference: old/lib_sparse/sparse_pack.py:27-92 + sparse.py:154-210 (pack:
 // tile kernel, torch.cumsum, compaction kernel that re-reads the tile, cursor
 // index_add_), old/lib_sparse/sparse_unpack.py:5-147 (unpack / mask / grad).
-// Pack here is ONE kernel: each CTA owns one tile (taken by ticket, so tiles
-// run in order), builds mask words and in-tile ranks in registers, stages the
-// compacted values in shared memory, finds its offset by decoupled look-back
-// over the preceding tiles, and the last tile writes prefix[num_tiles] and
-// advances the device cursor.
+// Pack here is three launches over independent tiles, none waiting on
+// another: (1) each CTA reads one tile, writes its mask words and its count;
+// (2) one CTA scans the counts into prefix[], reads the arena cursor and
+// advances it (sffn_tile_scan_counts); (3) each CTA reads its tile again,
+// ranks the set elements in registers, stages them in shared memory and
+// writes them at vals[cursor + prefix[t]].  (A single pass whose tiles found
+// their offsets by a decoupled look-back over their predecessors ran at a
+// third of the HBM rate: every tile's store waited on that chain.)
 //
 // Thread layout per tile: NT = min(256, BM*BN/8) threads, U iterations, 8
 // consecutive in-tile elements (one mask byte) per thread per iteration; in
 // iteration `it` thread `tid` owns in-tile offsets f = 8*(it*NT + tid) + j.
 #include "common.cuh"
+#include "sm100.cuh"
 
 namespace sffn {
 namespace {
@@ -101,53 +105,119 @@ __device__ __forceinline__ uint32_t mask_byte(const uint8_t* __restrict__ tile_m
 }
 
 // ----------------------------------------------------------------- pack ----
-template <typename B, int BM, int BN>
+// Eight consecutive elements of a tile row held as packed 32-bit words
+// (four for 16-bit types, eight for 32-bit ones), loaded with 16-byte loads
+// where the row allows.
+template <typename B>
+struct Words8 {
+    static constexpr int NW = (int)sizeof(B) * 2;
+    uint32_t w[NW];
+    __device__ void load(const B* __restrict__ row, long long gc, long long N, bool vec) {
+        if (vec && gc + 8 <= N) {
+#pragma unroll
+            for (int k = 0; k < NW / 4; ++k) {
+                const uint4 q = __ldcs(reinterpret_cast<const uint4*>(row + gc) + k);
+                w[4 * k] = q.x;
+                w[4 * k + 1] = q.y;
+                w[4 * k + 2] = q.z;
+                w[4 * k + 3] = q.w;
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < NW; ++k) w[k] = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (gc + j < N) set(j, row[gc + j]);
+        }
+    }
+    __device__ void zero() {
+#pragma unroll
+        for (int k = 0; k < NW; ++k) w[k] = 0;
+    }
+    __device__ void set(int j, B v) {
+        if constexpr (sizeof(B) == 2) {
+            const int sh = 16 * (j & 1);
+            w[j >> 1] = (w[j >> 1] & ~(0xFFFFu << sh)) | ((uint32_t)v << sh);
+        } else {
+            w[j] = v;
+        }
+    }
+    // bit j set iff element j > 0 (sign clear, non-zero, not NaN): x - 1 below
+    // +inf as an unsigned integer of the element's width.
+    __device__ uint32_t positive_byte(uint16_t inf16) const {
+        uint32_t b = 0;
+        if constexpr (sizeof(B) == 2) {
+            const uint32_t inf2 = (uint32_t)inf16 | ((uint32_t)inf16 << 16);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t m = __vcmpltu2(__vsub2(w[q], 0x00010001u), inf2);
+                b |= ((m & 1u) | ((m >> 15) & 2u)) << (2 * q);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) b |= (uint32_t)(w[j] - 1u < 0x7F800000u) << j;
+        }
+        return b;
+    }
+    // The set elements to consecutive shared-memory places from byte address
+    // `da` (predicated stores; the address steps by each bit).
+    __device__ void put_set(uint32_t bits, uint32_t da) const {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t bj = (bits >> j) & 1u;
+            if constexpr (sizeof(B) == 2) {
+                const uint16_t v = (uint16_t)(w[j >> 1] >> (16 * (j & 1)));
+                asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.shared.u16 [%0], %1;\n\t}" ::"r"(da),
+                             "h"(v), "r"(bj)
+                             : "memory");
+            } else {
+                asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.shared.u32 [%0], %1;\n\t}" ::"r"(da),
+                             "r"(w[j]), "r"(bj)
+                             : "memory");
+            }
+            da += (uint32_t)sizeof(B) * bj;
+        }
+    }
+};
+
+// COUNT: mask words and counts[t].  VALUES: the set elements of tile t at
+// vals[*vals_offset + prefix[t] ...] (never past cap).
+template <typename B, int BM, int BN, bool VALUES>
 __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
     const B* __restrict__ dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
-    uint8_t* __restrict__ bitmask, int* __restrict__ prefix, B* __restrict__ vals, long long cap,
-    int* __restrict__ cursor, int* __restrict__ vals_offset_out,
-    unsigned long long* __restrict__ states, unsigned* __restrict__ ticket,
-    uint32_t* __restrict__ status, long long gn, long long ntiles) {
+    uint8_t* __restrict__ bitmask, int* __restrict__ counts, const int* __restrict__ prefix,
+    const int* __restrict__ vals_offset, B* __restrict__ vals, long long cap, uint32_t* __restrict__ status,
+    long long gn) {
     using C = TileCfg<BM, BN>;
     extern __shared__ __align__(128) unsigned char smem_raw[];
     B* s_vals = reinterpret_cast<B*>(smem_raw);
     __shared__ int s_wx[C::NE];
     __shared__ int s_agg;
-    __shared__ int s_cursor;
-    __shared__ long long s_tile;
-    __shared__ unsigned long long s_excl;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid == 0) {
-        s_tile = atomicAdd(ticket, 1u);
-        // Every tile reads the cursor before publishing its count; the last
-        // tile writes it only after seeing all counts (see lookback()).
-        s_cursor = *reinterpret_cast<volatile int*>(cursor);
-    }
-    __syncthreads();
-    const long long t = s_tile;
+    const long long t = blockIdx.x;
     const long long tm = t / gn, tn = t % gn;
     const long long row0 = tm * BM, col0 = tn * BN;
     uint8_t* tmask = bitmask + t * C::TB;
 
-    B v[C::U][8];
+    Words8<B> v[C::U];
+#pragma unroll
+    for (int it = 0; it < C::U; ++it) {  // every load issued before any use
+        const int f = 8 * (it * C::NT + tid);
+        const long long gr = row0 + f / BN, gc = col0 + f % BN;
+        if (gr < M) v[it].load(dense + gr * ld, gc, N, vec != 0);
+        else v[it].zero();
+    }
     uint32_t bits[C::U];
     int lex[C::U];
 #pragma unroll
     for (int it = 0; it < C::U; ++it) {
         const int f = 8 * (it * C::NT + tid);
-        const long long gr = row0 + f / BN, gc = col0 + f % BN;
-        if (gr < M) {
-            load8_row(dense + gr * ld, gc, N, vec != 0, v[it]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[it][j] = B(0);
-        }
-        uint32_t b = 0;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) b |= (uint32_t)positive_bits(v[it][j], inf16) << j;
+        const uint32_t b = v[it].positive_byte(inf16);
         bits[it] = b;
-        const uint32_t w = bytes_to_word(b, lane);
-        if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(tmask + (f >> 3)) = w;
+        if constexpr (!VALUES) {
+            const uint32_t w = bytes_to_word(b, lane);
+            if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(tmask + (f >> 3)) = w;
+        }
         const int c = __popc(b);
         const int inc = warp_incl_scan(c, lane);
         lex[it] = inc - c;
@@ -156,41 +226,22 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_pack_kernel(
     __syncthreads();
     if (warp == 0) scan_small<C::NE>(s_wx, &s_agg, lane);
     __syncthreads();
+    if constexpr (!VALUES) {
+        if (tid == 0) counts[t] = s_agg;
+        return;
+    } else {
+        const uint32_t sb = smem_u32(s_vals);
 #pragma unroll
-    for (int it = 0; it < C::U; ++it) {
-        int r = s_wx[it * C::NW + warp] + lex[it];
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if ((bits[it] >> j) & 1u) s_vals[r++] = v[it][j];
-    }
-    const int agg = s_agg;
-    if (warp == 0) {
-        if (lane == 0) lookback_publish(states, t, (unsigned long long)agg);
-        __syncwarp();
-        unsigned long long ex = lookback<4>(states, t, (unsigned long long)agg, status, lane);
-        if (lane == 0) s_excl = ex;
-    }
-    __syncthreads();
-    const long long ex = (long long)s_excl;
-    const long long base = (long long)s_cursor + ex;
-    for (int i = tid; i < agg; i += C::NT) {
-        const long long p = base + i;
-        if (p >= 0 && p < cap) vals[p] = s_vals[i];
-    }
-    if (tid == 0) {
-        prefix[t] = (int)ex;
-        if (base < 0 || base + agg > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
-        if (t == 0) *vals_offset_out = s_cursor;
-        if (t == ntiles - 1) {
-            // Every other tile read the cursor before publishing its count,
-            // and this tile has seen all counts: the cursor can now move.
-            __threadfence();
-            const long long total = ex + agg;
-            prefix[ntiles] = (int)total;
-            const long long next = (long long)s_cursor + total;
-            if (next > 0x7FFFFFFFll) atomicOr(status, SFFN_STATUS_CURSOR_OVERFLOW);
-            *reinterpret_cast<volatile int*>(cursor) = (int)(next > 0x7FFFFFFFll ? 0x7FFFFFFFll : next);
+        for (int it = 0; it < C::U; ++it)
+            v[it].put_set(bits[it], sb + (uint32_t)((s_wx[it * C::NW + warp] + lex[it]) * (int)sizeof(B)));
+        __syncthreads();
+        const int agg = s_agg;
+        const long long base = (long long)*vals_offset + prefix[t];
+        for (int i = tid; i < agg; i += C::NT) {
+            const long long p = base + i;
+            if (p >= 0 && p < cap) vals[p] = s_vals[i];
         }
+        if (tid == 0 && (base < 0 || base + agg > cap)) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
     }
 }
 
@@ -363,12 +414,6 @@ inline cudaError_t prep_smem(K kernel, int bytes) {
     return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-struct TileWs {
-    unsigned* ticket;
-    unsigned long long* states;
-    size_t used;
-};
-
 inline long long num_tiles(long long M, long long N, int BM, int BN) {
     return ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
 }
@@ -376,15 +421,19 @@ inline long long num_tiles(long long M, long long N, int BM, int BN) {
 template <typename B, int BM, int BN>
 int launch_pack(const void* dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
                 uint8_t* bitmask, int* prefix, void* vals, long long cap, int* cursor,
-                int* vals_offset_out, const TileWs& w, uint32_t* status, cudaStream_t st) {
+                int* vals_offset_out, int* counts, uint32_t* status, cudaStream_t st) {
     using C = TileCfg<BM, BN>;
     const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
     const int smem = C::TILE * (int)sizeof(B);
-    auto k = tile_pack_kernel<B, BM, BN>;
-    SFFN_CUDA_TRY(prep_smem(k, smem));
-    k<<<(unsigned)nt, C::NT, smem, st>>>((const B*)dense, M, N, ld, vec, inf16, bitmask, prefix,
-                                         (B*)vals, cap, cursor, vals_offset_out, w.states, w.ticket,
-                                         status, gn, nt);
+    auto kc = tile_pack_kernel<B, BM, BN, false>;
+    kc<<<(unsigned)nt, C::NT, 0, st>>>((const B*)dense, M, N, ld, vec, inf16, bitmask, counts, nullptr, nullptr,
+                                       nullptr, 0, status, gn);
+    SFFN_CHECK_LAUNCH();
+    if (int rc = sffn_tile_scan_counts(counts, 1, nt, prefix, cursor, vals_offset_out, status, st)) return rc;
+    auto kv = tile_pack_kernel<B, BM, BN, true>;
+    SFFN_CUDA_TRY(prep_smem(kv, smem));
+    kv<<<(unsigned)nt, C::NT, smem, st>>>((const B*)dense, M, N, ld, vec, inf16, bitmask, nullptr, prefix,
+                                          vals_offset_out, (B*)vals, cap, status, gn);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -462,11 +511,7 @@ extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N
     if (workspace_bytes < sffn_tile_workspace_bytes(M, N, BM, BN)) return SFFN_ERR_WORKSPACE;
     SFFN_BIND(dev_scope, dense);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    TileWs w;
-    w.ticket = reinterpret_cast<unsigned*>(workspace);
-    w.states = reinterpret_cast<unsigned long long*>(reinterpret_cast<char*>(workspace) + 16);
-    w.used = sffn_tile_workspace_bytes(M, N, BM, BN);
-    SFFN_CUDA_TRY(cudaMemsetAsync(workspace, 0, w.used, st));
+    int* counts = static_cast<int*>(workspace);  // one count per tile
     const int esz = esize_of(dtype);
     const int vec = vec_ok(dense, ld, esz) ? 1 : 0;
     const uint16_t inf16 = inf16_of(dtype);
@@ -474,10 +519,10 @@ extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N
     if (BM == a && BN == b) {                                                                        \
         if (esz == 4)                                                                                \
             return launch_pack<uint32_t, a, b>(dense, M, N, ld, vec, inf16, bitmask, prefix, vals,   \
-                                               vals_capacity, offset_dev, vals_offset_dev, w,        \
+                                               vals_capacity, offset_dev, vals_offset_dev, counts,   \
                                                status_dev, st);                                      \
         return launch_pack<uint16_t, a, b>(dense, M, N, ld, vec, inf16, bitmask, prefix, vals,       \
-                                           vals_capacity, offset_dev, vals_offset_dev, w,            \
+                                           vals_capacity, offset_dev, vals_offset_dev, counts,       \
                                            status_dev, st);                                          \
     }
     SFFN_TILE_SHAPES(SFFN_PACK_CASE)

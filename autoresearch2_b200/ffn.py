@@ -253,11 +253,15 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
     dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
     del row_offsets
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
-    grad_W2 = submit_grad(G.mm(grad_output.T, a))  # data parallel: reduce while dW1/dX run
+    # the weight gradients contract over tokens: per 256 columns of the
+    # activation, 64-token blocks that are zero there are skipped (dW2 as
+    # (a^T @ dout)^T, so that the lists index its M tiles)
+    tl, tc = G.live_kblocks_t(z_sparse.bitmask, T, Fd)
+    grad_W2 = submit_grad(G.mm_t(a.T, grad_output, kb_list=tl, kb_count=tc))  # reduced while dW1/dX run
     del a
     # dW1 before dX: under data parallelism its all-reduce then overlaps dX, and
     # no weight-gradient reduction is left without compute to hide behind
-    grad_W1 = submit_grad(G.mm(dpre.T, x))
+    grad_W1 = submit_grad(G.mm(dpre.T, x, kb_list=tl, kb_count=tc))
     if use_ck:
         # dpre is zero wherever z is: compact it in place to the live columns
         # and gather the matching rows of W1

@@ -58,6 +58,37 @@ def mm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, kb_list=None,
     return out
 
 
+def mm_t(A: torch.Tensor, B: torch.Tensor, kb_list=None, kb_count=None):
+    """(A @ B)^T [N, M] (bf16) on the tcgen05 kernel, the product stored
+    transposed by its epilogue; kb_list / kb_count as in mm (per 256 rows of A)."""
+    _lib.require_cuda(A, B)
+    if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
+        raise TypeError("mm_t takes bfloat16 operands")
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(B.shape)}")
+    lda, a_mn = _operand(A, 0)
+    ldb, b_mn = _operand(B, 1)
+    out = torch.empty(N, M, dtype=torch.bfloat16, device=A.device)
+    stride = kb_list.shape[1] if kb_list is not None else 0
+    call("sffn_gemm_bf16_ct", ptr(A), lda, a_mn, ptr(B), ldb, b_mn, ptr(out), out.stride(0), M, N, K,
+         ptr(kb_list), ptr(kb_count), stride, ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+    return out
+
+
+def live_kblocks_t(bitmask: torch.Tensor, M: int, N: int):
+    """(kb_list [ceil(N/256), ceil(M/64)] int32, kb_count [ceil(N/256)] int32):
+    for each 256-column tile of a tiled 128x128 bitmask of [M, N], the 64-row
+    blocks holding any set bit (the token-skip lists of dpre^T @ x and
+    a^T @ dout)."""
+    gp, nkb = -(-N // 256), -(-M // 64)
+    kb_list = torch.empty(gp, nkb, dtype=torch.int32, device=bitmask.device)
+    kb_count = torch.empty(gp, dtype=torch.int32, device=bitmask.device)
+    call("sffn_live_kblocks_t", ptr(bitmask), M, N, ptr(kb_list), ptr(kb_count), stream_ptr(bitmask.device))
+    return kb_list, kb_count
+
+
 def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
     """(kb_list [ceil(M/256), ceil(N/64)] int32, kb_count [ceil(M/256)] int32):
     per 256-row tile, the 64-column blocks holding any set bit of a tiled

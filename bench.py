@@ -351,7 +351,7 @@ def bench_pack(device, p=PACK_P, reps=20):
     L = _lib.load()
     vbuf = torch.empty(n, dtype=d.dtype, device=device)
     nnz_d = torch.zeros(2, dtype=torch.int64, device=device)
-    ws = _lib.workspace(L.sffn_flat_workspace_bytes(n), device)
+    ws = _lib.workspace(L.sffn_flat_pack_workspace_bytes(n, _lib.BF16), device)
     out = torch.empty_like(d)
     st = _lib.stream_ptr(device)
     status = _lib.status_word(device)

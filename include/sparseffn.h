@@ -73,24 +73,39 @@ const char* sffn_last_cuda_error(void);
  * elements in row-major order.  Tail bits of the last byte are 0.
  */
 
-/* Scratch needed by sffn_flat_pack / sffn_flat_unpack for n elements:
- * 16 bytes plus 8 per 8192 elements. */
+/* Scratch needed by sffn_flat_unpack for n elements: 16 bytes plus 8 per
+ * 8192 elements. */
 size_t sffn_flat_workspace_bytes(int64_t n);
+
+/* Scratch needed by sffn_flat_pack (and its two halves) for n elements of
+ * dtype: the unpack's tables plus a staging area of n elements rounded up
+ * to 8192 (0 for a bad dtype). */
+size_t sffn_flat_pack_workspace_bytes(int64_t n, int dtype);
 
 /* bitsparse_pack(dense, block) -> (vals, packed_mask)
  *   replaces old/sparse_pack.py:66-106 (kernels :6-63) and
  *   old/bitpack/train.py:65-103 (compress_dense).
- * Two kernels: the first reads dense once for the mask bytes and per-tile
- * counts, the second reads it again to compact the nonzeros (see
- * sffn_flat_pack_noalloc for a single-read form).  Writes ceil(n/8) bytes to
- * packed_mask, the nonzeros
- * to vals[0, nnz) (at most vals_capacity are written; more sets
- * SFFN_STATUS_VALS_OVERFLOW), and nnz to *nnz_dev (device int64).
- * dense must be 16-byte aligned, packed_mask 4-byte aligned. */
+ * Two kernels: the first reads dense once, writing the mask bytes, per-tile
+ * counts and each tile's set elements to its own segment of the workspace's
+ * staging area; the second moves the values to their offsets.  Writes
+ * ceil(n/8) bytes to packed_mask, the nonzeros to vals[0, nnz) (at most
+ * vals_capacity are written; more sets SFFN_STATUS_VALS_OVERFLOW), and nnz
+ * to *nnz_dev (device int64).  dense and workspace must be 16-byte aligned,
+ * packed_mask 4-byte aligned; workspace_bytes >= sffn_flat_pack_workspace_bytes. */
 int sffn_flat_pack(const void* dense, int dtype, int64_t n,
                    uint8_t* packed_mask, void* vals, int64_t vals_capacity,
                    int64_t* nnz_dev, void* workspace, size_t workspace_bytes,
                    uint32_t* status_dev, void* stream);
+
+/* The two halves of sffn_flat_pack, for callers that size vals from the
+ * count (as the reference does, old/sparse_pack.py:98): _count reads dense,
+ * writes the mask and the staged values into the workspace and the total
+ * into *nnz_dev; _values (same n, dtype and workspace, whose contents it
+ * reads) writes the values to vals, as sffn_flat_pack does. */
+int sffn_flat_pack_count(const void* dense, int dtype, int64_t n, uint8_t* packed_mask, int64_t* nnz_dev,
+                         void* workspace, size_t workspace_bytes, void* stream);
+int sffn_flat_pack_values(int dtype, int64_t n, void* vals, int64_t vals_capacity, int64_t* nnz_dev,
+                          void* workspace, size_t workspace_bytes, uint32_t* status_dev, void* stream);
 
 /* bitsparse_unpack(vals, packed_mask, shape, block) -> dense
  *   replaces old/sparse_unpack.py:57-97 (kernels :6-54) and
@@ -140,9 +155,11 @@ size_t sffn_tile_workspace_bytes(int64_t M, int64_t N, int BM, int BN);
 /* dense_to_tilesparse(dense, vals, offset, BLOCK_M, BLOCK_N) -> BitsparseTensor
  *   replaces old/lib_sparse/sparse.py:154-210 (kernels sparse_pack.py:27-92)
  *   and old/full_matmul/sparse_pack.py:95-146.
- * One pass.  Reads the int32 arena cursor *offset_dev, writes it to
- * *vals_offset_dev, writes bitmask, prefix[num_tiles+1] and the values to
- * vals[cursor + prefix[t] ...] (never past vals_capacity), then advances
+ * Three launches over independent tiles: mask words and per-tile counts
+ * (into the workspace), one scan of the counts, then each tile read again
+ * and its values written.  Reads the int32 arena cursor *offset_dev, writes
+ * it to *vals_offset_dev, writes bitmask, prefix[num_tiles+1] and the values
+ * to vals[cursor + prefix[t] ...] (never past vals_capacity), and advances
  * *offset_dev by the total -- all on the device, no host sync. */
 int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld,
                    int BM, int BN, uint8_t* bitmask, int32_t* prefix,
@@ -197,6 +214,18 @@ int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
                    const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
                    uint32_t* status_dev, void* stream);
 
+/* sffn_gemm_bf16 with C stored transposed: Ct[n*ldct + m] = C[m][n] (Ct
+ * 16-byte aligned, ldct*2 a multiple of 16).  With kb_list/kb_count the K
+ * skipping applies per 256-row tile of A as in sffn_gemm_bf16; the weight
+ * gradient dW2 = dout^T @ a is computed as (a^T @ dout)^T so that the skip
+ * lists of sffn_live_kblocks_t (per 256 activation columns) apply.  No
+ * reference counterpart (the reference's dW2 is a dense torch matmul inside
+ * spAx, old/lib_sparse/sparse.py:305-351). */
+int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                      void* Ct, int64_t ldct, int64_t M, int64_t N, int64_t K,
+                      const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
+                      uint32_t* status_dev, void* stream);
+
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
  * (unless act_out is NULL: the compacted-K down-projection needs none), the
@@ -248,6 +277,14 @@ int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t
  * down-projection is dense, sparse.py:75,118). */
 int sffn_live_kblocks(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
                       int32_t* kb_count, void* stream);
+
+/* The transposed lists, for the weight gradients (contractions over the M
+ * rows of the activation): for each 256-column tile p of the [M, N] tiled
+ * bitmask, kb_count[p] and the ascending list kb_list[p*ceil(M/64) ...] of
+ * 64-row blocks holding any set bit.  Used by dW1 = dpre^T @ x and
+ * dW2 = (a^T @ dout)^T (no reference counterpart, as above). */
+int sffn_live_kblocks_t(const uint8_t* bitmask, int64_t M, int64_t N, int32_t* kb_list,
+                        int32_t* kb_count, void* stream);
 
 /* ---- compacted-K down-projection -----------------------------------------
  * The bitmask-sparse down-projection out = act(z) @ W2^T (and dX = dpre @ W1)

@@ -109,12 +109,38 @@ def test_flat_full_size_round_trip(p):
     assert torch.equal(vals, d.view(-1)[keep.view(-1)])
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_flat_pack_sizes_vals_exactly_and_the_async_form(dtype):
+    """bitsparse_pack returns a vals buffer of exactly nnz elements; the
+    sync-free bitsparse_pack_async writes the same values into a caller's
+    upper-bound buffer and leaves the count on the device; a bound below the
+    count clips and flags SFFN_STATUS_VALS_OVERFLOW.  All against the oracle."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import _lib
+    d = flat_case(300, 1111, 0.15, dtype, seed=17).to(DEV)
+    ov, om = oracle.flat_pack(to_np(d))
+    vals, mask = sf.bitsparse_pack(d)
+    assert vals.numel() == len(ov) and vals.untyped_storage().nbytes() == len(ov) * d.element_size()
+    bits_equal(to_np(vals), ov)
+    bits_equal(to_np(mask), om)
+    arena = torch.full((d.numel(),), 5, dtype=dtype, device=DEV)
+    va, ma, nnz = sf.bitsparse_pack_async(d, arena)
+    assert va is arena and int(nnz.item()) == len(ov)
+    bits_equal(to_np(arena[:len(ov)]), ov)
+    bits_equal(to_np(ma), om)
+    assert bool((arena[len(ov):] == 5).all())
+    small = torch.full((len(ov) // 2,), 5, dtype=dtype, device=DEV)
+    sf.bitsparse_pack_async(d, small)
+    assert _lib.check_status(DEV, raise_on_error=False) == 1  # SFFN_STATUS_VALS_OVERFLOW
+    bits_equal(to_np(small), ov[:len(ov) // 2])
+
+
 def _flat_capi(dtype, n, p, seed):
     from autoresearch2_b200 import _lib
     d = flat_case(1, n, p, dtype, seed=seed).view(-1)
     ov, om = oracle.flat_pack(to_np(d))
     L = _lib.load()
-    ws = _lib.workspace(L.sffn_flat_workspace_bytes(n), DEV)
+    ws = _lib.workspace(L.sffn_flat_pack_workspace_bytes(n, _lib.dtype_code(d)), DEV)
     return _lib, d.to(DEV), ov, om, ws
 
 

@@ -100,6 +100,55 @@ def test_live_kblocks_matches_mask():
         assert torch.equal(kb_list[tp, :n].cpu(), want)
 
 
+@pytest.mark.parametrize("T,F", [(384, 640), (1024, 256), (256, 1152)])
+def test_live_kblocks_transposed_lists(T, F):
+    """Token-skip lists: per 256 activation columns, the 64-row blocks with
+    any nonzero (odd numbers of 128-column tiles included)."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    z = torch.zeros(T, F, device=DEV, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(T + F)
+    live = torch.rand(T // 64, F // 128, generator=g) < 0.3
+    for kb in range(T // 64):
+        for tn in range(F // 128):
+            if live[kb, tn]:
+                z[kb * 64 + 13, tn * 128 + 100] = 2.0
+    arena = torch.empty(T * F, device=DEV, dtype=torch.bfloat16)
+    off = torch.zeros(1, dtype=torch.int32, device=DEV)
+    x = sf.dense_to_tilesparse(z, arena, off, 128, 128)
+    kb_list, kb_count = gemm.live_kblocks_t(x.bitmask, T, F)
+    for tp in range(-(-F // 256)):
+        want = torch.nonzero(live[:, 2 * tp:2 * tp + 2].any(1)).flatten().int()
+        n = int(kb_count[tp])
+        assert n == want.numel()
+        assert torch.equal(kb_list[tp, :n].cpu(), want)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 384), (640, 256, 1024), (2048, 1024, 4096)])
+def test_transposed_store_gemm_with_token_lists(M, N, K):
+    """(A @ B)^T stored by the epilogue, A = a^T for an activation a [K, M]
+    whose zero 64-row blocks per 256 columns are skipped."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    dead = torch.rand(K // 128, -(-M // 128), device=DEV, generator=g) < 0.5
+    keep = ~dead.repeat_interleave(128, 0).repeat_interleave(128, 1)[:K, :M]
+    a = torch.where(keep & (torch.rand(K, M, device=DEV, generator=g) < 0.3),
+                    torch.randn(K, M, device=DEV, generator=g), 0).to(torch.bfloat16)
+    B = torch.randn(K, N, device=DEV, generator=g).to(torch.bfloat16)
+    arena = torch.empty(K * M, device=DEV, dtype=torch.bfloat16)
+    off = torch.zeros(1, dtype=torch.int32, device=DEV)
+    zs = sf.dense_to_tilesparse(a.abs(), arena, off, 128, 128)
+    tl, tc = gemm.live_kblocks_t(zs.bitmask, K, M)
+    want = (a.float().T @ B.float()).T
+    for lists in ((None, None), (tl, tc)):
+        got = gemm.mm_t(a.T, B, kb_list=lists[0], kb_count=lists[1])
+        assert got.shape == (N, M)
+        err = (got.float() - want).abs().max().item()
+        assert err <= 2e-2 * want.abs().max().item() + 1e-3
+    sf.check_status()
+
+
 @pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("T,D,F,bias", [(256, 128, 384, True), (300, 72, 200, False),
                                         (1024, 512, 1536, True)])

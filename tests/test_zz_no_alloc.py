@@ -58,7 +58,7 @@ def _pack(d, noalloc, cap=None, vals_offset=0):
         rc = L.sffn_flat_pack_noalloc(_lib.ptr(d), code, n, _lib.ptr(mask), _lib.ptr(vals), cap,
                                       nnz_p, status_p, st)
     else:
-        ws = _lib.workspace(L.sffn_flat_workspace_bytes(n), d.device)
+        ws = _lib.workspace(L.sffn_flat_pack_workspace_bytes(n, code), d.device)
         rc = L.sffn_flat_pack(_lib.ptr(d), code, n, _lib.ptr(mask), _lib.ptr(vals), cap, nnz_p,
                               _lib.ptr(ws), ws.numel(), status_p, st)
     assert rc == 0, L.sffn_error_string(rc)
