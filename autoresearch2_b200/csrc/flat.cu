@@ -813,27 +813,51 @@ __global__ void __launch_bounds__(FS_T) flat_pack_stage_kernel(const B* __restri
     for (int i = EPV * nvec + tid; i < total; i += FS_T) so[i] = s_val[i];
 }
 
-// Pack, second kernel: each tile's values from its staging segment to
-// vals[offset ...] (never past cap), the offset from the tile counts and
-// group sums; the last tile writes the total count.
+// Pack, second kernel: MV_TPB consecutive tiles per block, their values from
+// the staging segments to vals[offset ...] (never past cap).  The offset of
+// the block's first tile comes from the tile counts and group sums; the
+// others add the block's counts before them.  The last tile writes the total.
+constexpr int MV_TPB = 16;
 template <typename B>
 __global__ void __launch_bounds__(FS_T) flat_pack_move_kernel(const B* __restrict__ stage, TileSums ts, long long nt,
                                                               B* __restrict__ vals, long long cap,
                                                               long long* __restrict__ nnz_out,
                                                               uint32_t* __restrict__ status) {
     __shared__ long long s_red[FS_W];
-    const long long t = (long long)blockIdx.x;
-    const int tid = threadIdx.x;
-    const int total = __ldg(ts.counts + t);
-    const long long ex = tile_offset(ts, t, s_red);
-    if (tid == 0) {
-        if (t + 1 >= nt) *nnz_out = ex + total;
-        if (ex + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+    __shared__ int s_cnt[MV_TPB], s_pre[MV_TPB + 1];
+    const long long t0 = (long long)blockIdx.x * MV_TPB;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ntb = (int)min((long long)MV_TPB, nt - t0);
+    if (tid < MV_TPB) s_cnt[tid] = tid < ntb ? __ldg(ts.counts + t0 + tid) : 0;
+    const long long ex0 = tile_offset(ts, t0, s_red);  // its barrier also publishes s_cnt
+    if (warp == 0) {
+        const int c = lane < MV_TPB ? s_cnt[lane] : 0;
+        const int inc = warp_incl_scan(c, lane);
+        if (lane < MV_TPB) s_pre[lane] = inc - c;
+        if (lane == MV_TPB - 1) s_pre[MV_TPB] = inc;
     }
-    const int lim = (int)max(0ll, min((long long)total, cap - ex));
-    const B* si = stage + t * FS_TILE;
-    B* vo = vals + ex;
-    for (int i = tid; i < lim; i += FS_T) vo[i] = __ldcs(si + i);
+    __syncthreads();
+    const long long total = s_pre[MV_TPB];
+    if (tid == 0) {
+        if (t0 + ntb >= nt) *nnz_out = ex0 + total;
+        if (ex0 + total > cap) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+    }
+    // warp w moves tiles w, w + 8: each tile's values are one contiguous run
+    for (int k = warp; k < ntb; k += FS_W) {
+        const long long ex = ex0 + s_pre[k];
+        const int lim = (int)max(0ll, min((long long)s_cnt[k], cap - ex));
+        const B* si = stage + (t0 + k) * FS_TILE;
+        B* vo = vals + ex;
+        int i = lane;
+        for (; i + 96 < lim; i += 128) {  // four loads in flight per lane
+            const B a0 = __ldcs(si + i), a1 = __ldcs(si + i + 32), a2 = __ldcs(si + i + 64), a3 = __ldcs(si + i + 96);
+            vo[i] = a0;
+            vo[i + 32] = a1;
+            vo[i + 64] = a2;
+            vo[i + 96] = a3;
+        }
+        for (; i < lim; i += 32) vo[i] = __ldcs(si + i);
+    }
 }
 
 // The total count (sum of the group sums) into *nnz_out: one warp.
@@ -985,8 +1009,8 @@ int launch_pack_values(long long n, void* vals, long long cap, int64_t* nnz_dev,
     const long long nt = (n + FS_TILE - 1) / FS_TILE;
     const TileSums ts = tile_sums(ws, nt);
     const B* stage = reinterpret_cast<const B*>(static_cast<const char*>(ws) + pack_stage_offset(nt));
-    flat_pack_move_kernel<B><<<(unsigned)nt, FS_T, 0, st>>>(stage, ts, nt, static_cast<B*>(vals), cap,
-                                                            reinterpret_cast<long long*>(nnz_dev), status);
+    flat_pack_move_kernel<B><<<(unsigned)((nt + MV_TPB - 1) / MV_TPB), FS_T, 0, st>>>(
+        stage, ts, nt, static_cast<B*>(vals), cap, reinterpret_cast<long long*>(nnz_dev), status);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

@@ -70,6 +70,11 @@ AUTO_MIN_SPARSITY = 0.945
 # (128-row tile, column) pairs live.
 _COMPACT_K = "auto"
 CK_AUTO_MAX_LIVE = 0.35
+# The weight gradients skip 64-token blocks that are zero across 256 columns
+# of the activation (dW2 then through a transposed-store epilogue, which
+# costs ~4% when nothing is skipped): taken when the layer's previous step
+# had at most this fraction of its (128-row tile, column) pairs live.
+TOKEN_SKIP_MAX_LIVE = 0.9
 # per layer (keyed by W1's storage and the shapes): pinned [activation count,
 # live (tile, column) count], its copy's event, the element count, the last
 # sparsity and live fraction read
@@ -146,16 +151,16 @@ def _ck_ok(T, D, Fd, W1):
     return live is not None and live <= CK_AUTO_MAX_LIVE
 
 
-def _auto():
-    return _SPARSE_MMA == "auto" or _COMPACT_K == "auto"
+def _token_skip(T, D, Fd, key):
+    _, live = _stats(T, D, Fd, key)
+    return live is not None and live <= TOKEN_SKIP_MAX_LIVE
 
 
 def _observe(W1, prefix, kcount, T, D, Fd):
-    """Auto modes: copy this step's activation count (prefix[-1]) and live
-    (tile, column) count (the sum of kcount, or -1) to pinned host memory
-    without waiting; a later step reads them once the copy's event completed."""
-    if not _auto():
-        return
+    """Copy this step's activation count (prefix[-1]) and live (tile, column)
+    count (the sum of kcount, or -1) to pinned host memory without waiting;
+    a later step reads them once the copy's event completed (the auto modes
+    and the weight gradients' token skipping decide from them)."""
     key = (W1.data_ptr(), T, D, Fd)
     ent = _observed.get(key)
     if ent is None:
@@ -195,7 +200,7 @@ def _fused_forward(x, W1, W2, vals, offset, b1, act):
     use_sp24 = _sp24_ok(T, D, Fd, W1)
     use_ck = not use_sp24 and _ck_ok(T, D, Fd, W1)
     _last_path = "sp24" if use_sp24 else "ck" if use_ck else "dense"
-    want_live = use_ck or (_COMPACT_K == "auto" and G.ck_supported(T, D, Fd))
+    want_live = use_ck or G.ck_supported(T, D, Fd)
     colmask = torch.empty(-(-T // 128) * -(-Fd // 128) * 4, dtype=torch.int32, device=x.device) \
         if want_live else None
     # with sp24 the up-projection epilogue writes a in the 2:4 form directly;
@@ -255,9 +260,14 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
     grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
     # the weight gradients contract over tokens: per 256 columns of the
     # activation, 64-token blocks that are zero there are skipped (dW2 as
-    # (a^T @ dout)^T, so that the lists index its M tiles)
-    tl, tc = G.live_kblocks_t(z_sparse.bitmask, T, Fd)
-    grad_W2 = submit_grad(G.mm_t(a.T, grad_output, kb_list=tl, kb_count=tc))  # reduced while dW1/dX run
+    # (a^T @ dout)^T, so that the lists index its M tiles), when the layer's
+    # activation leaves enough such blocks
+    if _token_skip(T, D, Fd, W1 if stats_key is None else stats_key):
+        tl, tc = G.live_kblocks_t(z_sparse.bitmask, T, Fd)
+        grad_W2 = submit_grad(G.mm_t(a.T, grad_output, kb_list=tl, kb_count=tc))  # reduced while dW1/dX run
+    else:
+        tl = tc = None
+        grad_W2 = submit_grad(G.mm(grad_output.T, a))
     del a
     # dW1 before dX: under data parallelism its all-reduce then overlaps dX, and
     # no weight-gradient reduction is left without compute to hide behind
@@ -287,7 +297,7 @@ def down_proj(z_sparse, W2, act=G.ACT_RELU2):
         raise ValueError("down_proj takes a bf16 128x128-tile activation and bf16 weights")
     global _last_path
     use_ck = _ck_ok(T, D, Fd, W2)
-    if use_ck or (_COMPACT_K == "auto" and G.ck_supported(T, D, Fd)):
+    if use_ck or G.ck_supported(T, D, Fd):
         # statistics for the auto rule are kept under W2 here
         colmask = G.tile_colmask(z_sparse)
         idx, kcount, colpref = G.ck_lists(colmask, T, Fd, counts_only=not use_ck)

@@ -645,11 +645,9 @@ def workload_config(tpg, world, tokens, s_meas=None):
 
 # -------------------------------------------------------------- roofline ----
 # DRAM traffic per launch of the roofline kernels at T=16384: dram__bytes_read.sum
-# + dram__bytes_write.sum of one ncu capture of the kernels at T=4096 (up 299.9 + 126.5 MB,
-# activation gradient 331.8 + 200.9 MB)
-# times 4 -- activations, masks and the weight re-reads per row tile all grow
-# with the tokens.
-TRAFFIC_BYTES = {"sffn_ffn_up": 4 * (299.9e6 + 126.5e6), "sffn_ffn_dgrad": 4 * (331.8e6 + 200.9e6)}
+# + dram__bytes_write.sum of one ncu capture of each kernel at that size
+# (bench.py --micro up / dgrad: up 1440 + 555 MB, activation gradient 1393 + 906 MB).
+TRAFFIC_BYTES = {"sffn_ffn_up": 1440e6 + 555e6, "sffn_ffn_dgrad": 1393e6 + 906e6}
 
 
 def kernel_breakdown(timer, steps_recorded, step_ms):
@@ -728,6 +726,86 @@ def step_flops(step, ms, s, pk):
     return r
 
 
+# ------------------------------------------------------------ micro ----
+def micro(case, device, reps=3):
+    """A few launches of one group of kernels at a stated size, for kernel
+    timing and profiler captures; prints one JSON line of CUDA-event times
+    (mean ms per call after one warm-up call).
+      flat   flat pack and unpack, [65536, 4096] bf16, p = 0.1
+      tile   tiled pack (128 x 128) and unpack of the clustered activation
+             [8192, 28672] bf16, plus the per-row offsets of its tiles
+      up     the fused up-projection GEMM (+ tile scan and slot gather) of the
+             headline layer, `tokens` tokens, 90% zeros
+      dgrad  the fused activation-gradient GEMM of the same layer
+      ck     the compacted-K GEMM of the clustered workload's down-projection"""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import _lib, gemm as G, sp24
+    res = {"case": case}
+
+    def run(name, fn):
+        fn()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize(device)
+        res[name + "_ms"] = round(a.elapsed_time(b) / reps, 4)
+
+    if case == "flat":
+        g = torch.Generator(device=device).manual_seed(0)
+        d = torch.where(torch.rand(*PACK_SHAPE, device=device, generator=g) < PACK_P,
+                        torch.randn(*PACK_SHAPE, device=device, generator=g).abs() + 1e-3, 0.0).to(torch.bfloat16)
+        vals, mask = sf.bitsparse_pack(d)
+        run("pack", lambda: sf.bitsparse_pack_async(d, torch.empty_like(d).view(-1)))
+        run("unpack", lambda: sf.bitsparse_unpack(vals, mask, d.shape))
+    elif case == "tile":
+        z = clustered_activation(CL_TOKENS, CL_F, device)
+        arena = torch.empty(z.numel() // 2, dtype=z.dtype, device=device)
+        off = torch.zeros(1, dtype=torch.int32, device=device)
+
+        def pk():
+            off.zero_()
+            return sf.dense_to_tilesparse(z, arena, off, 128, 128)
+        zs = pk()
+        run("tile_pack", pk)
+        run("tile_unpack", lambda: sf.tile_unpack(zs))
+        run("tile_row_offsets", lambda: G.tile_row_offsets(zs))
+    elif case in ("up", "dgrad"):
+        x, W1, W2, b1, dout = make_ffn_inputs(micro.tokens, D_MODEL, D_FF, SPARSITY, device)
+        arena = torch.empty(micro.tokens * D_FF, dtype=torch.bfloat16, device=device)
+        off = torch.zeros(1, dtype=torch.int32, device=device)
+
+        def up():
+            off.zero_()
+            return G.ffn_up(x, W1, b1, G.ACT_RELU2, arena, off)
+        _, bm, pf, vo, ro = up()
+        zs = sf.BitsparseTensor(arena, bm, pf, vo, -(-micro.tokens // 128), D_FF // 128, 128, 128,
+                                (micro.tokens, D_FF))
+        if case == "up":
+            run("ffn_up", up)
+        else:
+            run("ffn_dgrad", lambda: G.ffn_dgrad(dout, W2, G.ACT_RELU2, zs, ro))
+    elif case == "ck":
+        x, W1, W2, z, dout = make_clustered_inputs(CL_TOKENS, CL_D, CL_F, device)
+        arena = torch.empty(z.numel() // 2, dtype=z.dtype, device=device)
+        off = torch.zeros(1, dtype=torch.int32, device=device)
+        zs = sf.dense_to_tilesparse(z, arena, off, 128, 128)
+        cm = G.tile_colmask(zs)
+        idx, kc, cp = G.ck_lists(cm, CL_TOKENS, CL_F)
+        ac = G.ck_gather_packed(zs, G.tile_row_offsets(zs), cm, cp, kc, G.ACT_RELU2)
+        W2t = sp24.transpose(W2)
+        run("gemm_ck", lambda: G.ck_mm(ac, W2t, idx, kc))
+    else:
+        raise SystemExit(f"unknown micro case {case}")
+    sf.check_status(device)
+    print(json.dumps(res), flush=True)
+
+
+micro.tokens = T_PER_GPU
+
+
 # ------------------------------------------------------------------ main ----
 def main():
     ap = argparse.ArgumentParser()
@@ -748,8 +826,17 @@ def main():
     ap.add_argument("--sparse-mma", default="auto", choices=["auto", "on", "off"],
                     help="path of the products with a sparse operand: 2:4 sparse tensor cores "
                          "chosen by the observed sparsity (auto), always, or never")
+    ap.add_argument("--micro", choices=["flat", "tile", "up", "dgrad", "ck"],
+                    help="time one group of kernels at a stated size (and nothing else)")
+    ap.add_argument("--reps", type=int, default=3, help="calls timed by --micro")
     args = ap.parse_args()
     tpg = args.tokens
+    if args.micro:
+        device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        torch.cuda.set_device(device)
+        micro.tokens = tpg
+        micro(args.micro, device, args.reps)
+        return
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))

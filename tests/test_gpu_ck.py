@@ -176,19 +176,23 @@ def test_clustered_workload_reduced_tokens(mode):
     T, D, F = 1024, 8192, 28672
     x, W1, W2, z, dout = bench.make_clustered_inputs(T, D, F, DEV, seed=1)
     zs = _pack(z)
-    out = sf.ffn.down_proj(zs, W2)
-    assert sf.ffn.last_path() == ("ck" if mode == "on" else "dense")
-    gx, gW1, gW2 = sf.ffn.packed_backward(dout, x, W1, W2, zs)
     zf = z.float()
     a = (zf * zf).to(torch.bfloat16).float()
-    close(out, a @ W2.float().T, what="out")
-    close(gW2, dout.float().T @ a, what="dW2")
-    del a
     dA = (dout.float() @ W2.float()).to(torch.bfloat16).float()
     dpre = ((dA * 2.0).to(torch.bfloat16).float() * zf).to(torch.bfloat16).float()
     del dA
-    close(gx, dpre @ W1.float(), what="dx")
-    close(gW1, dpre.T @ x.float(), what="dW1")
+    # the second step reads the live fraction the first observed: the weight
+    # gradients then skip the zero token blocks
+    for step in range(2):
+        out = sf.ffn.down_proj(zs, W2)
+        assert sf.ffn.last_path() == ("ck" if mode == "on" else "dense")
+        gx, gW1, gW2 = sf.ffn.packed_backward(dout, x, W1, W2, zs)
+        torch.cuda.synchronize()
+        close(out, a @ W2.float().T, what=f"out {step}")
+        close(gW2, dout.float().T @ a, what=f"dW2 {step}")
+        close(gx, dpre @ W1.float(), what=f"dx {step}")
+        close(gW1, dpre.T @ x.float(), what=f"dW1 {step}")
+    assert sf.ffn._token_skip(T, D, F, W2)
 
 
 @pytest.mark.parametrize("p_cluster,expect", [(0.9, "ck"), (0.5, "dense")])
