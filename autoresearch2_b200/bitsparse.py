@@ -217,7 +217,9 @@ def spAx(x_sparse: BitsparseTensor, W: torch.Tensor, square: bool = False,
          row_batch: int = 2048) -> torch.Tensor:
     """y = W @ x_sparse (or W @ x_sparse**2) as in old/lib_sparse/sparse.py:305-351:
     x_sparse [M, N], W [K, M] -> [K, N], unpacked in row batches of `row_batch`
-    rows (a multiple of BLOCK_M) and accumulated in fp32 by cuBLAS."""
+    rows (a multiple of BLOCK_M), each batch's product on this library's
+    tcgen05 GEMM (split-bf16 for float32 / float16), accumulated in fp32."""
+    from .gemm import matmul
     M, N = x_sparse.shape
     if W.shape[1] != M:
         raise ValueError(f"W.shape must be [K, {M}] for W @ sparse_x, got {tuple(W.shape)}")
@@ -226,12 +228,12 @@ def spAx(x_sparse: BitsparseTensor, W: torch.Tensor, square: bool = False,
     row_batch = max(BM, (row_batch // BM) * BM)
     K = W.shape[0]
     if M <= row_batch:
-        return torch.mm(W, tile_unpack(x_sparse, 0, M, square=square).to(W.dtype))
+        return matmul(W, tile_unpack(x_sparse, 0, M, square=square).to(W.dtype))
     acc = torch.zeros(K, N, device=W.device, dtype=torch.float32)
     for m0 in range(0, M, row_batch):
         m1 = min(m0 + row_batch, M)
         dense = tile_unpack(x_sparse, m0, m1, square=square).to(W.dtype)
-        acc += torch.mm(W[:, m0:m1], dense).float()
+        acc += matmul(W[:, m0:m1], dense).float()
     return acc.to(W.dtype)
 
 

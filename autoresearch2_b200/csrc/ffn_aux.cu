@@ -15,6 +15,8 @@
 //                       the ascending list of 64-column blocks holding any set
 //                       bit: the down-projection skips the others.  One warp
 //                       per k-block; the last CTA of a tile compacts.
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace sffn {
@@ -150,6 +152,91 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
     }
 }
 
+// Like tile_rows_kernel's slot copy, but the values come from the dense
+// matrix itself (the up-projection's ReLU output, which is z): per warp, for
+// each of its 32 rows, lane k reads the row's columns 4k .. 4k+3 of the tile
+// (one 8-byte load, eight rows' loads in flight), ranks its set ones by a
+// warp scan and writes them to the row's place in the arena.  Also writes
+// row_offsets and colmask like tile_rows_kernel.  The tile grid is gm x gn;
+// rows past M and columns past N hold no set bits and are not read.
+__global__ void __launch_bounds__(128) tile_rows_dense_kernel(const uint8_t* __restrict__ mask,
+                                                              const int* __restrict__ prefix,
+                                                              int* __restrict__ row_offsets,
+                                                              const uint16_t* __restrict__ src, long long ld,
+                                                              long long M, long long N, long long gn,
+                                                              const int* __restrict__ vals_offset,
+                                                              uint16_t* __restrict__ vals, long long cap,
+                                                              uint32_t* __restrict__ status,
+                                                              uint4* __restrict__ colmask) {
+    __shared__ int s_warp[4];
+    __shared__ uint4 s_or[4];
+    const long long t = blockIdx.x;
+    const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
+    const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
+    const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
+    const int inc = warp_incl_scan(cnt, lane);
+    if (lane == 31) s_warp[warp] = inc;
+    if (colmask) {
+        const uint4 o = make_uint4(__reduce_or_sync(FULL, mw.x), __reduce_or_sync(FULL, mw.y),
+                                   __reduce_or_sync(FULL, mw.z), __reduce_or_sync(FULL, mw.w));
+        if (lane == 0) s_or[warp] = o;
+    }
+    __syncthreads();
+    if (colmask && r == 0) {
+        uint4 o = s_or[0];
+#pragma unroll
+        for (int w = 1; w < 4; ++w) {
+            o.x |= s_or[w].x;
+            o.y |= s_or[w].y;
+            o.z |= s_or[w].z;
+            o.w |= s_or[w].w;
+        }
+        colmask[t] = o;
+    }
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += s_warp[w];
+    const int roff = prefix[t] + before + inc - cnt;
+    if (row_offsets) row_offsets[t * 128 + r] = roff;
+    const long long base = (long long)*vals_offset;
+    const long long tm = t / gn, tn = t % gn;
+    const long long col = tn * 128 + 4 * lane;  // this lane's four columns
+    const bool col_ok = col < N;                 // N % 4 == 0: whole groups
+    const int word = lane >> 3, sh = 4 * (lane & 7);
+    bool overflow = false;
+#pragma unroll 1
+    for (int i0 = 0; i0 < 32; i0 += 8) {
+        uint2 v[8];
+        uint32_t nib[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {  // loads first
+            const int i = i0 + u;
+            const uint32_t mx = __shfl_sync(FULL, mw.x, i), my = __shfl_sync(FULL, mw.y, i);
+            const uint32_t mz = __shfl_sync(FULL, mw.z, i), mq = __shfl_sync(FULL, mw.w, i);
+            const uint32_t w = word == 0 ? mx : word == 1 ? my : word == 2 ? mz : mq;
+            nib[u] = (w >> sh) & 15u;
+            const long long row = tm * 128 + warp * 32 + i;
+            v[u] = make_uint2(0, 0);
+            if (nib[u] && col_ok && row < M) v[u] = __ldcs(reinterpret_cast<const uint2*>(src + row * ld + col));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int i = i0 + u;
+            const int c = __popc(nib[u]);
+            const int pos = warp_incl_scan(c, lane) - c;
+            long long p = base + __shfl_sync(FULL, roff, i) + pos;
+            const uint32_t h[4] = {v[u].x & 0xFFFFu, v[u].x >> 16, v[u].y & 0xFFFFu, v[u].y >> 16};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if ((nib[u] >> j) & 1u) {
+                    if (p >= 0 && p < cap) vals[p] = (uint16_t)h[j];
+                    else overflow = true;
+                    ++p;
+                }
+        }
+    }
+    if (overflow) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+}
+
 // Grid (pair tile, group of 8 k-blocks); warp w of a CTA tests k-block
 // 8*group + w over the pair's two 128-row format tiles with all loads issued
 // at once, and writes a 0/1 flag into kb_list[tile][kb].  The last CTA of a
@@ -251,6 +338,37 @@ __global__ void __launch_bounds__(LIVE_WARPS * 32) live_kblocks_t_kernel(const u
         n += __popc(b);
     }
     if (lane == 0) kb_count[tp] = n;
+}
+
+// Three-term bf16 split of a float32 (or float16) matrix for the split-bf16
+// products: x = hi + mid + lo with hi = bf16(x), mid = bf16(x - hi),
+// lo = bf16(x - hi - mid) (each difference exact in float32), so the three
+// pieces carry x's 24 significant bits.  Row r of dst holds six blocks of
+// `cols` elements, the pieces in the order `order` gives (two bits per
+// block: 0 hi, 1 mid, 2 lo); src element (r, c) is at src[r*s_row + c*s_col].
+// The product of an A split in the order hi hi mid hi lo mid with a B split
+// in the order hi mid hi lo hi mid, contracted over the 6*cols columns,
+// sums hi*hi + hi*mid + mid*hi + hi*lo + lo*hi + mid*mid: the float32
+// product up to terms of relative size 2^-24.
+template <typename S>
+__global__ void __launch_bounds__(256) split3_kernel(const S* __restrict__ src, long long rows, long long cols,
+                                                     long long s_row, long long s_col, uint16_t* __restrict__ dst,
+                                                     long long ld_dst, uint32_t order) {
+    const long long n = rows * cols;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const long long r = i / cols, c = i - r * cols;
+        float x;
+        if constexpr (sizeof(S) == 4) x = __ldg(src + r * s_row + c * s_col);
+        else x = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const uint16_t*>(src) + r * s_row + c * s_col)));
+        const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+        const float r1 = x - __bfloat162float(hi);
+        const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+        const uint16_t piece[3] = {__bfloat16_as_ushort(hi), __bfloat16_as_ushort(mid), __bfloat16_as_ushort(lo)};
+        uint16_t* d = dst + r * ld_dst + c;
+#pragma unroll
+        for (int b = 0; b < 6; ++b) d[b * cols] = piece[(order >> (2 * b)) & 3u];
+    }
 }
 
 // dst[c][r] = src[r][c] for 16-bit elements: a 64 x 64 tile per CTA, read
@@ -621,6 +739,47 @@ extern "C" int sffn_live_kblocks_t(const uint8_t* bitmask, int64_t M, int64_t N,
     SFFN_CUDA_TRY(cudaMemsetAsync(kb_count, 0, (size_t)gp * sizeof(int32_t), st));
     const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));
     live_kblocks_t_kernel<<<grid, LIVE_WARPS * 32, 0, st>>>(bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list, kb_count);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_split_bf16x3(const void* src, int dtype, int64_t rows, int64_t cols, int64_t s_row, int64_t s_col,
+                                 void* dst, int64_t ld_dst, int b_order, void* stream) {
+    if (dtype != SFFN_F32 && dtype != SFFN_F16) return SFFN_ERR_DTYPE;
+    if (rows <= 0 || cols <= 0 || !src || !dst || ld_dst < 6 * cols) return SFFN_ERR_ARG;
+    // A: hi hi mid hi lo mid; B: hi mid hi lo hi mid (two bits per block)
+    const uint32_t order = b_order ? (0u | 1u << 2 | 0u << 4 | 2u << 6 | 0u << 8 | 1u << 10)
+                                   : (0u | 0u << 2 | 1u << 4 | 0u << 6 | 2u << 8 | 1u << 10);
+    DeviceScope dev_scope;
+    if (int rc = dev_scope.bind_same(dst, {src})) return rc;
+    const long long n = rows * cols;
+    const unsigned grid = (unsigned)std::min<long long>((n + 255) / 256, 148ll * 16);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == SFFN_F32)
+        split3_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(src), rows, cols, s_row, s_col,
+                                                   static_cast<uint16_t*>(dst), ld_dst, order);
+    else
+        split3_kernel<uint16_t><<<grid, 256, 0, st>>>(static_cast<const uint16_t*>(src), rows, cols, s_row, s_col,
+                                                      static_cast<uint16_t*>(dst), ld_dst, order);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_tile_gather_dense(const void* dense, int64_t ld, int64_t M, int64_t N, const uint8_t* bitmask,
+                                      const int32_t* prefix, const int32_t* vals_offset_dev, void* vals,
+                                      int64_t vals_capacity, int32_t* row_offsets, uint32_t* colmask,
+                                      uint32_t* status_dev, void* stream) {
+    if (M <= 0 || N <= 0 || N % 4 || ld < N || ld % 4 || !dense || !bitmask || !prefix || !vals_offset_dev || !vals ||
+        !status_dev)
+        return SFFN_ERR_ARG;
+    if (!aligned16(bitmask) || !aligned16(colmask) || (reinterpret_cast<uintptr_t>(dense) & 7u)) return SFFN_ERR_ALIGN;
+    const long long gm = (M + 127) / 128, gn = (N + 127) / 128;
+    if (gm * gn > 0x7FFFFFFFll) return SFFN_ERR_ARG;
+    DeviceScope dev_scope;
+    if (int rc = dev_scope.bind_same(vals, {dense, bitmask})) return rc;
+    tile_rows_dense_kernel<<<(unsigned)(gm * gn), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        bitmask, prefix, row_offsets, static_cast<const uint16_t*>(dense), ld, M, N, gn, vals_offset_dev,
+        static_cast<uint16_t*>(vals), vals_capacity, status_dev, reinterpret_cast<uint4*>(colmask));
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

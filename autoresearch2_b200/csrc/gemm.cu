@@ -106,6 +106,9 @@ struct GemmArgs {
     const int* vals_offset;
     float* colsum;  // DGRAD: optional fp32 [N] += column sums of dpre
     int c_trans;    // STORE: write C^T ([N][ldc]) instead of C
+    float* out_f32; // STORE: C in float32 ([M][ldc]) instead of bf16
+    int acc_f32;    // with out_f32: C += the product (round to nearest, on the CUDA cores)
+    int kb0;        // first K block of the product (K blocks kb0 .. kb0 + ceil(K/64) - 1)
     int sp_on;      // UP: a, DGRAD: dpre, dpre^T and a^T in 2:4 form instead of dense
     Sp24Out sp[3];  // UP: [0] a; DGRAD: [0] dpre, [1] dpre^T, [2] a^T
     uint32_t* status;
@@ -334,7 +337,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     if ((int)(kc & 1) != par) continue;
                     const int stage = (int)(kc % G_STAGES);
                     const uint32_t phase = (uint32_t)((kc / G_STAGES) & 1);
-                    const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : i;
+                    const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : args.kb0 + i;
                     // the stage is free once the leader's MMAs reading it are done
                     if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
                         atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
@@ -477,6 +480,32 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     uint32_t r[32];
                     tmem_ld32(tbase + c * 32, r);
                     tmem_wait_ld();
+                    if (args.out_f32) {
+                        // float32 C: each lane stores its row's 32 values (128 contiguous bytes)
+                        const int gcol = gcol0 + c * 32;
+                        if (row_ok && gcol < args.N) {
+                            float* frow = args.out_f32 + (size_t)grow * args.ldc + gcol;
+                            if (vec && gcol + 32 <= args.N) {
+#pragma unroll
+                                for (int q = 0; q < 8; ++q) {
+                                    float4 v = nkb ? make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                                                 __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+                                    if (args.acc_f32) {
+                                        const float4 o = reinterpret_cast<const float4*>(frow)[q];
+                                        v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
+                                    }
+                                    reinterpret_cast<float4*>(frow)[q] = v;
+                                }
+                            } else {
+                                for (int j = 0; j < 32 && gcol + j < args.N; ++j) {
+                                    const float v = nkb ? __uint_as_float(r[j]) : 0.f;
+                                    frow[j] = args.acc_f32 ? frow[j] + v : v;
+                                }
+                            }
+                        }
+                        continue;
+                    }
                     uint32_t w[16];
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
@@ -509,7 +538,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         named_bar_sync(bar_id, 128);
                     }
                     // this row's z values go to its own 128-element segment of the slot
-                    uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;
+                    uint16_t* slot_row = args.slots ? args.slots + tf * FT_ELEMS + row * FT : nullptr;
                     uint32_t words[4];
                     uint32_t mw[4] = {0, 0, 0, 0};  // 2:4 metadata words (sp_on)
                     int cnt = 0;
@@ -555,13 +584,18 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             else if (row_ok) store_row32(orow, gcol, args.N, false, w);
                         }
                         // this chunk's z values, in column order, to the row's slot segment
+                        // (no slots: the dense output holds z itself, ReLU)
+                        if (args.slots) {
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            const uint32_t b2 = (bits >> (2 * q)) & 3u;
-                            if (b2) {
-                                if (b2 & 1u) slot_row[cnt++] = (uint16_t)zw[q];
-                                if (b2 & 2u) slot_row[cnt++] = (uint16_t)(zw[q] >> 16);
+                            for (int q = 0; q < 16; ++q) {
+                                const uint32_t b2 = (bits >> (2 * q)) & 3u;
+                                if (b2) {
+                                    if (b2 & 1u) slot_row[cnt++] = (uint16_t)zw[q];
+                                    if (b2 & 2u) slot_row[cnt++] = (uint16_t)(zw[q] >> 16);
+                                }
                             }
+                        } else {
+                            cnt += __popc(bits);
                         }
                         words[c] = bits;
                     }
@@ -1401,19 +1435,23 @@ bool device_is_sm100() {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 int launch_gemm(const void* A, long long lda, const void* B, long long ldb, GemmArgs args,
-                cudaStream_t st) {
+                cudaStream_t st, long long kmap = -1) {
     CUtensorMap ta, tb;
+    // K extent of the operands' tensor maps (beyond the K blocks this launch reads)
+    const long long KM = kmap > 0 ? kmap : args.K;
     // K-major operand [rows][K]: inner = K; MN-major operand [K][rows]: inner = rows.
-    const bool okA = A_MN ? make_tmap(&ta, A, args.M, args.K, lda, 64, G_BK)
-                          : make_tmap(&ta, A, args.K, args.M, lda, G_BK, G_BM);
-    const bool okB = B_MN ? make_tmap(&tb, B, args.N, args.K, ldb, 64, G_BK)
-                          : make_tmap(&tb, B, args.K, args.N, ldb, G_BK, BN / G_CTAS);
+    const bool okA = A_MN ? make_tmap(&ta, A, args.M, KM, lda, 64, G_BK)
+                          : make_tmap(&ta, A, KM, args.M, lda, G_BK, G_BM);
+    const bool okB = B_MN ? make_tmap(&tb, B, args.N, KM, ldb, 64, G_BK)
+                          : make_tmap(&tb, B, KM, args.N, ldb, G_BK, BN / G_CTAS);
     if (!okA || !okB) return SFFN_ERR_CUDA;
     // outputs: 32 x 32 boxes with 64-byte swizzle for the epilogue's bulk stores
     CUtensorMap tc, tc2;
     memset(&tc, 0, sizeof(tc));
     memset(&tc2, 0, sizeof(tc2));
-    if (args.c_trans) {
+    if (args.out_f32) {
+        // plain vector stores from the epilogue; no tensor map
+    } else if (args.c_trans) {
         if (!make_tmap(&tc, args.out, args.M, args.N, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return SFFN_ERR_CUDA;
     } else if (args.vec_out) {
@@ -1433,6 +1471,16 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     k<<<clusters * G_CTAS, G_THREADS, smem, st>>>(ta, tb, tc, tc2, args);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
+}
+
+template <int EPI>
+int dispatch_kmap(bool a_mn, bool b_mn, const void* A, long long lda, const void* B, long long ldb,
+                  GemmArgs args, long long kmap, cudaStream_t st) {
+    constexpr int BN = 256;
+    if (!a_mn && !b_mn) return launch_gemm<BN, false, false, EPI>(A, lda, B, ldb, args, st, kmap);
+    if (!a_mn && b_mn) return launch_gemm<BN, false, true, EPI>(A, lda, B, ldb, args, st, kmap);
+    if (a_mn && b_mn) return launch_gemm<BN, true, true, EPI>(A, lda, B, ldb, args, st, kmap);
+    return launch_gemm<BN, true, false, EPI>(A, lda, B, ldb, args, st, kmap);
 }
 
 template <int EPI>
@@ -1593,6 +1641,35 @@ extern "C" int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const voi
     return dispatch<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, uint32_t* status_dev,
+                                     void* stream) {
+    // C (float32) = A @ B, bf16 operands as sffn_gemm_bf16 takes them.
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
+    if (rc) return rc;
+    if (!C || ldc < N || !status_dev) return SFFN_ERR_ARG;
+    // The tensor cores' float32 accumulation does not round to nearest: over
+    // K of 18k (six split terms of 3072) its error grew to ~5e-5.  K runs in
+    // chunks of kFp32ChunkK (at most 64 MMA steps each), each chunk's sum
+    // added into C by the epilogue in float32 with round to nearest.
+    constexpr long long kFp32ChunkK = 1024;
+    for (long long k0 = 0; k0 < K; k0 += kFp32ChunkK) {
+        const long long kc = std::min(kFp32ChunkK, K - k0);
+        GemmArgs a = base_args(M, N, k0 + kc, nullptr, ldc);  // the maps cover K columns up to this chunk's end
+        a.K = (int)kc;
+        a.kb0 = (int)(k0 / G_BK);
+        a.out_f32 = C;
+        a.acc_f32 = k0 > 0;
+        a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
+        a.status = status_dev;
+        if (int r2 = dispatch_kmap<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, k0 + kc,
+                                              reinterpret_cast<cudaStream_t>(stream)))
+            return r2;
+    }
+    return SFFN_OK;
+}
+
 extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
                            int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
                            uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
@@ -1601,7 +1678,10 @@ extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t l
     int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
-    if ((act_out && ld_act < F) || !bitmask || !tile_counts || !slots || !status_dev) return SFFN_ERR_ARG;
+    if ((act_out && ld_act < F) || !bitmask || !tile_counts || !status_dev) return SFFN_ERR_ARG;
+    // without slots the dense output must be z itself (ReLU), from which
+    // sffn_tile_gather_dense fills the arena
+    if (!slots && !(act_out && act == ACT_RELU)) return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
     if (T * F > 0x7FFFFFFFll) return SFFN_ERR_ARG;
     GemmArgs a = base_args(T, F, D, act_out, act_out ? ld_act : F);

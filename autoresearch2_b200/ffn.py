@@ -15,8 +15,9 @@ applies bias + ReLU/ReLU^2 and emits the bitmask, counts and compacted z (a
 that are zero in a whole 128-row tile; the backward's dout @ W2 epilogue
 applies the mask / 2z gradient from the packed z and emits the activation
 for dW2, so no dense z is kept between forward and backward.  float32 and
-float16 inputs run cuBLAS matmuls with this library's pack/mask kernels
-(64x64 tiles, as in the reference).  Forward and backward each run as one
+float16 inputs run their products as split-bf16 products on the same tcgen05
+GEMM (three bf16 pieces per operand, fp32 accumulation: float32 accuracy)
+with this library's pack/mask kernels (64x64 tiles, as in the reference).  Forward and backward each run as one
 torch.library op (sparseffn::ffn_fwd, sparseffn::ffn_bwd, registered in
 library.py), so torch.compile traces these Functions without a graph break.
 
@@ -326,13 +327,15 @@ def packed_backward(grad_output, x, W1, W2, z_sparse, act=G.ACT_RELU2):
 
 
 def _unfused_forward(x, W1, W2, vals, offset, b1, act):
-    """float32 / float16 (or unaligned) forward: cuBLAS matmuls and this
-    library's 64x64-tile pack.  Returns (out, z_sparse)."""
-    preact = x @ W1.T
+    """float32 / float16 forward: the products on this library's tcgen05 GEMM
+    (split-bf16 for these dtypes, gemm.matmul), the reference's elementwise
+    steps (bias, ReLU, square) in torch, and the 64x64-tile pack.  Returns
+    (out, z_sparse)."""
+    preact = G.matmul(x, W1.T)
     if b1 is not None:
         preact += b1
     z = F.relu(preact)
-    output = (z * z if act == G.ACT_RELU2 else z) @ W2.T
+    output = G.matmul(z * z if act == G.ACT_RELU2 else z, W2.T)
     z_sparse = bs.dense_to_tilesparse(z, vals, offset)
     return output, z_sparse
 
@@ -341,7 +344,7 @@ def _unfused_backward(grad_output, x, W1, W2, z_sparse, has_bias, act):
     """-> (grad_x, grad_W1, grad_W2, grad_b1 or None), old/lib_sparse/sparse.py:84-109
     (ReLU) and :129-151 (ReLU^2)."""
     grad_output = grad_output.contiguous()
-    grad_z = grad_output @ W2
+    grad_z = G.matmul(grad_output, W2)
     if act == G.ACT_RELU2:
         # grad_pre = grad_z * 2z; dW2 takes z^2, which the reference stores over
         # z in place (sparse.py:136-147) -- here it is formed while unpacking, the
@@ -352,8 +355,8 @@ def _unfused_backward(grad_output, x, W1, W2, z_sparse, has_bias, act):
         grad_W2 = submit_grad(bs.spAx(z_sparse, grad_output.T))
         bs.mask_with_bitmask_(grad_z, z_sparse)
     grad_b1 = submit_grad(grad_z.sum(0)) if has_bias else None
-    grad_W1 = submit_grad(grad_z.T @ x)
-    grad_x = grad_z @ W1
+    grad_W1 = submit_grad(G.matmul(grad_z.T, x))
+    grad_x = G.matmul(grad_z, W1)
     return grad_x, grad_W1, grad_W2, grad_b1
 
 

@@ -58,6 +58,40 @@ def mm(A: torch.Tensor, B: torch.Tensor, out: torch.Tensor = None, kb_list=None,
     return out
 
 
+def split3(X: torch.Tensor, b_order: bool) -> torch.Tensor:
+    """[rows, 6 * cols] bf16: the three-term bf16 split of a 2-D float32 /
+    float16 tensor (any strides), blocks hi hi mid hi lo mid (A) or hi mid hi
+    lo hi mid (b_order, for B^T)."""
+    rows, cols = X.shape
+    ld = -(-6 * cols // 8) * 8  # 16-byte aligned rows for the TMA loads
+    out = torch.empty(rows, ld, dtype=torch.bfloat16, device=X.device)
+    call("sffn_split_bf16x3", ptr(X), _lib.dtype_code(X), rows, cols, X.stride(0), X.stride(1), ptr(out), ld,
+         int(bool(b_order)), stream_ptr(X.device))
+    return out
+
+
+def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """A @ B on this library's tcgen05 GEMM, in A's dtype.  bfloat16 runs
+    directly (fp32 accumulation); float32 and float16 run as the split-bf16
+    product (three bf16 pieces per operand, six cross products, fp32
+    accumulation and output): the float32 product up to terms of relative
+    size 2^-24, where a TF32 product keeps 2^-11."""
+    _lib.require_cuda(A, B)
+    if A.dtype != B.dtype:
+        raise TypeError("matmul operands must share a dtype")
+    if A.dtype == torch.bfloat16:
+        return mm(A, B)
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(B.shape)}")
+    a3, b3 = split3(A, False), split3(B.T, True)
+    C = torch.empty(M, N, dtype=torch.float32, device=A.device)
+    call("sffn_gemm_bf16_f32out", ptr(a3), a3.stride(0), 0, ptr(b3), b3.stride(0), 0, ptr(C), C.stride(0), M, N,
+         6 * K, ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+    return C if A.dtype == torch.float32 else C.to(A.dtype)
+
+
 def mm_t(A: torch.Tensor, B: torch.Tensor, kb_list=None, kb_count=None):
     """(A @ B)^T [N, M] (bf16) on the tcgen05 kernel, the product stored
     transposed by its epilogue; kb_list / kb_count as in mm (per 256 rows of A)."""
@@ -116,7 +150,10 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     nt = gm * gn
     bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
     counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
-    slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
+    # ReLU with a dense output: that output is z, and the arena is filled from
+    # it -- no per-row slots (a [T, F] transient) and no slot stores
+    from_dense = act == ACT_RELU and write_act and not sp24 and F % 4 == 0
+    slots = None if from_dense else torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
     prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
     vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
     row_offsets = torch.empty(nt * 128, dtype=torch.int32, device=dev)
@@ -134,8 +171,12 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
              ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
-    call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
-         ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)
+    if from_dense:
+        call("sffn_tile_gather_dense", ptr(act_out), F, T, F, ptr(bitmask), ptr(prefix), ptr(vals_offset),
+             ptr(vals), vals.numel(), ptr(row_offsets), ptr(colmask), status, st)
+    else:
+        call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
+             ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)
     return act_out, bitmask, prefix, vals_offset, row_offsets
 
 

@@ -226,12 +226,31 @@ int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const void* B, int64
                       const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
                       uint32_t* status_dev, void* stream);
 
+/* float32 / float16 products on the bf16 tensor cores.  sffn_split_bf16x3
+ * writes src (rows x cols, element (r, c) at src[r*s_row + c*s_col], dtype
+ * SFFN_F32 or SFFN_F16) as six blocks of cols bf16 per row of dst (ld_dst >=
+ * 6*cols): x = hi + mid + lo (hi = bf16(x), mid = bf16(x - hi), lo =
+ * bf16(x - hi - mid)), the blocks ordered hi hi mid hi lo mid (b_order 0,
+ * for A [M][K]) or hi mid hi lo hi mid (b_order 1, for B^T [N][K]).
+ * sffn_gemm_bf16_f32out multiplies such an A by such a B over 6*cols (C in
+ * float32): hi*hi + hi*mid + mid*hi + hi*lo + lo*hi + mid*mid, the float32
+ * product up to terms of relative size 2^-24, accumulated in float32.  They
+ * replace the float32 torch matmuls of old/lib_sparse/sparse.py:72-75,
+ * 92,106-107,116-118,132,148-149 and spAx's (sparse.py:305-351). */
+int sffn_split_bf16x3(const void* src, int dtype, int64_t rows, int64_t cols, int64_t s_row, int64_t s_col,
+                      void* dst, int64_t ld_dst, int b_order, void* stream);
+int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, uint32_t* status_dev,
+                          void* stream);
+
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
  * (unless act_out is NULL: the compacted-K down-projection needs none), the
  * tiled 128x128 bitmask of z > 0 (ceil(T/128)*ceil(F/128) tiles of 2048 B),
  * four partial counts per tile (tile_counts[t*4 .. t*4+3]) and, for tile t,
- * row r's z values in order at slots[t*16384 + r*128 ...].  Follow with
+ * row r's z values in order at slots[t*16384 + r*128 ...] (slots may be NULL
+ * for ReLU with act_out given: act_out is z, and sffn_tile_gather_dense reads
+ * the values from it).  Follow with
  * sffn_tile_scan_counts (parts = 4) and sffn_tile_gather_slots to finish the
  * BitsparseTensor.
  *   replaces old/lib_sparse/sparse.py:72-77,116-120 (matmul, relu, square,
@@ -261,6 +280,15 @@ int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int3
                            const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
                            int64_t vals_capacity, int dtype, int32_t* row_offsets,
                            uint32_t* colmask, uint32_t* status_dev, void* stream);
+
+/* sffn_tile_gather_slots with the values taken from the dense [M, N] 16-bit
+ * matrix itself (row stride ld; N and ld multiples of 4, dense 8-byte
+ * aligned): for ReLU the up-projection's dense output is z, so it needs no
+ * slots (sffn_ffn_up with slots NULL).  Same outputs as sffn_tile_gather_slots. */
+int sffn_tile_gather_dense(const void* dense, int64_t ld, int64_t M, int64_t N, const uint8_t* bitmask,
+                           const int32_t* prefix, const int32_t* vals_offset_dev, void* vals,
+                           int64_t vals_capacity, int32_t* row_offsets, uint32_t* colmask,
+                           uint32_t* status_dev, void* stream);
 
 /* row_offsets[t*128 + r] = prefix[t] + number of values in rows < r of tile t,
  * for a tiled 128x128 bitmask (the per-row index sffn_ffn_dgrad reads; the

@@ -212,3 +212,35 @@ def test_ffn_dgrad_fused(act):
     assert torch.equal(act2, want_a.to(torch.bfloat16))
     # exact: elements off the mask are (signed) zero
     assert torch.count_nonzero(dpre[z == 0]) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 768), (300, 200, 1000), (8192, 768, 3072), (3072, 768, 8192)])
+@pytest.mark.parametrize("trans", ["nn", "nt", "tn"])
+def test_split_bf16_float32_product(M, N, K, trans):
+    """float32 products on the tcgen05 GEMM as split-bf16 (three pieces per
+    operand, six cross products, fp32 accumulation): within 1e-5 of the float64
+    product (elementwise, absolute floor 1e-5 x max |ref|), for row-major and
+    transposed views, K not a multiple of 64 included."""
+    from autoresearch2_b200 import gemm
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    A = torch.randn(M, K, device=DEV, generator=g) if trans[0] == "n" else \
+        torch.randn(K, M, device=DEV, generator=g).T
+    B = torch.randn(K, N, device=DEV, generator=g) / K ** 0.5 if trans[1] == "n" else \
+        (torch.randn(N, K, device=DEV, generator=g) / K ** 0.5).T
+    got = gemm.matmul(A, B)
+    want = A.double() @ B.double()
+    assert got.dtype == torch.float32
+    err = (got.double() - want).abs()
+    assert bool((err <= 1e-5 * want.abs() + 1e-5 * want.abs().max()).all()), err.max().item()
+
+
+def test_split_bf16_float16_product():
+    from autoresearch2_b200 import gemm
+    g = torch.Generator(device=DEV).manual_seed(5)
+    A = torch.randn(512, 384, device=DEV, generator=g).half()
+    B = (torch.randn(384, 256, device=DEV, generator=g) / 20).half()
+    got = gemm.matmul(A, B)
+    want = (A.double() @ B.double()).half().double()
+    assert got.dtype == torch.float16
+    err = (got.double() - want).abs()
+    assert bool((err <= 1e-3 * want.abs() + 1e-3 * want.abs().max()).all())
