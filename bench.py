@@ -469,36 +469,40 @@ def bench_deep(device):
 
 
 # --------------------------------------------------------------- gpt ----
-def bench_gpt(device, pk, steps=5, warmup=3):
+def bench_gpt(device, pk, steps=5, warmup=3, world=1, rank=0):
     """GPT-style training step with the sparse ReLU^2 MLPs against the same
     model with dense torch MLPs: 12 layers, width 768, 12 heads, hidden 3072,
-    vocab 50304, 1024-token sequences, batch 32 (32768 tokens per step),
-    bf16, N(0, 0.02) weights, uniform random token ids (seed 0), fused AdamW.
-    tokens/s from CUDA events over `steps` steps after `warmup`; MFU against
-    the measured sustained bf16 figure; peak MB from torch's allocator."""
+    vocab 50304, 1024-token sequences, batch 32 per GPU (32768 tokens per
+    GPU per step), bf16, N(0, 0.02) weights, uniform random token ids (seed
+    0 + rank), fused AdamW; with N GPUs data-parallel (torch's
+    DistributedDataParallel over NCCL, weak scaling).  Whole-job tokens/s from
+    CUDA events over `steps` steps after `warmup`, max over ranks; MFU per GPU
+    against the measured sustained bf16 figure; peak MB from torch's allocator."""
     from autoresearch2_b200 import gpt
     cfg = gpt.GPTConfig()
     batch = 32
-    idx, tgt = gpt.synthetic_batch(cfg, batch, device)
+    idx, tgt = gpt.synthetic_batch(cfg, batch, device, seed=rank)
     res = {"config": {"n_layer": cfg.n_layer, "n_embd": cfg.n_embd, "n_head": cfg.n_head,
                       "ffn_hidden": cfg.ffn_hidden, "vocab": cfg.vocab, "seq_len": cfg.seq_len,
                       "batch": batch, "mlp": "relu2"},
            "flops_per_token": gpt.flops_per_token(cfg)}
+    res["n_gpus"] = world
     for name, sparse in (("sparse", True), ("dense", False)):
         model = gpt.GPT(cfg, sparse=sparse, device=device)
-        step = gpt.TrainStep(model, idx, tgt)
+        net = torch.nn.parallel.DistributedDataParallel(model, device_ids=[device.index]) if world > 1 else model
+        step = gpt.TrainStep(net, idx, tgt)
         torch.cuda.reset_peak_memory_stats(device)
         ms = time_steps(step, steps, warmup, device)
         loss = float(step())
-        tps = batch * cfg.seq_len / (ms / 1e3)
+        tps = world * batch * cfg.seq_len / (ms / 1e3)
         res[name] = {"tokens_per_s": round(tps, 1), "ms_per_step": round(ms, 3),
-                     "mfu_of_measured_sustained": round(gpt.mfu(tps, cfg, pk["bf16_tflops_sustained"]), 3),
+                     "mfu_of_measured_sustained": round(gpt.mfu(tps / world, cfg, pk["bf16_tflops_sustained"]), 3),
                      "peak_mb": round(torch.cuda.max_memory_allocated(device) / 2 ** 20, 1),
                      "loss_after": round(loss, 4)}
         if sparse:
             res[name]["activation_zeros"] = round(
                 1 - model.arena.used() / (batch * cfg.seq_len * cfg.ffn_hidden * cfg.n_layer), 4)
-        del step, model
+        del step, net, model
         torch.cuda.empty_cache()
     import autoresearch2_b200 as sf
     sf.check_status(device)
@@ -982,6 +986,9 @@ def main():
         clustered = bench_clustered(device, group, world, max(3, args.steps // 4), args.warmup, pk, rank)
     flops = step_flops(step, ms, s_meas, pk) if rank == 0 else None
     pack = codec = deep_ffn = gpt_step = None
+    if not args.quick and world > 1:
+        # the GPT harness data-parallel on every rank (its gradients all-reduced)
+        gpt_step = bench_gpt(device, peaks(), world=world, rank=rank)
     if rank == 0 and not args.quick:
         pack = bench_pack(device)
         pack["pack_frac_of_measured_hbm"] = round(pack["pack_gbs"] / pk["hbm_gbs"], 3)
