@@ -63,11 +63,11 @@ SIGNATURES = {
     "sffn_gemm_bf16": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp,
                               _vp, _int, _vp, _vp]),
     "sffn_ffn_up": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
-                           _vp, _vp, _vp]),
+                           _vp, _vp, _vp, _vp]),
+    "sffn_tile_copy_slots": (_int, [_vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sffn_tile_scan_counts": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sffn_tile_gather_slots": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _int, _vp, _vp, _vp, _vp]),
     "sffn_tile_row_offsets": (_int, [_vp, _vp, _i64, _vp, _vp, _vp]),
-    "sffn_tile_gather_dense": (_int, [_vp, _i64, _i64, _i64, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp]),
     "sffn_ck_lists": (_int, [_vp, _i64, _i64, _vp, _i64, _vp, _vp, _vp]),
     "sffn_ck_gather_packed": (_int, [_vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp,
                                      _i64, _vp, _vp]),
@@ -116,7 +116,7 @@ LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_a
              "sffn_ffn_dgrad": 1, "sffn_codec15_compress": 1, "sffn_codec15_uncompress": 1,
              "sffn_wait_probe": 1, "sffn_ck_lists": 1, "sffn_ck_gather_packed": 1,
              "sffn_ck_compact_rows": 1, "sffn_gemm_ck": 1, "sffn_live_kblocks_t": 1, "sffn_gemm_bf16_ct": 1,
-             "sffn_split_bf16x3": 1, "sffn_gemm_bf16_f32out": 1, "sffn_tile_gather_dense": 1}
+             "sffn_split_bf16x3": 1, "sffn_gemm_bf16_f32out": 1, "sffn_tile_copy_slots": 1}
 launch_count = 0
 
 # Per-entry-point CUDA event pairs, recorded while a KernelTimer is active.

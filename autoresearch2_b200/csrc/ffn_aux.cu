@@ -123,118 +123,117 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
     if (!slots) return;
     const long long base = (long long)*vals_offset;
     // Warp-cooperative, coalesced copy of the warp's 32 row segments (lane k
-    // moves value k of a row), eight rows at a time with all loads issued
-    // before any store, so a warp waits for one memory round trip per batch.
+    // moves value k of a row), all 32 rows' loads issued before any store,
+    // so a warp waits for one memory round trip per 32 values of its rows.
     int maxc = cnt;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) maxc = max(maxc, __shfl_xor_sync(FULL, maxc, o));
     const uint16_t* wsrc = slots + t * 16384 + warp * 32 * 128;
     for (int k0 = 0; k0 < maxc; k0 += 32) {
         const int k = k0 + lane;
+        uint16_t v[32];
 #pragma unroll
-        for (int i0 = 0; i0 < 32; i0 += 8) {
-            uint16_t v[8];
+        for (int u = 0; u < 32; ++u) {
+            const int c = __shfl_sync(FULL, cnt, u);
+            v[u] = k < c ? __ldcs(wsrc + u * 128 + k) : (uint16_t)0;
+        }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int c = __shfl_sync(FULL, cnt, i0 + u);
-                v[u] = k < c ? __ldcs(wsrc + (i0 + u) * 128 + k) : (uint16_t)0;
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                const int c = __shfl_sync(FULL, cnt, i0 + u);
-                const long long p = base + __shfl_sync(FULL, roff, i0 + u) + k;
-                if (k < c) {
-                    if (p >= 0 && p < cap) vals[p] = v[u];
-                    else atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
-                }
+        for (int u = 0; u < 32; ++u) {
+            const int c = __shfl_sync(FULL, cnt, u);
+            const long long p = base + __shfl_sync(FULL, roff, u) + k;
+            if (k < c) {
+                if (p >= 0 && p < cap) vals[p] = v[u];
+                else atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
             }
         }
     }
 }
 
-// Like tile_rows_kernel's slot copy, but the values come from the dense
-// matrix itself (the up-projection's ReLU output, which is z): per warp, for
-// each of its 32 rows, lane k reads the row's columns 4k .. 4k+3 of the tile
-// (one 8-byte load, eight rows' loads in flight), ranks its set ones by a
-// warp scan and writes them to the row's place in the arena.  Also writes
-// row_offsets and colmask like tile_rows_kernel.  The tile grid is gm x gn;
-// rows past M and columns past N hold no set bits and are not read.
-__global__ void __launch_bounds__(128) tile_rows_dense_kernel(const uint8_t* __restrict__ mask,
-                                                              const int* __restrict__ prefix,
-                                                              int* __restrict__ row_offsets,
-                                                              const uint16_t* __restrict__ src, long long ld,
-                                                              long long M, long long N, long long gn,
-                                                              const int* __restrict__ vals_offset,
-                                                              uint16_t* __restrict__ vals, long long cap,
-                                                              uint32_t* __restrict__ status,
-                                                              uint4* __restrict__ colmask) {
-    __shared__ int s_warp[4];
+// Copy of n 16-bit values from src (16-byte aligned) to dst, where dst + H is
+// 16-byte aligned (H = 0..7): H head values one by one, then 16-byte stores
+// whose eight values straddle two aligned source vectors (shifted by H
+// values), then the tail.  Source reads stay below the aligned end of
+// src[0 .. n+7), inside the tile's 16384-value slot.
+template <int H>
+__device__ __forceinline__ void copy_run(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int n,
+                                         int r) {
+    const int body = n > H ? (n - H) >> 3 : 0;
+    const int tail0 = n > H ? H + body * 8 : n;
+    if (r < H && r < n) dst[r] = src[r];
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+    uint4* d4 = reinterpret_cast<uint4*>(dst + H);
+#pragma unroll 4
+    for (int k = r; k < body; k += 128) {
+        if constexpr (H == 0) {
+            d4[k] = __ldcs(s4 + k);
+        } else {
+            const uint4 a = __ldg(s4 + k), b = __ldg(s4 + k + 1);
+            const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+            uint32_t o[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if constexpr (H % 2 == 0) o[j] = w[j + H / 2];
+                else o[j] = __funnelshift_r(w[j + H / 2], w[j + H / 2 + 1], 16);
+            }
+            d4[k] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    }
+    for (int i = tail0 + r; i < n; i += 128) dst[i] = src[i];
+}
+
+// One CTA (128 threads) per 128x128 tile, after the up-projection wrote the
+// tile's values packed in arena order at slots[t*16384] and the in-tile row
+// offsets: the values move to the arena as one contiguous run, the row
+// offsets gain prefix[t], and (optionally) colmask receives the tile's live
+// columns.
+__global__ void __launch_bounds__(128) tile_copy_kernel(const uint16_t* __restrict__ slots,
+                                                        const int* __restrict__ prefix,
+                                                        const int* __restrict__ vals_offset,
+                                                        uint16_t* __restrict__ vals, long long cap,
+                                                        int* __restrict__ row_offsets,
+                                                        const uint8_t* __restrict__ mask,
+                                                        uint4* __restrict__ colmask,
+                                                        uint32_t* __restrict__ status) {
     __shared__ uint4 s_or[4];
     const long long t = blockIdx.x;
     const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
-    const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
-    const int cnt = __popc(mw.x) + __popc(mw.y) + __popc(mw.z) + __popc(mw.w);
-    const int inc = warp_incl_scan(cnt, lane);
-    if (lane == 31) s_warp[warp] = inc;
+    const int p0 = prefix[t], n = prefix[t + 1] - p0;
+    if (row_offsets) row_offsets[t * 128 + r] += p0;
     if (colmask) {
+        const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
         const uint4 o = make_uint4(__reduce_or_sync(FULL, mw.x), __reduce_or_sync(FULL, mw.y),
                                    __reduce_or_sync(FULL, mw.z), __reduce_or_sync(FULL, mw.w));
         if (lane == 0) s_or[warp] = o;
+        __syncthreads();
+        if (r == 0)
+            colmask[t] = make_uint4(s_or[0].x | s_or[1].x | s_or[2].x | s_or[3].x,
+                                    s_or[0].y | s_or[1].y | s_or[2].y | s_or[3].y,
+                                    s_or[0].z | s_or[1].z | s_or[2].z | s_or[3].z,
+                                    s_or[0].w | s_or[1].w | s_or[2].w | s_or[3].w);
     }
-    __syncthreads();
-    if (colmask && r == 0) {
-        uint4 o = s_or[0];
-#pragma unroll
-        for (int w = 1; w < 4; ++w) {
-            o.x |= s_or[w].x;
-            o.y |= s_or[w].y;
-            o.z |= s_or[w].z;
-            o.w |= s_or[w].w;
+    if (n <= 0) return;
+    const long long base = (long long)*vals_offset + p0;
+    const uint16_t* src = slots + t * 16384;
+    if (base < 0 || base + n > cap || n > 16384) {
+        // past the arena: the values that fit, and the overflow flag
+        for (int i = r; i < n && i < 16384; i += 128) {
+            const long long p = base + i;
+            if (p >= 0 && p < cap) vals[p] = src[i];
         }
-        colmask[t] = o;
+        if (r == 0) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+        return;
     }
-    int before = 0;
-    for (int w = 0; w < warp; ++w) before += s_warp[w];
-    const int roff = prefix[t] + before + inc - cnt;
-    if (row_offsets) row_offsets[t * 128 + r] = roff;
-    const long long base = (long long)*vals_offset;
-    const long long tm = t / gn, tn = t % gn;
-    const long long col = tn * 128 + 4 * lane;  // this lane's four columns
-    const bool col_ok = col < N;                 // N % 4 == 0: whole groups
-    const int word = lane >> 3, sh = 4 * (lane & 7);
-    bool overflow = false;
-#pragma unroll 1
-    for (int i0 = 0; i0 < 32; i0 += 8) {
-        uint2 v[8];
-        uint32_t nib[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {  // loads first
-            const int i = i0 + u;
-            const uint32_t mx = __shfl_sync(FULL, mw.x, i), my = __shfl_sync(FULL, mw.y, i);
-            const uint32_t mz = __shfl_sync(FULL, mw.z, i), mq = __shfl_sync(FULL, mw.w, i);
-            const uint32_t w = word == 0 ? mx : word == 1 ? my : word == 2 ? mz : mq;
-            nib[u] = (w >> sh) & 15u;
-            const long long row = tm * 128 + warp * 32 + i;
-            v[u] = make_uint2(0, 0);
-            if (nib[u] && col_ok && row < M) v[u] = __ldcs(reinterpret_cast<const uint2*>(src + row * ld + col));
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const int i = i0 + u;
-            const int c = __popc(nib[u]);
-            const int pos = warp_incl_scan(c, lane) - c;
-            long long p = base + __shfl_sync(FULL, roff, i) + pos;
-            const uint32_t h[4] = {v[u].x & 0xFFFFu, v[u].x >> 16, v[u].y & 0xFFFFu, v[u].y >> 16};
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-                if ((nib[u] >> j) & 1u) {
-                    if (p >= 0 && p < cap) vals[p] = (uint16_t)h[j];
-                    else overflow = true;
-                    ++p;
-                }
-        }
+    uint16_t* dst = vals + base;
+    switch ((int)((16u - (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 1) {
+        case 0: copy_run<0>(src, dst, n, r); break;
+        case 1: copy_run<1>(src, dst, n, r); break;
+        case 2: copy_run<2>(src, dst, n, r); break;
+        case 3: copy_run<3>(src, dst, n, r); break;
+        case 4: copy_run<4>(src, dst, n, r); break;
+        case 5: copy_run<5>(src, dst, n, r); break;
+        case 6: copy_run<6>(src, dst, n, r); break;
+        default: copy_run<7>(src, dst, n, r); break;
     }
-    if (overflow) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
 }
 
 // Grid (pair tile, group of 8 k-blocks); warp w of a CTA tests k-block
@@ -649,6 +648,23 @@ extern "C" int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask,
     return SFFN_OK;
 }
 
+extern "C" int sffn_tile_copy_slots(const void* slots, const int32_t* prefix, const int32_t* vals_offset_dev,
+                                    int64_t ntiles, void* vals, int64_t vals_capacity, int32_t* row_offsets,
+                                    const uint8_t* bitmask, uint32_t* colmask, uint32_t* status_dev, void* stream) {
+    if (ntiles <= 0 || ntiles > 0x7FFFFFFF || !slots || !prefix || !vals_offset_dev || !vals || !status_dev)
+        return SFFN_ERR_ARG;
+    if (colmask && !bitmask) return SFFN_ERR_ARG;
+    if (!aligned16(slots) || !aligned16(bitmask) || !aligned16(colmask) ||
+        (reinterpret_cast<uintptr_t>(vals) & 1u))
+        return SFFN_ERR_ALIGN;
+    SFFN_BIND(dev_scope, vals);
+    tile_copy_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint16_t*>(slots), prefix, vals_offset_dev, static_cast<uint16_t*>(vals), vals_capacity,
+        row_offsets, bitmask, reinterpret_cast<uint4*>(colmask), status_dev);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
 extern "C" int sffn_tile_row_offsets(const uint8_t* bitmask, const int32_t* prefix, int64_t ntiles,
                                      int32_t* row_offsets, uint32_t* colmask, void* stream) {
     if (ntiles <= 0 || !bitmask || !prefix || (!row_offsets && !colmask)) return SFFN_ERR_ARG;
@@ -765,21 +781,3 @@ extern "C" int sffn_split_bf16x3(const void* src, int dtype, int64_t rows, int64
     return SFFN_OK;
 }
 
-extern "C" int sffn_tile_gather_dense(const void* dense, int64_t ld, int64_t M, int64_t N, const uint8_t* bitmask,
-                                      const int32_t* prefix, const int32_t* vals_offset_dev, void* vals,
-                                      int64_t vals_capacity, int32_t* row_offsets, uint32_t* colmask,
-                                      uint32_t* status_dev, void* stream) {
-    if (M <= 0 || N <= 0 || N % 4 || ld < N || ld % 4 || !dense || !bitmask || !prefix || !vals_offset_dev || !vals ||
-        !status_dev)
-        return SFFN_ERR_ARG;
-    if (!aligned16(bitmask) || !aligned16(colmask) || (reinterpret_cast<uintptr_t>(dense) & 7u)) return SFFN_ERR_ALIGN;
-    const long long gm = (M + 127) / 128, gn = (N + 127) / 128;
-    if (gm * gn > 0x7FFFFFFFll) return SFFN_ERR_ARG;
-    DeviceScope dev_scope;
-    if (int rc = dev_scope.bind_same(vals, {dense, bitmask})) return rc;
-    tile_rows_dense_kernel<<<(unsigned)(gm * gn), 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        bitmask, prefix, row_offsets, static_cast<const uint16_t*>(dense), ld, M, N, gn, vals_offset_dev,
-        static_cast<uint16_t*>(vals), vals_capacity, status_dev, reinterpret_cast<uint4*>(colmask));
-    SFFN_CHECK_LAUNCH();
-    return SFFN_OK;
-}

@@ -64,7 +64,7 @@ namespace {
 constexpr int G_BM = 128;
 constexpr int G_BK = 64;
 constexpr int G_THREADS = 416;  // 4 control warps, 2 epilogue warpgroups (warps 4-11), 1 more producer
-constexpr int G_STAGES = 6;
+constexpr int G_STAGES = 6;  // even: two issuers per operand take alternate k-blocks
 constexpr int G_GROUP_M = 8;  // pair-tile rows per raster group (16 row tiles of 128)
 constexpr int G_CTAS = 2;     // CTA pairs (cta_group::2)
 constexpr int FT = 128;            // format tile (BLOCK_M = BLOCK_N = 128)
@@ -98,7 +98,8 @@ struct GemmArgs {
     const uint16_t* bias;  // UP: optional [N]
     uint8_t* mask;         // UP: written; DGRAD: read (tiled 128x128, grid_n = ceil(N/128))
     int* tile_counts;      // UP: [num_tiles][4] per-warp partial counts
-    uint16_t* slots;       // UP: [num_tiles][128 rows][128]: row r's z values at r*128
+    uint16_t* slots;       // UP: [num_tiles][16384]: z values per row at r*128, or tile-packed
+    int* slot_rows;        // UP: tile-packed slots; [num_tiles][128] row offsets in the tile
     uint16_t* out2;        // DGRAD: act2
     const uint16_t* vals;  // DGRAD
     long long vals_len;
@@ -264,6 +265,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     constexpr int TMEM_COLS = 2 * BN;
     constexpr uint32_t MN_LBO = G_BK * 128;  // MN-major: 64-element blocks are K rows x 128 B apart
     static_assert(BN_CTA % 64 == 0, "each CTA loads whole 64-row B blocks");
+    // the even / odd k-block issuers each own every other use of a stage only
+    // if the stage count is even (their final drain counts their own phases)
+    static_assert(G_STAGES % 2 == 0, "an even number of stages");
 
     extern __shared__ __align__(1024) unsigned char g_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -537,13 +541,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         sb[row] = gcol0 + row < args.N ? bf16_to_f(bias[gcol0 + row]) : 0.f;
                         named_bar_sync(bar_id, 128);
                     }
-                    // this row's z values go to its own 128-element segment of the slot
-                    uint16_t* slot_row = args.slots ? args.slots + tf * FT_ELEMS + row * FT : nullptr;
-                    uint32_t words[4];
-                    uint32_t mw[4] = {0, 0, 0, 0};  // 2:4 metadata words (sp_on)
-                    int cnt = 0;
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) {
+                    // Chunk c of this row from the accumulator: z (packed bf16
+                    // pairs), the activation words and the mask bits of z > 0.
+                    auto zchunk = [&](int c, uint32_t (&zw)[16], uint32_t (&w)[16]) -> uint32_t {
                         uint32_t r[32];
                         tmem_ld32(tbase + c * 32, r);
                         tmem_wait_ld();
@@ -551,7 +551,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         // columns past N (and rows past M) carry no bits
                         const int ncol = row_ok ? min(32, args.N - gcol) : 0;
                         const uint32_t colmask = ncol >= 32 ? 0xFFFFFFFFu : ((1u << max(ncol, 0)) - 1u);
-                        uint32_t zw[16], w[16], bits = 0;
+                        uint32_t bits = 0;
 #pragma unroll
                         for (int q = 0; q < 16; ++q) {
                             float v0 = nkb ? __uint_as_float(r[2 * q]) : 0.f;
@@ -574,18 +574,78 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             zw[q] = z;
                             w[q] = args.act == ACT_RELU2 ? bf162_bits(__hmul2(zb, zb)) : z;
                         }
-                        bits &= colmask;
-                        if (args.sp_on) {
-                            stage_words(sbuf, lane, w);  // own row: read back by this lane only
-                            mw[c] = sp24_emit(args.sp[0], w, grow, gcol, lane,
-                                              [&](int e) { return staged_elem(sbuf, lane, e); });
-                        } else if (args.out) {  // no dense activation when the caller passed none
-                            if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
-                            else if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                        return bits & colmask;
+                    };
+                    uint32_t words[4];
+                    int cnt = 0;
+                    if (args.slot_rows) {
+                        // Tile-packed slots: the format tile's values in arena order
+                        // from slots[tf * 16384].  Pass 1 counts the row (the bits
+                        // alone), a scan over the warpgroup's 128 rows gives its
+                        // offset in the tile; pass 2 reads the accumulator again and
+                        // stores z through the staging buffer, row by row with lane
+                        // = column, so each row's values leave as one contiguous run.
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            uint32_t zw[16], w[16];
+                            words[c] = zchunk(c, zw, w);
+                            cnt += __popc(words[c]);
                         }
-                        // this chunk's z values, in column order, to the row's slot segment
-                        // (no slots: the dense output holds z itself, ReLU)
-                        if (args.slots) {
+                        int total;
+                        int run = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
+                        args.slot_rows[tf * FT + row] = run;
+                        uint16_t* tslot = args.slots + tf * FT_ELEMS;
+                        const uint32_t lt = (1u << lane) - 1u;
+#pragma unroll 1
+                        for (int c = 0; c < 4; ++c) {
+                            const int gcol = gcol0 + c * 32;
+                            uint32_t zw[16], w[16];
+                            const uint32_t bits = zchunk(c, zw, w);
+                            if (lane == 0) bulk_wait_group_read0();  // the staging buffer is free
+                            __syncwarp();
+                            stage_words(sbuf, lane, zw);
+                            __syncwarp();
+#pragma unroll 8
+                            for (int i = 0; i < 32; ++i) {
+                                const uint32_t bi = __shfl_sync(FULL, bits, i);
+                                const int ri = __shfl_sync(FULL, run, i);
+                                if ((bi >> lane) & 1u)
+                                    tslot[ri + __popc(bi & lt)] = (uint16_t)staged_elem(sbuf, i, lane);
+                            }
+                            run += __popc(bits);
+                            __syncwarp();
+                            if (args.out) {
+                                if (!vec) {
+                                    if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                                } else if (args.act == ACT_RELU) {  // the staged z is the output
+                                    fence_proxy_async_smem();
+                                    __syncwarp();
+                                    if (lane == 0) {
+                                        tma_store_2d(&tmC, sbuf, gcol, row0);
+                                        bulk_commit_group();
+                                    }
+                                } else {
+                                    stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                                }
+                            }
+                        }
+                    } else {
+                        // Per-row slots: row r's values at slots[tf * 16384 + r * 128].
+                        uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;
+                        uint32_t mw[4] = {0, 0, 0, 0};  // 2:4 metadata words (sp_on)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int gcol = gcol0 + c * 32;
+                            uint32_t zw[16], w[16];
+                            const uint32_t bits = zchunk(c, zw, w);
+                            if (args.sp_on) {
+                                stage_words(sbuf, lane, w);  // own row: read back by this lane only
+                                mw[c] = sp24_emit(args.sp[0], w, grow, gcol, lane,
+                                                  [&](int e) { return staged_elem(sbuf, lane, e); });
+                            } else if (args.out) {  // no dense activation when the caller passed none
+                                if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                                else if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                            }
 #pragma unroll
                             for (int q = 0; q < 16; ++q) {
                                 const uint32_t b2 = (bits >> (2 * q)) & 3u;
@@ -594,16 +654,14 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                     if (b2 & 2u) slot_row[cnt++] = (uint16_t)(zw[q] >> 16);
                                 }
                             }
-                        } else {
-                            cnt += __popc(bits);
+                            words[c] = bits;
                         }
-                        words[c] = bits;
+                        if (args.sp_on)  // the 128 columns are one K block of the 2:4 form
+                            reinterpret_cast<uint4*>(args.sp[0].meta)[((long long)tm * args.sp[0].nkb + gcol0 / 128) * 128 +
+                                                                      ew * 32 + lane] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
                     }
                     *reinterpret_cast<uint4*>(args.mask + tf * FT_BYTES + row * 16) =
                         make_uint4(words[0], words[1], words[2], words[3]);
-                    if (args.sp_on)  // the 128 columns are one K block of the 2:4 form
-                        reinterpret_cast<uint4*>(args.sp[0].meta)[((long long)tm * args.sp[0].nkb + gcol0 / 128) * 128 +
-                                                                  ew * 32 + lane] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
                     // per-warp partial count of the tile (summed by the scan kernel)
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(FULL, cnt, o);
@@ -1672,16 +1730,14 @@ extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const
 
 extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
                            int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
-                           uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
-                           void* stream) {
+                           uint8_t* bitmask, int32_t* tile_counts, void* slots, int32_t* slot_rows,
+                           uint32_t* status_dev, void* stream) {
     DeviceScope dev_scope;
     int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
     if ((act_out && ld_act < F) || !bitmask || !tile_counts || !status_dev) return SFFN_ERR_ARG;
-    // without slots the dense output must be z itself (ReLU), from which
-    // sffn_tile_gather_dense fills the arena
-    if (!slots && !(act_out && act == ACT_RELU)) return SFFN_ERR_ARG;
+    if (!slots) return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
     if (T * F > 0x7FFFFFFFll) return SFFN_ERR_ARG;
     GemmArgs a = base_args(T, F, D, act_out, act_out ? ld_act : F);
@@ -1691,6 +1747,7 @@ extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t l
     a.mask = bitmask;
     a.tile_counts = tile_counts;
     a.slots = static_cast<uint16_t*>(slots);
+    a.slot_rows = slot_rows;
     a.status = status_dev;
     return dispatch<EPI_UP>(false, false, x, ldx, w1, ldw1, a, reinterpret_cast<cudaStream_t>(stream));
 }

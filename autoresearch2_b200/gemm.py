@@ -150,10 +150,11 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     nt = gm * gn
     bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
     counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
-    # ReLU with a dense output: that output is z, and the arena is filled from
-    # it -- no per-row slots (a [T, F] transient) and no slot stores
-    from_dense = act == ACT_RELU and write_act and not sp24 and F % 4 == 0
-    slots = None if from_dense else torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
+    # The epilogue writes each tile's z values packed in arena order into the
+    # tile's slot (and the in-tile row offsets into row_offsets); one
+    # contiguous copy per tile then fills the arena.  The 2:4 form keeps
+    # per-row slots (row r of tile t at t*16384 + r*128).
+    slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
     prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
     vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
     row_offsets = torch.empty(nt * 128, dtype=torch.int32, device=dev)
@@ -168,12 +169,12 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     else:
         act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev) if write_act else None
         call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
-             ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), status, st)
+             ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), ptr(row_offsets), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
-    if from_dense:
-        call("sffn_tile_gather_dense", ptr(act_out), F, T, F, ptr(bitmask), ptr(prefix), ptr(vals_offset),
-             ptr(vals), vals.numel(), ptr(row_offsets), ptr(colmask), status, st)
+    if not sp24:
+        call("sffn_tile_copy_slots", ptr(slots), ptr(prefix), ptr(vals_offset), nt, ptr(vals), vals.numel(),
+             ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
     else:
         call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
              ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)

@@ -247,19 +247,22 @@ int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, i
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
  * (unless act_out is NULL: the compacted-K down-projection needs none), the
  * tiled 128x128 bitmask of z > 0 (ceil(T/128)*ceil(F/128) tiles of 2048 B),
- * four partial counts per tile (tile_counts[t*4 .. t*4+3]) and, for tile t,
- * row r's z values in order at slots[t*16384 + r*128 ...] (slots may be NULL
- * for ReLU with act_out given: act_out is z, and sffn_tile_gather_dense reads
- * the values from it).  Follow with
- * sffn_tile_scan_counts (parts = 4) and sffn_tile_gather_slots to finish the
- * BitsparseTensor.
+ * four partial counts per tile (tile_counts[t*4 .. t*4+3]) and z's values:
+ *  - slot_rows NULL: row r of tile t in order at slots[t*16384 + r*128 ...];
+ *    finish the BitsparseTensor with sffn_tile_scan_counts (parts = 4) and
+ *    sffn_tile_gather_slots;
+ *  - slot_rows given (tile-packed): tile t's values in the order of the
+ *    arena (row-major within the tile) at slots[t*16384 ...], and
+ *    slot_rows[t*128 + r] = the values in rows < r of tile t; finish with
+ *    sffn_tile_scan_counts and sffn_tile_copy_slots (one contiguous copy per
+ *    tile), passing slot_rows there as row_offsets.
  *   replaces old/lib_sparse/sparse.py:72-77,116-120 (matmul, relu, square,
  *   dense_to_tilesparse) and old/matmul_bitsparse/train.py:11-116
  *   (_matmul_sparse_kernel + compaction). */
 int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
                 int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
-                uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
-                void* stream);
+                uint8_t* bitmask, int32_t* tile_counts, void* slots, int32_t* slot_rows,
+                uint32_t* status_dev, void* stream);
 
 /* prefix[t] = sum over tiles < t of (tile_counts[t*parts] + ... + [t*parts+parts-1]),
  * prefix[ntiles] = total; *vals_offset_dev = *offset_dev; *offset_dev += total.
@@ -281,14 +284,17 @@ int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int3
                            int64_t vals_capacity, int dtype, int32_t* row_offsets,
                            uint32_t* colmask, uint32_t* status_dev, void* stream);
 
-/* sffn_tile_gather_slots with the values taken from the dense [M, N] 16-bit
- * matrix itself (row stride ld; N and ld multiples of 4, dense 8-byte
- * aligned): for ReLU the up-projection's dense output is z, so it needs no
- * slots (sffn_ffn_up with slots NULL).  Same outputs as sffn_tile_gather_slots. */
-int sffn_tile_gather_dense(const void* dense, int64_t ld, int64_t M, int64_t N, const uint8_t* bitmask,
-                           const int32_t* prefix, const int32_t* vals_offset_dev, void* vals,
-                           int64_t vals_capacity, int32_t* row_offsets, uint32_t* colmask,
-                           uint32_t* status_dev, void* stream);
+/* For 128x128 tiles and the tile-packed slots of sffn_ffn_up: copies tile t's
+ * prefix[t+1] - prefix[t] values from slots[t*16384 ...] to
+ * vals[*vals_offset_dev + prefix[t] ...] (16-bit dtypes; never past
+ * vals_capacity) and adds prefix[t] to row_offsets[t*128 .. t*128+127] (the
+ * in-tile row offsets sffn_ffn_up wrote), which then hold what
+ * sffn_tile_gather_slots writes there.  colmask (optional) as in
+ * sffn_tile_gather_slots, read from bitmask (which may be NULL without it).
+ *   replaces old/lib_sparse/sparse_pack.py:65-92 (_compact_vals_kernel). */
+int sffn_tile_copy_slots(const void* slots, const int32_t* prefix, const int32_t* vals_offset_dev,
+                         int64_t ntiles, void* vals, int64_t vals_capacity, int32_t* row_offsets,
+                         const uint8_t* bitmask, uint32_t* colmask, uint32_t* status_dev, void* stream);
 
 /* row_offsets[t*128 + r] = prefix[t] + number of values in rows < r of tile t,
  * for a tiled 128x128 bitmask (the per-row index sffn_ffn_dgrad reads; the

@@ -182,6 +182,50 @@ def test_ffn_up_fused(act, T, D, F, bias):
     assert int(voff.item()) == 17
 
 
+@pytest.mark.parametrize("start", range(8))
+def test_ffn_up_tile_copy_at_every_alignment(start):
+    """The up-projection's tile-packed slots reach the arena by one copy per
+    tile; the arena's start offset (0..7 values) sets how the copy's 16-byte
+    stores straddle the slot's vectors.  Arena, row offsets and live columns
+    must equal the standalone packer's (integer/byte work: exact), and nothing
+    outside the written range may change."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    T, D, F = 640, 256, 896
+    x = rand(T, D, seed=20 + start)
+    W1 = rand(F, D, seed=30 + start, scale=D ** -0.5)
+    b1 = torch.full((F,), -0.3 * (start % 4), device=DEV, dtype=torch.bfloat16)
+    arena = torch.full((T * F + 64,), 9.0, device=DEV, dtype=torch.bfloat16)
+    offset = torch.tensor([start], dtype=torch.int32, device=DEV)
+    colmask = torch.empty(-(-T // 128) * -(-F // 128) * 4, dtype=torch.int32, device=DEV)
+    a, bitmask, prefix, voff, ro = gemm.ffn_up(x, W1, b1, 1, arena, offset, colmask=colmask)
+    zs = sf.BitsparseTensor(arena, bitmask, prefix, voff, -(-T // 128), -(-F // 128), 128, 128, (T, F))
+    z_dev = zs.to_dense()
+    arena2 = torch.full_like(arena, 9.0)
+    off2 = torch.tensor([start], dtype=torch.int32, device=DEV)
+    y = sf.dense_to_tilesparse(z_dev, arena2, off2, 128, 128)
+    assert torch.equal(arena2.view(torch.int16), arena.view(torch.int16))
+    assert torch.equal(ro, gemm.tile_row_offsets(y))
+    assert torch.equal(colmask, gemm.tile_colmask(y))
+    assert torch.equal(a, (z_dev.float() * z_dev.float()).to(torch.bfloat16))
+    sf.check_status()
+
+
+def test_ffn_up_arena_too_small_flags_and_stays_in_bounds():
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    T, D, F = 256, 128, 512
+    x = rand(T, D, seed=41)
+    W1 = rand(F, D, seed=42, scale=D ** -0.5)
+    big = torch.full((T * F,), 9.0, device=DEV, dtype=torch.bfloat16)
+    cap = 1000
+    arena = big[:cap]
+    offset = torch.tensor([3], dtype=torch.int32, device=DEV)
+    gemm.ffn_up(x, W1, None, 1, arena, offset)
+    assert sf.check_status(raise_on_error=False) & 1  # SFFN_STATUS_VALS_OVERFLOW
+    assert bool((big[cap:] == 9.0).all())
+
+
 @pytest.mark.parametrize("act", [0, 1])
 def test_ffn_dgrad_fused(act):
     import autoresearch2_b200 as sf
