@@ -70,8 +70,20 @@ constexpr int G_CTAS = 2;     // CTA pairs (cta_group::2)
 constexpr int FT = 128;            // format tile (BLOCK_M = BLOCK_N = 128)
 constexpr int FT_BYTES = FT * FT / 8;
 constexpr int FT_ELEMS = FT * FT;
-
 enum { EPI_STORE = 0, EPI_UP = 1, EPI_DGRAD = 2 };
+// The activation-gradient epilogue prefetches each tile's packed z values into
+// shared memory (one buffer per warpgroup: a whole 128x128 format tile's
+// values plus 16-byte alignment slack); its ring has four stages to make room
+// (the main loop runs as fast with four as with six).
+constexpr int G_ZBUF = FT_ELEMS * 2 + 64;
+template <int EPI>
+constexpr int gemm_stages() { return EPI == EPI_DGRAD ? 4 : G_STAGES; }
+template <int EPI>
+constexpr int gemm_smem_bytes(int BN) {
+    return gemm_stages<EPI>() * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 8 * 2048 +
+           (EPI == EPI_DGRAD ? 2 * G_ZBUF : 0) + 1024;
+}
+
 enum { ACT_RELU = 0, ACT_RELU2 = 1 };
 
 // One matrix written in the 2:4 form of sp24.cu by a fused epilogue.
@@ -267,19 +279,22 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     static_assert(BN_CTA % 64 == 0, "each CTA loads whole 64-row B blocks");
     // the even / odd k-block issuers each own every other use of a stage only
     // if the stage count is even (their final drain counts their own phases)
-    static_assert(G_STAGES % 2 == 0, "an even number of stages");
+    constexpr int NST = gemm_stages<EPI>();
+    static_assert(NST % 2 == 0, "an even number of stages");
 
     extern __shared__ __align__(1024) unsigned char g_smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    __shared__ __align__(8) uint64_t full_bar[G_STAGES];
-    __shared__ __align__(8) uint64_t empty_bar[G_STAGES];
+    __shared__ __align__(8) uint64_t full_bar[NST];
+    __shared__ __align__(8) uint64_t empty_bar[NST];
     __shared__ __align__(8) uint64_t tfull_bar[2];
     __shared__ __align__(8) uint64_t tempty_bar[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     __shared__ int s_scan[2][2][4];     // [warpgroup][tile parity][warp]
     __shared__ float s_bias[2][2][FT];  // [warpgroup][tile parity][column]
+    __shared__ __align__(8) uint64_t z_bar[2];  // DGRAD: the z buffer of each warpgroup has landed
+    __shared__ long long s_zb0[2];              // DGRAD: arena index of the buffer's first value, or -1
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // Pair tiles: 256 rows (two 128-row tiles, one per CTA) x BN columns.
@@ -292,13 +307,14 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     const int tile_stride = (int)cluster_count_x();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < G_STAGES; ++s) {
+        for (int s = 0; s < NST; ++s) {
             mbar_init(&full_bar[s], 1);   // leader: its own arrive.expect_tx for both CTAs' bytes
             mbar_init(&empty_bar[s], 1);  // one multicast commit per use
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull_bar[a], 1);
             mbar_init(&tempty_bar[a], 8 * G_CTAS);  // every epilogue warp of both CTAs
+            mbar_init(&z_bar[a], 1);
         }
         s_abort = 0;
         fence_mbar_init();
@@ -328,7 +344,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
         const bool loads_a = warp == 0 || warp == 2;
         const int par = (warp == 0 || warp == 3) ? 0 : 1;
         if (lane == 0) {
-            int armed[G_STAGES] = {0};
+            int armed[NST] = {0};
             long long kc = 0;  // k-blocks of this CTA so far (all tiles)
             for (int tile = first_tile; tile < ntiles && !s_abort; tile += tile_stride) {
                 int pm, tn;
@@ -339,8 +355,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                 bool stop = false;
                 for (int i = 0; i < nkb; ++i, ++kc) {
                     if ((int)(kc & 1) != par) continue;
-                    const int stage = (int)(kc % G_STAGES);
-                    const uint32_t phase = (uint32_t)((kc / G_STAGES) & 1);
+                    const int stage = (int)(kc % NST);
+                    const uint32_t phase = (uint32_t)((kc / NST) & 1);
                     const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : args.kb0 + i;
                     // the stage is free once the leader's MMAs reading it are done
                     if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
@@ -379,7 +395,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
             // operands: once the last phases armed by this thread complete, no
             // copy of those stages is still landing in either CTA.
             if (leader && loads_a)
-                for (int s = 0; s < G_STAGES; ++s)
+                for (int s = 0; s < NST; ++s)
                     if (armed[s]) (void)mbar_wait_bounded(&full_bar[s], (uint32_t)(armed[s] - 1) & 1u);
         }
         __syncwarp();
@@ -423,7 +439,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         tc_mma_f16_pair(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
                     }
                     tc_commit_pair_multicast(&empty_bar[stage], 0x3);
-                    if (++stage == G_STAGES) {
+                    if (++stage == NST) {
                         stage = 0;
                         phase ^= 1u;
                     }
@@ -455,12 +471,54 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
         int acc = 0;
         uint32_t acc_phase = 0;
         int it = 0;
+        uint32_t z_phase = 0;
         for (int tile = first_tile; tile < ntiles; tile += tile_stride, ++it) {
             int pm, tn;
             raster(tile, tiles_mp, args.tiles_n, pm, tn);
             const int tm = pm * G_CTAS + (int)rank;  // this CTA's 128-row tile
             const bool tile_ok = tm < args.tiles_m;   // false for the empty half of an odd last pair
             const int nkb = args.kb_count ? args.kb_count[pm] : nkb_full;
+            // DGRAD: the format tile's packed z values are one contiguous run of
+            // the arena; one bulk copy brings it (16-byte aligned superset) into
+            // this warpgroup's buffer while the tile's MMAs still run.  A run
+            // whose aligned superset would leave the arena is read from global
+            // memory instead (zb0 = -1).
+            long long zb0 = -1;
+            if constexpr (EPI == EPI_DGRAD) {
+                if (tile_ok && tn * BN + wg * HALF < args.N) {  // uniform over the warpgroup
+                    named_bar_sync(bar_id, 128);  // the previous tile's reads of the buffer are done
+                    if (ew == 0 && lane == 0) {
+                        long long b0 = -1;
+                        const long long tfz = (long long)tm * gn_f + (tn * BN + wg * HALF) / FT;
+                        const uint4 m127 = __ldg(reinterpret_cast<const uint4*>(args.mask + tfz * FT_BYTES + 127 * 16));
+                        const long long base = (long long)*args.vals_offset;
+                        const long long start = base + __ldg(args.row_offsets + tfz * FT);
+                        const long long end = base + __ldg(args.row_offsets + tfz * FT + 127) + __popc(m127.x) +
+                                              __popc(m127.y) + __popc(m127.z) + __popc(m127.w);
+                        if (start >= 0 && end > start && end <= args.vals_len && end - start <= FT_ELEMS) {
+                            const uintptr_t vp = reinterpret_cast<uintptr_t>(args.vals);
+                            const uintptr_t lo = (vp + 2 * (uintptr_t)start) & ~(uintptr_t)15;
+                            const uintptr_t hi = (vp + 2 * (uintptr_t)end + 15) & ~(uintptr_t)15;
+                            if (lo >= vp && hi <= vp + 2 * (uintptr_t)args.vals_len) {
+                                b0 = (long long)((lo - vp) >> 1);
+                                unsigned char* zbuf = smem + (size_t)NST * STAGE_BYTES + 8 * 2048 + (size_t)wg * G_ZBUF;
+                                mbar_arrive_expect_tx(&z_bar[wg], (uint32_t)(hi - lo));
+                                bulk_g2s(zbuf, reinterpret_cast<const void*>(lo), (uint32_t)(hi - lo), &z_bar[wg]);
+                            }
+                        }
+                        s_zb0[wg] = b0;
+                    }
+                    named_bar_sync(bar_id, 128);
+                    zb0 = s_zb0[wg];
+                    if (zb0 >= 0) {
+                        if (!__all_sync(FULL, mbar_wait_bounded(&z_bar[wg], z_phase))) {
+                            if (lane == 0) atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);
+                            break;
+                        }
+                        z_phase ^= 1u;
+                    }
+                }
+            }
             // every lane must take the same branch before the warp-collective tcgen05.ld
             const bool ok = __all_sync(FULL, mbar_wait_bounded(&tfull_bar[acc], acc_phase));
             if (!ok || __any_sync(FULL, s_abort != 0)) {
@@ -476,7 +534,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
             const bool vec = args.vec_out != 0;
             const int par = it & 1;
             const int row0 = tm * G_BM + ew * 32;  // first row of this warp
-            unsigned char* sbuf = smem + (size_t)G_STAGES * STAGE_BYTES + (size_t)(warp - 4) * 2048;
+            unsigned char* sbuf = smem + (size_t)NST * STAGE_BYTES + (size_t)(warp - 4) * 2048;
 
             if constexpr (EPI == EPI_STORE) {
 #pragma unroll 1
@@ -502,9 +560,12 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                     reinterpret_cast<float4*>(frow)[q] = v;
                                 }
                             } else {
-                                for (int j = 0; j < 32 && gcol + j < args.N; ++j) {
-                                    const float v = nkb ? __uint_as_float(r[j]) : 0.f;
-                                    frow[j] = args.acc_f32 ? frow[j] + v : v;
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) {
+                                    if (gcol + j < args.N) {
+                                        const float v = nkb ? __uint_as_float(r[j]) : 0.f;
+                                        frow[j] = args.acc_f32 ? frow[j] + v : v;
+                                    }
                                 }
                             }
                         }
@@ -668,6 +729,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     if (lane == 0) args.tile_counts[tf * 4 + ew] = cnt;
                 }
             } else {  // EPI_DGRAD
+                const uint32_t zsm = smem_u32(smem + (size_t)NST * STAGE_BYTES + 8 * 2048 + (size_t)wg * G_ZBUF);
                 if (gcol0 < args.N && tile_ok) {  // uniform over the warpgroup
                     uint16_t* orow2 = args.out2 + (size_t)grow * args.ldc;
                     const long long tf = (long long)tm * gn_f + gcol0 / FT;
@@ -680,20 +742,37 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     // chunk c (columns gcol0 + 32c ..): dpre and the activation, from
                     // the accumulator and z gathered from the packed values
                     auto chunk = [&](int c, uint32_t bits, uint32_t (&wd)[16], uint32_t (&wa)[16]) {
-                        // gather this chunk's z first: read-only loads, free to run ahead
+                        // gather this chunk's z first (from the tile's buffer, or
+                        // global memory): read-only loads, free to run ahead
+                        // (one branch per chunk, so each path's loads issue together)
                         uint32_t zb[16];
+                        if (zb0 >= 0) {
+                            const long long k0 = vbase - zb0;  // this row's first value in the buffer
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            uint32_t lo = 0, hi = 0;
-                            if ((bits >> (2 * q)) & 1u) {
-                                const long long p = vbase + __popc(bits & ((1u << (2 * q)) - 1u));
-                                if (p < args.vals_len) lo = __ldg(vals + p);
+                            for (int q = 0; q < 16; ++q) {
+                                uint16_t lo = 0, hi = 0;
+                                const long long k1 = k0 + __popc(bits & ((1u << (2 * q)) - 1u));
+                                const long long k2 = k0 + __popc(bits & ((2u << (2 * q)) - 1u));
+                                if (((bits >> (2 * q)) & 1u) && k1 >= 0 && k1 < G_ZBUF / 2)
+                                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(lo) : "r"(zsm + 2u * (uint32_t)k1));
+                                if (((bits >> (2 * q + 1)) & 1u) && k2 >= 0 && k2 < G_ZBUF / 2)
+                                    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(hi) : "r"(zsm + 2u * (uint32_t)k2));
+                                zb[q] = (uint32_t)lo | ((uint32_t)hi << 16);
                             }
-                            if ((bits >> (2 * q + 1)) & 1u) {
-                                const long long p = vbase + __popc(bits & ((2u << (2 * q)) - 1u));
-                                if (p < args.vals_len) hi = __ldg(vals + p);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                uint32_t lo = 0, hi = 0;
+                                if ((bits >> (2 * q)) & 1u) {
+                                    const long long p = vbase + __popc(bits & ((1u << (2 * q)) - 1u));
+                                    if (p < args.vals_len) lo = __ldg(vals + p);
+                                }
+                                if ((bits >> (2 * q + 1)) & 1u) {
+                                    const long long p = vbase + __popc(bits & ((2u << (2 * q)) - 1u));
+                                    if (p < args.vals_len) hi = __ldg(vals + p);
+                                }
+                                zb[q] = lo | (hi << 16);
                             }
-                            zb[q] = lo | (hi << 16);
                         }
                         vbase += __popc(bits);
                         uint32_t r[32];
@@ -1519,8 +1598,8 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
             !make_tmap(&tc2, args.out2, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return SFFN_ERR_CUDA;
     }
-    // stages + 8 epilogue warps x 2 KB staging + alignment slack
-    constexpr int smem = G_STAGES * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 8 * 2048 + 1024;
+    // stages + 8 epilogue warps x 2 KB staging (+ the z buffers) + alignment slack
+    constexpr int smem = gemm_smem_bytes<EPI>(BN);
     auto k = gemm_kernel<BN, A_MN, B_MN, EPI>;
     SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int npairs = ((args.tiles_m + 1) / 2) * args.tiles_n;
