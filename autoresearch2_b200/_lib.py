@@ -64,7 +64,7 @@ SIGNATURES = {
                               _vp, _int, _vp, _vp]),
     "sffn_ffn_up": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
                            _vp, _vp, _vp, _vp]),
-    "sffn_tile_copy_slots": (_int, [_vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
+    "sffn_tile_copy_slots": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sffn_tile_scan_counts": (_int, [_vp, _int, _i64, _vp, _vp, _vp, _vp, _vp]),
     "sffn_tile_gather_slots": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _int, _vp, _vp, _vp, _vp]),
     "sffn_tile_row_offsets": (_int, [_vp, _vp, _i64, _vp, _vp, _vp]),

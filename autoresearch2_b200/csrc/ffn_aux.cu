@@ -149,12 +149,12 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
     }
 }
 
-// Copy of n 16-bit values from src (16-byte aligned) to dst, where dst + H is
-// 16-byte aligned (H = 0..7): H head values one by one, then 16-byte stores
-// whose eight values straddle two aligned source vectors (shifted by H
-// values), then the tail.  Source reads stay below the aligned end of
-// src[0 .. n+7), inside the tile's 16384-value slot.
-template <int H>
+// Copy of n 16-bit values from src (16-byte aligned) to dst by the NT threads
+// r = 0 .. NT-1, where dst + H is 16-byte aligned (H = 0..7): H head values one
+// by one, then 16-byte stores whose eight values straddle two aligned source
+// vectors (shifted by H values), then the tail.  Source reads stay below the
+// aligned end of src[0 .. n+7).
+template <int H, int NT>
 __device__ __forceinline__ void copy_run(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int n,
                                          int r) {
     const int body = n > H ? (n - H) >> 3 : 0;
@@ -163,7 +163,7 @@ __device__ __forceinline__ void copy_run(const uint16_t* __restrict__ src, uint1
     const uint4* s4 = reinterpret_cast<const uint4*>(src);
     uint4* d4 = reinterpret_cast<uint4*>(dst + H);
 #pragma unroll 4
-    for (int k = r; k < body; k += 128) {
+    for (int k = r; k < body; k += NT) {
         if constexpr (H == 0) {
             d4[k] = __ldcs(s4 + k);
         } else {
@@ -178,15 +178,18 @@ __device__ __forceinline__ void copy_run(const uint16_t* __restrict__ src, uint1
             d4[k] = make_uint4(o[0], o[1], o[2], o[3]);
         }
     }
-    for (int i = tail0 + r; i < n; i += 128) dst[i] = src[i];
+    for (int i = tail0 + r; i < n; i += NT) dst[i] = src[i];
 }
 
-// One CTA (128 threads) per 128x128 tile, after the up-projection wrote the
-// tile's values packed in arena order at slots[t*16384] and the in-tile row
-// offsets: the values move to the arena as one contiguous run, the row
-// offsets gain prefix[t], and (optionally) colmask receives the tile's live
-// columns.
+// One CTA (128 threads) per 128x128 tile, after the up-projection wrote each
+// warp's 32 rows of the tile packed in arena order at slots[t*16384 + w*4096]
+// (warp w, count counts[t*4 + w]) and each row's offset in its warp's run:
+// warp w moves its segment to the arena as one contiguous run, the row
+// offsets gain prefix[t] and the counts of the warps before, and
+// (optionally) colmask receives the tile's live columns.
+constexpr int SEG = 4096;  // values of one warp's segment of a tile slot
 __global__ void __launch_bounds__(128) tile_copy_kernel(const uint16_t* __restrict__ slots,
+                                                        const int* __restrict__ counts,
                                                         const int* __restrict__ prefix,
                                                         const int* __restrict__ vals_offset,
                                                         uint16_t* __restrict__ vals, long long cap,
@@ -197,8 +200,11 @@ __global__ void __launch_bounds__(128) tile_copy_kernel(const uint16_t* __restri
     __shared__ uint4 s_or[4];
     const long long t = blockIdx.x;
     const int r = threadIdx.x, lane = r & 31, warp = r >> 5;
-    const int p0 = prefix[t], n = prefix[t + 1] - p0;
-    if (row_offsets) row_offsets[t * 128 + r] += p0;
+    const int4 cw = *reinterpret_cast<const int4*>(counts + t * 4);
+    const int before = (warp > 0 ? cw.x : 0) + (warp > 1 ? cw.y : 0) + (warp > 2 ? cw.z : 0);
+    const int n = warp == 0 ? cw.x : warp == 1 ? cw.y : warp == 2 ? cw.z : cw.w;
+    const long long p0 = (long long)prefix[t] + before;
+    if (row_offsets) row_offsets[t * 128 + r] += (int)p0;
     if (colmask) {
         const uint4 mw = __ldg(reinterpret_cast<const uint4*>(mask + t * 2048 + r * 16));
         const uint4 o = make_uint4(__reduce_or_sync(FULL, mw.x), __reduce_or_sync(FULL, mw.y),
@@ -213,26 +219,26 @@ __global__ void __launch_bounds__(128) tile_copy_kernel(const uint16_t* __restri
     }
     if (n <= 0) return;
     const long long base = (long long)*vals_offset + p0;
-    const uint16_t* src = slots + t * 16384;
-    if (base < 0 || base + n > cap || n > 16384) {
+    const uint16_t* src = slots + t * 16384 + warp * SEG;
+    if (base < 0 || base + n > cap || n > SEG) {
         // past the arena: the values that fit, and the overflow flag
-        for (int i = r; i < n && i < 16384; i += 128) {
+        for (int i = lane; i < n && i < SEG; i += 32) {
             const long long p = base + i;
             if (p >= 0 && p < cap) vals[p] = src[i];
         }
-        if (r == 0) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
+        if (lane == 0) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
         return;
     }
     uint16_t* dst = vals + base;
     switch ((int)((16u - (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 1) {
-        case 0: copy_run<0>(src, dst, n, r); break;
-        case 1: copy_run<1>(src, dst, n, r); break;
-        case 2: copy_run<2>(src, dst, n, r); break;
-        case 3: copy_run<3>(src, dst, n, r); break;
-        case 4: copy_run<4>(src, dst, n, r); break;
-        case 5: copy_run<5>(src, dst, n, r); break;
-        case 6: copy_run<6>(src, dst, n, r); break;
-        default: copy_run<7>(src, dst, n, r); break;
+        case 0: copy_run<0, 32>(src, dst, n, lane); break;
+        case 1: copy_run<1, 32>(src, dst, n, lane); break;
+        case 2: copy_run<2, 32>(src, dst, n, lane); break;
+        case 3: copy_run<3, 32>(src, dst, n, lane); break;
+        case 4: copy_run<4, 32>(src, dst, n, lane); break;
+        case 5: copy_run<5, 32>(src, dst, n, lane); break;
+        case 6: copy_run<6, 32>(src, dst, n, lane); break;
+        default: copy_run<7, 32>(src, dst, n, lane); break;
     }
 }
 
@@ -648,19 +654,21 @@ extern "C" int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask,
     return SFFN_OK;
 }
 
-extern "C" int sffn_tile_copy_slots(const void* slots, const int32_t* prefix, const int32_t* vals_offset_dev,
-                                    int64_t ntiles, void* vals, int64_t vals_capacity, int32_t* row_offsets,
-                                    const uint8_t* bitmask, uint32_t* colmask, uint32_t* status_dev, void* stream) {
-    if (ntiles <= 0 || ntiles > 0x7FFFFFFF || !slots || !prefix || !vals_offset_dev || !vals || !status_dev)
+extern "C" int sffn_tile_copy_slots(const void* slots, const int32_t* tile_counts, const int32_t* prefix,
+                                    const int32_t* vals_offset_dev, int64_t ntiles, void* vals,
+                                    int64_t vals_capacity, int32_t* row_offsets, const uint8_t* bitmask,
+                                    uint32_t* colmask, uint32_t* status_dev, void* stream) {
+    if (ntiles <= 0 || ntiles > 0x7FFFFFFF || !slots || !tile_counts || !prefix || !vals_offset_dev || !vals ||
+        !status_dev)
         return SFFN_ERR_ARG;
     if (colmask && !bitmask) return SFFN_ERR_ARG;
-    if (!aligned16(slots) || !aligned16(bitmask) || !aligned16(colmask) ||
+    if (!aligned16(slots) || !aligned16(tile_counts) || !aligned16(bitmask) || !aligned16(colmask) ||
         (reinterpret_cast<uintptr_t>(vals) & 1u))
         return SFFN_ERR_ALIGN;
     SFFN_BIND(dev_scope, vals);
     tile_copy_kernel<<<(unsigned)ntiles, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        static_cast<const uint16_t*>(slots), prefix, vals_offset_dev, static_cast<uint16_t*>(vals), vals_capacity,
-        row_offsets, bitmask, reinterpret_cast<uint4*>(colmask), status_dev);
+        static_cast<const uint16_t*>(slots), tile_counts, prefix, vals_offset_dev, static_cast<uint16_t*>(vals),
+        vals_capacity, row_offsets, bitmask, reinterpret_cast<uint4*>(colmask), status_dev);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

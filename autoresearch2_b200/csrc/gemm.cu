@@ -71,17 +71,19 @@ constexpr int FT = 128;            // format tile (BLOCK_M = BLOCK_N = 128)
 constexpr int FT_BYTES = FT * FT / 8;
 constexpr int FT_ELEMS = FT * FT;
 enum { EPI_STORE = 0, EPI_UP = 1, EPI_DGRAD = 2 };
-// The activation-gradient epilogue prefetches each tile's packed z values into
-// shared memory (one buffer per warpgroup: a whole 128x128 format tile's
-// values plus 16-byte alignment slack); its ring has four stages to make room
-// (the main loop runs as fast with four as with six).
+// The fused epilogues keep more in shared memory: the activation gradient
+// prefetches each tile's packed z values (one buffer per warpgroup: a whole
+// 128x128 format tile's values plus 16-byte alignment slack), the
+// up-projection gathers each row's z values (256 bytes per row, 8 KB per
+// warp).  Their rings have four stages to make room (the main loop runs as
+// fast with four as with six).
 constexpr int G_ZBUF = FT_ELEMS * 2 + 64;
 template <int EPI>
-constexpr int gemm_stages() { return EPI == EPI_DGRAD ? 4 : G_STAGES; }
+constexpr int gemm_stages() { return EPI == EPI_STORE ? G_STAGES : 4; }
 template <int EPI>
 constexpr int gemm_smem_bytes(int BN) {
     return gemm_stages<EPI>() * (G_BM * G_BK * 2 + (BN / G_CTAS) * G_BK * 2) + 8 * 2048 +
-           (EPI == EPI_DGRAD ? 2 * G_ZBUF : 0) + 1024;
+           (EPI == EPI_DGRAD ? 2 * G_ZBUF : EPI == EPI_UP ? 8 * 32 * 256 : 0) + 1024;
 }
 
 enum { ACT_RELU = 0, ACT_RELU2 = 1 };
@@ -144,9 +146,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 }
 __device__ __forceinline__ float bf16_to_f(uint16_t b) { return __uint_as_float(((uint32_t)b) << 16); }
 __device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) { return *reinterpret_cast<uint32_t*>(&v); }
-__device__ __forceinline__ uint16_t f_to_bf16(float f) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
-}
 
 // Store 32 bf16 values (16 packed words) to row[gcol .. gcol+32), bounds-checked.
 __device__ __forceinline__ void store_row32(uint16_t* row, int gcol, int N, bool vec, const uint32_t (&w)[16]) {
@@ -248,22 +247,6 @@ __device__ __forceinline__ uint32_t sp24_emit(const Sp24Out& o, const uint32_t (
     return sp24_lane_word(nib, lane);
 }
 
-// 128-thread exclusive scan of one count per epilogue thread (ew = warp 0..3).
-__device__ __forceinline__ int epi_scan128(int cnt, int ew, int lane, int* s_part, int* total, int bar_id) {
-    const int inc = warp_incl_scan(cnt, lane);
-    if (lane == 31) s_part[ew] = inc;
-    named_bar_sync(bar_id, 128);
-    int before = 0, all = 0;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) {
-        const int v = s_part[w];
-        if (w < ew) before += v;
-        all += v;
-    }
-    *total = all;
-    return before + inc - cnt;
-}
-
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -291,7 +274,6 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     __shared__ __align__(8) uint64_t tempty_bar[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
-    __shared__ int s_scan[2][2][4];     // [warpgroup][tile parity][warp]
     __shared__ float s_bias[2][2][FT];  // [warpgroup][tile parity][column]
     __shared__ __align__(8) uint64_t z_bar[2];  // DGRAD: the z buffer of each warpgroup has landed
     __shared__ long long s_zb0[2];              // DGRAD: arena index of the buffer's first value, or -1
@@ -640,56 +622,58 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     uint32_t words[4];
                     int cnt = 0;
                     if (args.slot_rows) {
-                        // Tile-packed slots: the format tile's values in arena order
-                        // from slots[tf * 16384].  Pass 1 counts the row (the bits
-                        // alone), a scan over the warpgroup's 128 rows gives its
-                        // offset in the tile; pass 2 reads the accumulator again and
-                        // stores z through the staging buffer, row by row with lane
-                        // = column, so each row's values leave as one contiguous run.
+                        // Warp-packed slots: the warp's 32 rows' values in arena order
+                        // from slots[tf * 16384 + ew * 4096].  In one pass over the
+                        // accumulator each lane appends its row's values to the row's
+                        // 256-byte area in shared memory (rotated by 2 * lane values
+                        // so that lanes writing the same position hit different
+                        // banks); a warp scan of the row counts gives each row's
+                        // offset in the warp's run, and each row then leaves as one
+                        // coalesced run (lane = value).
+                        const uint32_t zrows = smem_u32(smem + (size_t)NST * STAGE_BYTES + 8 * 2048 +
+                                                        (size_t)(warp - 4) * (32 * 256));
+                        const uint32_t ra = zrows + (uint32_t)lane * 256u;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            uint32_t zw[16], w[16];
-                            words[c] = zchunk(c, zw, w);
-                            cnt += __popc(words[c]);
-                        }
-                        int total;
-                        int run = epi_scan128(cnt, ew, lane, s_scan[wg][par], &total, bar_id);
-                        args.slot_rows[tf * FT + row] = run;
-                        uint16_t* tslot = args.slots + tf * FT_ELEMS;
-                        const uint32_t lt = (1u << lane) - 1u;
-#pragma unroll 1
                         for (int c = 0; c < 4; ++c) {
                             const int gcol = gcol0 + c * 32;
                             uint32_t zw[16], w[16];
                             const uint32_t bits = zchunk(c, zw, w);
-                            if (lane == 0) bulk_wait_group_read0();  // the staging buffer is free
-                            __syncwarp();
-                            stage_words(sbuf, lane, zw);
-                            __syncwarp();
-#pragma unroll 8
-                            for (int i = 0; i < 32; ++i) {
-                                const uint32_t bi = __shfl_sync(FULL, bits, i);
-                                const int ri = __shfl_sync(FULL, run, i);
-                                if ((bi >> lane) & 1u)
-                                    tslot[ri + __popc(bi & lt)] = (uint16_t)staged_elem(sbuf, i, lane);
-                            }
-                            run += __popc(bits);
-                            __syncwarp();
                             if (args.out) {
-                                if (!vec) {
-                                    if (row_ok) store_row32(orow, gcol, args.N, false, w);
-                                } else if (args.act == ACT_RELU) {  // the staged z is the output
-                                    fence_proxy_async_smem();
-                                    __syncwarp();
-                                    if (lane == 0) {
-                                        tma_store_2d(&tmC, sbuf, gcol, row0);
-                                        bulk_commit_group();
-                                    }
-                                } else {
-                                    stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                                if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
+                                else if (row_ok) store_row32(orow, gcol, args.N, false, w);
+                            }
+#pragma unroll
+                            for (int q = 0; q < 16; ++q) {
+                                if ((bits >> (2 * q)) & 1u) {
+                                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(ra + 2u * (uint32_t)((cnt + 2 * lane) & 127)),
+                                                 "h"((uint16_t)zw[q]) : "memory");
+                                    ++cnt;
+                                }
+                                if ((bits >> (2 * q + 1)) & 1u) {
+                                    asm volatile("st.shared.u16 [%0], %1;" ::"r"(ra + 2u * (uint32_t)((cnt + 2 * lane) & 127)),
+                                                 "h"((uint16_t)(zw[q] >> 16)) : "memory");
+                                    ++cnt;
                                 }
                             }
+                            words[c] = bits;
                         }
+                        const int incl = warp_incl_scan(cnt, lane);
+                        args.slot_rows[tf * FT + row] = incl - cnt;  // offset in the warp's run
+                        uint16_t* wslot = args.slots + tf * FT_ELEMS + ew * (FT_ELEMS / 4);
+                        __syncwarp();
+#pragma unroll 1
+                        for (int i = 0; i < 32; ++i) {
+                            const int ci = __shfl_sync(FULL, cnt, i);
+                            const int ri = __shfl_sync(FULL, incl, i) - ci;
+                            for (int j = lane; j < ci; j += 32) {
+                                uint16_t v;
+                                asm volatile("ld.shared.u16 %0, [%1];"
+                                             : "=h"(v)
+                                             : "r"(zrows + (uint32_t)i * 256u + 2u * (uint32_t)((j + 2 * i) & 127)));
+                                wslot[ri + j] = v;
+                            }
+                        }
+                        __syncwarp();  // the row areas are read before the next tile writes them
                     } else {
                         // Per-row slots: row r's values at slots[tf * 16384 + r * 128].
                         uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;

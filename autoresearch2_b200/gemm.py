@@ -150,9 +150,9 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     nt = gm * gn
     bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
     counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
-    # The epilogue writes each tile's z values packed in arena order into the
-    # tile's slot (and the in-tile row offsets into row_offsets); one
-    # contiguous copy per tile then fills the arena.  The 2:4 form keeps
+    # The epilogue writes each group of 32 rows' z values packed in arena order
+    # into its quarter of the tile's slot (and the rows' offsets in that run
+    # into row_offsets); one contiguous copy per group then fills the arena.  The 2:4 form keeps
     # per-row slots (row r of tile t at t*16384 + r*128).
     slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
     prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
@@ -173,8 +173,8 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
     if not sp24:
-        call("sffn_tile_copy_slots", ptr(slots), ptr(prefix), ptr(vals_offset), nt, ptr(vals), vals.numel(),
-             ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
+        call("sffn_tile_copy_slots", ptr(slots), ptr(counts), ptr(prefix), ptr(vals_offset), nt, ptr(vals),
+             vals.numel(), ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
     else:
         call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
              ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)

@@ -251,11 +251,12 @@ int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, i
  *  - slot_rows NULL: row r of tile t in order at slots[t*16384 + r*128 ...];
  *    finish the BitsparseTensor with sffn_tile_scan_counts (parts = 4) and
  *    sffn_tile_gather_slots;
- *  - slot_rows given (tile-packed): tile t's values in the order of the
- *    arena (row-major within the tile) at slots[t*16384 ...], and
- *    slot_rows[t*128 + r] = the values in rows < r of tile t; finish with
- *    sffn_tile_scan_counts and sffn_tile_copy_slots (one contiguous copy per
- *    tile), passing slot_rows there as row_offsets.
+ *  - slot_rows given (warp-packed): rows 32w .. 32w+31 of tile t in the order
+ *    of the arena (row-major) at slots[t*16384 + w*4096 ...] (their count is
+ *    tile_counts[t*4 + w]), and slot_rows[t*128 + r] = the values in the rows
+ *    of r's group of 32 before r; finish with sffn_tile_scan_counts and
+ *    sffn_tile_copy_slots (one contiguous copy per group), passing slot_rows
+ *    there as row_offsets.
  *   replaces old/lib_sparse/sparse.py:72-77,116-120 (matmul, relu, square,
  *   dense_to_tilesparse) and old/matmul_bitsparse/train.py:11-116
  *   (_matmul_sparse_kernel + compaction). */
@@ -284,17 +285,20 @@ int sffn_tile_gather_slots(const void* slots, const uint8_t* bitmask, const int3
                            int64_t vals_capacity, int dtype, int32_t* row_offsets,
                            uint32_t* colmask, uint32_t* status_dev, void* stream);
 
-/* For 128x128 tiles and the tile-packed slots of sffn_ffn_up: copies tile t's
- * prefix[t+1] - prefix[t] values from slots[t*16384 ...] to
- * vals[*vals_offset_dev + prefix[t] ...] (16-bit dtypes; never past
- * vals_capacity) and adds prefix[t] to row_offsets[t*128 .. t*128+127] (the
- * in-tile row offsets sffn_ffn_up wrote), which then hold what
- * sffn_tile_gather_slots writes there.  colmask (optional) as in
- * sffn_tile_gather_slots, read from bitmask (which may be NULL without it).
+/* For 128x128 tiles and the warp-packed slots of sffn_ffn_up: for each group
+ * w = 0..3 of 32 rows of tile t, copies tile_counts[t*4 + w] values from
+ * slots[t*16384 + w*4096 ...] to vals[*vals_offset_dev + prefix[t] + the
+ * counts of the groups before w ...] (16-bit dtypes; never past
+ * vals_capacity) and adds prefix[t] plus those counts to the group's
+ * row_offsets (the offsets in the group's run sffn_ffn_up wrote), which then
+ * hold what sffn_tile_gather_slots writes there.  tile_counts 16-byte
+ * aligned.  colmask (optional) as in sffn_tile_gather_slots, read from
+ * bitmask (which may be NULL without it).
  *   replaces old/lib_sparse/sparse_pack.py:65-92 (_compact_vals_kernel). */
-int sffn_tile_copy_slots(const void* slots, const int32_t* prefix, const int32_t* vals_offset_dev,
-                         int64_t ntiles, void* vals, int64_t vals_capacity, int32_t* row_offsets,
-                         const uint8_t* bitmask, uint32_t* colmask, uint32_t* status_dev, void* stream);
+int sffn_tile_copy_slots(const void* slots, const int32_t* tile_counts, const int32_t* prefix,
+                         const int32_t* vals_offset_dev, int64_t ntiles, void* vals, int64_t vals_capacity,
+                         int32_t* row_offsets, const uint8_t* bitmask, uint32_t* colmask,
+                         uint32_t* status_dev, void* stream);
 
 /* row_offsets[t*128 + r] = prefix[t] + number of values in rows < r of tile t,
  * for a tiled 128x128 bitmask (the per-row index sffn_ffn_dgrad reads; the
