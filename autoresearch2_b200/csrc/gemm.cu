@@ -845,11 +845,11 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                     const int col = gcol0 + c * 32 + lane;
                                     if (col < args.N) atomicAdd(args.colsum + col, acc);
                                 }
-                                stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
+                                if (args.out2) stage_store32(&tmC2, sbuf, lane, wa, gcol0 + c * 32, row0);
                             } else {
                                 if (row_ok) {
                                     store_row32(orow, gcol0 + c * 32, args.N, false, wd);
-                                    store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
+                                    if (args.out2) store_row32(orow2, gcol0 + c * 32, args.N, false, wa);
                                 }
                                 if (args.colsum) {
                                     // column sums by shuffles (rows past M contribute zeros)
@@ -1578,7 +1578,7 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     } else if (args.vec_out) {
         if (!make_tmap(&tc, args.out, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return SFFN_ERR_CUDA;
-        if (EPI == EPI_DGRAD &&
+        if (EPI == EPI_DGRAD && args.out2 &&
             !make_tmap(&tc2, args.out2, args.N, args.M, args.ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))
             return SFFN_ERR_CUDA;
     }
@@ -1825,11 +1825,10 @@ extern "C" int sffn_ffn_dgrad(const void* dout, int64_t ld_dout, const void* w2,
     int rc = check_operands(dev_scope, dout, ld_dout, false, w2, ldw2, true, T, F, D);
     if (rc) return rc;
     if (act != ACT_RELU && act != ACT_RELU2) return SFFN_ERR_ARG;
-    if (!vals || !bitmask || !row_offsets || !vals_offset_dev || !dpre_out || !act_out || ld_out < F ||
-        !status_dev)
+    if (!vals || !bitmask || !row_offsets || !vals_offset_dev || !dpre_out || ld_out < F || !status_dev)
         return SFFN_ERR_ARG;
     if (!aligned16(bitmask)) return SFFN_ERR_ALIGN;
-    if (!aligned16(dpre_out) != !aligned16(act_out)) return SFFN_ERR_ALIGN;
+    if (act_out && !aligned16(dpre_out) != !aligned16(act_out)) return SFFN_ERR_ALIGN;
     GemmArgs a = base_args(T, F, D, dpre_out, ld_out);
     a.act = act;
     a.out2 = static_cast<uint16_t*>(act_out);

@@ -266,9 +266,34 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_unpack_kernel(
     const long long t = tm * gn + tn;
     const long long row0 = tm * BM, col0 = tn * BN;
     const long long start = (long long)*vals_offset + prefix[t];
-    const int cnt = prefix[t + 1] - prefix[t];
-    for (int i = tid; i < cnt && i < C::TILE; i += C::NT)
-        s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+    const int cnt = min(prefix[t + 1] - prefix[t], C::TILE);
+    // The tile's values into shared memory: whole 16-byte vectors from the
+    // aligned address at or below the run's start (value i then sits at
+    // s_vals[sh + i]); per value where the run is not inside vals or vals is
+    // not 16-byte aligned.
+    constexpr int EPV = 16 / (int)sizeof(B);
+    int sh = 0;
+    if ((reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && cnt > 0 && start >= 0 && start + cnt <= vals_len) {
+        const long long a0 = start & ~(long long)(EPV - 1);
+        sh = (int)(start - a0);
+        const int nv = (sh + cnt + EPV - 1) / EPV;
+        const uint4* v4 = reinterpret_cast<const uint4*>(vals + a0);
+        uint4* s4 = reinterpret_cast<uint4*>(s_vals);
+#pragma unroll 4
+        for (int q = tid; q < nv; q += C::NT) {
+            if (a0 + (long long)(q + 1) * EPV <= vals_len) {
+                s4[q] = __ldg(v4 + q);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPV; ++e)
+                    s_vals[q * EPV + e] = a0 + q * EPV + e < vals_len ? vals[a0 + q * EPV + e] : B(0);
+            }
+        }
+    } else {
+#pragma unroll 4
+        for (int i = tid; i < cnt; i += C::NT)
+            s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+    }
 
     uint32_t bits[C::U];
     int lex[C::U];
@@ -289,18 +314,18 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_unpack_kernel(
     for (int it = 0; it < C::U; ++it) {
         const int f = 8 * (it * C::NT + tid);
         const long long gr = row0 + f / BN, gc = col0 + f % BN;
-        int r = s_wx[it * C::NW + warp] + lex[it];
+        int r = sh + s_wx[it * C::NW + warp] + lex[it];
         O o[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             B z = B(0);
             if ((bits[it] >> j) & 1u) {
-                z = r < C::TILE ? s_vals[r] : B(0);
+                z = r < C::TILE + 2 * EPV ? s_vals[r] : B(0);
                 ++r;
-            }
-            if (square) {
-                const float zf = Elt<DT>::to_f(z);
-                z = Elt<DT>::from_f(zf * zf);
+                if (square) {
+                    const float zf = Elt<DT>::to_f(z);
+                    z = Elt<DT>::from_f(zf * zf);
+                }
             }
             if constexpr (OUT_F32) o[j] = __float_as_uint(Elt<DT>::to_f(z));
             else o[j] = z;
@@ -349,9 +374,34 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_grad_relu2_kernel(
     const long long t = blockIdx.x;
     const long long row0 = (t / gn) * BM, col0 = (t % gn) * BN;
     const long long start = (long long)*vals_offset + prefix[t];
-    const int cnt = prefix[t + 1] - prefix[t];
-    for (int i = tid; i < cnt && i < C::TILE; i += C::NT)
-        s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+    const int cnt = min(prefix[t + 1] - prefix[t], C::TILE);
+    // The tile's values into shared memory: whole 16-byte vectors from the
+    // aligned address at or below the run's start (value i then sits at
+    // s_vals[sh + i]); per value where the run is not inside vals or vals is
+    // not 16-byte aligned.
+    constexpr int EPV = 16 / (int)sizeof(B);
+    int sh = 0;
+    if ((reinterpret_cast<uintptr_t>(vals) & 15u) == 0 && cnt > 0 && start >= 0 && start + cnt <= vals_len) {
+        const long long a0 = start & ~(long long)(EPV - 1);
+        sh = (int)(start - a0);
+        const int nv = (sh + cnt + EPV - 1) / EPV;
+        const uint4* v4 = reinterpret_cast<const uint4*>(vals + a0);
+        uint4* s4 = reinterpret_cast<uint4*>(s_vals);
+#pragma unroll 4
+        for (int q = tid; q < nv; q += C::NT) {
+            if (a0 + (long long)(q + 1) * EPV <= vals_len) {
+                s4[q] = __ldg(v4 + q);
+            } else {
+#pragma unroll
+                for (int e = 0; e < EPV; ++e)
+                    s_vals[q * EPV + e] = a0 + q * EPV + e < vals_len ? vals[a0 + q * EPV + e] : B(0);
+            }
+        }
+    } else {
+#pragma unroll 4
+        for (int i = tid; i < cnt; i += C::NT)
+            s_vals[i] = (start + i >= 0 && start + i < vals_len) ? vals[start + i] : B(0);
+    }
 
     uint32_t bits[C::U];
     int lex[C::U];
@@ -373,14 +423,14 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_grad_relu2_kernel(
         const int f = 8 * (it * C::NT + tid);
         const long long gr = row0 + f / BN, gc = col0 + f % BN;
         if (gr >= M) continue;
-        int r = s_wx[it * C::NW + warp] + lex[it];
+        int r = sh + s_wx[it * C::NW + warp] + lex[it];
         B g[8];
         load8_row(grad + gr * ld, gc, N, vec != 0, g);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             float z = 0.0f;
             if ((bits[it] >> j) & 1u) {
-                z = r < C::TILE ? Elt<DT>::to_f(s_vals[r]) : 0.0f;
+                z = r < C::TILE + 2 * EPV ? Elt<DT>::to_f(s_vals[r]) : 0.0f;
                 ++r;
             }
             // (g * 2.0) * z rounded to the storage dtype; g*2 is exact.
@@ -389,9 +439,9 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_grad_relu2_kernel(
         store8_row(grad + gr * ld, gc, N, vec != 0, g);
     }
     if (square) {
-        for (int i = tid; i < cnt && i < C::TILE; i += C::NT) {
+        for (int i = tid; i < cnt; i += C::NT) {
             if (start + i < 0 || start + i >= vals_len) continue;
-            const float z = Elt<DT>::to_f(s_vals[i]);
+            const float z = Elt<DT>::to_f(s_vals[sh + i]);
             vals[start + i] = Elt<DT>::from_f(z * z);
         }
     }
@@ -446,7 +496,7 @@ int launch_unpack(const void* vals, long long vals_len, const uint8_t* bitmask, 
     using B = typename Elt<DT>::bits;
     using O = typename std::conditional<OF, uint32_t, B>::type;
     const long long gn = (N + BN - 1) / BN;
-    const int smem = C::TILE * (int)sizeof(B);
+    const int smem = (C::TILE + 32 / (int)sizeof(B)) * (int)sizeof(B);  // + two vectors of alignment slack
     auto k = tile_unpack_kernel<DT, OF, BM, BN>;
     SFFN_CUDA_TRY(prep_smem(k, smem));
     k<<<(unsigned)(trows * gn), C::NT, smem, st>>>((const B*)vals, bitmask, vals_len, prefix, voff,
@@ -472,7 +522,7 @@ int launch_relu2(void* grad, long long M, long long N, long long ld, void* vals,
     using C = TileCfg<BM, BN>;
     using B = typename Elt<DT>::bits;
     const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
-    const int smem = C::TILE * (int)sizeof(B);
+    const int smem = (C::TILE + 32 / (int)sizeof(B)) * (int)sizeof(B);  // + two vectors of alignment slack
     auto k = tile_grad_relu2_kernel<DT, BM, BN>;
     SFFN_CUDA_TRY(prep_smem(k, smem));
     k<<<(unsigned)nt, C::NT, smem, st>>>((B*)grad, M, N, ld, (B*)vals, vals_len, bitmask, prefix,

@@ -113,6 +113,29 @@ def compact_k() -> str:
     return _COMPACT_K
 
 
+# The bf16 backward's activation a (z*z or z) for dW2: "fused" -- written by
+# the activation-gradient epilogue beside dpre (two dense [T, F] transients
+# live together); "lean" -- rebuilt from the packed z by an unpack first, dW2
+# computed and a freed before the activation gradient writes dpre (at most one
+# dense [T, F] transient at a time).
+_BACKWARD = "fused"
+
+
+def set_backward(mode: str):
+    """Choose how the fused bf16 backward gets the activation for dW2:
+    "fused" (beside dpre, in the activation-gradient epilogue) or "lean"
+    (unpacked from z first and freed before dpre is written: half the dense
+    transients)."""
+    global _BACKWARD
+    if mode not in ("fused", "lean"):
+        raise ValueError("backward mode is 'fused' or 'lean'")
+    _BACKWARD = mode
+
+
+def backward_mode() -> str:
+    return _BACKWARD
+
+
 def last_path():
     """The products' path of the last fused forward: "sp24", "ck" (compacted
     K), "dense" or None."""
@@ -256,9 +279,12 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
         grad_x = sp24.mm(dpre, W1)
         return grad_x, grad_W1, grad_W2, grad_b1
     use_ck = _ck_ok(T, D, Fd, W1 if stats_key is None else stats_key)
-    dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
-    del row_offsets
-    grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
+    lean = _BACKWARD == "lean"
+    if lean:
+        # a rebuilt from the packed z (squared in bf16 for ReLU^2, the forward's rounding)
+        a = z_sparse.to_dense(square=act == G.ACT_RELU2)
+    else:
+        dpre, a = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1)
     # the weight gradients contract over tokens: per 256 columns of the
     # activation, 64-token blocks that are zero there are skipped (dW2 as
     # (a^T @ dout)^T, so that the lists index its M tiles), when the layer's
@@ -270,6 +296,10 @@ def _fused_backward(grad_output, x, W1, W2, z_sparse, row_offsets, kb_list, kb_c
         tl = tc = None
         grad_W2 = submit_grad(G.mm(grad_output.T, a))
     del a
+    if lean:
+        dpre, _ = G.ffn_dgrad(grad_output, W2, act, z_sparse, row_offsets, db1=db1, want_act=False)
+    del row_offsets
+    grad_b1 = submit_grad(db1.to(dpre.dtype)) if has_bias else None
     # dW1 before dX: under data parallelism its all-reduce then overlaps dX, and
     # no weight-gradient reduction is left without compute to hide behind
     grad_W1 = submit_grad(G.mm(dpre.T, x, kb_list=tl, kb_count=tc))

@@ -265,9 +265,10 @@ def ck_mm(ac, B_rows, idx, kcount, out=None):
     return out
 
 
-def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None, sp24=False):
+def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None, sp24=False, want_act=True):
     """Fused dout @ W2 with the activation gradient; returns (dpre, act2)
-    where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F].  z_sparse is a
+    where act2 = z*z (ReLU^2) or z (ReLU), both dense [T, F] (act2 None with
+    want_act=False).  z_sparse is a
     128x128-tile BitsparseTensor; row_offsets its per-row offsets (computed
     here if not given).  db1: optional zeroed float32 [F] that receives the
     column sums of dpre (the bias gradient).  With sp24=True the outputs are
@@ -290,7 +291,7 @@ def ffn_dgrad(dout, W2, act, z_sparse, row_offsets=None, db1=None, sp24=False):
              ptr(_lib.status_word(dev)), stream_ptr(dev))
         return outs
     dpre = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
-    act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev)
+    act2 = torch.empty(T, F, dtype=torch.bfloat16, device=dev) if want_act else None
     call("sffn_ffn_dgrad", ptr(dout), dout.stride(0), ptr(W2), W2.stride(0), T, D, F, act,
          ptr(z_sparse.vals), z_sparse.vals.numel(), ptr(z_sparse.bitmask), ptr(row_offsets),
          ptr(z_sparse.vals_offset), ptr(dpre), ptr(act2), dpre.stride(0), ptr(db1),

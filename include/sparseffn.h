@@ -374,7 +374,8 @@ int sffn_gemm_ck(const void* A, int64_t lda, int64_t kmax, const void* B, int64_
  * ReLU^2 (act = 1): dpre = bf16((g*2) * z) and act_out = bf16(z*z); ReLU
  * (act = 0): dpre = bit ? g : 0 and act_out = z -- z gathered from the
  * tiled 128x128 BitsparseTensor (vals, bitmask, *vals_offset_dev) at the
- * row offsets of sffn_tile_row_offsets.
+ * row offsets of sffn_tile_row_offsets.  act_out may be NULL (no second
+ * output: a caller that rebuilt the activation already).
  * If db1_sum is not NULL, the column sums of dpre (the bias gradient, over
  * the T rows) are added into db1_sum[F] in fp32 (zero it first; the order of
  * the additions is not fixed).

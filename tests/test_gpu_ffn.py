@@ -128,3 +128,35 @@ def test_auto_mode_follows_observed_sparsity(shift, expect):
         assert (outs[-1] - outs[0]).abs().max().item() <= 2e-2 * scale
     finally:
         sf.ffn.set_sparse_mma(prev)
+
+
+@pytest.mark.parametrize("act", ["relu", "relu2"])
+@pytest.mark.parametrize("T,D,F", [(384, 256, 640), (1024, 512, 2048)])
+def test_lean_backward_gives_the_same_bits(act, T, D, F):
+    """The lean backward rebuilds the activation from the packed z by an
+    unpack (squared in bf16 for ReLU^2) instead of taking it from the
+    activation-gradient epilogue; the activation is the same bits either way,
+    so every gradient must be bit-identical between the two modes."""
+    import autoresearch2_b200 as sf
+    prev_mma, prev_bw = sf.sparse_mma(), sf.backward_mode()
+    sf.set_sparse_mma("off")
+    g = torch.Generator(device=DEV).manual_seed(T + F)
+    x = torch.randn(T, D, device=DEV, generator=g).to(torch.bfloat16)
+    W1 = (torch.randn(F, D, device=DEV, generator=g) * D ** -0.5).to(torch.bfloat16)
+    W2 = (torch.randn(D, F, device=DEV, generator=g) * F ** -0.5).to(torch.bfloat16)
+    b1 = torch.full((F,), -0.8, device=DEV, dtype=torch.bfloat16)
+    dout = torch.randn(T, D, device=DEV, generator=g).to(torch.bfloat16)
+    fn = sf.FFNSparse if act == "relu" else sf.FFNSpRelu2
+    res = {}
+    try:
+        for mode in ("fused", "lean"):
+            sf.set_backward(mode)
+            ps = [t.clone().requires_grad_() for t in (x, W1, W2, b1)]
+            out = fn.apply(ps[0], ps[1], ps[2], None, ps[3])
+            out.backward(dout)
+            res[mode] = [out.detach()] + [p.grad for p in ps]
+    finally:
+        sf.set_sparse_mma(prev_mma)
+        sf.set_backward(prev_bw)
+    for name, a, b in zip(("out", "dx", "dW1", "dW2", "db1"), res["fused"], res["lean"]):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16)), name
