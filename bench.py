@@ -650,8 +650,8 @@ def workload_config(tpg, world, tokens, s_meas=None):
 # -------------------------------------------------------------- roofline ----
 # DRAM traffic per launch of the roofline kernels at T=16384: dram__bytes_read.sum
 # + dram__bytes_write.sum of one ncu capture of each kernel at that size
-# (bench.py --micro up / dgrad: up 1440 + 555 MB, activation gradient 1393 + 906 MB).
-TRAFFIC_BYTES = {"sffn_ffn_up": 1440e6 + 555e6, "sffn_ffn_dgrad": 1393e6 + 906e6}
+# (bench.py --micro up / dgrad: up 1105 + 534 MB, activation gradient 1366 + 908 MB).
+TRAFFIC_BYTES = {"sffn_ffn_up": 1105e6 + 534e6, "sffn_ffn_dgrad": 1366e6 + 908e6}
 
 
 def kernel_breakdown(timer, steps_recorded, step_ms):
