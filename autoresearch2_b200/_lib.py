@@ -55,6 +55,8 @@ SIGNATURES = {
     "sffn_tile_workspace_bytes": (_sz, [_i64, _i64, _int, _int]),
     "sffn_tile_pack": (_int, [_vp, _int, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp,
                               _vp, _vp, _sz, _vp, _vp]),
+    "sffn_tile_pack_values": (_int, [_vp, _int, _i64, _i64, _i64, _int, _int, _vp, _vp, _vp, _i64, _vp, _vp,
+                                     _vp]),
     "sffn_tile_unpack": (_int, [_vp, _i64, _vp, _vp, _vp, _int, _i64, _i64, _int, _int, _i64,
                                 _i64, _int, _vp, _int, _i64, _vp]),
     "sffn_tile_mask_grad": (_int, [_vp, _int, _i64, _i64, _i64, _vp, _int, _int, _vp]),
@@ -109,7 +111,7 @@ def load():
 LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_add": 1,
              "sffn_ffn_up_sp24": 1, "sffn_ffn_dgrad_sp24": 1, "sffn_sp24_mm": 1, "sffn_transpose16": 1,
              "sffn_flat_pack": 2, "sffn_flat_pack_count": 2, "sffn_flat_pack_values": 1,
-             "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 1,
+             "sffn_flat_pack_noalloc": 1, "sffn_flat_unpack": 2, "sffn_tile_pack": 3, "sffn_tile_pack_values": 1,
              "sffn_tile_unpack": 1, "sffn_tile_mask_grad": 1, "sffn_tile_grad_relu2": 1,
              "sffn_gemm_bf16": 1, "sffn_ffn_up": 1, "sffn_tile_scan_counts": 1,
              "sffn_tile_gather_slots": 1, "sffn_tile_row_offsets": 1, "sffn_live_kblocks": 1,

@@ -149,38 +149,6 @@ __global__ void __launch_bounds__(128) tile_rows_kernel(const uint8_t* __restric
     }
 }
 
-// Copy of n 16-bit values from src (16-byte aligned) to dst by the NT threads
-// r = 0 .. NT-1, where dst + H is 16-byte aligned (H = 0..7): H head values one
-// by one, then 16-byte stores whose eight values straddle two aligned source
-// vectors (shifted by H values), then the tail.  Source reads stay below the
-// aligned end of src[0 .. n+7).
-template <int H, int NT>
-__device__ __forceinline__ void copy_run(const uint16_t* __restrict__ src, uint16_t* __restrict__ dst, int n,
-                                         int r) {
-    const int body = n > H ? (n - H) >> 3 : 0;
-    const int tail0 = n > H ? H + body * 8 : n;
-    if (r < H && r < n) dst[r] = src[r];
-    const uint4* s4 = reinterpret_cast<const uint4*>(src);
-    uint4* d4 = reinterpret_cast<uint4*>(dst + H);
-#pragma unroll 4
-    for (int k = r; k < body; k += NT) {
-        if constexpr (H == 0) {
-            d4[k] = __ldcs(s4 + k);
-        } else {
-            const uint4 a = __ldg(s4 + k), b = __ldg(s4 + k + 1);
-            const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                if constexpr (H % 2 == 0) o[j] = w[j + H / 2];
-                else o[j] = __funnelshift_r(w[j + H / 2], w[j + H / 2 + 1], 16);
-            }
-            d4[k] = make_uint4(o[0], o[1], o[2], o[3]);
-        }
-    }
-    for (int i = tail0 + r; i < n; i += NT) dst[i] = src[i];
-}
-
 // One CTA (128 threads) per 128x128 tile, after the up-projection wrote each
 // warp's 32 rows of the tile packed in arena order at slots[t*16384 + w*4096]
 // (warp w, count counts[t*4 + w]) and each row's offset in its warp's run:
@@ -229,17 +197,7 @@ __global__ void __launch_bounds__(128) tile_copy_kernel(const uint16_t* __restri
         if (lane == 0) atomicOr(status, SFFN_STATUS_VALS_OVERFLOW);
         return;
     }
-    uint16_t* dst = vals + base;
-    switch ((int)((16u - (uint32_t)(reinterpret_cast<uintptr_t>(dst) & 15u)) & 15u) >> 1) {
-        case 0: copy_run<0, 32>(src, dst, n, lane); break;
-        case 1: copy_run<1, 32>(src, dst, n, lane); break;
-        case 2: copy_run<2, 32>(src, dst, n, lane); break;
-        case 3: copy_run<3, 32>(src, dst, n, lane); break;
-        case 4: copy_run<4, 32>(src, dst, n, lane); break;
-        case 5: copy_run<5, 32>(src, dst, n, lane); break;
-        case 6: copy_run<6, 32>(src, dst, n, lane); break;
-        default: copy_run<7, 32>(src, dst, n, lane); break;
-    }
+    copy_run16<32>(src, vals + base, n, lane);
 }
 
 // Grid (pair tile, group of 8 k-blocks); warp w of a CTA tests k-block

@@ -848,6 +848,11 @@ __global__ void __launch_bounds__(FS_T) flat_pack_move_kernel(const B* __restric
         const int lim = (int)max(0ll, min((long long)s_cnt[k], cap - ex));
         const B* si = stage + (t0 + k) * FS_TILE;
         B* vo = vals + ex;
+        if constexpr (sizeof(B) == 2) {
+            // 16-byte stores realigned from the (16-byte aligned) staging segment
+            if (lim > 0) copy_run16<32>(si, vo, lim, lane);
+            continue;
+        }
         int i = lane;
         for (; i + 96 < lim; i += 128) {  // four loads in flight per lane
             const B a0 = __ldcs(si + i), a1 = __ldcs(si + i + 32), a2 = __ldcs(si + i + 64), a3 = __ldcs(si + i + 96);

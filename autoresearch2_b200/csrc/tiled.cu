@@ -469,6 +469,11 @@ inline long long num_tiles(long long M, long long N, int BM, int BN) {
 }
 
 template <typename B, int BM, int BN>
+int launch_pack_values(const void* dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
+                       uint8_t* bitmask, const int* prefix, void* vals, long long cap, const int* vals_offset,
+                       uint32_t* status, cudaStream_t st);
+
+template <typename B, int BM, int BN>
 int launch_pack(const void* dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
                 uint8_t* bitmask, int* prefix, void* vals, long long cap, int* cursor,
                 int* vals_offset_out, int* counts, uint32_t* status, cudaStream_t st) {
@@ -480,10 +485,22 @@ int launch_pack(const void* dense, long long M, long long N, long long ld, int v
                                        nullptr, 0, status, gn);
     SFFN_CHECK_LAUNCH();
     if (int rc = sffn_tile_scan_counts(counts, 1, nt, prefix, cursor, vals_offset_out, status, st)) return rc;
+    if (!vals) return SFFN_OK;  // counts, prefix and cursor only (sffn_tile_pack_values follows)
+    return launch_pack_values<B, BM, BN>(dense, M, N, ld, vec, inf16, bitmask, prefix, vals, cap, vals_offset_out,
+                                         status, st);
+}
+
+template <typename B, int BM, int BN>
+int launch_pack_values(const void* dense, long long M, long long N, long long ld, int vec, uint16_t inf16,
+                       uint8_t* bitmask, const int* prefix, void* vals, long long cap, const int* vals_offset,
+                       uint32_t* status, cudaStream_t st) {
+    using C = TileCfg<BM, BN>;
+    const long long gn = (N + BN - 1) / BN, nt = num_tiles(M, N, BM, BN);
+    const int smem = C::TILE * (int)sizeof(B);
     auto kv = tile_pack_kernel<B, BM, BN, true>;
     SFFN_CUDA_TRY(prep_smem(kv, smem));
     kv<<<(unsigned)nt, C::NT, smem, st>>>((const B*)dense, M, N, ld, vec, inf16, bitmask, nullptr, prefix,
-                                          vals_offset_out, (B*)vals, cap, status, gn);
+                                          vals_offset, (B*)vals, cap, status, gn);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }
@@ -556,6 +573,7 @@ extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N
     if (M * N > 0x7FFFFFFFll) return SFFN_ERR_ARG;  // int32 prefix, as in the reference
     if (!dense || !bitmask || !prefix || !offset_dev || !vals_offset_dev || !status_dev || !workspace)
         return SFFN_ERR_ARG;
+    if (!vals && vals_capacity != 0) return SFFN_ERR_ARG;  // NULL vals: counts and cursor only
     if (offset_dev == vals_offset_dev) return SFFN_ERR_ARG;
     if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
     if (workspace_bytes < sffn_tile_workspace_bytes(M, N, BM, BN)) return SFFN_ERR_WORKSPACE;
@@ -577,6 +595,35 @@ extern "C" int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N
     }
     SFFN_TILE_SHAPES(SFFN_PACK_CASE)
 #undef SFFN_PACK_CASE
+    return SFFN_ERR_UNSUPPORTED;
+}
+
+extern "C" int sffn_tile_pack_values(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld, int BM,
+                                     int BN, const uint8_t* bitmask, const int32_t* prefix, void* vals,
+                                     int64_t vals_capacity, const int32_t* vals_offset_dev, uint32_t* status_dev,
+                                     void* stream) {
+    if (!dtype_ok(dtype)) return SFFN_ERR_DTYPE;
+    if (!tile_shape_ok(BM, BN)) return SFFN_ERR_UNSUPPORTED;
+    if (M <= 0 || N <= 0 || ld < N || vals_capacity < 0) return SFFN_ERR_ARG;
+    if (M * N > 0x7FFFFFFFll) return SFFN_ERR_ARG;
+    if (!dense || !bitmask || !prefix || !vals || !vals_offset_dev || !status_dev) return SFFN_ERR_ARG;
+    if (reinterpret_cast<uintptr_t>(bitmask) & 3u) return SFFN_ERR_ALIGN;
+    SFFN_BIND(dev_scope, dense);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int esz = esize_of(dtype);
+    const int vec = vec_ok(dense, ld, esz) ? 1 : 0;
+    const uint16_t inf16 = inf16_of(dtype);
+    uint8_t* bm = const_cast<uint8_t*>(bitmask);
+#define SFFN_PACKV_CASE(a, b)                                                                            \
+    if (BM == a && BN == b) {                                                                           \
+        if (esz == 4)                                                                                   \
+            return launch_pack_values<uint32_t, a, b>(dense, M, N, ld, vec, inf16, bm, prefix, vals,    \
+                                                      vals_capacity, vals_offset_dev, status_dev, st); \
+        return launch_pack_values<uint16_t, a, b>(dense, M, N, ld, vec, inf16, bm, prefix, vals,        \
+                                                  vals_capacity, vals_offset_dev, status_dev, st);     \
+    }
+    SFFN_TILE_SHAPES(SFFN_PACKV_CASE)
+#undef SFFN_PACKV_CASE
     return SFFN_ERR_UNSUPPORTED;
 }
 

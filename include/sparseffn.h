@@ -160,13 +160,26 @@ size_t sffn_tile_workspace_bytes(int64_t M, int64_t N, int BM, int BN);
  * and its values written.  Reads the int32 arena cursor *offset_dev, writes
  * it to *vals_offset_dev, writes bitmask, prefix[num_tiles+1] and the values
  * to vals[cursor + prefix[t] ...] (never past vals_capacity), and advances
- * *offset_dev by the total -- all on the device, no host sync. */
+ * *offset_dev by the total -- all on the device, no host sync.  With vals
+ * NULL (and vals_capacity 0) only the first two launches run: bitmask,
+ * prefix and the cursor, so that a caller can size vals exactly from
+ * prefix[num_tiles] and then run sffn_tile_pack_values. */
 int sffn_tile_pack(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld,
                    int BM, int BN, uint8_t* bitmask, int32_t* prefix,
                    void* vals, int64_t vals_capacity,
                    int32_t* offset_dev, int32_t* vals_offset_dev,
                    void* workspace, size_t workspace_bytes,
                    uint32_t* status_dev, void* stream);
+
+/* The third launch of sffn_tile_pack alone: each tile of dense read again and
+ * its values written to vals[*vals_offset_dev + prefix[t] ...] (never past
+ * vals_capacity), after sffn_tile_pack with vals NULL made bitmask and
+ * prefix (no counterpart in the reference, which sizes vals with a host
+ * sync inside its pack, old/full_matmul/sparse_pack.py:128). */
+int sffn_tile_pack_values(const void* dense, int dtype, int64_t M, int64_t N, int64_t ld,
+                          int BM, int BN, const uint8_t* bitmask, const int32_t* prefix,
+                          void* vals, int64_t vals_capacity, const int32_t* vals_offset_dev,
+                          uint32_t* status_dev, void* stream);
 
 /* Unpack tile rows [tile_row0, tile_row0 + tile_rows) into out (row stride
  * ld_out; out row 0 = matrix row tile_row0*BM), optionally squaring each value

@@ -244,6 +244,8 @@ def test_tile128_variant_golden(name):
     g = golden(name)
     vals, meta = sf.tiled.dense_to_tilesparse(to_t(g["dense"]))
     bits_equal(to_np(vals), g["vals"])
+    # vals is its own allocation of exactly nnz values (no dense-size arena behind it)
+    assert vals.untyped_storage().nbytes() == vals.numel() * vals.element_size()
     bits_equal(to_np(meta["bitmask"]), g["bitmask"])
     bits_equal(to_np(meta["prefix"]), g["prefix"])
     out = sf.tiled.bitsparse_unpack(to_t(g["vals"]), meta, tuple(g["shape"]))
