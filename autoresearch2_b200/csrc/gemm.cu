@@ -339,7 +339,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                     if ((int)(kc & 1) != par) continue;
                     const int stage = (int)(kc % NST);
                     const uint32_t phase = (uint32_t)((kc / NST) & 1);
-                    const int kb = args.kb_list ? args.kb_list[(size_t)pm * args.kb_stride + i] : args.kb0 + i;
+                    // a full list (every block live) is not read: no dependent load per k-block
+                    const int kb = args.kb_list && nkb != nkb_full ? args.kb_list[(size_t)pm * args.kb_stride + i]
+                                                                   : args.kb0 + i;
                     // the stage is free once the leader's MMAs reading it are done
                     if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u)) {
                         atomicOr(args.status, SFFN_STATUS_WAIT_TIMEOUT);

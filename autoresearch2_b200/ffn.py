@@ -76,6 +76,9 @@ CK_AUTO_MAX_LIVE = 0.35
 # costs ~4% when nothing is skipped): taken when the layer's previous step
 # had at most this fraction of its (128-row tile, column) pairs live.
 TOKEN_SKIP_MAX_LIVE = 0.9
+# The forward builds no K-block lists when at least this fraction of the
+# layer's (128-row tile, column) pairs was live in its previous step.
+FULL_KBLOCKS_MIN_LIVE = 0.99
 # per layer (keyed by W1's storage and the shapes): pinned [activation count,
 # live (tile, column) count], its copy's event, the element count, the last
 # sparsity and live fraction read
@@ -228,7 +231,8 @@ def _fused_forward(x, W1, W2, vals, offset, b1, act):
     colmask = torch.empty(-(-T // 128) * -(-Fd // 128) * 4, dtype=torch.int32, device=x.device) \
         if want_live else None
     # with sp24 the up-projection epilogue writes a in the 2:4 form directly;
-    # with ck it writes no dense activation at all
+    # with ck it writes no dense activation at all.  (Running the arena fill
+    # on a second stream beside the down-projection measured no faster.)
     a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24,
                                                      write_act=not use_ck, colmask=colmask)
     if use_ck:
@@ -238,8 +242,16 @@ def _fused_forward(x, W1, W2, vals, offset, b1, act):
     else:
         kcount = None
     _observe(W1, prefix, kcount, T, D, Fd)
-    # the K-block lists also serve dX when the backward takes the dense path
-    kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
+    # the K-block lists also serve dX when the backward takes the dense path;
+    # when the layer's last observed step had nearly every (tile, column)
+    # pair live, a whole 64-column block of 256 rows is dead only by freak
+    # chance: the counts alone say "all live" (the GEMM then reads no list;
+    # a block it could have skipped is computed, which changes nothing)
+    _, live = _stats(T, D, Fd, W1)
+    if live is not None and live >= FULL_KBLOCKS_MIN_LIVE and not use_ck:
+        kb_list, kb_count = G.full_kblocks(T, Fd, x.device)
+    else:
+        kb_list, kb_count = G.live_kblocks(bitmask, T, Fd)
     if use_sp24:
         # 2:4 part on the sparse tensor cores, overflow rows k of W2^T
         out = sp24.mm(a, W2.T, bt=sp24.transpose(W2))

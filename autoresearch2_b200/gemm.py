@@ -123,6 +123,15 @@ def live_kblocks_t(bitmask: torch.Tensor, M: int, N: int):
     return kb_list, kb_count
 
 
+def full_kblocks(M, N, device):
+    """The (kb_list, kb_count) of live_kblocks for a matrix with every 64-wide
+    block of every 256-row tile live: kb_count[m] = ceil(N/64), the list left
+    unwritten (the GEMM reads no list whose count is full)."""
+    gm, nkb = -(-M // 256), -(-N // 64)
+    return (torch.empty(gm, nkb, dtype=torch.int32, device=device),
+            torch.full((gm,), nkb, dtype=torch.int32, device=device))
+
+
 def live_kblocks(bitmask: torch.Tensor, M: int, N: int):
     """(kb_list [ceil(M/256), ceil(N/64)] int32, kb_count [ceil(M/256)] int32):
     per 256-row tile, the 64-column blocks holding any set bit of a tiled

@@ -160,3 +160,33 @@ def test_lean_backward_gives_the_same_bits(act, T, D, F):
         sf.set_backward(prev_bw)
     for name, a, b in zip(("out", "dx", "dW1", "dW2", "db1"), res["fused"], res["lean"]):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16)), name
+
+
+def test_second_step_without_kblock_lists_gives_the_same_bits():
+    """After a step whose activation had (nearly) every (tile, column) pair
+    live, the next step builds no K-block lists (full counts only) and the
+    GEMMs read none; outputs and gradients must be the same bits as the first
+    step's, which ran with the lists."""
+    import autoresearch2_b200 as sf
+    prev = sf.sparse_mma()
+    sf.set_sparse_mma("off")
+    T, D, F = 1024, 256, 1024
+    g = torch.Generator(device=DEV).manual_seed(77)
+    x = torch.randn(T, D, device=DEV, generator=g).to(torch.bfloat16)
+    W1 = (torch.randn(F, D, device=DEV, generator=g) * D ** -0.5).to(torch.bfloat16).requires_grad_()
+    W2 = (torch.randn(D, F, device=DEV, generator=g) * F ** -0.5).to(torch.bfloat16).requires_grad_()
+    dout = torch.randn(T, D, device=DEV, generator=g).to(torch.bfloat16)
+    runs = []
+    try:
+        for _ in range(2):
+            W1.grad = W2.grad = None
+            out = sf.FFNSpRelu2.apply(x, W1, W2)
+            out.backward(dout)
+            torch.cuda.synchronize()
+            runs.append([out.detach().clone(), W1.grad.clone(), W2.grad.clone()])
+        _, live = sf.ffn._stats(T, D, F, W1)  # (setting the mode again forgets the statistics)
+    finally:
+        sf.set_sparse_mma(prev)
+    assert live is not None and live >= sf.ffn.FULL_KBLOCKS_MIN_LIVE
+    for a, b in zip(*runs):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
