@@ -190,3 +190,24 @@ def test_second_step_without_kblock_lists_gives_the_same_bits():
     assert live is not None and live >= sf.ffn.FULL_KBLOCKS_MIN_LIVE
     for a, b in zip(*runs):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+
+
+@pytest.mark.parametrize("act", ["relu", "relu2"])
+@pytest.mark.parametrize("backward", ["fused", "lean"])
+@pytest.mark.parametrize("T,D,F", [(300, 72, 200), (130, 264, 392), (1000, 136, 136)])
+def test_ffn_ragged_shapes_against_oracle(act, backward, T, D, F):
+    """Shapes whose tokens and hidden width are not multiples of the 128x128
+    format tile: the last tiles are partial (rows past T, columns past F), so
+    the up-projection's warp-packed slots, the per-group copy into the arena,
+    the activation gradient's prefetched z tile and the K-block lists all
+    meet their edge cases.  bf16 against the float64 oracle, both backward
+    modes."""
+    import autoresearch2_b200 as sf
+    prev_mma, prev_bw = sf.ffn.sparse_mma(), sf.backward_mode()
+    sf.ffn.set_sparse_mma("off")
+    sf.set_backward(backward)
+    try:
+        _ffn_against_oracle(sf, act, torch.bfloat16, T, D, F)
+    finally:
+        sf.ffn.set_sparse_mma(prev_mma)
+        sf.set_backward(prev_bw)
