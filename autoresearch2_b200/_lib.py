@@ -39,7 +39,7 @@ SIGNATURES = {
     "sffn_codec15_uncompress": (_int, [_vp, _i64, _i64, _vp, _vp]),
     "sffn_sp24_mm": (_int, [_vp, _i64, _i64, _vp, _i64, _int, _vp, _i64, _vp, _i64, _int, _i64, _vp, _vp]),
     "sffn_ffn_up_sp24": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _int, _vp, _vp, _vp, _vp,
-                                _vp, _vp]),
+                                _vp, _vp, _vp]),
     "sffn_ffn_dgrad_sp24": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp, _vp,
                                    _vp, _vp, _vp, _vp, _vp, _vp]),
     "sffn_version": (_int, []),

@@ -635,12 +635,17 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         const uint32_t zrows = smem_u32(smem + (size_t)NST * STAGE_BYTES + 8 * 2048 +
                                                         (size_t)(warp - 4) * (32 * 256));
                         const uint32_t ra = zrows + (uint32_t)lane * 256u;
+                        uint32_t mw[4] = {0, 0, 0, 0};  // 2:4 metadata words (sp_on)
 #pragma unroll
                         for (int c = 0; c < 4; ++c) {
                             const int gcol = gcol0 + c * 32;
                             uint32_t zw[16], w[16];
                             const uint32_t bits = zchunk(c, zw, w);
-                            if (args.out) {
+                            if (args.sp_on) {
+                                stage_words(sbuf, lane, w);  // own row: read back by this lane only
+                                mw[c] = sp24_emit(args.sp[0], w, grow, gcol, lane,
+                                                  [&](int e) { return staged_elem(sbuf, lane, e); });
+                            } else if (args.out) {
                                 if (vec) stage_store32(&tmC, sbuf, lane, w, gcol, row0);
                                 else if (row_ok) store_row32(orow, gcol, args.N, false, w);
                             }
@@ -676,6 +681,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             }
                         }
                         __syncwarp();  // the row areas are read before the next tile writes them
+                        if (args.sp_on)  // the 128 columns are one K block of the 2:4 form
+                            reinterpret_cast<uint4*>(args.sp[0].meta)[((long long)tm * args.sp[0].nkb + gcol0 / 128) * 128 +
+                                                                      ew * 32 + lane] = make_uint4(mw[0], mw[1], mw[2], mw[3]);
                     } else {
                         // Per-row slots: row r's values at slots[tf * 16384 + r * 128].
                         uint16_t* slot_row = args.slots + tf * FT_ELEMS + row * FT;
@@ -1866,8 +1874,8 @@ bool sp24_dims_ok(long long T, long long F) {
 
 extern "C" int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
                                 int64_t T, int64_t D, int64_t F, int act, const sffn_sp24_mat* out,
-                                uint8_t* bitmask, int32_t* tile_counts, void* slots, uint32_t* status_dev,
-                                void* stream) {
+                                uint8_t* bitmask, int32_t* tile_counts, void* slots, int32_t* slot_rows,
+                                uint32_t* status_dev, void* stream) {
     DeviceScope dev_scope;
     int rc = check_operands(dev_scope, x, ldx, false, w1, ldw1, false, T, F, D);
     if (rc) return rc;
@@ -1885,6 +1893,7 @@ extern "C" int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int6
     a.mask = bitmask;
     a.tile_counts = tile_counts;
     a.slots = static_cast<uint16_t*>(slots);
+    a.slot_rows = slot_rows;
     a.status = status_dev;
     return dispatch<EPI_UP>(false, false, x, ldx, w1, ldw1, a, st);
 }

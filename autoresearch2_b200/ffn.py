@@ -46,14 +46,14 @@ __all__ = ["FFNSparse", "FFNSpRelu2", "set_sparse_mma", "sparse_mma", "set_compa
 # its overflow on the CUDA cores.  "off": dense tcgen05 GEMMs; "on": sp24
 # whenever the shapes allow it (T and F multiples of 128, up to 65536, D a
 # multiple of 32); "auto" (default): sp24 when the same layer's previous step
-# had at least AUTO_MIN_SPARSITY zeros in its activation.  Measured on B200s at
-# T=16384, D=4096, F=14336 (ReLU^2, step ms, dense / sp24): 90% zeros 8.00 /
-# 8.63; 94% 8.69 / 8.42; 95% 7.73 / 7.69 on one box and 8.64 / 8.15 on a more
-# power-limited one; 96% 8.57 / 8.07; 99% 8.00 / 7.16 -- the overflow of the
+# had at least AUTO_MIN_SPARSITY zeros in its activation.  Measured on a B200
+# at T=16384, D=4096, F=14336 (ReLU^2, step ms, dense / sp24, medians of four
+# alternating samples in one process): 85% zeros 8.35 / 9.74; 88% 8.31 / 9.09;
+# 90% 8.18 / 8.34; 92% 8.44 / 8.10; and 95% 7.97 / 7.19 -- the overflow of the
 # 2:4 split shrinks with the density, the saving of the sparse products does
-# not, and the sparse products draw less power per step.
+# not.
 _SPARSE_MMA = "auto"
-AUTO_MIN_SPARSITY = 0.945
+AUTO_MIN_SPARSITY = 0.915
 # The down-projection and dX contract over F.  With the compacted-K path
 # ("ck") each 128-row tile of tokens contracts over its live columns only --
 # the columns of z holding a non-zero in any of the tile's rows -- with the

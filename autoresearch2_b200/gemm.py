@@ -161,8 +161,7 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
     # The epilogue writes each group of 32 rows' z values packed in arena order
     # into its quarter of the tile's slot (and the rows' offsets in that run
-    # into row_offsets); one contiguous copy per group then fills the arena.  The 2:4 form keeps
-    # per-row slots (row r of tile t at t*16384 + r*128).
+    # into row_offsets); one contiguous copy per group then fills the arena.
     slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
     prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
     vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
@@ -174,19 +173,15 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
         act_out = Sp24.empty(T, F, dev)
         d = act_out.desc()
         call("sffn_ffn_up_sp24", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
-             ctypes.addressof(d), ptr(bitmask), ptr(counts), ptr(slots), status, st)
+             ctypes.addressof(d), ptr(bitmask), ptr(counts), ptr(slots), ptr(row_offsets), status, st)
     else:
         act_out = torch.empty(T, F, dtype=torch.bfloat16, device=dev) if write_act else None
         call("sffn_ffn_up", ptr(x), x.stride(0), ptr(W1), W1.stride(0), ptr(b1), T, D, F, act,
              ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), ptr(row_offsets), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
-    if not sp24:
-        call("sffn_tile_copy_slots", ptr(slots), ptr(counts), ptr(prefix), ptr(vals_offset), nt, ptr(vals),
-             vals.numel(), ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
-    else:
-        call("sffn_tile_gather_slots", ptr(slots), ptr(bitmask), ptr(prefix), ptr(vals_offset), nt,
-             ptr(vals), vals.numel(), _lib.BF16, ptr(row_offsets), ptr(colmask), status, st)
+    call("sffn_tile_copy_slots", ptr(slots), ptr(counts), ptr(prefix), ptr(vals_offset), nt, ptr(vals),
+         vals.numel(), ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
     return act_out, bitmask, prefix, vals_offset, row_offsets
 
 

@@ -458,12 +458,14 @@ int sffn_sp24_mm(const sffn_sp24_mat* a, int64_t M, int64_t K, const void* B, in
                  uint32_t* status_dev, void* stream);
 
 /* sffn_ffn_up with the activation a written in the 2:4 form (out, K = F)
- * instead of dense; bitmask, tile counts and slots as there.  T and F
- * multiples of 128, F <= 65536.  The 2:4 form is bit-identical to
- * sffn_sp24_compress of the dense a (overflow order aside). */
+ * instead of dense; bitmask, tile counts, slots and slot_rows (NULL: per-row
+ * slots; given: warp-packed) as there.  T and F multiples of 128,
+ * F <= 65536.  The 2:4 form is bit-identical to sffn_sp24_compress of the
+ * dense a (overflow order aside). */
 int sffn_ffn_up_sp24(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1, int64_t T,
                      int64_t D, int64_t F, int act, const sffn_sp24_mat* out, uint8_t* bitmask,
-                     int32_t* tile_counts, void* slots, uint32_t* status_dev, void* stream);
+                     int32_t* tile_counts, void* slots, int32_t* slot_rows, uint32_t* status_dev,
+                     void* stream);
 
 /* sffn_ffn_dgrad with its outputs in the 2:4 form instead of dense:
  * dpre [T, F] (K = F, for dX = dpre @ W1), dpre^T [F, T] and act^T [F, T]
