@@ -288,3 +288,42 @@ def test_split_bf16_float16_product():
     assert got.dtype == torch.float16
     err = (got.double() - want).abs()
     assert bool((err <= 1e-3 * want.abs() + 1e-3 * want.abs().max()).all())
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_per_row_slots_route_matches_the_warp_packed_route(act):
+    """sffn_ffn_up with slot_rows NULL writes per-row slots, which
+    sffn_tile_gather_slots moves into the arena; with slot_rows given it
+    writes warp-packed slots for sffn_tile_copy_slots.  Arena, mask, prefix
+    and row offsets must be the same bits (integer/byte results)."""
+    from autoresearch2_b200 import _lib, gemm
+    from autoresearch2_b200._lib import ptr
+    T, D, F = 384, 128, 640
+    x = rand(T, D, seed=51)
+    W1 = rand(F, D, seed=52, scale=D ** -0.5)
+    b1 = torch.full((F,), -0.4, device=DEV, dtype=torch.bfloat16)
+    arena = torch.full((T * F + 40,), 9.0, device=DEV, dtype=torch.bfloat16)
+    offset = torch.tensor([5], dtype=torch.int32, device=DEV)
+    a, bitmask, prefix, voff, ro = gemm.ffn_up(x, W1, b1, act, arena, offset)
+    nt = -(-T // 128) * -(-F // 128)
+    bm2 = torch.empty(nt * 2048, dtype=torch.uint8, device=DEV)
+    counts = torch.empty(nt * 4, dtype=torch.int32, device=DEV)
+    slots = torch.empty(nt * 16384, dtype=torch.bfloat16, device=DEV)
+    act2 = torch.empty(T, F, dtype=torch.bfloat16, device=DEV)
+    pf2 = torch.empty(nt + 1, dtype=torch.int32, device=DEV)
+    vo2 = torch.empty(1, dtype=torch.int32, device=DEV)
+    ro2 = torch.empty(nt * 128, dtype=torch.int32, device=DEV)
+    arena2 = torch.full_like(arena, 9.0)
+    off2 = torch.tensor([5], dtype=torch.int32, device=DEV)
+    status = ptr(_lib.status_word(x.device))
+    st = _lib.stream_ptr(x.device)
+    _lib.call("sffn_ffn_up", ptr(x), D, ptr(W1), D, ptr(b1), T, D, F, act, ptr(act2), F, ptr(bm2), ptr(counts),
+              ptr(slots), None, status, st)
+    _lib.call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(pf2), ptr(off2), ptr(vo2), status, st)
+    _lib.call("sffn_tile_gather_slots", ptr(slots), ptr(bm2), ptr(pf2), ptr(vo2), nt, ptr(arena2),
+              arena2.numel(), _lib.BF16, ptr(ro2), None, status, st)
+    torch.cuda.synchronize()
+    assert torch.equal(bm2, bitmask) and torch.equal(pf2, prefix) and torch.equal(ro2, ro)
+    assert torch.equal(arena2.view(torch.int16), arena.view(torch.int16))
+    assert torch.equal(act2.view(torch.int16), a.view(torch.int16))
+    assert int(off2.item()) == int(offset.item())
