@@ -56,7 +56,10 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks ----
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs.
+    Entering waits (up to 10 s) for nvidia-smi's first sample and then drops
+    it, so that every kept sample falls inside the region (nvidia-smi takes a
+    few hundred ms to start, longer than a short timed region)."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
@@ -74,6 +77,10 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
+            t0 = time.perf_counter()
+            while not self.lines and self.proc.poll() is None and time.perf_counter() - t0 < 10.0:
+                time.sleep(0.005)
+            self.lines.clear()
         except OSError:
             self.proc = None
         return self
