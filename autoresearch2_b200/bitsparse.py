@@ -214,12 +214,14 @@ def tile_unpack(x: BitsparseTensor, row_start: int = 0, row_end: int = None, squ
 
 
 def spAx(x_sparse: BitsparseTensor, W: torch.Tensor, square: bool = False,
-         row_batch: int = 2048) -> torch.Tensor:
+         row_batch: int = 4096) -> torch.Tensor:
     """y = W @ x_sparse (or W @ x_sparse**2) as in old/lib_sparse/sparse.py:305-351:
     x_sparse [M, N], W [K, M] -> [K, N], unpacked in row batches of `row_batch`
     rows (a multiple of BLOCK_M), each batch's product on this library's
-    tcgen05 GEMM (split-bf16 for float32 / float16), accumulated in fp32."""
-    from .gemm import matmul
+    tcgen05 GEMM, accumulated in fp32: bf16 batches add straight into the
+    float32 result in the GEMM's epilogue, float32 / float16 ones run as
+    split-bf16 products."""
+    from .gemm import matmul, mm_f32acc
     M, N = x_sparse.shape
     if W.shape[1] != M:
         raise ValueError(f"W.shape must be [K, {M}] for W @ sparse_x, got {tuple(W.shape)}")
@@ -229,11 +231,16 @@ def spAx(x_sparse: BitsparseTensor, W: torch.Tensor, square: bool = False,
     K = W.shape[0]
     if M <= row_batch:
         return matmul(W, tile_unpack(x_sparse, 0, M, square=square).to(W.dtype))
-    acc = torch.zeros(K, N, device=W.device, dtype=torch.float32)
+    acc = torch.empty(K, N, device=W.device, dtype=torch.float32)
     for m0 in range(0, M, row_batch):
         m1 = min(m0 + row_batch, M)
         dense = tile_unpack(x_sparse, m0, m1, square=square).to(W.dtype)
-        acc += matmul(W[:, m0:m1], dense).float()
+        if W.dtype == torch.bfloat16:
+            mm_f32acc(W[:, m0:m1], dense, acc, accumulate=m0 > 0)
+        elif m0 == 0:
+            acc.copy_(matmul(W[:, m0:m1], dense).float())
+        else:
+            acc += matmul(W[:, m0:m1], dense).float()
     return acc.to(W.dtype)
 
 

@@ -1801,6 +1801,22 @@ extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const
     return SFFN_OK;
 }
 
+extern "C" int sffn_gemm_bf16_f32acc(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int accumulate,
+                                     uint32_t* status_dev, void* stream) {
+    // C (float32) = A @ B, or C += A @ B with accumulate, in one pass over K.
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
+    if (rc) return rc;
+    if (!C || ldc < N || !status_dev) return SFFN_ERR_ARG;
+    GemmArgs a = base_args(M, N, K, nullptr, ldc);
+    a.out_f32 = C;
+    a.acc_f32 = accumulate != 0;
+    a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
+    a.status = status_dev;
+    return dispatch<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int sffn_ffn_up(const void* x, int64_t ldx, const void* w1, int64_t ldw1, const void* b1,
                            int64_t T, int64_t D, int64_t F, int act, void* act_out, int64_t ld_act,
                            uint8_t* bitmask, int32_t* tile_counts, void* slots, int32_t* slot_rows,

@@ -92,6 +92,23 @@ def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     return C if A.dtype == torch.float32 else C.to(A.dtype)
 
 
+def mm_f32acc(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, accumulate: bool):
+    """C (float32 [M, N], row-major) = A @ B, or += with accumulate, bf16
+    operands, on the tcgen05 kernel (the epilogue adds into C)."""
+    _lib.require_cuda(A, B, C)
+    if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16 or C.dtype != torch.float32:
+        raise TypeError("mm_f32acc takes bfloat16 operands and a float32 C")
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2 or tuple(C.shape) != (M, N) or C.stride(1) != 1:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(B.shape)} -> {tuple(C.shape)}")
+    lda, a_mn = _operand(A, 0)
+    ldb, b_mn = _operand(B, 1)
+    call("sffn_gemm_bf16_f32acc", ptr(A), lda, a_mn, ptr(B), ldb, b_mn, ptr(C), C.stride(0), M, N, K,
+         int(bool(accumulate)), ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+    return C
+
+
 def mm_t(A: torch.Tensor, B: torch.Tensor, kb_list=None, kb_count=None):
     """(A @ B)^T [N, M] (bf16) on the tcgen05 kernel, the product stored
     transposed by its epilogue; kb_list / kb_count as in mm (per 256 rows of A)."""

@@ -256,6 +256,15 @@ int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, i
                           float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, uint32_t* status_dev,
                           void* stream);
 
+/* C (float32, [M][ldc]) = A @ B, or C += A @ B with accumulate != 0 (the
+ * epilogue adds into C in float32, round to nearest), bf16 operands as
+ * sffn_gemm_bf16 takes them, in one pass over K: spAx's row batches
+ * accumulate into one float32 result this way (old/lib_sparse/sparse.py:
+ * 321-351 accumulates them in the storage dtype with a separate add). */
+int sffn_gemm_bf16_f32acc(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int accumulate,
+                          uint32_t* status_dev, void* stream);
+
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
  * (unless act_out is NULL: the compacted-K down-projection needs none), the

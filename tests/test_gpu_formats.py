@@ -347,3 +347,23 @@ def test_spAx_matches_oracle():
             np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-5 * np.abs(want).max())
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("square", [False, True])
+def test_spAx_bf16_batches_accumulate_in_fp32(square):
+    """bf16 spAx over more rows than one batch (two full batches and a part):
+    each batch's product is added into one float32 result by the GEMM's
+    epilogue.  Against float64 of the same bf16 operands: the only rounding
+    left is the final bf16 one (and the bf16 square of z), so 1e-2."""
+    import autoresearch2_b200 as sf
+    g = torch.Generator().manual_seed(6)
+    M, N, K = 9000, 256, 72
+    z = torch.relu(torch.randn(M, N, generator=g) - 1.0).to(torch.bfloat16)
+    W = (torch.randn(K, M, generator=g) * 0.05).to(torch.bfloat16)
+    arena = torch.empty(z.numel(), device=DEV, dtype=torch.bfloat16)
+    offset = torch.zeros(1, dtype=torch.int32, device=DEV)
+    x = sf.dense_to_tilesparse(z.to(DEV), arena, offset, 64, 64)
+    got = sf.spAx(x, W.to(DEV), square=square).double().cpu().numpy()
+    zz = (z.float() * z.float()).to(torch.bfloat16) if square else z
+    want = (W.double() @ zz.double()).numpy()
+    np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-2 * np.abs(want).max())
