@@ -1,9 +1,12 @@
 """The 128x128 (vals, meta) variant of the tiled format.
 
 Mirrors old/full_matmul/sparse_pack.py:95-146 (dense_to_tilesparse(dense,
-BLOCK_M=128, BLOCK_N=128) -> (vals, meta)) and old/full_matmul/sparse_unpack.py:44-73
-(bitsparse_unpack(vals, meta, shape) -> float32 dense).  It shares its name
-with the flat bitsparse_unpack, so it lives in its own namespace.
+BLOCK_M=128, BLOCK_N=128) -> (vals, meta)), old/full_matmul/sparse_unpack.py:44-73
+(bitsparse_unpack(vals, meta, shape) -> float32 dense; the same function as
+old/matmul_bitsparse/sparse_unpack.py) and old/matmul_bitsparse/train.py:69-116
+(sparse_relu_Ax(W1, x) -> (vals, meta), the product and its ReLU packed by
+one kernel).  bitsparse_unpack shares its name with the flat one, so these
+live in their own namespace.
 """
 import torch
 
@@ -11,7 +14,7 @@ from . import _lib
 from ._lib import call, dtype_code, ptr, stream_ptr
 from .bitsparse import BitsparseTensor, tile_unpack
 
-__all__ = ["dense_to_tilesparse", "bitsparse_unpack"]
+__all__ = ["dense_to_tilesparse", "bitsparse_unpack", "sparse_relu_Ax"]
 
 
 def dense_to_tilesparse(dense: torch.Tensor, BLOCK_M: int = 128, BLOCK_N: int = 128):
@@ -53,3 +56,56 @@ def bitsparse_unpack(vals: torch.Tensor, meta: dict, shape) -> torch.Tensor:
     x = BitsparseTensor(vals.contiguous(), meta["bitmask"], meta["prefix"], zero, meta["grid_m"],
                         meta["grid_n"], meta["BLOCK_M"], meta["BLOCK_N"], tuple(shape))
     return tile_unpack(x, out_dtype=torch.float32)
+
+
+def sparse_relu_Ax(W1: torch.Tensor, x: torch.Tensor, BLOCK_M: int = 128, BLOCK_N: int = 128,
+                   input_precision: str = "tf32"):
+    """relu(x @ W1.T) ([M, N], M = rows of x, N = rows of W1) in x's dtype,
+    returned as (vals, meta) of the BLOCK_M x BLOCK_N tiled format
+    (meta: bitmask, prefix, grid_m, grid_n, BLOCK_M, BLOCK_N, shape), as
+    old/matmul_bitsparse/train.py:69-116.  bf16 with 128x128 tiles: one
+    tcgen05 GEMM whose epilogue applies the ReLU and writes the bitmask, the
+    counts and the values packed per 32 rows; one device sync for the total
+    (the reference's .item(), train.py:96), then one copy per 32 rows into a
+    vals of exactly nnz elements.  Other dtypes or tile shapes: the product
+    on this library's GEMM (float32 and float16 as the split-bf16 product,
+    which keeps float32 accuracy where the reference's default rounds the
+    inputs to tf32; input_precision is accepted for that reason and not
+    needed), its ReLU, then the tiled pack."""
+    from . import gemm as G
+    _lib.require_cuda(W1, x)
+    if x.dim() != 2 or W1.dim() != 2 or x.shape[1] != W1.shape[1]:
+        raise ValueError(f"x [M, K] and W1 [N, K] expected, got {tuple(x.shape)} and {tuple(W1.shape)}")
+    if x.dtype != W1.dtype:
+        raise TypeError("x and W1 must share a dtype")
+    M, K = x.shape
+    N = W1.shape[0]
+    dev = x.device
+    fused = (x.dtype == torch.bfloat16 and BLOCK_M == 128 and BLOCK_N == 128 and K % 8 == 0 and N % 8 == 0
+             and M * N < 2 ** 31)
+    if not fused:
+        z = torch.relu(G.matmul(x.contiguous(), W1.contiguous().T)).to(x.dtype)
+        return dense_to_tilesparse(z, BLOCK_M, BLOCK_N)
+    x, W1 = x.contiguous(), W1.contiguous()
+    gm, gn = -(-M // 128), -(-N // 128)
+    nt = gm * gn
+    bitmask = torch.empty(nt * 2048, dtype=torch.uint8, device=dev)
+    counts = torch.empty(nt * 4, dtype=torch.int32, device=dev)
+    slots = torch.empty(nt * 128 * 128, dtype=torch.bfloat16, device=dev)
+    row_offsets = torch.empty(nt * 128, dtype=torch.int32, device=dev)
+    prefix = torch.empty(nt + 1, dtype=torch.int32, device=dev)
+    offset = torch.zeros(1, dtype=torch.int32, device=dev)
+    vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
+    status = ptr(_lib.status_word(dev))
+    st = stream_ptr(dev)
+    call("sffn_ffn_up", ptr(x), K, ptr(W1), K, None, M, K, N, G.ACT_RELU, None, N, ptr(bitmask), ptr(counts),
+         ptr(slots), ptr(row_offsets), status, st)
+    call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset), status, st)
+    nnz = int(offset.item())
+    vals = torch.empty(nnz, dtype=x.dtype, device=dev)
+    if nnz:
+        call("sffn_tile_copy_slots", ptr(slots), ptr(counts), ptr(prefix), ptr(vals_offset), nt, ptr(vals), nnz,
+             ptr(row_offsets), ptr(bitmask), None, status, st)
+    meta = {"bitmask": bitmask, "prefix": prefix, "grid_m": gm, "grid_n": gn,
+            "BLOCK_M": 128, "BLOCK_N": 128, "shape": (M, N)}
+    return vals, meta

@@ -327,3 +327,49 @@ def test_per_row_slots_route_matches_the_warp_packed_route(act):
     assert torch.equal(arena2.view(torch.int16), arena.view(torch.int16))
     assert torch.equal(act2.view(torch.int16), a.view(torch.int16))
     assert int(off2.item()) == int(offset.item())
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 128, 384), (1000, 256, 640), (130, 72, 200)])
+def test_sparse_relu_Ax_fused_bf16(M, K, N):
+    """tiled.sparse_relu_Ax (old/matmul_bitsparse/train.py:69-116) on bf16 with
+    128x128 tiles runs the fused up-projection: its (vals, meta) must be the
+    same bits as packing relu(x @ W1.T) from this library's plain GEMM (the
+    same main loop and the same round-to-nearest of the accumulator), vals of
+    exactly nnz elements, and the unpacked result within the bf16 bar of the
+    float32 product."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    x = rand(M, K, seed=61)
+    W1 = rand(N, K, seed=62, scale=K ** -0.5)
+    vals, meta = sf.tiled.sparse_relu_Ax(W1, x)
+    z = torch.relu(gemm.mm(x, W1.T))
+    want_vals, want_meta = sf.tiled.dense_to_tilesparse(z)
+    assert torch.equal(meta["bitmask"], want_meta["bitmask"]) and torch.equal(meta["prefix"], want_meta["prefix"])
+    assert torch.equal(vals.view(torch.int16), want_vals.view(torch.int16))
+    assert vals.untyped_storage().nbytes() == vals.numel() * 2
+    y = sf.tiled.bitsparse_unpack(vals, meta, (M, N))
+    assert_close_rel(y, torch.relu(x.float() @ W1.float().T), 1e-2)
+    sf.check_status()
+
+
+@pytest.mark.parametrize("dtype,BM,BN", [(torch.float32, 128, 128), (torch.bfloat16, 64, 64)])
+def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
+    """The unfused route: float32 (split-bf16 product, float32 accuracy) and
+    bf16 with 64x64 tiles; unpacked against the float32 product."""
+    import autoresearch2_b200 as sf
+    g = torch.Generator(device=DEV).manual_seed(63)
+    M, K, N = 384, 96, 256
+    x = torch.randn(M, K, device=DEV, generator=g).to(dtype)
+    W1 = (torch.randn(N, K, device=DEV, generator=g) * K ** -0.5).to(dtype)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        vals, meta = sf.tiled.sparse_relu_Ax(W1, x, BLOCK_M=BM, BLOCK_N=BN)
+        assert vals.dtype == dtype and meta["BLOCK_M"] == BM
+        y = sf.tiled.bitsparse_unpack(vals, meta, (M, N))
+        want = torch.relu(x.float() @ W1.float().T)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert_close_rel(y, want, tol)
+    sf.check_status()
