@@ -123,6 +123,7 @@ struct GemmArgs {
     int c_trans;    // STORE: write C^T ([N][ldc]) instead of C
     float* out_f32; // STORE: C in float32 ([M][ldc]) instead of bf16
     int acc_f32;    // with out_f32: C += the product (round to nearest, on the CUDA cores)
+    int relu_f32;   // with out_f32: C = max(C, 0) as stored
     int kb0;        // first K block of the product (K blocks kb0 .. kb0 + ceil(K/64) - 1)
     int sp_on;      // UP: a, DGRAD: dpre, dpre^T and a^T in 2:4 form instead of dense
     Sp24Out sp[3];  // UP: [0] a; DGRAD: [0] dpre, [1] dpre^T, [2] a^T
@@ -247,7 +248,7 @@ __device__ __forceinline__ uint32_t sp24_emit(const Sp24Out& o, const uint32_t (
     return sp24_lane_word(nib, lane);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool TF32 = false>
 __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmC2,
@@ -256,7 +257,12 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     constexpr int A_BYTES = G_BM * G_BK * 2;
     constexpr int B_BYTES = BN_CTA * G_BK * 2;
     constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-    constexpr uint32_t IDESC = idesc_bf16_f32(G_BM * G_CTAS, BN, A_MN, B_MN);
+    // TF32: float32 operands, the same 128-byte k-block rows holding 32 K
+    // elements instead of 64 (K-major operands, plain or float32 C only)
+    constexpr uint32_t IDESC = TF32 ? idesc_tf32_f32(G_BM * G_CTAS, BN, A_MN, B_MN)
+                                    : idesc_bf16_f32(G_BM * G_CTAS, BN, A_MN, B_MN);
+    constexpr int KB_ELEMS = TF32 ? G_BK / 2 : G_BK;  // K elements per k-block
+    static_assert(!TF32 || (!A_MN && !B_MN && EPI == EPI_STORE), "tf32: K-major operands, plain epilogue");
     constexpr int TMEM_COLS = 2 * BN;
     constexpr uint32_t MN_LBO = G_BK * 128;  // MN-major: 64-element blocks are K rows x 128 B apart
     static_assert(BN_CTA % 64 == 0, "each CTA loads whole 64-row B blocks");
@@ -282,7 +288,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
     // Pair tiles: 256 rows (two 128-row tiles, one per CTA) x BN columns.
     const int tiles_mp = (args.tiles_m + 1) / 2;
     const int ntiles = tiles_mp * args.tiles_n;
-    const int nkb_full = (args.K + G_BK - 1) / G_BK;
+    const int nkb_full = (args.K + KB_ELEMS - 1) / KB_ELEMS;
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
     const int first_tile = (int)cluster_id_x();
@@ -357,7 +363,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                             ++armed[stage];
                         }
                         if constexpr (!A_MN) {
-                            tma_load_2d_pair(sa, &tmA, kb * G_BK, arow, &full_bar[stage]);
+                            tma_load_2d_pair(sa, &tmA, kb * KB_ELEMS, arow, &full_bar[stage]);
                         } else {
 #pragma unroll
                             for (int j = 0; j < G_BM / 64; ++j)
@@ -365,7 +371,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                         }
                     } else {
                         if constexpr (!B_MN) {
-                            tma_load_2d_pair(sb, &tmB, kb * G_BK, brow, &full_bar[stage]);
+                            tma_load_2d_pair(sb, &tmB, kb * KB_ELEMS, brow, &full_bar[stage]);
                         } else {
 #pragma unroll
                             for (int j = 0; j < BN_CTA / 64; ++j)
@@ -420,7 +426,10 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                                  : umma_desc_sw128(sa + k * 32, 16, 1024);
                         const uint64_t bd = B_MN ? umma_desc_sw128(sb + k * 2048, MN_LBO, 1024)
                                                  : umma_desc_sw128(sb + k * 32, 16, 1024);
-                        tc_mma_f16_pair(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
+                        if constexpr (TF32)
+                            tc_mma_tf32_pair(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
+                        else
+                            tc_mma_f16_pair(d, ad, bd, IDESC, (i | k) != 0 ? 1u : 0u);
                     }
                     tc_commit_pair_multicast(&empty_bar[stage], 0x3);
                     if (++stage == NST) {
@@ -541,6 +550,9 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                         const float4 o = reinterpret_cast<const float4*>(frow)[q];
                                         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
                                     }
+                                    if (args.relu_f32)
+                                        v = make_float4(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f), fmaxf(v.z, 0.f),
+                                                        fmaxf(v.w, 0.f));
                                     reinterpret_cast<float4*>(frow)[q] = v;
                                 }
                             } else {
@@ -548,7 +560,8 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                 for (int j = 0; j < 32; ++j) {
                                     if (gcol + j < args.N) {
                                         const float v = nkb ? __uint_as_float(r[j]) : 0.f;
-                                        frow[j] = args.acc_f32 ? frow[j] + v : v;
+                                        const float o = args.acc_f32 ? frow[j] + v : v;
+                                        frow[j] = args.relu_f32 ? fmaxf(o, 0.f) : o;
                                     }
                                 }
                             }
@@ -1496,18 +1509,19 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D bf16 tensor map: `inner` contiguous elements per row, `outer` rows,
-// row stride `ld` elements, box = box_inner x box_outer, 128-byte swizzle.
+// 2-D bf16 (or float32) tensor map: `inner` contiguous elements per row,
+// `outer` rows, row stride `ld` elements, box = box_inner x box_outer,
+// 128-byte swizzle.
 bool make_tmap(CUtensorMap* m, const void* base, long long inner, long long outer, long long ld,
                int box_inner, int box_outer,
-               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+               CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B, bool f32 = false) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * (f32 ? 4 : 2))};
     cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
     cuuint32_t estr[2] = {1, 1};
-    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+    const CUresult r = fn(m, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
@@ -1564,17 +1578,20 @@ bool device_is_sm100() {
     return major == 10;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool TF32 = false>
 int launch_gemm(const void* A, long long lda, const void* B, long long ldb, GemmArgs args,
                 cudaStream_t st, long long kmap = -1) {
     CUtensorMap ta, tb;
     // K extent of the operands' tensor maps (beyond the K blocks this launch reads)
     const long long KM = kmap > 0 ? kmap : args.K;
     // K-major operand [rows][K]: inner = K; MN-major operand [K][rows]: inner = rows.
+    // TF32 (K-major only): float32 elements, 32 of them per 128-byte box row.
+    constexpr int KB_ELEMS = TF32 ? G_BK / 2 : G_BK;
+    const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
     const bool okA = A_MN ? make_tmap(&ta, A, args.M, KM, lda, 64, G_BK)
-                          : make_tmap(&ta, A, KM, args.M, lda, G_BK, G_BM);
+                          : make_tmap(&ta, A, KM, args.M, lda, KB_ELEMS, G_BM, sw, TF32);
     const bool okB = B_MN ? make_tmap(&tb, B, args.N, KM, ldb, 64, G_BK)
-                          : make_tmap(&tb, B, KM, args.N, ldb, G_BK, BN / G_CTAS);
+                          : make_tmap(&tb, B, KM, args.N, ldb, KB_ELEMS, BN / G_CTAS, sw, TF32);
     if (!okA || !okB) return SFFN_ERR_CUDA;
     // outputs: 32 x 32 boxes with 64-byte swizzle for the epilogue's bulk stores
     CUtensorMap tc, tc2;
@@ -1594,7 +1611,7 @@ int launch_gemm(const void* A, long long lda, const void* B, long long ldb, Gemm
     }
     // stages + 8 epilogue warps x 2 KB staging (+ the z buffers) + alignment slack
     constexpr int smem = gemm_smem_bytes<EPI>(BN);
-    auto k = gemm_kernel<BN, A_MN, B_MN, EPI>;
+    auto k = gemm_kernel<BN, A_MN, B_MN, EPI, TF32>;
     SFFN_CUDA_TRY(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int npairs = ((args.tiles_m + 1) / 2) * args.tiles_n;
     const int clusters = std::min(npairs, max_active_clusters(k, smem));
@@ -1799,6 +1816,25 @@ extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const
             return r2;
     }
     return SFFN_OK;
+}
+
+extern "C" int sffn_gemm_tf32(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                              int64_t M, int64_t N, int64_t K, int relu, uint32_t* status_dev, void* stream) {
+    // C (float32 [M][ldc]) = A [M][lda] @ B^T with B given as [N][ldb] (both
+    // row-major, K contiguous), the inputs read as TF32 by the tensor cores,
+    // C = max(C, 0) with relu.
+    DeviceScope dev_scope;
+    if (M <= 0 || N <= 0 || K <= 0 || M > 0x7FFFFFFF || N > 0x7FFFFFFF || K > 0x7FFFFFFF) return SFFN_ERR_ARG;
+    if (!A || !B || !C || !status_dev || lda < K || ldb < K || ldc < N) return SFFN_ERR_ARG;
+    if (!aligned16(A) || !aligned16(B) || (lda * 4) % 16 || (ldb * 4) % 16) return SFFN_ERR_ALIGN;
+    if (int rc = dev_scope.bind_same(A, {B, C})) return rc;
+    if (!device_is_sm100()) return SFFN_ERR_DEVICE;
+    GemmArgs a = base_args(M, N, K, nullptr, ldc);
+    a.out_f32 = C;
+    a.relu_f32 = relu != 0;
+    a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
+    a.status = status_dev;
+    return launch_gemm<256, false, false, EPI_STORE, true>(A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int sffn_gemm_bf16_f32acc(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,

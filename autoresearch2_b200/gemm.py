@@ -92,6 +92,33 @@ def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     return C if A.dtype == torch.float32 else C.to(A.dtype)
 
 
+def matmul_tf32(A: torch.Tensor, Bt: torch.Tensor, relu: bool = False) -> torch.Tensor:
+    """A @ Bt.T in float32 on the tcgen05 kind::tf32 path: A [M, K] and Bt
+    [N, K] float32, read as TF32 by the tensor cores (10 mantissa bits),
+    float32 accumulation; max(., 0) applied by the epilogue with relu.  The
+    precision of a Triton tl.dot with input_precision="tf32"."""
+    _lib.require_cuda(A, Bt)
+    if A.dtype != torch.float32 or Bt.dtype != torch.float32:
+        raise TypeError("matmul_tf32 takes float32 operands")
+    if A.dim() != 2 or Bt.dim() != 2 or A.shape[1] != Bt.shape[1]:
+        raise ValueError(f"A [M, K] and Bt [N, K] expected, got {tuple(A.shape)} and {tuple(Bt.shape)}")
+    M, K = A.shape
+    N = Bt.shape[0]
+
+    def _rows(X):  # row-major with a 16-byte row stride and base
+        if X.stride(1) != 1 or X.stride(0) % 4 or X.data_ptr() % 16:
+            Y = torch.zeros(X.shape[0], -(-X.shape[1] // 4) * 4, dtype=X.dtype, device=X.device)
+            Y[:, :X.shape[1]] = X
+            return Y
+        return X
+
+    A, Bt = _rows(A), _rows(Bt)
+    C = torch.empty(M, N, dtype=torch.float32, device=A.device)
+    call("sffn_gemm_tf32", ptr(A), A.stride(0), ptr(Bt), Bt.stride(0), ptr(C), C.stride(0), M, N, K,
+         int(bool(relu)), ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+    return C
+
+
 def mm_f32acc(A: torch.Tensor, B: torch.Tensor, C: torch.Tensor, accumulate: bool):
     """C (float32 [M, N], row-major) = A @ B, or += with accumulate, bf16
     operands, on the tcgen05 kernel (the epilogue adds into C)."""

@@ -67,20 +67,25 @@ def sparse_relu_Ax(W1: torch.Tensor, x: torch.Tensor, BLOCK_M: int = 128, BLOCK_
     tcgen05 GEMM whose epilogue applies the ReLU and writes the bitmask, the
     counts and the values packed per 32 rows; one device sync for the total
     (the reference's .item(), train.py:96), then one copy per 32 rows into a
-    vals of exactly nnz elements.  Other dtypes or tile shapes: the product
+    vals of exactly nnz elements.  float32 with input_precision "tf32" (the
+    reference's default, Triton's tl.dot input_precision): the tcgen05
+    kind::tf32 GEMM with the ReLU in its epilogue, then the tiled pack.
+    float32 with "tf32x3" or "ieee", float16, other tile shapes: the product
     on this library's GEMM (float32 and float16 as the split-bf16 product,
-    which keeps float32 accuracy where the reference's default rounds the
-    inputs to tf32; input_precision is accepted for that reason and not
-    needed), its ReLU, then the tiled pack."""
+    float32 accuracy up to terms of 2^-24), its ReLU, then the tiled pack."""
     from . import gemm as G
     _lib.require_cuda(W1, x)
     if x.dim() != 2 or W1.dim() != 2 or x.shape[1] != W1.shape[1]:
         raise ValueError(f"x [M, K] and W1 [N, K] expected, got {tuple(x.shape)} and {tuple(W1.shape)}")
     if x.dtype != W1.dtype:
         raise TypeError("x and W1 must share a dtype")
+    if input_precision not in ("tf32", "tf32x3", "ieee"):
+        raise ValueError(f"input_precision must be 'tf32', 'tf32x3' or 'ieee', got {input_precision!r}")
     M, K = x.shape
     N = W1.shape[0]
     dev = x.device
+    if x.dtype == torch.float32 and input_precision == "tf32":
+        return dense_to_tilesparse(G.matmul_tf32(x, W1, relu=True), BLOCK_M, BLOCK_N)
     fused = (x.dtype == torch.bfloat16 and BLOCK_M == 128 and BLOCK_N == 128 and K % 8 == 0 and N % 8 == 0
              and M * N < 2 ** 31)
     if not fused:

@@ -265,6 +265,15 @@ int sffn_gemm_bf16_f32acc(const void* A, int64_t lda, int a_mn, const void* B, i
                           float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int accumulate,
                           uint32_t* status_dev, void* stream);
 
+/* C (float32, [M][ldc]) = A @ B^T, A [M][lda] and B [N][ldb] float32
+ * row-major (16-byte aligned bases, lda and ldb multiples of 4), read as
+ * TF32 by the tensor cores (tcgen05 kind::tf32), float32 accumulation;
+ * relu != 0 stores max(C, 0).  The float32 product of sparse_relu_Ax at its
+ * default input_precision "tf32" (old/matmul_bitsparse/train.py:45-52,
+ * tl.dot(..., input_precision="tf32") then tl.maximum(acc, 0)). */
+int sffn_gemm_tf32(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                   int64_t M, int64_t N, int64_t K, int relu, uint32_t* status_dev, void* stream);
+
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely
  * (unless act_out is NULL: the compacted-K down-projection needs none), the

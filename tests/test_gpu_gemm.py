@@ -354,8 +354,9 @@ def test_sparse_relu_Ax_fused_bf16(M, K, N):
 
 @pytest.mark.parametrize("dtype,BM,BN", [(torch.float32, 128, 128), (torch.bfloat16, 64, 64)])
 def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
-    """The unfused route: float32 (split-bf16 product, float32 accuracy) and
-    bf16 with 64x64 tiles; unpacked against the float32 product."""
+    """The unfused route: float32 with input_precision "ieee" (split-bf16
+    product, float32 accuracy) and bf16 with 64x64 tiles; unpacked against
+    the float32 product."""
     import autoresearch2_b200 as sf
     g = torch.Generator(device=DEV).manual_seed(63)
     M, K, N = 384, 96, 256
@@ -364,7 +365,7 @@ def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        vals, meta = sf.tiled.sparse_relu_Ax(W1, x, BLOCK_M=BM, BLOCK_N=BN)
+        vals, meta = sf.tiled.sparse_relu_Ax(W1, x, BLOCK_M=BM, BLOCK_N=BN, input_precision="ieee")
         assert vals.dtype == dtype and meta["BLOCK_M"] == BM
         y = sf.tiled.bitsparse_unpack(vals, meta, (M, N))
         want = torch.relu(x.float() @ W1.float().T)
@@ -372,4 +373,57 @@ def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
         torch.backends.cuda.matmul.allow_tf32 = prev
     tol = 1e-5 if dtype == torch.float32 else 1e-2
     assert_close_rel(y, want, tol)
+    sf.check_status()
+
+
+def _tf32_bound(A, Bt):
+    """|C - A @ Bt.T| for TF32 inputs (10 mantissa bits, rounded or
+    truncated: relative error below 2^-10 each) and float32 accumulation over
+    K terms, from float64 |A| @ |Bt|.T."""
+    K = A.shape[1]
+    return (2.0 ** -9 + K * 2.0 ** -23) * (A.double().abs() @ Bt.double().abs().T) + 1e-30
+
+
+@pytest.mark.parametrize("M,K,N", [(384, 96, 256), (130, 70, 200), (700, 1000, 520), (256, 4096, 512)])
+def test_matmul_tf32_within_the_tf32_bound(M, K, N):
+    """gemm.matmul_tf32 (tcgen05 kind::tf32): ragged M / N, K not a multiple
+    of the 32-element k-block (70 also not of 4: the operands are padded),
+    several K blocks; within the TF32 error bound of the float64 product and
+    clearly coarser than float32 (the inputs really are read as TF32);
+    relu=True stores exactly max(C, 0) of the same product."""
+    from autoresearch2_b200 import gemm
+    g = torch.Generator(device=DEV).manual_seed(M + K + N)
+    A = torch.randn(M, K, device=DEV, generator=g)
+    Bt = torch.randn(N, K, device=DEV, generator=g) * K ** -0.5
+    C = gemm.matmul_tf32(A, Bt)
+    want = A.double() @ Bt.double().T
+    assert ((C.double() - want).abs() <= _tf32_bound(A, Bt)).all()
+    rel = ((C.double() - want).norm() / want.norm()).item()
+    assert 1e-5 < rel < 2e-3, rel
+    Cr = gemm.matmul_tf32(A, Bt, relu=True)
+    assert torch.equal(Cr, torch.clamp_min(C, 0.0))
+    from autoresearch2_b200 import _lib
+    _lib.check_status()
+
+
+def test_sparse_relu_Ax_float32_tf32_default():
+    """float32 sparse_relu_Ax at the reference's default input_precision
+    "tf32" (old/matmul_bitsparse/train.py:45-52): the TF32 GEMM with the ReLU
+    in its epilogue and the tiled pack; the unpacked result within the TF32
+    bound of relu of the float64 product (relu is 1-Lipschitz), only
+    positive values stored, 64x64 tiles too; an unknown precision raises."""
+    import autoresearch2_b200 as sf
+    g = torch.Generator(device=DEV).manual_seed(64)
+    M, K, N = 1000, 512, 640
+    x = torch.randn(M, K, device=DEV, generator=g)
+    W1 = torch.randn(N, K, device=DEV, generator=g) * K ** -0.5
+    want = torch.relu(x.double() @ W1.double().T)
+    for BM, BN in ((128, 128), (64, 64)):
+        vals, meta = sf.tiled.sparse_relu_Ax(W1, x, BLOCK_M=BM, BLOCK_N=BN)
+        assert vals.dtype == torch.float32 and (vals > 0).all()
+        assert meta["BLOCK_M"] == BM and meta["BLOCK_N"] == BN
+        y = sf.tiled.bitsparse_unpack(vals, meta, (M, N))
+        assert ((y.double() - want).abs() <= _tf32_bound(x, W1)).all()
+    with pytest.raises(ValueError):
+        sf.tiled.sparse_relu_Ax(W1, x, input_precision="fp64")
     sf.check_status()
