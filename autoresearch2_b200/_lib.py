@@ -79,10 +79,14 @@ SIGNATURES = {
     "sffn_live_kblocks": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sffn_live_kblocks_t": (_int, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "sffn_split_bf16x3": (_int, [_vp, _int, _i64, _i64, _i64, _i64, _vp, _i64, _int, _vp]),
-    "sffn_gemm_bf16_f32out": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "sffn_gemm_bf16_f32out": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _int, _vp,
+                                     _vp]),
+    "sffn_gemm_relu": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _int, _i64, _i64, _i64, _i64, _vp, _vp, _int,
+                              _vp, _vp]),
     "sffn_gemm_bf16_f32acc": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _int,
                                      _vp, _vp]),
     "sffn_gemm_tf32": (_int, [_vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _vp]),
+    "sffn_round_tf32": (_int, [_vp, _vp, _i64, _vp]),
     "sffn_gemm_bf16_ct": (_int, [_vp, _i64, _int, _vp, _i64, _int, _vp, _i64, _i64, _i64, _i64, _vp,
                                  _vp, _int, _vp, _vp]),
     "sffn_ffn_dgrad": (_int, [_vp, _i64, _vp, _i64, _i64, _i64, _i64, _int, _vp, _i64, _vp, _vp,
@@ -122,7 +126,8 @@ LAUNCHING = {"sffn_sp24_compress": 1, "sffn_gemm_sp24": 1, "sffn_sp24_overflow_a
              "sffn_wait_probe": 1, "sffn_ck_lists": 1, "sffn_ck_gather_packed": 1,
              "sffn_ck_compact_rows": 1, "sffn_gemm_ck": 1, "sffn_live_kblocks_t": 1, "sffn_gemm_bf16_ct": 1,
              "sffn_split_bf16x3": 1, "sffn_gemm_bf16_f32out": 1, "sffn_tile_copy_slots": 1,
-             "sffn_gemm_bf16_f32acc": 1, "sffn_gemm_tf32": 1}
+             "sffn_gemm_bf16_f32acc": 1, "sffn_gemm_tf32": 1, "sffn_gemm_relu": 1,
+             "sffn_round_tf32": 1}
 launch_count = 0
 
 # Per-entry-point CUDA event pairs, recorded while a KernelTimer is active.

@@ -187,10 +187,12 @@ def dense_to_tilesparse(dense: torch.Tensor, vals: torch.Tensor, offset: torch.T
 
 
 def tile_unpack(x: BitsparseTensor, row_start: int = 0, row_end: int = None, square=False,
-                out=None, out_dtype=None):
+                out=None, out_dtype=None, round_tf32=False):
     """Dense rows [row_start, row_end) of a BitsparseTensor (row_start a
-    multiple of BLOCK_M), optionally squared in the storage dtype.
-    Follows old/lib_sparse/sparse_unpack.py:5-55 with column bounds."""
+    multiple of BLOCK_M), optionally squared in the storage dtype; float32
+    output rounded to the nearest TF32 values with round_tf32 (the operand
+    of a TF32 product).  Follows old/lib_sparse/sparse_unpack.py:5-55 with
+    column bounds."""
     M, N = x.shape
     row_end = M if row_end is None else min(row_end, M)
     BM, BN = x.BLOCK_M, x.BLOCK_N
@@ -208,7 +210,8 @@ def tile_unpack(x: BitsparseTensor, row_start: int = 0, row_end: int = None, squ
     trows = (row_end + BM - 1) // BM - tr0
     # Passing row_end as the row count makes the kernel skip rows past it.
     call("sffn_tile_unpack", ptr(x.vals), x.vals.numel(), ptr(x.bitmask), ptr(x.prefix),
-         ptr(x.vals_offset), code, row_end, N, BM, BN, tr0, trows, int(bool(square)), ptr(out),
+         ptr(x.vals_offset), code, row_end, N, BM, BN, tr0, trows, int(bool(square)) | 2 * int(bool(round_tf32)),
+         ptr(out),
          ocode, out.stride(0), stream_ptr(x.vals.device))
     return out
 

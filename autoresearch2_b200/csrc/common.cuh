@@ -84,6 +84,13 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // ---------------------------------------------------------------------------
 // x != 0: magnitude bits non-zero (-0.0 -> false, NaN -> true).
 __device__ __forceinline__ bool nonzero_bits(uint16_t b) { return (b & 0x7FFFu) != 0; }
+// The float32 bit pattern `u` rounded to the nearest TF32 value (10 explicit
+// mantissa bits), ties away from zero: half of the 13 dropped bits' weight
+// added to the magnitude, then those bits cleared (a carry moves into the
+// exponent, up to infinity); infinities and NaNs unchanged.
+__device__ __forceinline__ uint32_t tf32_round_bits(uint32_t u) {
+    return (u & 0x7F800000u) == 0x7F800000u ? u : (u + 0x1000u) & 0xFFFFE000u;
+}
 __device__ __forceinline__ bool nonzero_bits(uint32_t b) { return (b & 0x7FFFFFFFu) != 0; }
 
 // x > 0: sign clear, non-zero, not NaN.  INF16 is the +inf pattern of the

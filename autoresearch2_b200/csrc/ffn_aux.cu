@@ -334,6 +334,20 @@ __global__ void __launch_bounds__(256) split3_kernel(const S* __restrict__ src, 
     }
 }
 
+// dst[i] = src[i] rounded to TF32 (tf32_round_bits), four at a time when
+// both are 16-byte aligned (vec), else one at a time.
+__global__ void __launch_bounds__(256) round_tf32_kernel(const uint32_t* src, uint32_t* dst, long long n, int vec) {
+    const long long n4 = vec ? n / 4 : 0;
+    const long long stride = (long long)gridDim.x * blockDim.x;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        uint4 v = __ldcs(reinterpret_cast<const uint4*>(src) + i);
+        v = make_uint4(tf32_round_bits(v.x), tf32_round_bits(v.y), tf32_round_bits(v.z), tf32_round_bits(v.w));
+        __stcs(reinterpret_cast<uint4*>(dst) + i, v);
+    }
+    for (long long i = 4 * n4 + (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        dst[i] = tf32_round_bits(src[i]);
+}
+
 // dst[c][r] = src[r][c] for 16-bit elements: a 64 x 64 tile per CTA, read
 // and written in 16-byte rows through shared memory padded to 66 elements a
 // row (column reads of 2-byte elements then fall in distinct banks).
@@ -721,6 +735,19 @@ extern "C" int sffn_live_kblocks_t(const uint8_t* bitmask, int64_t M, int64_t N,
     SFFN_CUDA_TRY(cudaMemsetAsync(kb_count, 0, (size_t)gp * sizeof(int32_t), st));
     const dim3 grid((unsigned)gp, (unsigned)((nkb + LIVE_WARPS - 1) / LIVE_WARPS));
     live_kblocks_t_kernel<<<grid, LIVE_WARPS * 32, 0, st>>>(bitmask, (int)gm, (int)gn_f, (int)nkb, kb_list, kb_count);
+    SFFN_CHECK_LAUNCH();
+    return SFFN_OK;
+}
+
+extern "C" int sffn_round_tf32(const float* src, float* dst, int64_t n, void* stream) {
+    if (n < 0 || (n > 0 && (!src || !dst))) return SFFN_ERR_ARG;
+    if (n == 0) return SFFN_OK;
+    DeviceScope dev_scope;
+    if (int rc = dev_scope.bind_same(dst, {src})) return rc;
+    const int vec = aligned16(src) && aligned16(dst);
+    const unsigned grid = (unsigned)std::min<long long>((n / 4 + 255) / 256 + 1, 148ll * 16);
+    round_tf32_kernel<<<grid, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const uint32_t*>(src), reinterpret_cast<uint32_t*>(dst), n, vec);
     SFFN_CHECK_LAUNCH();
     return SFFN_OK;
 }

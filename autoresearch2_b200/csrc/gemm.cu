@@ -123,7 +123,7 @@ struct GemmArgs {
     int c_trans;    // STORE: write C^T ([N][ldc]) instead of C
     float* out_f32; // STORE: C in float32 ([M][ldc]) instead of bf16
     int acc_f32;    // with out_f32: C += the product (round to nearest, on the CUDA cores)
-    int relu_f32;   // with out_f32: C = max(C, 0) as stored
+    int relu_out;   // STORE: C = max(C, 0) as stored (bf16 or float32)
     int kb0;        // first K block of the product (K blocks kb0 .. kb0 + ceil(K/64) - 1)
     int sp_on;      // UP: a, DGRAD: dpre, dpre^T and a^T in 2:4 form instead of dense
     Sp24Out sp[3];  // UP: [0] a; DGRAD: [0] dpre, [1] dpre^T, [2] a^T
@@ -550,7 +550,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                         const float4 o = reinterpret_cast<const float4*>(frow)[q];
                                         v = make_float4(o.x + v.x, o.y + v.y, o.z + v.z, o.w + v.w);
                                     }
-                                    if (args.relu_f32)
+                                    if (args.relu_out)
                                         v = make_float4(fmaxf(v.x, 0.f), fmaxf(v.y, 0.f), fmaxf(v.z, 0.f),
                                                         fmaxf(v.w, 0.f));
                                     reinterpret_cast<float4*>(frow)[q] = v;
@@ -561,7 +561,7 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
                                     if (gcol + j < args.N) {
                                         const float v = nkb ? __uint_as_float(r[j]) : 0.f;
                                         const float o = args.acc_f32 ? frow[j] + v : v;
-                                        frow[j] = args.relu_f32 ? fmaxf(o, 0.f) : o;
+                                        frow[j] = args.relu_out ? fmaxf(o, 0.f) : o;
                                     }
                                 }
                             }
@@ -572,6 +572,12 @@ __global__ void __cluster_dims__(G_CTAS, 1, 1) __launch_bounds__(G_THREADS, 1)
 #pragma unroll
                     for (int q = 0; q < 16; ++q)
                         w[q] = nkb ? pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1])) : 0u;
+                    if (args.relu_out) {
+                        // max(x, 0) on the packed halves: a set sign bit (negative or -0) gives +0
+#pragma unroll
+                        for (int q = 0; q < 16; ++q)
+                            w[q] &= ((w[q] & 0x8000u) ? 0u : 0xFFFFu) | ((w[q] & 0x80000000u) ? 0u : 0xFFFF0000u);
+                    }
                     if (args.c_trans) {
                         // the 32 x 32 block transposed through the staging buffer:
                         // lane takes column `lane`, row gcol0 + 32c + lane of C^T
@@ -1769,6 +1775,30 @@ extern "C" int sffn_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
     return dispatch<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
 }
 
+extern "C" int sffn_gemm_relu(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                              void* C, int out_f32, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                              const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
+                              uint32_t* status_dev, void* stream) {
+    // C = max(A @ B, 0), bf16 operands as sffn_gemm_bf16 takes them, C bf16
+    // (out_f32 == 0) or float32, the ReLU applied by the epilogue.
+    DeviceScope dev_scope;
+    int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
+    if (rc) return rc;
+    if (!C || ldc < N || !status_dev) return SFFN_ERR_ARG;
+    if ((kb_list == nullptr) != (kb_count == nullptr)) return SFFN_ERR_ARG;
+    GemmArgs a = base_args(M, N, K, out_f32 ? nullptr : C, ldc);
+    if (out_f32) {
+        a.out_f32 = static_cast<float*>(C);
+        a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
+    }
+    a.relu_out = 1;
+    a.kb_list = kb_list;
+    a.kb_count = kb_count;
+    a.kb_stride = kb_stride;
+    a.status = status_dev;
+    return dispatch<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));
+}
+
 extern "C" int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
                                  void* Ct, int64_t ldct, int64_t M, int64_t N, int64_t K, const int32_t* kb_list,
                                  const int32_t* kb_count, int kb_stride, uint32_t* status_dev, void* stream) {
@@ -1790,8 +1820,8 @@ extern "C" int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const voi
 }
 
 extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
-                                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, uint32_t* status_dev,
-                                     void* stream) {
+                                     float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int relu,
+                                     uint32_t* status_dev, void* stream) {
     // C (float32) = A @ B, bf16 operands as sffn_gemm_bf16 takes them.
     DeviceScope dev_scope;
     int rc = check_operands(dev_scope, A, lda, a_mn, B, ldb, b_mn, M, N, K);
@@ -1809,6 +1839,7 @@ extern "C" int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const
         a.kb0 = (int)(k0 / G_BK);
         a.out_f32 = C;
         a.acc_f32 = k0 > 0;
+        a.relu_out = relu != 0 && k0 + kc >= K;  // after the last chunk's sum
         a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
         a.status = status_dev;
         if (int r2 = dispatch_kmap<EPI_STORE>(a_mn != 0, b_mn != 0, A, lda, B, ldb, a, k0 + kc,
@@ -1831,7 +1862,7 @@ extern "C" int sffn_gemm_tf32(const float* A, int64_t lda, const float* B, int64
     if (!device_is_sm100()) return SFFN_ERR_DEVICE;
     GemmArgs a = base_args(M, N, K, nullptr, ldc);
     a.out_f32 = C;
-    a.relu_f32 = relu != 0;
+    a.relu_out = relu != 0;
     a.vec_out = aligned16(C) && (ldc * 4) % 16 == 0;
     a.status = status_dev;
     return launch_gemm<256, false, false, EPI_STORE, true>(A, lda, B, ldb, a, reinterpret_cast<cudaStream_t>(stream));

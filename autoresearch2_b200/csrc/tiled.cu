@@ -322,13 +322,15 @@ __global__ void __launch_bounds__(TileCfg<BM, BN>::NT) tile_unpack_kernel(
             if ((bits[it] >> j) & 1u) {
                 z = r < C::TILE + 2 * EPV ? s_vals[r] : B(0);
                 ++r;
-                if (square) {
+                if (square & 1) {
                     const float zf = Elt<DT>::to_f(z);
                     z = Elt<DT>::from_f(zf * zf);
                 }
             }
             if constexpr (OUT_F32) o[j] = __float_as_uint(Elt<DT>::to_f(z));
             else o[j] = z;
+            if constexpr (sizeof(O) == 4)
+                if (square & 2) o[j] = tf32_round_bits(o[j]);
         }
         if (gr < M) store8_row(out + (gr - tile_row0 * BM) * ld_out, gc, N, vec != 0, o);
     }

@@ -70,17 +70,18 @@ def split3(X: torch.Tensor, b_order: bool) -> torch.Tensor:
     return out
 
 
-def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
-    """A @ B on this library's tcgen05 GEMM, in A's dtype.  bfloat16 runs
-    directly (fp32 accumulation); float32 and float16 run as the split-bf16
-    product (three bf16 pieces per operand, six cross products, fp32
-    accumulation and output): the float32 product up to terms of relative
-    size 2^-24, where a TF32 product keeps 2^-11."""
+def matmul(A: torch.Tensor, B: torch.Tensor, relu: bool = False) -> torch.Tensor:
+    """A @ B on this library's tcgen05 GEMM, in A's dtype (max(., 0) of it
+    with relu, applied by the epilogue).  bfloat16 runs directly (fp32
+    accumulation); float32 and float16 run as the split-bf16 product (three
+    bf16 pieces per operand, six cross products, fp32 accumulation and
+    output): the float32 product up to terms of relative size 2^-24, where a
+    TF32 product keeps 2^-11."""
     _lib.require_cuda(A, B)
     if A.dtype != B.dtype:
         raise TypeError("matmul operands must share a dtype")
     if A.dtype == torch.bfloat16:
-        return mm(A, B)
+        return mm_relu(A, B) if relu else mm(A, B)
     M, K = A.shape
     K2, N = B.shape
     if K != K2:
@@ -88,15 +89,53 @@ def matmul(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
     a3, b3 = split3(A, False), split3(B.T, True)
     C = torch.empty(M, N, dtype=torch.float32, device=A.device)
     call("sffn_gemm_bf16_f32out", ptr(a3), a3.stride(0), 0, ptr(b3), b3.stride(0), 0, ptr(C), C.stride(0), M, N,
-         6 * K, ptr(_lib.status_word(A.device)), stream_ptr(A.device))
+         6 * K, int(bool(relu)), ptr(_lib.status_word(A.device)), stream_ptr(A.device))
     return C if A.dtype == torch.float32 else C.to(A.dtype)
 
 
-def matmul_tf32(A: torch.Tensor, Bt: torch.Tensor, relu: bool = False) -> torch.Tensor:
+def mm_relu(A: torch.Tensor, B: torch.Tensor, out_dtype=torch.bfloat16, kb_list=None, kb_count=None):
+    """max(A @ B, 0) (bf16 operands, fp32 accumulation) in bf16 or float32,
+    the ReLU applied by the GEMM's epilogue; kb_list / kb_count as in mm."""
+    _lib.require_cuda(A, B)
+    if A.dtype != torch.bfloat16 or B.dtype != torch.bfloat16:
+        raise TypeError("mm_relu takes bfloat16 operands")
+    if out_dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("mm_relu stores bfloat16 or float32")
+    M, K = A.shape
+    K2, N = B.shape
+    if K != K2:
+        raise ValueError(f"shape mismatch {tuple(A.shape)} @ {tuple(B.shape)}")
+    lda, a_mn = _operand(A, 0)
+    ldb, b_mn = _operand(B, 1)
+    out = torch.empty(M, N, dtype=out_dtype, device=A.device)
+    stride = kb_list.shape[1] if kb_list is not None else 0
+    call("sffn_gemm_relu", ptr(A), lda, a_mn, ptr(B), ldb, b_mn, ptr(out), int(out_dtype == torch.float32),
+         out.stride(0), M, N, K, ptr(kb_list), ptr(kb_count), stride, ptr(_lib.status_word(A.device)),
+         stream_ptr(A.device))
+    return out
+
+
+def round_tf32(X: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+    """X (float32) rounded to the nearest TF32 values (ties away from zero),
+    into out (a new tensor by default; out=X rounds in place)."""
+    _lib.require_cuda(X)
+    if X.dtype != torch.float32:
+        raise TypeError("round_tf32 takes float32")
+    X = X.contiguous()
+    out = torch.empty_like(X) if out is None else out
+    if out.shape != X.shape or out.dtype != torch.float32 or not out.is_contiguous():
+        raise ValueError("out must be a contiguous float32 tensor of X's shape")
+    call("sffn_round_tf32", ptr(X), ptr(out), X.numel(), stream_ptr(X.device))
+    return out
+
+
+def matmul_tf32(A: torch.Tensor, Bt: torch.Tensor, relu: bool = False, round_inputs: bool = False) -> torch.Tensor:
     """A @ Bt.T in float32 on the tcgen05 kind::tf32 path: A [M, K] and Bt
-    [N, K] float32, read as TF32 by the tensor cores (10 mantissa bits),
-    float32 accumulation; max(., 0) applied by the epilogue with relu.  The
-    precision of a Triton tl.dot with input_precision="tf32"."""
+    [N, K] float32, read as TF32 by the tensor cores, float32 accumulation;
+    max(., 0) applied by the epilogue with relu.  The tensor cores keep the
+    top 19 bits of each operand (truncation: the products of a Triton tl.dot
+    at input_precision="tf32"); round_inputs rounds both operands to the
+    nearest TF32 values first (the products of cuBLAS's TF32 GEMMs)."""
     _lib.require_cuda(A, Bt)
     if A.dtype != torch.float32 or Bt.dtype != torch.float32:
         raise TypeError("matmul_tf32 takes float32 operands")
@@ -113,6 +152,8 @@ def matmul_tf32(A: torch.Tensor, Bt: torch.Tensor, relu: bool = False) -> torch.
         return X
 
     A, Bt = _rows(A), _rows(Bt)
+    if round_inputs:
+        A, Bt = round_tf32(A), round_tf32(Bt)
     C = torch.empty(M, N, dtype=torch.float32, device=A.device)
     call("sffn_gemm_tf32", ptr(A), A.stride(0), ptr(Bt), Bt.stride(0), ptr(C), C.stride(0), M, N, K,
          int(bool(relu)), ptr(_lib.status_word(A.device)), stream_ptr(A.device))

@@ -182,9 +182,11 @@ int sffn_tile_pack_values(const void* dense, int dtype, int64_t M, int64_t N, in
                           uint32_t* status_dev, void* stream);
 
 /* Unpack tile rows [tile_row0, tile_row0 + tile_rows) into out (row stride
- * ld_out; out row 0 = matrix row tile_row0*BM), optionally squaring each value
- * in the storage dtype (spAx(..., square=True)).  out_dtype is dtype or
- * SFFN_F32 (old/full_matmul/sparse_unpack.py:62 returns float32).
+ * ld_out; out row 0 = matrix row tile_row0*BM).  `square` holds flags: bit 0
+ * squares each value in the storage dtype (spAx(..., square=True)), bit 1
+ * rounds float32 output values to the nearest TF32 value (ties away from
+ * zero; the operand of a TF32 product).  out_dtype is dtype or SFFN_F32
+ * (old/full_matmul/sparse_unpack.py:62 returns float32).
  *   replaces old/lib_sparse/sparse_unpack.py:5-55 (_unpack_batch_kernel, with
  *   column bounds added), old/full_matmul/sparse_unpack.py:6-73,
  *   old/full_matmul/train.py:89-137. */
@@ -253,8 +255,19 @@ int sffn_gemm_bf16_ct(const void* A, int64_t lda, int a_mn, const void* B, int64
 int sffn_split_bf16x3(const void* src, int dtype, int64_t rows, int64_t cols, int64_t s_row, int64_t s_col,
                       void* dst, int64_t ld_dst, int b_order, void* stream);
 int sffn_gemm_bf16_f32out(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
-                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, uint32_t* status_dev,
-                          void* stream);
+                          float* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int relu,
+                          uint32_t* status_dev, void* stream);
+
+/* C = max(A @ B, 0): bf16 operands and optional K-block lists as
+ * sffn_gemm_bf16 takes them, C bf16 (out_f32 == 0) or float32 [M][ldc], the
+ * ReLU applied by the epilogue.  The products of relu_spAx
+ * (old/full_matmul/train.py:140-184: F.relu(F.linear(unpacked rows, W2)))
+ * and relu_sparse_Ax (old/sparse_matmul/train.py:56-76: relu(A @ x) stored
+ * in float32). */
+int sffn_gemm_relu(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn,
+                   void* C, int out_f32, int64_t ldc, int64_t M, int64_t N, int64_t K,
+                   const int32_t* kb_list, const int32_t* kb_count, int kb_stride,
+                   uint32_t* status_dev, void* stream);
 
 /* C (float32, [M][ldc]) = A @ B, or C += A @ B with accumulate != 0 (the
  * epilogue adds into C in float32, round to nearest), bf16 operands as
@@ -273,6 +286,14 @@ int sffn_gemm_bf16_f32acc(const void* A, int64_t lda, int a_mn, const void* B, i
  * tl.dot(..., input_precision="tf32") then tl.maximum(acc, 0)). */
 int sffn_gemm_tf32(const float* A, int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
                    int64_t M, int64_t N, int64_t K, int relu, uint32_t* status_dev, void* stream);
+
+/* dst[i] = src[i] rounded to the nearest TF32 value (ties away from zero),
+ * as float32 (in place when dst == src).  The tensor cores' kind::tf32 read
+ * keeps the top 19 bits of each operand (truncation, as Triton's tl.dot at
+ * input_precision "tf32"); operands rounded first give the products of
+ * cuBLAS's TF32 GEMMs behind F.linear under set_float32_matmul_precision
+ * ("high") (old/full_matmul/train.py:35,177-178). */
+int sffn_round_tf32(const float* src, float* dst, int64_t n, void* stream);
 
 /* Fused up-projection: pre = bf16(x @ W1^T [+ b1]), z = relu(pre).
  * Writes act_out = z*z (act = 1, ReLU^2) or z (act = 0, ReLU) densely

@@ -427,3 +427,201 @@ def test_sparse_relu_Ax_float32_tf32_default():
     with pytest.raises(ValueError):
         sf.tiled.sparse_relu_Ax(W1, x, input_precision="fp64")
     sf.check_status()
+
+
+def test_mm_relu_equals_relu_of_the_product():
+    """gemm.mm_relu (sffn_gemm_relu): the ReLU applied by the epilogue gives
+    the values of relu(gemm.mm) in bf16 (rounding keeps the sign) and of
+    relu(mm_f32acc) in float32, with and without K-block lists; the
+    split-bf16 matmul(relu=True) gives relu of matmul (the ReLU after the
+    last K chunk's sum)."""
+    from autoresearch2_b200 import gemm
+    M, K, N = 700, 320, 520
+    A = rand(M, K, seed=71)
+    B = rand(K, N, seed=72, scale=K ** -0.5)
+    got = gemm.mm_relu(A, B)
+    assert got.dtype == torch.bfloat16
+    assert torch.equal(got.float(), torch.relu(gemm.mm(A, B).float()))
+    C = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    gemm.mm_f32acc(A, B, C, False)
+    assert torch.equal(gemm.mm_relu(A, B, out_dtype=torch.float32), torch.relu(C))
+    # zero 64-wide K blocks in every 256-row tile, skipped through the lists
+    Az = A.clone()
+    Az[:, 64:192] = 0
+    import autoresearch2_b200 as sf
+    _, meta = sf.tiled.dense_to_tilesparse(Az)
+    kl, kc = gemm.live_kblocks(meta["bitmask"], M, K)
+    assert int(kc.max()) < -(-K // 64)
+    assert torch.equal(gemm.mm_relu(Az, B, kb_list=kl, kb_count=kc).float(), torch.relu(gemm.mm(Az, B).float()))
+    g = torch.Generator(device=DEV).manual_seed(73)
+    A32 = torch.randn(300, 2100, device=DEV, generator=g)
+    B32 = torch.randn(2100, 200, device=DEV, generator=g)
+    assert torch.equal(gemm.matmul(A32, B32, relu=True), torch.relu(gemm.matmul(A32, B32)))
+    sf.check_status()
+
+
+def _relu_layer_input(M, K, seed, dtype):
+    """relu of shifted xavier-like values, as the reference's two-layer
+    harness draws its sparse operand (old/sparse_matmul/prepare.py:7-17)."""
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    A = torch.randn(M, K, device=DEV, generator=g) * (2.0 / (M + K)) ** 0.5
+    return torch.relu(A + 0.1 * A.std()).to(dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_relu_spAx_forms(dtype):
+    """tiled.relu_spAx (old/full_matmul/train.py:140-184): relu(A @ W2.T) from
+    the packed A.  bf16: the same values as relu of this library's plain GEMM
+    on the unpacked A, in one batch and in 256-row batches; float32: within
+    the TF32 bound with allow_tf32 and within 1e-5 without; float16 within
+    its rounding of the float32 product."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    M, K, N = 1000, 512, 384
+    A = _relu_layer_input(M, K, 74, dtype)
+    g = torch.Generator(device=DEV).manual_seed(75)
+    W2 = (torch.randn(N, K, device=DEV, generator=g) * K ** -0.5).to(dtype)
+    vals, meta = sf.tiled.dense_to_tilesparse(A)
+    want64 = torch.relu(A.double() @ W2.double().T)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        if dtype == torch.bfloat16:
+            y = sf.tiled.relu_spAx(vals, meta, W2)
+            assert y.dtype == dtype and y.shape == (M, N)
+            want = torch.relu(gemm.mm(A, W2.T).float())
+            assert torch.equal(y.float(), want)
+            assert torch.equal(sf.tiled.relu_spAx(vals, meta, W2, row_batch=256).float(), want)
+        elif dtype == torch.float32:
+            torch.backends.cuda.matmul.allow_tf32 = True
+            y = sf.tiled.relu_spAx(vals, meta, W2)
+            assert ((y.double() - want64).abs() <= _tf32_bound(A, W2)).all()
+            torch.backends.cuda.matmul.allow_tf32 = False
+            y = sf.tiled.relu_spAx(vals, meta, W2, row_batch=512)
+            assert_close_rel(y, want64.float(), 1e-5)
+        else:
+            y = sf.tiled.relu_spAx(vals, meta, W2)
+            assert y.dtype == dtype
+            assert_close_rel(y.float(), want64.float(), 1e-3)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    with pytest.raises(ValueError):
+        sf.tiled.relu_spAx(vals, meta, W2[:, :-8])
+    sf.check_status()
+
+
+@pytest.mark.parametrize("dtype,tf32", [(torch.bfloat16, False), (torch.float16, False), (torch.float32, False),
+                                        (torch.float32, True)])
+def test_relu_sparse_Ax_forms(dtype, tf32):
+    """tiled.relu_sparse_Ax (old/sparse_matmul/train.py:56-76): relu(A @ x) in
+    float32 with both operands taken in `dtype`.  bf16 / float16: the exact
+    products of the rounded operands summed in float32 (bound K * 2^-23 of
+    |A| |x|); float32: 1e-5 of the float64 product, or the TF32 bound."""
+    import autoresearch2_b200 as sf
+    M, K, N = 640, 384, 1000
+    A = _relu_layer_input(M, K, 76, torch.float32)
+    g = torch.Generator(device=DEV).manual_seed(77)
+    x = torch.randn(K, N, device=DEV, generator=g)
+    vals, meta = sf.tiled.dense_to_tilesparse(A)
+    y = sf.tiled.relu_sparse_Ax(vals, meta, x, dtype=dtype, tf32=tf32)
+    assert y.dtype == torch.float32 and y.shape == (M, N)
+    Ad, xd = A.to(dtype).double(), x.to(dtype).double()
+    want = torch.relu(Ad @ xd)
+    if dtype == torch.float32 and not tf32:
+        assert_close_rel(y, want.float(), 1e-5)
+    elif tf32:
+        assert ((y.double() - want).abs() <= _tf32_bound(A, x.T)).all()
+    else:
+        assert ((y.double() - want).abs() <= K * 2.0 ** -23 * (Ad.abs() @ xd.abs()) + 1e-30).all()
+    sf.check_status()
+
+
+def test_sp_relu_Ax_follows_torch_tf32_setting():
+    """tiled.sp_relu_Ax (old/full_matmul/train.py:21-76) takes F.linear's
+    float32 precision from torch's global setting: with allow_tf32 its vals
+    are the pack of the TF32 GEMM on operands rounded to nearest (cuBLAS's
+    TF32 products), without it sparse_relu_Ax at "ieee"; sparse_relu_Ax at
+    "tf32" keeps Triton's truncated operands."""
+    import autoresearch2_b200 as sf
+    g = torch.Generator(device=DEV).manual_seed(78)
+    x = torch.randn(300, 256, device=DEV, generator=g)
+    W1 = torch.randn(512, 256, device=DEV, generator=g) * 256 ** -0.5
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        from autoresearch2_b200 import gemm
+        torch.backends.cuda.matmul.allow_tf32 = True
+        v1, m1 = sf.tiled.sp_relu_Ax(W1, x)
+        v2, m2 = sf.tiled.dense_to_tilesparse(gemm.matmul_tf32(x, W1, relu=True, round_inputs=True))
+        assert torch.equal(v1, v2) and torch.equal(m1["bitmask"], m2["bitmask"])
+        assert m1["shape"] == (300, 512)
+        v3, _ = sf.tiled.sparse_relu_Ax(W1, x)
+        v4, _ = sf.tiled.dense_to_tilesparse(gemm.matmul_tf32(x, W1, relu=True))
+        assert torch.equal(v3, v4)
+        torch.backends.cuda.matmul.allow_tf32 = False
+        v1, m1 = sf.tiled.sp_relu_Ax(W1, x)
+        v2, m2 = sf.tiled.sparse_relu_Ax(W1, x, input_precision="ieee")
+        assert torch.equal(v1, v2) and torch.equal(m1["bitmask"], m2["bitmask"])
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    sf.check_status()
+
+
+def _tf32_round_np(x):
+    """Round-to-nearest TF32 (ties away from zero) of float32 values, on the
+    bit patterns: half of the 13 dropped bits' weight added to the
+    magnitude, those bits cleared; infinities and NaNs unchanged."""
+    import numpy as np
+    u = x.view(np.uint32).astype(np.uint64)
+    special = (u & 0x7F800000) == 0x7F800000
+    r = ((u + 0x1000) & 0xFFFFE000).astype(np.uint32)
+    return np.where(special, x.view(np.uint32), r).view(np.float32)
+
+
+def test_round_tf32_bits_and_fused_unpack_rounding():
+    """sffn_round_tf32 against the bit formula on random values, exact ties
+    (both signs), the largest finite value (rounds to infinity), subnormals,
+    infinities and NaN; an unaligned view takes the scalar path and in-place
+    rounding works; tile_unpack(round_tf32=True) equals rounding the plain
+    unpack."""
+    import numpy as np
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    rng = np.random.default_rng(79)
+    x = (rng.standard_normal(100003) * 10.0 ** rng.integers(-30, 30, 100003)).astype(np.float32)
+    specials = np.array([1.0 + 2.0 ** -11, -(1.0 + 2.0 ** -11), 1.0 + 3 * 2.0 ** -11, np.finfo(np.float32).max,
+                         1e-40, -1e-42, np.inf, -np.inf, np.nan, 0.0, -0.0], dtype=np.float32)
+    x[:specials.size] = specials
+    want = _tf32_round_np(x)
+    X = torch.from_numpy(x).to(DEV)
+    got = gemm.round_tf32(X).cpu().numpy()
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert np.isinf(got[3]) and got[0] == np.float32(1.0 + 2.0 ** -10) and got[2] == np.float32(1.0 + 2.0 ** -9)
+    V = torch.empty(X.numel() + 3, device=DEV)[1:1 + X.numel()]  # 4-byte aligned only: the scalar path
+    V.copy_(X)
+    gemm.round_tf32(V, out=V)
+    assert np.array_equal(V.cpu().numpy().view(np.uint32), want.view(np.uint32))
+    A = _relu_layer_input(300, 520, 80, torch.float32)
+    vals, meta = sf.tiled.dense_to_tilesparse(A)
+    z = sf.tiled._as_bitsparse(vals, meta)
+    plain = sf.bitsparse.tile_unpack(z)
+    assert torch.equal(sf.bitsparse.tile_unpack(z, round_tf32=True), gemm.round_tf32(plain))
+    sf.check_status()
+
+
+def test_relu_spAx_float32_tf32_rounds_its_operands():
+    """relu_spAx in float32 with TF32 allowed equals the kind::tf32 GEMM on
+    operands rounded to the nearest TF32 values (cuBLAS's TF32 products)."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    M, K, N = 520, 384, 300
+    A = _relu_layer_input(M, K, 81, torch.float32)
+    g = torch.Generator(device=DEV).manual_seed(82)
+    W2 = torch.randn(N, K, device=DEV, generator=g) * K ** -0.5
+    vals, meta = sf.tiled.dense_to_tilesparse(A)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = True
+        y = sf.tiled.relu_spAx(vals, meta, W2)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert torch.equal(y, gemm.matmul_tf32(A, W2, relu=True, round_inputs=True))
+    sf.check_status()
