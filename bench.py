@@ -748,7 +748,12 @@ def micro(case, device, reps=3):
       up     the fused up-projection GEMM (+ tile scan and slot gather) of the
              headline layer, `tokens` tokens, 90% zeros
       dgrad  the fused activation-gradient GEMM of the same layer
-      ck     the compacted-K GEMM of the clustered workload's down-projection"""
+      ck     the compacted-K GEMM of the clustered workload's down-projection
+      relu_ax  relu(x @ W1.T) at old/matmul_bitsparse's largest harness shape
+             (x [10000, 4096], W1 [16384, 4096], shifted inputs): the float32
+             kind::tf32 GEMM alone (ReLU in the epilogue), then the whole of
+             tiled.sparse_relu_Ax in float32 and in bf16 (the fused
+             up-projection)"""
     import autoresearch2_b200 as sf
     from autoresearch2_b200 import _lib, gemm as G, sp24
     res = {"case": case}
@@ -808,6 +813,18 @@ def micro(case, device, reps=3):
         ac = G.ck_gather_packed(zs, G.tile_row_offsets(zs), cm, cp, kc, G.ACT_RELU2)
         W2t = sp24.transpose(W2)
         run("gemm_ck", lambda: G.ck_mm(ac, W2t, idx, kc))
+    elif case == "relu_ax":
+        g = torch.Generator(device=device).manual_seed(1)
+        rows, tokens = 4096, 10000
+        W1 = torch.empty(4 * rows, rows, device=device)
+        torch.nn.init.xavier_uniform_(W1, generator=g)
+        x = torch.randn(tokens, rows, device=device, generator=g)
+        W1, x = W1 + 0.1 * W1.std(), x - 0.1 * x.std()
+        run("gemm_tf32", lambda: G.matmul_tf32(x, W1, relu=True))
+        res["gemm_tf32_tflops"] = round(2.0 * tokens * rows * 4 * rows / res["gemm_tf32_ms"] / 1e9, 1)
+        run("sparse_relu_Ax_f32", lambda: sf.tiled.sparse_relu_Ax(W1, x))
+        W1b, xb = W1.bfloat16(), x.bfloat16()
+        run("sparse_relu_Ax_bf16", lambda: sf.tiled.sparse_relu_Ax(W1b, xb))
     else:
         raise SystemExit(f"unknown micro case {case}")
     sf.check_status(device)
@@ -837,7 +854,7 @@ def main():
     ap.add_argument("--sparse-mma", default="auto", choices=["auto", "on", "off"],
                     help="path of the products with a sparse operand: 2:4 sparse tensor cores "
                          "chosen by the observed sparsity (auto), always, or never")
-    ap.add_argument("--micro", choices=["flat", "tile", "up", "dgrad", "ck"],
+    ap.add_argument("--micro", choices=["flat", "tile", "up", "dgrad", "ck", "relu_ax"],
                     help="time one group of kernels at a stated size (and nothing else)")
     ap.add_argument("--reps", type=int, default=3, help="calls timed by --micro")
     args = ap.parse_args()
