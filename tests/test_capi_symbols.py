@@ -76,6 +76,24 @@ def test_host_side_rejections(lib):
     # unpack row range past the matrix
     assert lib.sffn_tile_unpack(dummy, 10, dummy, dummy, dummy, 1, 64, 64, 64, 64, 0, 2, 0, dummy,
                                 1, 64, None) == 1
+    # TF32 GEMM: empty shape, row stride below K, a row stride that is not 16 bytes, misaligned base
+    i64 = ctypes.c_int64
+    assert lib.sffn_gemm_tf32(dummy, i64(64), dummy, i64(64), dummy, i64(64), i64(0), i64(64), i64(64), 0,
+                              dummy, None) == 1
+    assert lib.sffn_gemm_tf32(dummy, i64(32), dummy, i64(64), dummy, i64(64), i64(64), i64(64), i64(64), 0,
+                              dummy, None) == 1
+    assert lib.sffn_gemm_tf32(dummy, i64(66), dummy, i64(64), dummy, i64(64), i64(64), i64(64), i64(64), 0,
+                              dummy, None) == 3
+    assert lib.sffn_gemm_tf32(vp(260), i64(64), dummy, i64(64), dummy, i64(64), i64(64), i64(64), i64(64), 0,
+                              dummy, None) == 3
+    # ReLU GEMM: empty shape, row stride below K
+    assert lib.sffn_gemm_relu(dummy, i64(64), 0, dummy, i64(64), 0, dummy, 0, i64(64), i64(0), i64(64),
+                              i64(64), None, None, 0, dummy, None) == 1
+    assert lib.sffn_gemm_relu(dummy, i64(32), 0, dummy, i64(64), 0, dummy, 1, i64(64), i64(64), i64(64),
+                              i64(64), None, None, 0, dummy, None) == 1
+    assert lib.sffn_round_tf32(dummy, dummy, i64(-1), None) == 1
+    assert lib.sffn_round_tf32(None, dummy, i64(4), None) == 1
+    assert lib.sffn_round_tf32(None, None, i64(0), None) == 0
 
 
 def test_codec15_host_checks(lib):
