@@ -352,7 +352,8 @@ def test_sparse_relu_Ax_fused_bf16(M, K, N):
     sf.check_status()
 
 
-@pytest.mark.parametrize("dtype,BM,BN", [(torch.float32, 128, 128), (torch.bfloat16, 64, 64)])
+@pytest.mark.parametrize("dtype,BM,BN", [(torch.float32, 128, 128), (torch.bfloat16, 64, 64),
+                                         (torch.float16, 128, 128)])
 def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
     """The unfused route: float32 with input_precision "ieee" (split-bf16
     product, float32 accuracy) and bf16 with 64x64 tiles; unpacked against
@@ -371,7 +372,7 @@ def test_sparse_relu_Ax_other_forms(dtype, BM, BN):
         want = torch.relu(x.float() @ W1.float().T)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
-    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    tol = 1e-5 if dtype == torch.float32 else 1e-3 if dtype == torch.float16 else 1e-2
     assert_close_rel(y, want, tol)
     sf.check_status()
 
@@ -624,4 +625,25 @@ def test_relu_spAx_float32_tf32_rounds_its_operands():
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
     assert torch.equal(y, gemm.matmul_tf32(A, W2, relu=True, round_inputs=True))
+    sf.check_status()
+
+
+@pytest.mark.parametrize("BM,BN", [(64, 64), (128, 64)])
+def test_relu_products_on_other_tile_shapes(BM, BN):
+    """relu_spAx (bf16, no K-block lists off 128x128 tiles) and relu_sparse_Ax
+    (bf16 default) from (vals, meta) packed with BM x BN tiles: the values of
+    relu of this library's GEMM on the unpacked operand."""
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    M, K, N = 390, 200, 264
+    A = _relu_layer_input(M, K, 83, torch.bfloat16)
+    g = torch.Generator(device=DEV).manual_seed(84)
+    W2 = (torch.randn(N, K, device=DEV, generator=g) * K ** -0.5).bfloat16()
+    vals, meta = sf.tiled.dense_to_tilesparse(A, BM, BN)
+    assert torch.equal(sf.tiled.relu_spAx(vals, meta, W2).float(), torch.relu(gemm.mm(A, W2.T).float()))
+    x = torch.randn(K, N, device=DEV, generator=g)
+    y = sf.tiled.relu_sparse_Ax(vals.float(), meta, x)
+    C = torch.empty(M, N, dtype=torch.float32, device=DEV)
+    gemm.mm_f32acc(A, x.bfloat16(), C, False)
+    assert torch.equal(y, torch.relu(C))
     sf.check_status()
