@@ -103,17 +103,19 @@ def arena_elements(tokens, hidm, layers, fill=0.55, expansion=5.25):
     return int(tokens * math.floor(hidm * expansion) * layers * fill)
 
 
-def run_step(x, model, sparse, steps=1):
+def run_step(x, model, sparse, steps=1, exact=False):
     """`steps` training steps (zero_grad, arena rewind, forward, loss =
     mean((y - x)^2), backward) after resetting the peak-memory counter;
     returns (loss, grad_stds * 1e3 with a leading 0, peak MB allocated,
-    ms per step), as old/lib_sparse/prepare.py:80-112."""
+    ms per step), as old/lib_sparse/prepare.py:80-112.  exact=True gives the
+    sparse layers no arena: each keeps a values tensor of exactly its nnz,
+    freed after its own backward."""
     dev = x.device
     gc.collect()
     torch.cuda.empty_cache()
     torch.cuda.reset_peak_memory_stats(dev)
     torch.cuda.synchronize(dev)
-    sparse_data = bs.get_globals()
+    sparse_data = None if exact else bs.get_globals()
     start = time.perf_counter()
     for _ in range(steps):
         model.zero_grad()
@@ -135,7 +137,9 @@ def memory_report(x, model, fill=0.55, steps=2):
     as MB above what was resident before the steps (weights, input, other
     live tensors; the arena counts in the sparse step's), the arena's
     capacity and the fraction of it the last sparse step used, and the
-    largest relative difference of loss and of gradient std between the two."""
+    largest relative difference of loss and of gradient std between the two;
+    then the sparse step again with no arena ("sparse_exact": each layer's
+    values in a tensor of exactly its nnz, freed after its own backward)."""
     layers = len(model.W1s)
     hidm = x.shape[-1]
     bs.init_sparse_buffer(0, x.device, x.dtype)  # no arena while the dense step is measured
@@ -150,6 +154,11 @@ def memory_report(x, model, fill=0.55, steps=2):
     loss_s, gs_s, peak_s, ms_s = run_step(x, model, sparse=True, steps=steps)
     bs.check_status(x.device)
     used = buf.used()
+    del buf
+    bs.init_sparse_buffer(0, x.device, x.dtype)  # the per-layer form holds no arena
+    run_step(x, model, sparse=True, steps=steps, exact=True)  # warm-up
+    loss_e, gs_e, peak_e, ms_e = run_step(x, model, sparse=True, steps=steps, exact=True)
+    bs.check_status(x.device)
     rel = lambda a, b: float(((a.float() - b.float()).abs() / b.float().abs().clamp_min(1e-30)).max())  # noqa: E731
     return {"tokens": x.shape[0], "hidm": hidm, "hidden": model.W1s[0].shape[0], "layers": layers,
             "dtype": str(x.dtype).replace("torch.", ""),
@@ -158,6 +167,9 @@ def memory_report(x, model, fill=0.55, steps=2):
                       "ms_per_step": round(ms_d, 3)},
             "sparse": {"peak_mb": round(peak_s, 1), "above_resident_mb": round(peak_s - resident, 1),
                        "ms_per_step": round(ms_s, 3)},
+            "sparse_exact": {"peak_mb": round(peak_e, 1), "above_resident_mb": round(peak_e - resident, 1),
+                             "ms_per_step": round(ms_e, 3), "loss_rel_diff": rel(loss_e, loss_d),
+                             "grad_std_rel_diff": rel(gs_e[1:], gs_d[1:])},
             "arena": {"capacity_mb": round(cap * x.element_size() / 1024 ** 2, 1),
                       "used_fraction": round(used / cap, 4),
                       "activation_zeros": round(1 - used / (x.shape[0] * model.W1s[0].shape[0] * layers), 4)},

@@ -235,6 +235,8 @@ def _fused_forward(x, W1, W2, vals, offset, b1, act):
     # on a second stream beside the down-projection measured no faster.)
     a, bitmask, prefix, voff, row_offsets = G.ffn_up(x, W1, b1, act, vals, offset, sp24=use_sp24,
                                                      write_act=not use_ck, colmask=colmask)
+    if callable(vals):  # exact-size values: the allocator kept the tensor it made
+        vals = vals.vals
     if use_ck:
         idx, kcount, colpref = G.ck_lists(colmask, T, Fd)
     elif want_live:
@@ -410,12 +412,37 @@ def _arena(sparse_data, numel, like):
     return vals, off
 
 
+class _ExactVals:
+    """Allocator for a layer's own values when no arena is given: called by
+    the up-projection with the layer's nnz once its tiles are counted."""
+
+    def __init__(self, like):
+        self.like, self.vals = like, None
+
+    def __call__(self, n):
+        # at n == 0 a zero-length view of one element: a valid pointer for the
+        # copy, which still writes the tiles' live-column masks
+        self.vals = torch.empty(max(n, 1), dtype=self.like.dtype, device=self.like.device)[:n]
+        return self.vals
+
+
 def _forward(ctx, x, W1, W2, sparse_data, b1, act):
-    vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
-    fused = _fused_ok(x, W1, W2, b1, vals)
-    # one sparseffn:: op (torch.library), so torch.compile traces through it
-    out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = torch.ops.sparseffn.ffn_fwd(
-        x, W1, W2, b1, vals, offset, act)
+    if sparse_data is None and not torch.compiler.is_compiling() and _fused_ok(x, W1, W2, b1, x):
+        # No arena: the layer's values get a tensor of exactly nnz elements
+        # (one device sync for the count), owned by this autograd node and
+        # freed with it after the layer's backward -- no worst-case buffer,
+        # and nothing kept alive for the rest of the backward.
+        holder = _ExactVals(x)
+        offset = torch.zeros(1, dtype=torch.int32, device=x.device)
+        out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = _fused_forward(
+            x, W1, W2, holder, offset, b1, act)
+        vals, fused = holder.vals, True
+    else:
+        vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
+        fused = _fused_ok(x, W1, W2, b1, vals)
+        # one sparseffn:: op (torch.library), so torch.compile traces through it
+        out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = torch.ops.sparseffn.ffn_fwd(
+            x, W1, W2, b1, vals, offset, act)
     T, Fd = x.shape[0], W1.shape[0]
     bm = 128 if fused else 64
     ctx.save_for_backward(x, W1, W2)

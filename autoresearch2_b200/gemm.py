@@ -236,7 +236,10 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
     dense, or with sp24=True an ``sp24.Sp24`` (2:4 form, K = F) written by the
     same epilogue (T, F multiples of 128), or None with write_act=False.
     colmask (optional int32 [tiles * 4]) receives each format tile's live
-    columns (the OR of its rows' mask words)."""
+    columns (the OR of its rows' mask words).  vals is the arena, or a
+    callable alloc(n) -> vals: then the cursor offset (zero on entry) is read
+    back once the tiles are counted (one device sync) and the values are
+    copied into alloc(nnz), a tensor of exactly nnz elements."""
     T, D = x.shape
     F = W1.shape[0]
     dev = x.device
@@ -265,6 +268,8 @@ def ffn_up(x, W1, b1, act, vals, offset, sp24=False, write_act=True, colmask=Non
              ptr(act_out), F, ptr(bitmask), ptr(counts), ptr(slots), ptr(row_offsets), status, st)
     call("sffn_tile_scan_counts", ptr(counts), 4, nt, ptr(prefix), ptr(offset), ptr(vals_offset),
          status, st)
+    if callable(vals):
+        vals = vals(int(offset.item()))
     call("sffn_tile_copy_slots", ptr(slots), ptr(counts), ptr(prefix), ptr(vals_offset), nt, ptr(vals),
          vals.numel(), ptr(row_offsets), ptr(bitmask), ptr(colmask), status, st)
     return act_out, bitmask, prefix, vals_offset, row_offsets

@@ -464,12 +464,20 @@ def bench_deep(device):
     Xavier weights; dense baseline (dense ReLU output kept per layer) against
     the sparse stack over one arena of 0.55 x the dense activation size.
     Peak MB from torch's allocator, ms per step by host clock around
-    synchronised steps (as the harness); eager, no torch.compile."""
+    synchronised steps (as the harness); eager, no torch.compile.  Also the
+    same report at the model's default depth of 12 layers (prepare.py:51),
+    where the arena's saving outgrows the fused path's per-layer transients."""
     from autoresearch2_b200 import deep
     g = torch.Generator(device=device).manual_seed(0)
     x = torch.randn(10000, 4096, generator=g, device=device, dtype=torch.bfloat16)
     model = deep.DeepFFN(torch.bfloat16, layers=4, hidm=4096, device=device)
     r = deep.memory_report(x, model)
+    del model
+    torch.cuda.empty_cache()
+    model = deep.DeepFFN(torch.bfloat16, layers=12, hidm=4096, device=device)
+    r12 = deep.memory_report(x, model)
+    r["layers_12"] = {k: r12[k] for k in ("resident_mb", "dense", "sparse", "sparse_exact", "arena",
+                                          "loss_rel_diff")}
     del model, x
     torch.cuda.empty_cache()
     return r

@@ -88,3 +88,38 @@ def test_memory_report_shows_the_saving():
     assert 0 < r["arena"]["used_fraction"] <= 1
     assert 0.4 < r["arena"]["activation_zeros"] < 0.6
     assert r["loss_rel_diff"] < 2e-2 and r["grad_std_rel_diff"] < 5e-2, r
+    # no arena: each layer's values exactly sized and freed after its backward
+    e = r["sparse_exact"]
+    assert e["peak_mb"] < r["sparse"]["peak_mb"], r
+    assert e["loss_rel_diff"] == r["loss_rel_diff"] and e["grad_std_rel_diff"] == r["grad_std_rel_diff"], r
+
+
+def test_exact_size_values_without_an_arena():
+    """FFNSparse / FFNSpRelu2 given no arena keep each layer's z in a values
+    tensor of exactly its nnz: the same output, gradients and packed z as the
+    same layer over an arena (bit for bit), vals sized to prefix[-1]."""
+    import autoresearch2_b200 as sf
+    for fn in (sf.FFNSparse, sf.FFNSpRelu2):
+        x = inputs(1000, 512, seed=5).requires_grad_()
+        model = deep.DeepFFN(torch.bfloat16, layers=1, hidm=512)
+        W1, W2 = model.W1s[0], model.W2s[0]
+        arena = (torch.empty(1000 * W1.shape[0], dtype=torch.bfloat16, device="cuda"),
+                 torch.zeros(1, dtype=torch.int32, device="cuda"))
+        outs, grads = [], []
+        for sd in (arena, None):
+            y = fn.apply(x, W1, W2, sd)
+            z = y.grad_fn.z_sparse
+            if sd is None:
+                assert z.vals.numel() == int(z.prefix[-1].item()) > 0
+                assert z.vals.untyped_storage().nbytes() == z.vals.numel() * 2
+            else:
+                packed = z.vals[:int(z.prefix[-1].item())].clone()
+            outs.append((y.detach().clone(), z.vals[:int(z.prefix[-1].item())].clone()))
+            g = torch.randn_like(y)
+            grads.append(torch.autograd.grad(y, (x, W1, W2), g if not grads else grads[0][3]))
+            grads[-1] = (*grads[-1], g)
+        assert torch.equal(outs[0][0], outs[1][0])
+        assert torch.equal(outs[1][1].view(torch.int16), packed.view(torch.int16))
+        for a, b in zip(grads[0][:3], grads[1][:3]):
+            assert torch.equal(a, b)
+    sf.check_status()
