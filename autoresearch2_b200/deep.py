@@ -130,6 +130,30 @@ def run_step(x, model, sparse, steps=1, exact=False):
     return loss.detach().cpu(), torch.stack(grad_stds) * 1e3, peak, ms
 
 
+def steady_ms(x, model, sparse, exact=False, steps=4, warmup=2):
+    """ms per training step as run_step takes it, but with the allocator's
+    cache kept between steps (run_step empties it first, so its first step
+    also pays for fresh device allocations): `warmup` untimed steps, then
+    `steps` timed by host clock around synchronised steps."""
+    dev = x.device
+    sparse_data = None if exact else bs.get_globals()
+
+    def step():
+        model.zero_grad()
+        bs.reset_sparse_globals()
+        y = model.forward_sparse(x, sparse_data) if sparse else model.forward_base(x, sparse_data)
+        (y - x).pow(2).mean().backward()
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    start = time.perf_counter()
+    for _ in range(steps):
+        step()
+    torch.cuda.synchronize(dev)
+    return (time.perf_counter() - start) * 1000 / steps
+
+
 def memory_report(x, model, fill=0.55, steps=2):
     """Dense and sparse steps of the same model on the same input, each after
     one warm-up step (the reference's evaluate(), prepare.py:115-148, with its
@@ -139,7 +163,8 @@ def memory_report(x, model, fill=0.55, steps=2):
     capacity and the fraction of it the last sparse step used, and the
     largest relative difference of loss and of gradient std between the two;
     then the sparse step again with no arena ("sparse_exact": each layer's
-    values in a tensor of exactly its nnz, freed after its own backward)."""
+    values in a tensor of exactly its nnz, freed after its own backward).
+    steady_ms_per_step: the same steps with the allocator's cache kept."""
     layers = len(model.W1s)
     hidm = x.shape[-1]
     bs.init_sparse_buffer(0, x.device, x.dtype)  # no arena while the dense step is measured
@@ -148,27 +173,31 @@ def memory_report(x, model, fill=0.55, steps=2):
     resident = torch.cuda.memory_allocated(x.device) / 1024 ** 2  # weights, input, anything else live
     run_step(x, model, sparse=False, steps=1)  # warm-up
     loss_d, gs_d, peak_d, ms_d = run_step(x, model, sparse=False, steps=steps)
+    st_d = steady_ms(x, model, sparse=False)
     cap = arena_elements(x.shape[0], hidm, layers, fill, model.W1s[0].shape[0] / hidm)
     buf = bs.init_sparse_buffer(cap, x.device, x.dtype)
     run_step(x, model, sparse=True, steps=steps)  # warm-up
     loss_s, gs_s, peak_s, ms_s = run_step(x, model, sparse=True, steps=steps)
+    st_s = steady_ms(x, model, sparse=True)
     bs.check_status(x.device)
     used = buf.used()
     del buf
     bs.init_sparse_buffer(0, x.device, x.dtype)  # the per-layer form holds no arena
     run_step(x, model, sparse=True, steps=steps, exact=True)  # warm-up
     loss_e, gs_e, peak_e, ms_e = run_step(x, model, sparse=True, steps=steps, exact=True)
+    st_e = steady_ms(x, model, sparse=True, exact=True)
     bs.check_status(x.device)
     rel = lambda a, b: float(((a.float() - b.float()).abs() / b.float().abs().clamp_min(1e-30)).max())  # noqa: E731
     return {"tokens": x.shape[0], "hidm": hidm, "hidden": model.W1s[0].shape[0], "layers": layers,
             "dtype": str(x.dtype).replace("torch.", ""),
             "resident_mb": round(resident, 1),
             "dense": {"peak_mb": round(peak_d, 1), "above_resident_mb": round(peak_d - resident, 1),
-                      "ms_per_step": round(ms_d, 3)},
+                      "ms_per_step": round(ms_d, 3), "steady_ms_per_step": round(st_d, 3)},
             "sparse": {"peak_mb": round(peak_s, 1), "above_resident_mb": round(peak_s - resident, 1),
-                       "ms_per_step": round(ms_s, 3)},
+                       "ms_per_step": round(ms_s, 3), "steady_ms_per_step": round(st_s, 3)},
             "sparse_exact": {"peak_mb": round(peak_e, 1), "above_resident_mb": round(peak_e - resident, 1),
-                             "ms_per_step": round(ms_e, 3), "loss_rel_diff": rel(loss_e, loss_d),
+                             "ms_per_step": round(ms_e, 3), "steady_ms_per_step": round(st_e, 3),
+                             "loss_rel_diff": rel(loss_e, loss_d),
                              "grad_std_rel_diff": rel(gs_e[1:], gs_d[1:])},
             "arena": {"capacity_mb": round(cap * x.element_size() / 1024 ** 2, 1),
                       "used_fraction": round(used / cap, 4),
