@@ -427,11 +427,14 @@ class _ExactVals:
 
 
 def _forward(ctx, x, W1, W2, sparse_data, b1, act):
-    if sparse_data is None and not torch.compiler.is_compiling() and _fused_ok(x, W1, W2, b1, x):
+    if (sparse_data is None and not torch.compiler.is_compiling() and _fused_ok(x, W1, W2, b1, x)
+            and not torch.cuda.is_current_stream_capturing()):
         # No arena: the layer's values get a tensor of exactly nnz elements
         # (one device sync for the count), owned by this autograd node and
         # freed with it after the layer's backward -- no worst-case buffer,
-        # and nothing kept alive for the rest of the backward.
+        # and nothing kept alive for the rest of the backward.  (Traced or
+        # captured into a CUDA graph, where the count cannot be read back, the
+        # layer takes a worst-case buffer instead.)
         holder = _ExactVals(x)
         offset = torch.zeros(1, dtype=torch.int32, device=x.device)
         out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = _fused_forward(
