@@ -161,11 +161,15 @@ def dense_to_tilesparse(dense: torch.Tensor, vals: torch.Tensor, offset: torch.T
     """Pack `dense` [M, N] into the tiled format (old/lib_sparse/sparse.py:154-210).
 
     Mutates the arena: values go to vals[offset + prefix[t] ...] and `offset`
-    (int32[1], device) advances by the number of values, with no host sync."""
-    require_cuda(dense, vals, offset)
+    (int32[1], device) advances by the number of values, with no host sync.
+    vals may instead be a callable alloc(n) -> vals (offset zero on entry):
+    the tiles are counted first, the total read back (one device sync), and
+    the values packed into alloc(nnz), a tensor of exactly nnz elements."""
+    exact = callable(vals)
+    require_cuda(dense, offset, *(() if exact else (vals,)))
     if dense.dim() != 2:
         raise ValueError("dense must be 2-D")
-    if vals.dtype != dense.dtype or vals.dim() != 1 or not vals.is_contiguous():
+    if not exact and (vals.dtype != dense.dtype or vals.dim() != 1 or not vals.is_contiguous()):
         raise ValueError("vals must be a contiguous 1-D tensor of dense's dtype")
     if offset.dtype != torch.int32 or offset.numel() != 1:
         raise ValueError("offset must be an int32 tensor with one element")
@@ -180,9 +184,20 @@ def dense_to_tilesparse(dense: torch.Tensor, vals: torch.Tensor, offset: torch.T
     vals_offset = torch.empty(1, dtype=torch.int32, device=dev)
     lib = _lib.load()
     ws = _lib.workspace(lib.sffn_tile_workspace_bytes(M, N, BLOCK_M, BLOCK_N), dev)
+    status = ptr(_lib.status_word(dev))
+    if exact:
+        # mask, prefix and cursor first (no values), then exactly nnz values
+        call("sffn_tile_pack", ptr(dense), code, M, N, dense.stride(0), BLOCK_M, BLOCK_N, ptr(bitmask),
+             ptr(prefix), None, 0, ptr(offset), ptr(vals_offset), ptr(ws), ws.numel(), status, stream_ptr(dev))
+        n = int(offset.item())
+        vals = vals(n)
+        if n:
+            call("sffn_tile_pack_values", ptr(dense), code, M, N, dense.stride(0), BLOCK_M, BLOCK_N,
+                 ptr(bitmask), ptr(prefix), ptr(vals), n, ptr(vals_offset), status, stream_ptr(dev))
+        return BitsparseTensor(vals, bitmask, prefix, vals_offset, gm, gn, BLOCK_M, BLOCK_N, (M, N))
     call("sffn_tile_pack", ptr(dense), code, M, N, dense.stride(0), BLOCK_M, BLOCK_N, ptr(bitmask),
          ptr(prefix), ptr(vals), vals.numel(), ptr(offset), ptr(vals_offset), ptr(ws), ws.numel(),
-         ptr(_lib.status_word(dev)), stream_ptr(dev))
+         status, stream_ptr(dev))
     return BitsparseTensor(vals, bitmask, prefix, vals_offset, gm, gn, BLOCK_M, BLOCK_N, (M, N))
 
 

@@ -427,8 +427,9 @@ class _ExactVals:
 
 
 def _forward(ctx, x, W1, W2, sparse_data, b1, act):
-    if (sparse_data is None and not torch.compiler.is_compiling() and _fused_ok(x, W1, W2, b1, x)
-            and not torch.cuda.is_current_stream_capturing()):
+    exact = (sparse_data is None and not torch.compiler.is_compiling()
+             and all(t.is_cuda for t in (x, W1, W2)) and not torch.cuda.is_current_stream_capturing())
+    if exact and _fused_ok(x, W1, W2, b1, x):
         # No arena: the layer's values get a tensor of exactly nnz elements
         # (one device sync for the count), owned by this autograd node and
         # freed with it after the layer's backward -- no worst-case buffer,
@@ -440,6 +441,16 @@ def _forward(ctx, x, W1, W2, sparse_data, b1, act):
         out, bitmask, prefix, voff, row_offsets, kb_list, kb_count = _fused_forward(
             x, W1, W2, holder, offset, b1, act)
         vals, fused = holder.vals, True
+    elif exact and x.dtype == W1.dtype == W2.dtype and x.dtype in (torch.float32, torch.float16):
+        # the float32 / float16 path likewise: the 64x64 pack counts first
+        holder = _ExactVals(x)
+        offset = torch.zeros(1, dtype=torch.int32, device=x.device)
+        out, z = _unfused_forward(x, W1, W2, holder, offset, b1, act)
+        vals, bitmask, prefix, voff = z.vals, z.bitmask, z.prefix, z.vals_offset
+        # no per-row offsets or K-block lists on this path (the op's empty forms)
+        row_offsets, kb_count = (torch.empty(0, dtype=torch.int32, device=x.device) for _ in range(2))
+        kb_list = torch.empty(0, 0, dtype=torch.int32, device=x.device)
+        fused = False
     else:
         vals, offset = _arena(sparse_data, x.shape[0] * W1.shape[0], x)
         fused = _fused_ok(x, W1, W2, b1, vals)

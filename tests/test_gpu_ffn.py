@@ -211,3 +211,33 @@ def test_ffn_ragged_shapes_against_oracle(act, backward, T, D, F):
     finally:
         sf.ffn.set_sparse_mma(prev_mma)
         sf.set_backward(prev_bw)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16])
+def test_exact_size_values_on_the_64x64_path(dtype):
+    """float32 / float16 layers given no arena: the 64x64 pack counts first
+    and keeps exactly nnz values; output and gradients the same bits as the
+    same layer over an arena, the packed values equal."""
+    import autoresearch2_b200 as sf
+    g = torch.Generator(device=DEV).manual_seed(91)
+    T, D, F = 300, 64, 200
+    x = torch.randn(T, D, device=DEV, generator=g).to(dtype).requires_grad_()
+    W1 = (torch.randn(F, D, device=DEV, generator=g) * D ** -0.5).to(dtype).requires_grad_()
+    W2 = (torch.randn(D, F, device=DEV, generator=g) * F ** -0.5).to(dtype).requires_grad_()
+    b1 = torch.full((F,), -0.3, device=DEV, dtype=dtype, requires_grad=True)
+    dout = torch.randn(T, D, device=DEV, generator=g).to(dtype)
+    res = []
+    for sd in ((torch.empty(T * F, dtype=dtype, device=DEV), torch.zeros(1, dtype=torch.int32, device=DEV)),
+               None):
+        out = sf.FFNSpRelu2.apply(x, W1, W2, sd, b1)
+        z = out.grad_fn.z_sparse
+        n = int(z.prefix[-1].item())
+        if sd is None:
+            assert z.vals.numel() == n > 0 and z.BLOCK_M == 64
+        vals = z.vals[int(z.vals_offset.item()):][:n].clone()
+        grads = torch.autograd.grad(out, (x, W1, W2, b1), dout)
+        res.append((out.detach(), vals, grads))
+    assert torch.equal(res[0][0], res[1][0]) and torch.equal(res[0][1], res[1][1])
+    for a, b in zip(res[0][2], res[1][2]):
+        assert torch.equal(a, b)
+    sf.check_status()
