@@ -118,3 +118,22 @@ def test_python_api_refuses_cpu_tensors():
     import autoresearch2_b200 as sf
     with pytest.raises(ValueError, match="CUDA"):
         sf.bitsparse_pack(torch.zeros(4, 4))
+
+
+def test_relu_products_refuse_cpu_tensors():
+    """The (vals, meta) products and the TF32 / ReLU GEMM helpers raise on CPU
+    tensors before any device call; an unknown input_precision is rejected."""
+    import torch
+    import autoresearch2_b200 as sf
+    from autoresearch2_b200 import gemm
+    x, W1 = torch.randn(64, 32), torch.randn(96, 32)
+    meta = {"bitmask": torch.zeros(1024, dtype=torch.uint8), "prefix": torch.zeros(2, dtype=torch.int32),
+            "grid_m": 1, "grid_n": 1, "BLOCK_M": 128, "BLOCK_N": 128, "shape": (64, 96)}
+    calls = [lambda: sf.tiled.sparse_relu_Ax(W1, x), lambda: sf.tiled.sp_relu_Ax(W1, x),
+             lambda: sf.tiled.relu_spAx(torch.zeros(4), meta, torch.randn(16, 96)),
+             lambda: sf.tiled.relu_sparse_Ax(torch.zeros(4), meta, torch.randn(96, 8)),
+             lambda: gemm.matmul_tf32(x, W1), lambda: gemm.round_tf32(x),
+             lambda: gemm.mm_relu(x.bfloat16(), W1.T.bfloat16())]
+    for c in calls:
+        with pytest.raises(ValueError, match="CUDA"):
+            c()
