@@ -89,6 +89,22 @@ def bitsparse_pack_async(dense: torch.Tensor, vals_out: torch.Tensor):
     return vals_out, mask, nnz
 
 
+def compress_dense(dense: torch.Tensor, shape, block: int = 2048):
+    """The flat pack under its earlier name and signature
+    (old/bitpack/train.py:65-103): dense [rows, cols] with shape = (rows,
+    cols) -> (vals, packed_mask), as bitsparse_pack."""
+    rows, cols = (int(d) for d in shape)
+    if dense.numel() != rows * cols:
+        raise ValueError(f"dense has {dense.numel()} elements, shape {tuple(shape)} needs {rows * cols}")
+    return bitsparse_pack(dense.reshape(rows, cols), block)
+
+
+def reconstruct_bitmask(vals: torch.Tensor, packed_mask: torch.Tensor, shape, block: int = 8192):
+    """The flat unpack under its earlier name (old/bitunpack/train.py:55-90),
+    as bitsparse_unpack."""
+    return bitsparse_unpack(vals, packed_mask, shape, block)
+
+
 def bitsparse_unpack(vals: torch.Tensor, packed_mask: torch.Tensor, shape, block: int = 8192):
     """Rebuild the dense tensor of `shape` (old/sparse_unpack.py:57-97)."""
     require_cuda(vals, packed_mask)

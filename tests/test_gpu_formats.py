@@ -82,6 +82,24 @@ def test_flat_against_oracle(dtype, rows, cols, p):
     bits_equal(to_np(out), oracle.flat_unpack(ov, om, d.shape))
 
 
+@pytest.mark.parametrize("rows,cols,p", [(3, 7, 0.5), (257, 333, 0.1)])
+def test_flat_under_its_earlier_names(rows, cols, p):
+    """compress_dense / reconstruct_bitmask (old/bitpack/train.py:65,
+    old/bitunpack/train.py:55) give the oracle's bits, the dense tensor
+    passed flat with its shape as the reference's harness does."""
+    import autoresearch2_b200 as sf
+    d = flat_case(rows, cols, p, torch.bfloat16, seed=rows + cols)
+    vals, mask = sf.compress_dense(d.to(DEV).flatten(), (rows, cols))
+    ov, om = oracle.flat_pack(to_np(d))
+    bits_equal(to_np(mask), om)
+    bits_equal(to_np(vals), ov)
+    out = sf.reconstruct_bitmask(vals, mask, (rows, cols))
+    assert tuple(out.shape) == (rows, cols)
+    bits_equal(to_np(out), oracle.flat_unpack(ov, om, d.shape))
+    with pytest.raises(ValueError):
+        sf.compress_dense(d.to(DEV), (rows, cols + 1))
+
+
 def test_flat_empty():
     import autoresearch2_b200 as sf
     d = torch.zeros(0, 5, device=DEV, dtype=torch.bfloat16)
