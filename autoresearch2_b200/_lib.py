@@ -161,6 +161,18 @@ class KernelTimer:
         return out
 
 
+def _launches(name, args):
+    """Kernels one successful call launched: LAUNCHING's count, except where
+    it depends on the arguments (the float32-output GEMM runs one launch per
+    K chunk of 1024; the tile pack without vals stops after count and scan)."""
+    if name == "sffn_gemm_bf16_f32out":
+        return -(-int(args[10]) // 1024)
+    if name == "sffn_tile_pack":
+        v = args[9]
+        return 2 if v is None or getattr(v, "value", v) in (None, 0) else 3
+    return LAUNCHING.get(name, 0)
+
+
 def call(name, *args):
     """Call a C-ABI entry point and raise SparseFFNError on a non-zero code."""
     global launch_count
@@ -174,7 +186,7 @@ def call(name, *args):
         b.record()
         timer.events.setdefault(name, []).append((a, b))
     if rc == 0:
-        launch_count += LAUNCHING.get(name, 0)
+        launch_count += _launches(name, args)
     if rc != 0:
         msg = lib.sffn_error_string(rc).decode()
         if rc == 5:
