@@ -220,6 +220,25 @@ def spAx(vals, bitmask, prefix, offset, shape, BM, BN, W, square=False):
     return from_f64(to_f64(W, code) @ dense, code)
 
 
+def relu_matmul(A, B, code=F32):
+    """relu(A @ B) in float64 from operands of dtype `code`: the product of
+    sparse_relu_Ax / sp_relu_Ax (relu(x @ W1.T), old/matmul_bitsparse/train.py:
+    45-52, old/full_matmul/train.py:35), relu_spAx (relu(unpack @ W2.T),
+    old/full_matmul/train.py:177-178) and relu_sparse_Ax (relu(A @ x),
+    old/sparse_matmul/train.py:44-50)."""
+    return np.maximum(to_f64(A, code) @ to_f64(B, code), 0.0)
+
+
+def relu_ax_pack(x, W1, BM=128, BN=128):
+    """sparse_relu_Ax (old/matmul_bitsparse/train.py:70-116) for float32: the
+    float64 product rounded to float32, then the tiled pack of its positive
+    entries -> (vals, bitmask, prefix)."""
+    z = relu_matmul(x, np.ascontiguousarray(W1).T).astype(np.float32)
+    arena = np.zeros(z.size, dtype=np.float32)
+    bitmask, prefix, total = tile_pack(z, BM, BN, arena, 0)
+    return arena[:total], bitmask, prefix
+
+
 # ---------------------------------------------------------------------------
 # FFN forward / backward (sparse.py:56-151, prepare_layer.py:12-29,117-162)
 # ---------------------------------------------------------------------------

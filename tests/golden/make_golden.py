@@ -19,6 +19,16 @@ arithmetic):
   * ``FFNSpRelu2.forward`` (``old/lib_sparse/sparse.py:120``) omits the vals
     arena arguments (TypeError in the reference) -> forward is re-run with the
     arena passed; ``backward`` is the reference's own.
+  * ``triton.autotune`` benchmarks its configurations through a GPU driver ->
+    the autotuned kernels of ``old/matmul_bitsparse/train.py`` and
+    ``old/sparse_matmul/train.py`` keep their first configuration only (a
+    single configuration is not benchmarked).
+  * ``old/sparse_matmul/sparse_unpack.py:45,58`` assert ``is_cuda`` -> the
+    ``bitsparse_unpack`` that ``relu_sparse_Ax`` calls launches its kernel the
+    same way without the asserts.
+  The (vals, meta) products use shapes whose sides are multiples of 128: the
+  reference's 128x128 tile kernels bound rows only, and ragged columns wrote
+  out of bounds under the interpreter.
 
 Usage:  python tests/golden/make_golden.py --ref /path/to/reference
 """
@@ -326,17 +336,85 @@ def gen_codec15(ref, out):
         assert math.prod(restored.shape) == n
 
 
+def _load_train(ref, subdir):
+    """train.py of one of the reference's (vals, meta) experiments, with the
+    sparse_pack / sparse_unpack modules it imports by bare name."""
+    path = os.path.join(ref, subdir)
+    sys.path.insert(0, path)
+    for m in ("train", "prepare", "sparse_pack", "sparse_unpack"):
+        sys.modules.pop(m, None)
+    mod = importlib.import_module("train")
+    pack, unpack = sys.modules.get("sparse_pack"), sys.modules.get("sparse_unpack")
+    sys.path.remove(path)
+    return mod, pack, unpack
+
+
+def gen_products(ref, out):
+    """The (vals, meta) products, float32: sparse_relu_Ax
+    (old/matmul_bitsparse/train.py:70-116), sp_relu_Ax + relu_spAx
+    (old/full_matmul/train.py:21-184) and relu_sparse_Ax
+    (old/sparse_matmul/train.py:56-76)."""
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(128, 64, generator=g)
+    W1 = torch.randn(256, 64, generator=g) / 8.0 + 0.02
+    W2 = torch.randn(32, 256, generator=g) / 16.0
+
+    mb, _, _ = _load_train(ref, "old/matmul_bitsparse")
+    mb._matmul_sparse_kernel.configs = mb._matmul_sparse_kernel.configs[:1]
+    vals, meta = mb.sparse_relu_Ax(W1, x)
+    out["products_sparse_relu_Ax_f32"] = dict(
+        x=_np(x), W1=_np(W1), vals=_np(vals), bitmask=_np(meta["bitmask"]), prefix=_np(meta["prefix"]),
+        grid=np.array([meta["grid_m"], meta["grid_n"]]))
+
+    fm, _, _ = _load_train(ref, "old/full_matmul")
+    vals, meta = fm.sp_relu_Ax(W1, x)
+    y = fm.relu_spAx(vals, meta, W2)
+    out["products_full_matmul_f32"] = dict(
+        x=_np(x), W1=_np(W1), W2=_np(W2), vals=_np(vals), bitmask=_np(meta["bitmask"]),
+        prefix=_np(meta["prefix"]), y=_np(y))
+
+    sm, sm_pack, sm_unpack = _load_train(ref, "old/sparse_matmul")
+    sm._matmul_relu_kernel.configs = sm._matmul_relu_kernel.configs[:1]
+
+    def unpack(vals, meta, shape):  # sparse_matmul/sparse_unpack.py:44-73 without its is_cuda asserts
+        outd = torch.empty(*shape, dtype=torch.float32)
+        bm, bn = meta["BLOCK_M"], meta["BLOCK_N"]
+        sm_unpack._unpack_tiles_kernel[(meta["grid_m"], meta["grid_n"])](
+            meta["bitmask"], vals, meta["prefix"], outd, meta["grid_n"], shape[0], shape[1],
+            BLOCK_M=bm, BLOCK_N=bn, TILE_NUMEL=bm * bn, TILE_BYTES=bm * bn // 8, num_warps=8, num_stages=2)
+        return outd
+
+    sm.bitsparse_unpack = unpack
+    A = torch.relu(torch.randn(256, 128, generator=g) + 0.1)
+    xs = torch.randn(128, 96, generator=g)
+    vals, meta = sm_pack.dense_to_tilesparse(A)
+    meta["shape"] = [256, 128]
+    y = sm.relu_sparse_Ax(vals, meta, xs, dtype=torch.float32)
+    out["products_relu_sparse_Ax_f32"] = dict(
+        A=_np(A), x=_np(xs), vals=_np(vals), bitmask=_np(meta["bitmask"]), prefix=_np(meta["prefix"]),
+        y=_np(y))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", required=True, help="path of a checkout of the reference")
+    ap.add_argument("--only", help="generate only the fixtures whose group starts with this "
+                                   "(flat, tiled, ffn, codec15, products)")
     args = ap.parse_args()
     torch.manual_seed(0)
     mods = _import_ref(args.ref)
     out = {}
-    gen_flat(mods, out)
-    gen_tiled(mods, out)
-    gen_ffn(mods, out)
-    gen_codec15(args.ref, out)
+    want = lambda name: args.only is None or name.startswith(args.only)  # noqa: E731
+    if want("flat"):
+        gen_flat(mods, out)
+    if want("tiled"):
+        gen_tiled(mods, out)
+    if want("ffn"):
+        gen_ffn(mods, out)
+    if want("codec15"):
+        gen_codec15(args.ref, out)
+    if want("products"):
+        gen_products(args.ref, out)
     for name, rec in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
         print(name, {k: v.shape for k, v in rec.items()})

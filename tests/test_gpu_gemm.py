@@ -647,3 +647,56 @@ def test_relu_products_on_other_tile_shapes(BM, BN):
     gemm.mm_f32acc(A, x.bfloat16(), C, False)
     assert torch.equal(y, torch.relu(C))
     sf.check_status()
+
+
+def _fixture(name):
+    from conftest import golden
+    return golden(name)
+
+
+@pytest.mark.parametrize("name", ["products_sparse_relu_Ax_f32", "products_full_matmul_f32"])
+def test_relu_Ax_against_the_reference_fixture(name):
+    """sparse_relu_Ax / sp_relu_Ax at float32 accuracy ("ieee"; TF32 off) on the
+    inputs of the reference's own run (tests/golden): mask and prefix the
+    reference's bit for bit (no product lies within 4e-6 of the largest of
+    zero there), values within 1e-5 of the largest."""
+    import autoresearch2_b200 as sf
+    g = _fixture(name)
+    x, W1 = torch.from_numpy(g["x"]).to(DEV), torch.from_numpy(g["W1"]).to(DEV)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    try:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        if name.endswith("full_matmul_f32"):
+            vals, meta = sf.tiled.sp_relu_Ax(W1, x)
+        else:
+            vals, meta = sf.tiled.sparse_relu_Ax(W1, x, input_precision="ieee")
+        assert torch.equal(meta["bitmask"].cpu(), torch.from_numpy(g["bitmask"]))
+        assert torch.equal(meta["prefix"].cpu(), torch.from_numpy(g["prefix"]))
+        want = torch.from_numpy(g["vals"])
+        assert float((vals.cpu() - want).abs().max()) <= 1e-5 * float(want.abs().max())
+        if name.endswith("full_matmul_f32"):
+            # layer 2 from the reference's own layer-1 values
+            W2 = torch.from_numpy(g["W2"]).to(DEV)
+            y = sf.tiled.relu_spAx(torch.from_numpy(g["vals"]).to(DEV),
+                                   {"bitmask": torch.from_numpy(g["bitmask"]).to(DEV),
+                                    "prefix": torch.from_numpy(g["prefix"]).to(DEV), "grid_m": 1,
+                                    "grid_n": 2, "BLOCK_M": 128, "BLOCK_N": 128, "shape": (128, 256)}, W2)
+            yw = torch.from_numpy(g["y"])
+            assert float((y.cpu() - yw).abs().max()) <= 1e-5 * float(yw.abs().max())
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    sf.check_status()
+
+
+def test_relu_sparse_Ax_against_the_reference_fixture():
+    """relu_sparse_Ax at float32 ("ieee") on the reference's packed A and x
+    (tests/golden): within 1e-5 of the largest output of its run."""
+    import autoresearch2_b200 as sf
+    g = _fixture("products_relu_sparse_Ax_f32")
+    meta = {"bitmask": torch.from_numpy(g["bitmask"]).to(DEV), "prefix": torch.from_numpy(g["prefix"]).to(DEV),
+            "grid_m": 2, "grid_n": 1, "BLOCK_M": 128, "BLOCK_N": 128, "shape": [256, 128]}
+    y = sf.tiled.relu_sparse_Ax(torch.from_numpy(g["vals"]).to(DEV), meta, torch.from_numpy(g["x"]).to(DEV),
+                                dtype=torch.float32)
+    yw = torch.from_numpy(g["y"])
+    assert y.dtype == torch.float32 and float((y.cpu() - yw).abs().max()) <= 1e-5 * float(yw.abs().max())
+    sf.check_status()

@@ -152,3 +152,41 @@ def test_codec15_sign_lands_on_the_next_field():
         if (15 * (i + 1)) % 8:
             want[i + 1] = 1
         np.testing.assert_array_equal(got, want)
+
+
+@pytest.mark.parametrize("name", ["products_sparse_relu_Ax_f32", "products_full_matmul_f32"])
+def test_relu_ax_pack_matches_reference(name):
+    """relu(x @ W1.T) packed as (vals, meta) by the reference (its Triton
+    product under the interpreter, or F.linear) against the oracle's float64
+    product rounded to float32: mask and prefix bit for bit, values within
+    1e-5 of the largest."""
+    g = golden(name)
+    vals, bitmask, prefix = oracle.relu_ax_pack(g["x"], g["W1"])
+    np.testing.assert_array_equal(bitmask, g["bitmask"])
+    np.testing.assert_array_equal(prefix, g["prefix"])
+    np.testing.assert_allclose(vals, g["vals"], rtol=0, atol=1e-5 * np.abs(vals).max())
+
+
+def test_relu_spAx_matches_reference():
+    """Layer 2 of old/full_matmul: relu(unpack(vals, meta) @ W2.T) from the
+    reference's own layer-1 values, within 1e-5 of the largest output."""
+    g = golden("products_full_matmul_f32")
+    M, N = g["x"].shape[0], g["W1"].shape[0]
+    A = oracle.tile_unpack(g["vals"], g["bitmask"], g["prefix"], 0, (M, N), 128, 128)
+    want = oracle.relu_matmul(A, np.ascontiguousarray(g["W2"]).T)
+    np.testing.assert_allclose(g["y"], want, rtol=0, atol=1e-5 * np.abs(want).max())
+
+
+def test_relu_sparse_Ax_matches_reference():
+    """old/sparse_matmul: the reference's pack of A round-trips through the
+    oracle, and relu(A @ x) (float32 operands, "ieee") is within 1e-5 of the
+    largest output."""
+    g = golden("products_relu_sparse_Ax_f32")
+    A = g["A"]
+    arena = np.zeros(A.size, dtype=np.float32)
+    bitmask, prefix, total = oracle.tile_pack(A, 128, 128, arena, 0)
+    np.testing.assert_array_equal(bitmask, g["bitmask"])
+    np.testing.assert_array_equal(prefix, g["prefix"])
+    np.testing.assert_array_equal(arena[:total].view(np.uint8), g["vals"].view(np.uint8))
+    want = oracle.relu_matmul(A, g["x"])
+    np.testing.assert_allclose(g["y"], want, rtol=0, atol=1e-5 * np.abs(want).max())
