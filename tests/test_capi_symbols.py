@@ -137,3 +137,18 @@ def test_relu_products_refuse_cpu_tensors():
     for c in calls:
         with pytest.raises(ValueError, match="CUDA"):
             c()
+
+
+def test_launch_accounting():
+    """Kernels counted per successful call (the bench's gpu_launches): the
+    table's count, one launch per 1024-wide K chunk of the float32-output
+    GEMM, two for the tile pack without values (count and scan), three with."""
+    from autoresearch2_b200 import _lib
+    vp = ctypes.c_void_p
+    assert _lib._launches("sffn_gemm_bf16_f32out", [None] * 10 + [6 * 3072]) == 18
+    assert _lib._launches("sffn_gemm_bf16_f32out", [None] * 10 + [100]) == 1
+    assert _lib._launches("sffn_tile_pack", [None] * 9 + [None]) == 2
+    assert _lib._launches("sffn_tile_pack", [None] * 9 + [vp(0)]) == 2
+    assert _lib._launches("sffn_tile_pack", [None] * 9 + [vp(4096)]) == 3
+    assert _lib._launches("sffn_ffn_up", []) == 1 and _lib._launches("sffn_version", []) == 0
+    assert set(_lib.LAUNCHING) <= set(_lib.SIGNATURES)
