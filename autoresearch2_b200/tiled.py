@@ -160,10 +160,9 @@ def relu_spAx(vals: torch.Tensor, meta: dict, W2: torch.Tensor, row_batch: int =
     if vals.dtype != W2.dtype:
         raise TypeError("vals and W2 must share a dtype")
     z = _as_bitsparse(vals, meta, (M, K))
-    BM = z.BLOCK_M
+    # batches start on 256-row boundaries: whole K-block list rows, and whole
+    # tile rows for every tile height the format has (32, 64, 128)
     row_batch = max(256, (row_batch // 256) * 256)
-    if row_batch % BM:
-        row_batch = BM * max(1, row_batch // BM)
     lists = None
     if W2.dtype == torch.bfloat16 and z.BLOCK_M == 128 and z.BLOCK_N == 128:
         lists = G.live_kblocks(z.bitmask, M, K)
